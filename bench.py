@@ -1,0 +1,515 @@
+#!/usr/bin/env python
+"""Benchmark of the KernelForge hot path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload ...]
+
+Headline: the RMSNorm bf16 sweep, rows x hidden in
+{4096, 32768, 262144} x {1024, 2048, 4096, 8192}. One STEP normalises all 12 sweep tensors
+once (18.4 GB of HBM traffic per GPU, far above the 126 MB L2). ``value`` is the aggregate
+achieved HBM GB/s over all ranks with inputs resident in HBM; ``e2e`` is the same metric with
+the inputs copied from pinned host memory and the outputs copied back inside the timed region.
+
+Secondary workloads in the same line (``workloads``): SANA linear attention configs
+(B=4,H=36,N=4096) and (B=2,H=70,N=16384), bf16 in/out, each step one ``qkv_attn_matmul`` call.
+
+Multi-GPU: one process per GPU (torchrun), weak scaling -- every rank processes its own
+full-size shard, no collective on the data path; NCCL only takes the max of the per-rank
+device times and gathers per-rank output checksums after the timed region.
+
+``--impl reference`` times the reference algorithm's CPU restatement (``oracle/``) on the
+host cores on a bounded sample of the same workload (rank 0 only).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+BASELINE_METRIC = "achieved HBM GB/s (RMSNorm, SANA-attn) & TFLOP/s (FA-JVP) vs B200 peak, 1–8 GPU"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+L2_BYTES = 126 * 1024 * 1024
+
+SWEEP_ROWS = (4096, 32768, 262144)
+SWEEP_HIDDEN = (1024, 2048, 4096, 8192)
+SANA_CONFIGS = (
+    {"name": "sana_cfg1", "B": 4, "H": 36, "N": 4096, "D": 32},
+    {"name": "sana_cfg2", "B": 2, "H": 70, "N": 16384, "D": 32},
+)
+
+# DRAM bytes per launch of the dominant RMSNorm launch (262144 x 8192 bf16) from ncu
+# (dram__bytes_read.sum + dram__bytes_write.sum); None until a capture is summarised in profiles/.
+RMSNORM_NCU_TRAFFIC_BYTES = None
+
+
+# ---------------------------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------------------------
+def load_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            return json.loads(path.read_text()), "measured"
+        except (OSError, ValueError):
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        self.enabled = self.world > 1
+
+    def init(self):
+        if self.enabled:
+            torch.cuda.set_device(self.local_rank)
+            torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=180),
+                                                 device_id=torch.device("cuda", self.local_rank))
+        else:
+            torch.cuda.set_device(0)
+
+    def barrier(self):
+        if self.enabled:
+            torch.distributed.barrier()
+
+    def max(self, value: float) -> float:
+        if not self.enabled:
+            return value
+        t = torch.tensor([value], dtype=torch.float64, device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    def gather(self, value: float):
+        if not self.enabled:
+            return [value]
+        t = torch.tensor([value], dtype=torch.float64, device="cuda")
+        out = [torch.zeros_like(t) for _ in range(self.world)]
+        torch.distributed.all_gather(out, t)
+        return [float(x.item()) for x in out]
+
+    def close(self):
+        if self.enabled:
+            torch.distributed.destroy_process_group()
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons while the timed regions run."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        self.file.seek(0)
+        rows = [line.strip().split(", ") for line in self.file.read().splitlines() if line.strip()]
+        os.unlink(self.file.name)
+        samples = []
+        for r in rows:
+            try:
+                samples.append(dict(sm=float(r[1]), smax=float(r[2]), util=float(r[4]),
+                                    hw=r[6] == "Active", hwt=r[7] == "Active", swt=r[8] == "Active",
+                                    pcap=r[9] == "Active"))
+            except (IndexError, ValueError):
+                continue
+        if not samples:
+            return None
+        loaded = [s for s in samples if s["util"] >= 50] or samples
+        reasons = sorted({name for s in loaded for name, key in (("hw_slowdown", "hw"),
+                          ("hw_thermal_slowdown", "hwt"), ("sw_thermal_slowdown", "swt"),
+                          ("sw_power_cap", "pcap")) if s[key]})
+        return {"sm_mhz": statistics.median(s["sm"] for s in loaded),
+                "sm_max_mhz": max(s["smax"] for s in loaded), "reasons": reasons,
+                "samples": len(samples), "samples_under_load": len([s for s in samples if s["util"] >= 50])}
+
+
+def time_region(step, steps, warmup, dist, dominant=None):
+    """Warm up, then time exactly `steps` calls of step(i) between barriers + synchronize.
+
+    Returns (max-over-ranks ms per step, average ms of the dominant launch or None)."""
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    if dominant is not None:
+        dominant.clear()
+    start.record()
+    for i in range(steps):
+        step(i)
+    end.record()
+    end.synchronize()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = dist.max(start.elapsed_time(end)) / steps
+    dom = None
+    if dominant:
+        dom = dist.max(sum(a.elapsed_time(b) for a, b in dominant) / len(dominant))
+    return ms, dom
+
+
+class LaunchTimer(list):
+    """Collects (start, end) CUDA event pairs around the dominant kernel's launches."""
+
+    def around(self, fn):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        out = fn()
+        b.record()
+        self.append((a, b))
+        return out
+
+
+def roofline(alg_bytes_or_flops, ms, peak, unit, bound, traffic=None):
+    achieved = alg_bytes_or_flops / (ms / 1e3) / 1e9 if unit == "GB/s" else alg_bytes_or_flops / (ms / 1e3) / 1e12
+    return {"bound": bound, "achieved": round(achieved, 1), "peak": peak, "unit": unit,
+            "frac": round(achieved / peak, 4), "traffic": traffic}
+
+
+def cpu_threads():
+    n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    return n
+
+
+# ---------------------------------------------------------------------------------------------
+# RMSNorm sweep
+# ---------------------------------------------------------------------------------------------
+def sweep_points():
+    return [(r, h) for r in SWEEP_ROWS for h in SWEEP_HIDDEN]
+
+
+def rmsnorm_bytes(rows, hidden):
+    return 2 * rows * hidden * 2 + 2 * hidden
+
+
+def bench_rmsnorm(args, dist, peaks, peak_kind):
+    from kernelforge_b200.rmsnorm import rms_norm, rmsnorm_into
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    gen = torch.Generator(device=dev).manual_seed(1234 + dist.rank)
+    xs, ws, ys = [], [], []
+    for rows, hidden in sweep_points():
+        xs.append(torch.randn(rows, hidden, device=dev, dtype=torch.bfloat16, generator=gen))
+        ws.append((1 + 0.1 * torch.randn(hidden, device=dev, generator=gen)).to(torch.bfloat16))
+        ys.append(torch.empty(rows, hidden, device=dev, dtype=torch.bfloat16))
+    dominant_index = len(xs) - 1  # 262144 x 8192
+    timer = LaunchTimer()
+
+    def step(_):
+        for j, (x, w, y) in enumerate(zip(xs, ws, ys)):
+            if j == dominant_index:
+                timer.around(lambda: rmsnorm_into(x, w, y, 1e-6))
+            else:
+                rmsnorm_into(x, w, y, 1e-6)
+
+    ms, dom_ms = time_region(step, args.steps, args.warmup, dist, timer)
+    per_gpu_bytes = sum(rmsnorm_bytes(r, h) for r, h in sweep_points())
+    value = dist.world * per_gpu_bytes / (ms / 1e3) / 1e9
+    checksums = dist.gather(float(sum(y.float().sum().item() for y in ys[:3])))
+    dom_bytes = rmsnorm_bytes(*sweep_points()[dominant_index])
+    result = {
+        "value": round(value, 1), "unit": "GB/s", "ms_per_step": round(ms, 4),
+        "gpu_launches": len(xs) * args.steps,
+        "roofline": roofline(dom_bytes, dom_ms, peaks["hbm_gbs"], "GB/s", "hbm",
+                             RMSNORM_NCU_TRAFFIC_BYTES),
+        "roofline_note": f"dominant launch rmsnorm 262144x8192 bf16, {dom_ms * 1e3:.1f} us avg; "
+                         f"peak = {peak_kind} HBM copy GB/s",
+        "gathered_checksums": len(checksums),
+    }
+    if not args.no_e2e:
+        result["e2e"] = rmsnorm_e2e(args, dist, xs, ws, rms_norm)
+    del xs, ys
+    torch.cuda.empty_cache()
+    if dist.world == 1 and dist.rank == 0 and not args.no_cpu:
+        result["cpu_baseline"] = rmsnorm_cpu_baseline(seconds=args.cpu_seconds)
+    return result
+
+
+def rmsnorm_e2e(args, dist, xs, ws, rms_norm):
+    """Same sweep through the public API, inputs from pinned host memory, outputs back to host."""
+    dev = xs[0].device
+    biggest = max(x.numel() for x in xs)
+    try:
+        host_in = torch.empty(biggest, dtype=torch.bfloat16, pin_memory=True)
+        host_out = torch.empty(biggest, dtype=torch.bfloat16, pin_memory=True)
+    except RuntimeError as exc:
+        return {"value": None, "unit": "GB/s", "error": f"pinned host allocation failed: {exc}"}
+    host_in.copy_(xs[-1].view(-1))  # real input data in the pinned staging buffer
+    dev_in = [torch.empty_like(x) for x in xs]
+    kernels = [rms_norm(1, x.shape[0], x.shape[1], 1e-6, "bfloat16") for x in xs]
+    h2d = sum(x.numel() * 2 for x in xs)
+    d2h = h2d
+
+    def step(_):
+        for x_dev, w, kern in zip(dev_in, ws, kernels):
+            n = x_dev.numel()
+            x_dev.view(-1).copy_(host_in[:n], non_blocking=True)
+            y = kern(x_dev.view(1, *x_dev.shape), w)
+            host_out[:n].copy_(y.view(-1), non_blocking=True)
+
+    steps = max(2, min(args.steps, args.e2e_steps))
+    ms, _ = time_region(step, steps, min(args.warmup, 2), dist)
+    per_gpu = sum(rmsnorm_bytes(r, h) for r, h in sweep_points())
+    del dev_in
+    return {"value": round(dist.world * per_gpu / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
+            "ms_per_step": round(ms, 3), "api": "kernelforge_b200.rmsnorm.rms_norm(...)(X, Weight)"}
+
+
+def rmsnorm_cpu_sample_rows():
+    return 1024
+
+
+def rmsnorm_cpu_baseline(seconds=10.0):
+    """oracle.rmsnorm on the host cores over a bounded sample: the first 1024 rows of each sweep
+    tensor (fp32 statistics, bf16 in/out), repeated until ~`seconds` elapsed."""
+    from oracle.rmsnorm import rmsnorm_forward
+
+    cores = cpu_threads()
+    g = torch.Generator().manual_seed(0)
+    rows = rmsnorm_cpu_sample_rows()
+    data = [(torch.randn(min(rows, r), h, generator=g).to(torch.bfloat16),
+             (1 + 0.1 * torch.randn(h, generator=g)).to(torch.bfloat16)) for r, h in sweep_points()]
+    nbytes = sum(rmsnorm_bytes(x.shape[0], x.shape[1]) for x, _ in data)
+    for x, w in data:  # warm-up
+        rmsnorm_forward(x, w, 1e-6)
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        for x, w in data:
+            rmsnorm_forward(x, w, 1e-6)
+        reps += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+            "sample": f"first {rows} rows of each of the 12 sweep tensors (bf16), {reps} passes of "
+                      f"{nbytes / 1e6:.0f} MB, oracle/rmsnorm.py (torch CPU, {cores} threads)"}
+
+
+# ---------------------------------------------------------------------------------------------
+# SANA linear attention
+# ---------------------------------------------------------------------------------------------
+def sana_bytes(cfg):
+    c = cfg["H"] * cfg["D"]
+    return 2 * cfg["B"] * cfg["N"] * 3 * c + 2 * cfg["B"] * cfg["N"] * c
+
+
+def bench_sana(args, dist, peaks, peak_kind, cfg):
+    from kernelforge_b200.SANA_LinearAttention import qkv_attn_matmul
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    B, H, N, D = cfg["B"], cfg["H"], cfg["N"], cfg["D"]
+    gen = torch.Generator(device=dev).manual_seed(77 + dist.rank)
+    one = 2 * B * N * 3 * H * D
+    copies = max(1, math.ceil(2 * L2_BYTES / one))  # rotate inputs so each step's data is not L2-hot
+    qkvs = [torch.randn(B, N, 3, H * D, device=dev, dtype=torch.bfloat16, generator=gen) for _ in range(copies)]
+    fn = qkv_attn_matmul(B, H, D, N, dtype="bfloat16", output_dtype="bfloat16")
+    outs = []
+    timer = LaunchTimer()
+
+    def step(i):
+        outs.append(timer.around(lambda: fn(qkvs[i % copies])))
+        if len(outs) > copies:
+            outs.pop(0)
+
+    ms, dom_ms = time_region(step, args.steps, args.warmup, dist, timer)
+    nbytes = sana_bytes(cfg)
+    value = dist.world * nbytes / (ms / 1e3) / 1e9
+    flops = 4 * B * H * N * D * (D + 1)
+    result = {
+        "value": round(value, 1), "unit": "GB/s", "ms_per_step": round(ms, 4),
+        "gpu_launches": 2 * args.steps,
+        "config": {"B": B, "H": H, "N": N, "D": D, "dtype_in": "bf16", "dtype_out": "bf16",
+                   "input_copies": copies, "l2": f"{copies} rotating qkv copies ({copies * one / 1e6:.0f} MB)"},
+        "roofline": roofline(nbytes, dom_ms, peaks["hbm_gbs"], "GB/s", "hbm"),
+        "roofline_note": f"producer + epilogue launches of one call, {dom_ms * 1e3:.1f} us avg; "
+                         f"{flops / (dom_ms / 1e3) / 1e12:.1f} TFLOP/s of algorithmic FMA work; "
+                         f"peak = {peak_kind} HBM copy GB/s",
+    }
+    if not args.no_e2e:
+        host_in = torch.empty(qkvs[0].shape, dtype=torch.bfloat16, pin_memory=True)
+        host_out = torch.empty(B, N, H * D, dtype=torch.bfloat16, pin_memory=True)
+        dev_in = torch.empty_like(qkvs[0])
+
+        def e2e_step(_):
+            dev_in.copy_(host_in, non_blocking=True)
+            host_out.copy_(fn(dev_in), non_blocking=True)
+
+        steps = max(3, min(args.steps, 4 * args.e2e_steps))
+        ems, _ = time_region(e2e_step, steps, args.warmup, dist)
+        result["e2e"] = {"value": round(dist.world * nbytes / (ems / 1e3) / 1e9, 2), "unit": "GB/s",
+                         "h2d_bytes_per_step": host_in.numel() * 2, "d2h_bytes_per_step": host_out.numel() * 2,
+                         "steps": steps, "ms_per_step": round(ems, 4),
+                         "api": "kernelforge_b200.SANA_LinearAttention.qkv_attn_matmul(...)(qkv)"}
+    if dist.world == 1 and dist.rank == 0 and not args.no_cpu:
+        result["cpu_baseline"] = sana_cpu_baseline(cfg, seconds=args.cpu_seconds / 2)
+    del qkvs, outs
+    torch.cuda.empty_cache()
+    return result
+
+
+def sana_cpu_baseline(cfg, seconds=5.0):
+    """oracle.sana (the reference's attn_matmul, bf16 matmuls) over a bounded token sample."""
+    from oracle.sana import qkv_attention_reference
+
+    cores = cpu_threads()
+    B, H, N, D = cfg["B"], cfg["H"], cfg["N"], cfg["D"]
+    n = min(N, 4096)
+    g = torch.Generator().manual_seed(0)
+    qkv = torch.randn(1, n, 3, H * D, generator=g).to(torch.bfloat16)
+    qkv_attention_reference(qkv, H, D)
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        qkv_attention_reference(qkv, H, D)
+        reps += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    nbytes = sana_bytes(dict(cfg, B=1, N=n))
+    return {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+            "sample": f"B=1, N={n} of (B={B},H={H},N={N},D={D}), {reps} passes, oracle/sana.py "
+                      f"(reference attn_matmul on torch CPU, {cores} threads)"}
+
+
+# ---------------------------------------------------------------------------------------------
+# reference arm: the reference algorithm on the host cores (oracle restatement)
+# ---------------------------------------------------------------------------------------------
+def run_reference(args):
+    from oracle.rmsnorm import rmsnorm_forward
+
+    cores = cpu_threads()
+    g = torch.Generator().manual_seed(0)
+    rows = rmsnorm_cpu_sample_rows()
+    data = [(torch.randn(min(rows, r), h, generator=g).to(torch.bfloat16),
+             (1 + 0.1 * torch.randn(h, generator=g)).to(torch.bfloat16)) for r, h in sweep_points()]
+    nbytes = sum(rmsnorm_bytes(x.shape[0], x.shape[1]) for x, _ in data)
+
+    def step():
+        for x, w in data:
+            rmsnorm_forward(x, w, 1e-6)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    value = round(nbytes / dt / 1e9, 3)
+    sample = (f"first {rows} rows of each of the 12 RMSNorm sweep tensors per step "
+              f"({nbytes / 1e6:.0f} MB), oracle/rmsnorm.py on torch CPU")
+    line = {
+        "impl": "reference", "metric": BASELINE_METRIC, "value": value, "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1))",
+        "config": {"workload": "rmsnorm_bf16_sweep (bounded CPU sample)", "rows": list(SWEEP_ROWS),
+                   "hidden": list(SWEEP_HIDDEN), "sample_rows": rows},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", choices=("all", "rmsnorm", "sana"), default="all")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    dist = Dist()
+    if args.impl == "reference":
+        if dist.rank == 0:
+            run_reference(args)
+        return
+    dist.init()
+    peaks, peak_kind = load_peaks()
+    sampler = ClockSampler(dist.local_rank)
+    sampler.start()
+    workloads = {}
+    head = None
+    if args.workload in ("all", "rmsnorm"):
+        head = bench_rmsnorm(args, dist, peaks, peak_kind)
+    if args.workload in ("all", "sana"):
+        for cfg in SANA_CONFIGS:
+            workloads[cfg["name"]] = bench_sana(args, dist, peaks, peak_kind, cfg)
+    clocks = sampler.stop()
+    if head is None:  # a single secondary workload was requested: promote it
+        name, head = next(iter(workloads.items()))
+        workload_name = name
+    else:
+        workload_name = "rmsnorm_bf16_sweep"
+    if dist.rank == 0:
+        line = {
+            "metric": BASELINE_METRIC, "value": head["value"], "unit": head["unit"],
+            "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) tensors generated on device)",
+            "config": {"workload": workload_name, "rows": list(SWEEP_ROWS), "hidden": list(SWEEP_HIDDEN),
+                       "eps": 1e-6, "l2": "inputs larger than L2: one step streams every sweep tensor",
+                       "parallelism": f"weak scaling, {dist.world} rank(s) x full sweep, no collective"},
+            "roofline": head["roofline"], "gpu_launches": head["gpu_launches"],
+            "peaks": {"kind": peak_kind, "hbm_gbs": peaks["hbm_gbs"], "bf16_tflops": peaks["bf16_tflops"]},
+        }
+        for key in ("e2e", "cpu_baseline", "roofline_note"):
+            if key in head:
+                line[key] = head[key]
+        if clocks:
+            line["clocks"] = clocks
+        line["workloads"] = workloads
+        print(json.dumps(line), flush=True)
+    dist.close()
+
+
+if __name__ == "__main__":
+    main()

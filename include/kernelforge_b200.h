@@ -1,0 +1,98 @@
+/*
+ * kernelforge_b200.h -- C ABI of the B200-native KernelForge hot path.
+ *
+ * Every entry point takes raw device pointers, sizes and strides (in ELEMENTS), a cudaStream_t
+ * passed as `void*` (NULL = legacy default stream), and returns a kf_status. None of them
+ * allocates device memory, synchronises the host, or keeps a pointer past the call: the caller
+ * owns every buffer, including the workspace where one is needed. Launches are asynchronous
+ * on `stream`; a kernel-side failure (a bounded wait that timed out) is recorded in a device
+ * error word that kf_query_device_error() reads.
+ *
+ * The Python modules under kernelforge_b200/ (rmsnorm/, SANA_LinearAttention/,
+ * flash_attention_jvp/) keep the reference's call signatures and call these functions.
+ * Each declaration names the reference interface it replaces (path:line in zzd1992/KernelForge).
+ */
+#ifndef KERNELFORGE_B200_H_
+#define KERNELFORGE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types (the reference's dtype strings "float" / "float16" / "bfloat16"). */
+typedef enum {
+  KF_DTYPE_F32 = 0,
+  KF_DTYPE_F16 = 1,
+  KF_DTYPE_BF16 = 2
+} kf_dtype;
+
+typedef enum {
+  KF_OK = 0,
+  KF_ERR_INVALID_ARGUMENT = 1,   /* bad size / stride / null pointer */
+  KF_ERR_UNSUPPORTED = 2,        /* dtype or shape outside the supported domain */
+  KF_ERR_MISALIGNED = 3,         /* pointer or stride alignment the kernel needs is missing */
+  KF_ERR_WORKSPACE = 4,          /* workspace missing or too small */
+  KF_ERR_CUDA = 5,               /* a CUDA runtime call or launch failed */
+  KF_ERR_DEVICE_TIMEOUT = 6      /* a kernel's bounded wait expired (see kf_query_device_error) */
+} kf_status;
+
+/* Human-readable name of a kf_status value (static storage). */
+const char* kf_status_string(int status);
+
+/* ABI version: bumped whenever a signature below changes. */
+int kf_abi_version(void);
+
+/*
+ * Reads (and clears) the device error words of every kernel module on the current device,
+ * after synchronising `stream`. *code receives 0 when no kernel reported a failure, else the
+ * kf_status of the first failure. Host-synchronising: a diagnostic, not a hot-path call.
+ */
+int kf_query_device_error(void* stream, int* code);
+
+/* ------------------------------------------------------------------------------------------
+ * RMSNorm forward.
+ * Replaces rms_norm(batch, seq_len, dim, eps, dtype) -> kernel(X, Weight) -> Output
+ * (rmsnorm/custom.py:11-75) and computes RMSNorm.forward (rmsnorm/original.py:40-52):
+ *   y[r, :] = cast(cast(x[r, :] * rsqrt(mean(x[r, :]^2) + eps)) * weight)
+ * with fp32 statistics and the reference's double rounding for 16-bit dtypes.
+ * x, y: `rows` rows of `dim` elements, row strides x_row_stride / y_row_stride (elements).
+ * weight: `dim` elements, or NULL for no weight (the no-weight comparator of
+ * rmsnorm/original.py:55-78). x, weight, y share `dtype`. rows == 0 is a no-op.
+ * ---------------------------------------------------------------------------------------- */
+int kf_rmsnorm_fwd(const void* x, const void* weight, void* y,
+                   int64_t rows, int64_t dim, int64_t x_row_stride, int64_t y_row_stride,
+                   float eps, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * SANA ReLU linear attention over packed QKV.
+ * Replaces qkv_attn_matmul(batch, heads, dim, seq_len, eps, dtype, output_dtype,
+ * reduce_splits) -> run(qkv) (SANA_LinearAttention/custom.py:340-388) and computes
+ * LiteLA.attn_matmul (SANA_LinearAttention/original.py:99-117) on the packed layout:
+ *   qkv [batch, seq_len, 3, heads*dim] (contiguous; q, k, v along axis 2)
+ *   out [batch, seq_len, heads*dim] in out_dtype
+ *   VK_h = sum_t v_t relu(k_t)^T,  ksum_h = sum_t relu(k_t)           (fp32 accumulation)
+ *   out[t, h*dim + r] = (VK_h relu(q_t))_r / (ksum_h . relu(q_t) + eps)
+ * The token axis is split into `splits` chunks whose fp32 partial sums live in `workspace`
+ * (size from kf_sana_linattn_workspace_size). The workspace must be zero-filled before its
+ * first use on a stream; every call leaves it ready for the next call (the per-head arrival
+ * counters are reset by the kernel that consumes them). Calls that share a workspace must be
+ * ordered on one stream. splits <= 0 selects the default split count for the shape.
+ * dim must divide 128 (the reference's constraint, custom.py:350-351).
+ * ---------------------------------------------------------------------------------------- */
+size_t kf_sana_linattn_workspace_size(int64_t batch, int64_t heads, int64_t dim, int64_t seq_len,
+                                      int64_t splits);
+
+int kf_sana_default_splits(int64_t batch, int64_t heads, int64_t dim, int64_t seq_len);
+
+int kf_sana_linattn_fwd(const void* qkv, void* out, void* workspace, size_t workspace_bytes,
+                        int64_t batch, int64_t heads, int64_t dim, int64_t seq_len, int64_t splits,
+                        float eps, int in_dtype, int out_dtype, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* KERNELFORGE_B200_H_ */

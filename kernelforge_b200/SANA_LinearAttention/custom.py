@@ -1,0 +1,102 @@
+"""SANA ReLU linear attention on the sm_100a kernels (``kf_sana_linattn_fwd``).
+
+Drop-in for the reference's ``qkv_attn_matmul`` (SANA_LinearAttention/custom.py:340-388):
+
+    run = qkv_attn_matmul(batch, heads, dim, seq_len, eps=1e-15, dtype="bfloat16",
+                          output_dtype="float", reduce_splits=True)
+    out = run(qkv)       # qkv [batch, seq_len, 3, heads*dim] -> out [batch, seq_len, heads*dim]
+
+computing ``LiteLA.attn_matmul`` (SANA_LinearAttention/original.py:99-117) on the packed
+layout with fp32 accumulation of K^T V and sum(ReLU(K)).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import _lib
+
+THREADS = 128
+TORCH_DTYPES = {torch.float16: "float16", torch.bfloat16: "bfloat16", torch.float32: "float"}
+
+
+class QKVAttnMatmul:
+    """Callable returned by :func:`qkv_attn_matmul`.
+
+    It owns a device workspace (fp32 split partials, the reduced K^T V / sum(ReLU(K)) and one
+    arrival counter per head group), allocated zero-filled on first use per device and reused
+    by every later call, so the callable is CUDA-graph capturable after its first call.
+    Calls through one callable must be ordered on one stream (they share the workspace).
+    """
+
+    def __init__(self, batch, heads, dim, seq_len, eps, dtype, output_dtype, splits=None):
+        self.batch, self.heads, self.dim, self.seq_len = batch, heads, dim, seq_len
+        self.eps = float(eps)
+        self.dtype = _lib.DTYPE_NAMES[dtype]
+        self.output_dtype = _lib.DTYPE_NAMES[output_dtype]
+        self.splits = int(splits) if splits else 0
+        self.workspace_bytes = _lib.lib.kf_sana_linattn_workspace_size(batch, heads, dim, seq_len, self.splits)
+        if self.workspace_bytes == 0:
+            raise ValueError("unsupported SANA attention shape")
+        self._workspaces = {}
+
+    def workspace(self, device: torch.device) -> torch.Tensor:
+        ws = self._workspaces.get(device)
+        if ws is None:
+            ws = torch.zeros(self.workspace_bytes, dtype=torch.uint8, device=device)
+            self._workspaces[device] = ws
+        return ws
+
+    def __call__(self, qkv: torch.Tensor) -> torch.Tensor:
+        expected = (self.batch, self.seq_len, 3, self.heads * self.dim)
+        if tuple(qkv.shape) != expected:
+            raise ValueError(f"qkv must have shape {expected}, got {tuple(qkv.shape)}")
+        if qkv.dtype != self.dtype:
+            raise ValueError(f"qkv must be {self.dtype}, got {qkv.dtype}")
+        _lib.require_cuda(qkv, "qkv")
+        qkv = qkv.contiguous()
+        out = torch.empty((self.batch, self.seq_len, self.heads * self.dim), dtype=self.output_dtype,
+                          device=qkv.device)
+        return sana_linattn_into(qkv, out, self.workspace(qkv.device), self.heads, self.dim,
+                                 self.eps, self.splits)
+
+
+def sana_linattn_into(qkv, out, workspace, heads, dim, eps, splits=0):
+    """Launch ``kf_sana_linattn_fwd`` on the current stream of ``qkv``'s device."""
+    batch, seq_len = qkv.shape[0], qkv.shape[1]
+    with torch.cuda.device(qkv.device):
+        status = _lib.lib.kf_sana_linattn_fwd(
+            qkv.data_ptr(), out.data_ptr(), workspace.data_ptr(), workspace.numel(),
+            batch, heads, dim, seq_len, int(splits or 0), float(eps),
+            _lib.dtype_code(qkv.dtype), _lib.dtype_code(out.dtype), _lib.stream_handle(qkv.device),
+        )
+    _lib.check(status, "kf_sana_linattn_fwd")
+    return out
+
+
+def qkv_attn_matmul(
+    batch: int,
+    heads: int,
+    dim: int,
+    seq_len: int,
+    eps: float = 1e-15,
+    dtype: str = "bfloat16",
+    output_dtype: str = "float",
+    reduce_splits: bool = True,
+):
+    """Return ``run(qkv)`` for packed ``[batch, seq_len, 3, heads*dim]`` QKV.
+
+    ``reduce_splits`` selected between two partial-reduction kernels in the reference; here the
+    split partials are always reduced once, by the last producer CTA of each head group, so
+    the flag is accepted for signature compatibility and does not change the result.
+    """
+    if dim <= 0 or dim > THREADS or THREADS % dim != 0:
+        raise ValueError(f"dim must divide {THREADS} and be at most {THREADS}")
+    if output_dtype not in ("float", "float16", "bfloat16"):
+        raise ValueError("output_dtype must be float, float16, or bfloat16")
+    if dtype not in ("float", "float16", "bfloat16"):
+        raise ValueError("dtype must be float, float16, or bfloat16")
+    if min(batch, heads, seq_len) <= 0:
+        raise ValueError("batch, heads and seq_len must be positive")
+    del reduce_splits
+    return QKVAttnMatmul(int(batch), int(heads), int(dim), int(seq_len), eps, dtype, output_dtype)

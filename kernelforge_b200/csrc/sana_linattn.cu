@@ -1,0 +1,654 @@
+// SANA ReLU linear attention over packed QKV for sm_100a.
+//
+// Computes LiteLA.attn_matmul (SANA_LinearAttention/original.py:99-117) as the reference's
+// split-sequence kernels do (SANA_LinearAttention/custom.py:98-388), in two launches:
+//
+//  1. sana_vk_producer   grid (splits, head groups, batch)
+//     Each CTA streams its token range of K and V for G heads through a TMA/mbarrier ring
+//     (SWIZZLE_128B boxes of 64 tokens x 2 heads) and accumulates, per head (one warp),
+//         VK[r][c] += v[t][r] * relu(k[t][c])      (mma.sync m16n8k16, fp32 accumulators)
+//         ksum[c]  += relu(k[t][c])                (fp32, from the same B fragments)
+//     It writes fp32 partials; the last CTA to finish a (batch, head group) -- an atomic
+//     arrival counter, no waiting -- sums the partials in split order (deterministic) into the
+//     final VK/ksum and resets the counter for the next call.
+//  2. sana_out_epilogue  grid (token tiles, head groups, batch)
+//     out[t][r] = (VK relu(q_t))_r / (ksum . relu(q_t) + eps). VK and ksum are split into
+//     hi + lo 16-bit halves (two MMAs) so the epilogue keeps ~16 mantissa bits of the fp32
+//     sums; ksum is the 33rd row of the B operand, like the reference's ones-row padding.
+//     The output tile is staged in shared memory and written with a TMA store.
+//
+// Intensity is ~16 flop/byte: the path is HBM-bound, K/V are read once by (1), Q read once
+// and out written once by (2). d = 32 is below tcgen05's minimum M (64), so the tensor work
+// uses the warp-level MMA; at the measured rates it is far from the bound.
+// Shapes outside the fast path (fp32 input, head dims other than 32, tiny tensors) run the
+// generic kernels below (same workspace protocol, CUDA-core fp32 arithmetic).
+#include "kf_sm100.cuh"
+
+#include <algorithm>
+#include <type_traits>
+
+namespace {
+
+__device__ unsigned int g_sana_error = 0;
+
+constexpr int kD = 32;                 // fast-path head dim
+constexpr int kTok = 64;               // tokens per tile / TMA box
+constexpr int kBoxBytes = kTok * 128;  // 64 tokens x 128 bytes
+constexpr int kRows = kD + 1;          // 32 VK rows + the ksum row
+constexpr int kMaxG = 4;
+
+struct Plan {
+  bool fast = false;
+  int G = 1;            // heads per CTA
+  int S = 1;            // splits
+  int tiles = 0;        // 64-token tiles
+  int tiles_per_split = 0;
+  int head_groups = 0;
+};
+
+int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+int default_splits(int64_t B, int64_t H, int64_t N) {
+  const int64_t units = B * ceil_div(H, kMaxG);
+  const int64_t tiles = std::max<int64_t>(1, ceil_div(N, kTok));
+  const int64_t target = static_cast<int64_t>(kf_host::current_device_sms()) * 2;
+  int64_t s = std::max<int64_t>(1, (target + units / 2) / std::max<int64_t>(units, 1));
+  s = std::min<int64_t>(s, std::max<int64_t>(1, tiles / 2));
+  return static_cast<int>(std::min<int64_t>(s, 1024));
+}
+
+int resolve_splits(int64_t B, int64_t H, int64_t N, int64_t splits) {
+  const int64_t tiles = std::max<int64_t>(1, ceil_div(N, kTok));
+  int64_t s = splits > 0 ? splits : default_splits(B, H, N);
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(s, tiles)));
+}
+
+struct WorkspaceLayout {
+  size_t partial_off, final_off, counter_off, total;
+};
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+WorkspaceLayout layout_for(int64_t B, int64_t H, int64_t d, int64_t S) {
+  WorkspaceLayout l;
+  const size_t per_head_partial = static_cast<size_t>(d + 1) * d;
+  const size_t per_head_final = static_cast<size_t>(d + 2) * d;
+  l.partial_off = 0;
+  l.final_off = align256(static_cast<size_t>(B * H * S) * per_head_partial * sizeof(float));
+  l.counter_off = l.final_off + align256(static_cast<size_t>(B * H) * per_head_final * sizeof(float));
+  l.total = l.counter_off + align256(static_cast<size_t>(B * H) * sizeof(unsigned int));
+  return l;
+}
+
+// ------------------------------------------------------------------------------------------
+// Block helpers
+// ------------------------------------------------------------------------------------------
+template <int NT>
+__device__ __forceinline__ float block_max(float v, float* scratch) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float m = 0.f;
+#pragma unroll
+  for (int w = 0; w < NT / 32; ++w) m = fmaxf(m, scratch[w]);
+  __syncthreads();
+  return m;
+}
+
+// Power-of-two scale that brings max|value| below 2^14 (fp16 operand range); 1 for bf16.
+__device__ __forceinline__ float operand_scale(float max_abs, bool fp16) {
+  if (!fp16 || !(max_abs > 0.f)) return 1.f;
+  const int e = static_cast<int>((__float_as_uint(max_abs) >> 23) & 0xffu) - 126;  // max < 2^e
+  const int k = 14 - e;
+  const int biased = min(max(127 + k, 1), 254);
+  return __uint_as_float(static_cast<uint32_t>(biased) << 23);
+}
+
+// Last-arriver reduction shared by the fast and generic producers: sums the S partials of
+// heads [h_first, h_first + nheads) in split order and resets the arrival counter.
+template <int NT>
+__device__ void reduce_partials(const float* __restrict__ partial, float* __restrict__ final_vk,
+                                unsigned int* counter, int b, int h_first, int nheads, int H,
+                                int S, int d, bool fp16, float* scratch) {
+  const int nelem = (d + 1) * d;
+  for (int g = 0; g < nheads; ++g) {
+    const int h = h_first + g;
+    const float* src = partial + (static_cast<size_t>(b) * H + h) * S * nelem;
+    float* dst = final_vk + (static_cast<size_t>(b) * H + h) * (d + 2) * d;
+    float local_max = 0.f;
+    for (int e = threadIdx.x; e < nelem; e += NT) {
+      float sum = 0.f;
+      for (int s = 0; s < S; ++s) sum += __ldcg(src + static_cast<size_t>(s) * nelem + e);
+      dst[e] = sum;
+      local_max = fmaxf(local_max, fabsf(sum));
+    }
+    const float scale = operand_scale(block_max<NT>(local_max, scratch), fp16);
+    if (scale != 1.f) {
+      for (int e = threadIdx.x; e < nelem; e += NT) dst[e] *= scale;
+    }
+    if (threadIdx.x == 0) dst[nelem] = scale;
+  }
+  if (threadIdx.x == 0) *counter = 0u;
+}
+
+// ------------------------------------------------------------------------------------------
+// Fast path, kernel 1: K^T V / ksum partials per split.
+// ------------------------------------------------------------------------------------------
+template <typename T, int G, int STAGES>
+__global__ void __launch_bounds__(G * 32)
+sana_vk_producer(const __grid_constant__ CUtensorMap qkv_map, float* __restrict__ partial,
+                 float* __restrict__ final_vk, unsigned int* __restrict__ counters, int H,
+                 int S, int tiles, int tiles_per_split) {
+  constexpr int kThreads = G * 32;
+  constexpr int kPairs = G / 2;
+  constexpr int kStageBytes = 2 * kPairs * kBoxBytes;  // K boxes, then V boxes
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (kf::smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
+  __shared__ int s_last;
+  __shared__ float s_scratch[kThreads / 32];
+
+  const int split = blockIdx.x, hg = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gid = lane >> 2, tig = lane & 3;
+  const int h0 = hg * G;
+  const int t_begin = split * tiles_per_split;
+  const int n_local = max(0, min(tiles, t_begin + tiles_per_split) - t_begin);
+
+  if (threadIdx.x == 0) {
+    kf::prefetch_tensormap(&qkv_map);
+    for (int s = 0; s < STAGES; ++s) kf::mbar_init(&full[s], 1);
+    kf::fence_mbar_init();
+  }
+  __syncthreads();
+
+  auto issue = [&](int local_tile, int stage) {
+    uint8_t* base = smem + stage * kStageBytes;
+    kf::mbar_arrive_expect_tx(&full[stage], kStageBytes);
+    const int tok = (t_begin + local_tile) * kTok;
+#pragma unroll
+    for (int p = 0; p < kPairs; ++p) {
+      const int c0 = (h0 + 2 * p) * kD;
+      kf::tma_load_4d(base + p * kBoxBytes, &qkv_map, &full[stage], c0, 1, tok, b);
+      kf::tma_load_4d(base + (kPairs + p) * kBoxBytes, &qkv_map, &full[stage], c0, 2, tok, b);
+    }
+  };
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES && i < n_local; ++i) issue(i, i);
+  }
+
+  float acc[2][4][4];
+  float ksum[4];
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt) {
+    ksum[nt] = 0.f;
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[mt][nt][j] = 0.f;
+  }
+  const int pair = warp >> 1, g = warp & 1;
+  const int sub = lane >> 3;
+  bool aborted = false;
+  for (int i = 0; i < n_local; ++i) {
+    const int stage = i % STAGES;
+    const bool ok = kf::mbar_wait_bounded(&full[stage], (i / STAGES) & 1, &g_sana_error);
+    if (ok) {
+      const uint32_t kbase = kf::smem_u32(smem + stage * kStageBytes + pair * kBoxBytes);
+      const uint32_t vbase = kf::smem_u32(smem + stage * kStageBytes + (kPairs + pair) * kBoxBytes);
+#pragma unroll
+      for (int ks = 0; ks < kTok / 16; ++ks) {
+        uint32_t a[2][4];
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          // A = V^T (M = v channel, K = token): transposed 8x8 loads of token-major rows.
+          const int row = ks * 16 + (lane & 7) + (sub >> 1) * 8;
+          const int chunk = g * 4 + mt * 2 + (sub & 1);
+          kf::ldsm_x4_t(vbase + kf::swz128(row, chunk), a[mt][0], a[mt][1], a[mt][2], a[mt][3]);
+        }
+        uint32_t bf[4][2];
+#pragma unroll
+        for (int np = 0; np < 2; ++np) {
+          // B = relu(K) (K = token, N = k channel), two n-tiles per x4 load.
+          const int row = ks * 16 + (lane & 7) + (sub & 1) * 8;
+          const int chunk = g * 4 + np * 2 + (sub >> 1);
+          kf::ldsm_x4_t(kbase + kf::swz128(row, chunk), bf[2 * np][0], bf[2 * np][1],
+                        bf[2 * np + 1][0], bf[2 * np + 1][1]);
+        }
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          bf[nt][0] = kf::Mma<T>::relu2(bf[nt][0]);
+          bf[nt][1] = kf::Mma<T>::relu2(bf[nt][1]);
+          const float2 x = kf::Mma<T>::to_f2(bf[nt][0]);
+          const float2 y = kf::Mma<T>::to_f2(bf[nt][1]);
+          ksum[nt] += (x.x + x.y) + (y.x + y.y);
+        }
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+          for (int nt = 0; nt < 4; ++nt) kf::Mma<T>::run(acc[mt][nt], a[mt], bf[nt]);
+      }
+    }
+    // Everyone is done with this stage (or everyone gives up together).
+    if (!__syncthreads_and(ok)) {
+      aborted = true;
+      break;
+    }
+    if (threadIdx.x == 0 && i + STAGES < n_local) issue(i + STAGES, stage);
+  }
+  if (aborted) return;
+
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt) {
+    ksum[nt] += __shfl_xor_sync(0xffffffffu, ksum[nt], 1);
+    ksum[nt] += __shfl_xor_sync(0xffffffffu, ksum[nt], 2);
+  }
+  const int h = h0 + warp;
+  if (h < H) {
+    float* dst = partial + ((static_cast<size_t>(b) * H + h) * S + split) * (kRows * kD);
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const int r = mt * 16 + gid, c = nt * 8 + tig * 2;
+        __stcg(reinterpret_cast<float2*>(dst + r * kD + c), make_float2(acc[mt][nt][0], acc[mt][nt][1]));
+        __stcg(reinterpret_cast<float2*>(dst + (r + 8) * kD + c), make_float2(acc[mt][nt][2], acc[mt][nt][3]));
+      }
+    if (tig == 0) {
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) __stcg(dst + kD * kD + nt * 8 + gid, ksum[nt]);
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  unsigned int* counter = counters + static_cast<size_t>(b) * gridDim.y + hg;
+  if (threadIdx.x == 0) s_last = (atomicAdd(counter, 1u) == static_cast<unsigned int>(S - 1));
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const int nheads = min(G, H - h0);
+  reduce_partials<kThreads>(partial, final_vk, counter, b, h0, nheads, H, S, kD,
+                            std::is_same<T, __half>::value, s_scratch);
+}
+
+// ------------------------------------------------------------------------------------------
+// Fast path, kernel 2: normalised output for a 64-token x G-head tile.
+// ------------------------------------------------------------------------------------------
+template <typename T, typename O, int G>
+__global__ void __launch_bounds__(G * 32)
+sana_out_epilogue(const __grid_constant__ CUtensorMap qkv_map,
+                  const __grid_constant__ CUtensorMap out_map, const float* __restrict__ final_vk,
+                  int H, int C, float eps) {
+  constexpr int kPairs = G / 2;
+  constexpr int kQBytes = kPairs * kBoxBytes;
+  constexpr int kOutBoxes = (G * kD * static_cast<int>(sizeof(O))) / 128;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (kf::smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t* qtile = smem;
+  uint8_t* otile = smem + kQBytes;
+  __shared__ uint64_t bar;
+
+  const int tt = blockIdx.x, hg = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gid = lane >> 2, tig = lane & 3;
+  const int h0 = hg * G;
+  const int t0 = tt * kTok;
+
+  if (threadIdx.x == 0) {
+    kf::prefetch_tensormap(&qkv_map);
+    kf::prefetch_tensormap(&out_map);
+    kf::mbar_init(&bar, 1);
+    kf::fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    kf::mbar_arrive_expect_tx(&bar, kQBytes);
+#pragma unroll
+    for (int p = 0; p < kPairs; ++p)
+      kf::tma_load_4d(qtile + p * kBoxBytes, &qkv_map, &bar, (h0 + 2 * p) * kD, 0, t0, b);
+  }
+
+  // B operand: VK^T (K = q channel, N = output row) as hi/lo halves, n-tile 4 = ksum row.
+  const int h = h0 + warp;
+  uint32_t bhi[2][5][2], blo[2][5][2];
+  float eps_scaled = eps;
+  {
+    const float* src = final_vk + (static_cast<size_t>(b) * H + min(h, H - 1)) * (kD + 2) * kD;
+    const bool valid = h < H;
+    if (valid) eps_scaled = eps * __ldcg(src + kRows * kD);
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks)
+#pragma unroll
+      for (int nt = 0; nt < 5; ++nt)
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int r = nt * 8 + gid;
+          const int c = ks * 16 + half * 8 + tig * 2;
+          float2 v = make_float2(0.f, 0.f);
+          if (valid && r <= kD) v = __ldcg(reinterpret_cast<const float2*>(src + r * kD + c));
+          const uint32_t hi = kf::Mma<T>::from_f2(v.x, v.y);
+          const float2 hf = kf::Mma<T>::to_f2(hi);
+          bhi[ks][nt][half] = hi;
+          blo[ks][nt][half] = kf::Mma<T>::from_f2(v.x - hf.x, v.y - hf.y);
+        }
+  }
+
+  const bool ok = kf::mbar_wait_bounded(&bar, 0, &g_sana_error);
+  if (!__syncthreads_and(ok)) return;
+
+  const int pair = warp >> 1, g = warp & 1;
+  const uint32_t qbase = kf::smem_u32(qtile + pair * kBoxBytes);
+#pragma unroll
+  for (int mt = 0; mt < kTok / 16; ++mt) {
+    uint32_t a[2][4];
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks) {
+      const int row = mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+      const int chunk = g * 4 + ks * 2 + (lane >> 4);
+      kf::ldsm_x4(qbase + kf::swz128(row, chunk), a[ks][0], a[ks][1], a[ks][2], a[ks][3]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) a[ks][j] = kf::Mma<T>::relu2(a[ks][j]);
+    }
+    float acc[5][4];
+#pragma unroll
+    for (int nt = 0; nt < 5; ++nt)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[nt][j] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks)
+#pragma unroll
+      for (int nt = 0; nt < 5; ++nt) {
+        kf::Mma<T>::run(acc[nt], a[ks], bhi[ks][nt]);
+        kf::Mma<T>::run(acc[nt], a[ks], blo[ks][nt]);
+      }
+    // Column 32 (n-tile 4, tig 0, first element) holds the denominators of rows gid, gid + 8.
+    const float den0 = __shfl_sync(0xffffffffu, acc[4][0], lane & ~3) + eps_scaled;
+    const float den1 = __shfl_sync(0xffffffffu, acc[4][2], lane & ~3) + eps_scaled;
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      const int cc = warp * kD + nt * 8 + tig * 2;  // channel within the CTA's G heads
+#pragma unroll
+      for (int rh = 0; rh < 2; ++rh) {
+        const int row = mt * 16 + gid + rh * 8;
+        const float den = rh ? den1 : den0;
+        const float v0 = acc[nt][rh * 2] / den;
+        const float v1 = acc[nt][rh * 2 + 1] / den;
+        if constexpr (sizeof(O) == 4) {
+          const int box = cc / 32, colb = (cc % 32) * 4;
+          float2* p = reinterpret_cast<float2*>(otile + box * kBoxBytes + kf::swz128(row, colb >> 4) + (colb & 15));
+          *p = make_float2(v0, v1);
+        } else {
+          const int box = cc / 64, colb = (cc % 64) * 2;
+          uint32_t* p = reinterpret_cast<uint32_t*>(otile + box * kBoxBytes + kf::swz128(row, colb >> 4) + (colb & 15));
+          *p = kf::Mma<O>::from_f2(v0, v1);
+        }
+      }
+    }
+  }
+  kf::fence_proxy_async_smem();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    constexpr int kChPerBox = 128 / static_cast<int>(sizeof(O));
+#pragma unroll
+    for (int box = 0; box < kOutBoxes; ++box) {
+      const int c0 = h0 * kD + box * kChPerBox;
+      if (c0 < C) kf::tma_store_3d(&out_map, otile + box * kBoxBytes, c0, t0, b);
+    }
+    kf::tma_store_commit();
+    kf::tma_store_wait_read0();
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// Generic path (fp32 input, any head dim dividing 128, small tensors): CUDA-core fp32.
+// ------------------------------------------------------------------------------------------
+constexpr int kGenThreads = 256;
+constexpr int kGenTok = 32;
+
+template <typename T>
+__global__ void __launch_bounds__(kGenThreads)
+sana_vk_generic(const T* __restrict__ qkv, float* __restrict__ partial, float* __restrict__ final_vk,
+                unsigned int* __restrict__ counters, int H, int d, int N, int S,
+                int tiles_per_split, int fp16) {
+  extern __shared__ float gsm[];
+  const int nelem = (d + 1) * d;
+  float* acc = gsm;
+  float* kt = acc + nelem;
+  float* vt = kt + kGenTok * d;
+  __shared__ int s_last;
+  __shared__ float s_scratch[kGenThreads / 32];
+  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int64_t C = static_cast<int64_t>(H) * d;
+  for (int e = threadIdx.x; e < nelem; e += kGenThreads) acc[e] = 0.f;
+  const int tok0 = split * tiles_per_split * kTok;
+  const int tok1 = min(N, tok0 + tiles_per_split * kTok);
+  for (int t0 = tok0; t0 < tok1; t0 += kGenTok) {
+    __syncthreads();
+    for (int e = threadIdx.x; e < kGenTok * d; e += kGenThreads) {
+      const int tt = e / d, c = e % d, tok = t0 + tt;
+      float kv = 0.f, vv = 0.f;
+      if (tok < tok1) {
+        const T* row = qkv + (static_cast<int64_t>(b) * N + tok) * 3 * C + static_cast<int64_t>(h) * d + c;
+        kv = fmaxf(kf::Elem<T>::to_f(row[C]), 0.f);
+        vv = kf::Elem<T>::to_f(row[2 * C]);
+      }
+      kt[e] = kv;
+      vt[e] = vv;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < nelem; e += kGenThreads) {
+      const int r = e / d, c = e % d;
+      float a = acc[e];
+      for (int tt = 0; tt < kGenTok; ++tt) a = fmaf(r < d ? vt[tt * d + r] : 1.f, kt[tt * d + c], a);
+      acc[e] = a;
+    }
+  }
+  __syncthreads();
+  float* dst = partial + ((static_cast<size_t>(b) * H + h) * S + split) * nelem;
+  for (int e = threadIdx.x; e < nelem; e += kGenThreads) __stcg(dst + e, acc[e]);
+  __threadfence();
+  __syncthreads();
+  unsigned int* counter = counters + static_cast<size_t>(b) * H + h;
+  if (threadIdx.x == 0) s_last = (atomicAdd(counter, 1u) == static_cast<unsigned int>(S - 1));
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  reduce_partials<kGenThreads>(partial, final_vk, counter, b, h, 1, H, S, d, fp16 != 0, s_scratch);
+}
+
+template <typename T, typename O>
+__global__ void __launch_bounds__(kGenThreads)
+sana_out_generic(const T* __restrict__ qkv, const float* __restrict__ final_vk, O* __restrict__ out,
+                 int H, int d, int N, float eps) {
+  extern __shared__ float gsm[];
+  const int nelem = (d + 1) * d;
+  float* vk = gsm;
+  float* qt = vk + nelem;
+  float* den = qt + kGenTok * d;
+  const int t0 = blockIdx.x * kGenTok, h = blockIdx.y, b = blockIdx.z;
+  const int64_t C = static_cast<int64_t>(H) * d;
+  const float* src = final_vk + (static_cast<size_t>(b) * H + h) * (d + 2) * d;
+  for (int e = threadIdx.x; e < nelem; e += kGenThreads) vk[e] = __ldcg(src + e);
+  const float eps_scaled = eps * __ldcg(src + nelem);
+  for (int e = threadIdx.x; e < kGenTok * d; e += kGenThreads) {
+    const int tt = e / d, c = e % d, tok = t0 + tt;
+    float qv = 0.f;
+    if (tok < N)
+      qv = fmaxf(kf::Elem<T>::to_f(qkv[(static_cast<int64_t>(b) * N + tok) * 3 * C + static_cast<int64_t>(h) * d + c]), 0.f);
+    qt[e] = qv;
+  }
+  __syncthreads();
+  if (threadIdx.x < kGenTok) {
+    float s = 0.f;
+    for (int c = 0; c < d; ++c) s = fmaf(vk[d * d + c], qt[threadIdx.x * d + c], s);
+    den[threadIdx.x] = s + eps_scaled;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < kGenTok * d; e += kGenThreads) {
+    const int tt = e / d, r = e % d, tok = t0 + tt;
+    if (tok >= N) continue;
+    float num = 0.f;
+    for (int c = 0; c < d; ++c) num = fmaf(vk[r * d + c], qt[tt * d + c], num);
+    out[(static_cast<int64_t>(b) * N + tok) * C + static_cast<int64_t>(h) * d + r] =
+        kf::Elem<O>::from_f(num / den[tt]);
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// Host side
+// ------------------------------------------------------------------------------------------
+constexpr int kFastStages = 3;
+
+template <typename T, int G>
+int launch_fast(const void* qkv, void* out, float* partial, float* final_vk, unsigned int* counters,
+                int B, int H, int N, int S, int tiles, int tps, float eps, int out_dtype,
+                cudaStream_t stream) {
+  const int C = H * kD;
+  const int in_dtype = std::is_same<T, __half>::value ? KF_DTYPE_F16 : KF_DTYPE_BF16;
+  const size_t es = 2;
+  CUtensorMap qkv_map, out_map;
+  {
+    const uint64_t dims[4] = {static_cast<uint64_t>(C), 3, static_cast<uint64_t>(N), static_cast<uint64_t>(B)};
+    const uint64_t strides[3] = {C * es, 3 * C * es, static_cast<uint64_t>(N) * 3 * C * es};
+    const uint32_t box[4] = {64, 1, kTok, 1};
+    if (!kf_host::encode_tiled(&qkv_map, kf_host::map_type(in_dtype), 4, qkv, dims, strides, box,
+                               CU_TENSOR_MAP_SWIZZLE_128B))
+      return KF_ERR_CUDA;
+  }
+  {
+    const size_t os = kf::dtype_size(out_dtype);
+    const uint64_t dims[3] = {static_cast<uint64_t>(C), static_cast<uint64_t>(N), static_cast<uint64_t>(B)};
+    const uint64_t strides[2] = {C * os, static_cast<uint64_t>(N) * C * os};
+    const uint32_t box[3] = {static_cast<uint32_t>(128 / os), kTok, 1};
+    if (!kf_host::encode_tiled(&out_map, kf_host::map_type(out_dtype), 3, out, dims, strides, box,
+                               CU_TENSOR_MAP_SWIZZLE_128B))
+      return KF_ERR_CUDA;
+  }
+  const int HG = (H + G - 1) / G;
+  {
+    auto kernel = sana_vk_producer<T, G, kFastStages>;
+    const int smem = kFastStages * 2 * (G / 2) * kBoxBytes + kFastStages * 8 + 1024;
+    KF_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    kernel<<<dim3(S, HG, B), G * 32, smem, stream>>>(qkv_map, partial, final_vk, counters, H, S, tiles, tps);
+    KF_LAUNCH_CHECK();
+  }
+  {
+    const int tiles_out = (N + kTok - 1) / kTok;
+    auto run = [&](auto kernel, int obytes) -> int {
+      const int smem = (G / 2) * kBoxBytes + (G * kD * obytes / 128) * kBoxBytes + 1024;
+      KF_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      kernel<<<dim3(tiles_out, HG, B), G * 32, smem, stream>>>(qkv_map, out_map, final_vk, H, C, eps);
+      KF_LAUNCH_CHECK();
+      return KF_OK;
+    };
+    switch (out_dtype) {
+      case KF_DTYPE_F32: return run(sana_out_epilogue<T, float, G>, 4);
+      case KF_DTYPE_F16: return run(sana_out_epilogue<T, __half, G>, 2);
+      default: return run(sana_out_epilogue<T, __nv_bfloat16, G>, 2);
+    }
+  }
+}
+
+template <typename T>
+int launch_generic(const void* qkv, void* out, float* partial, float* final_vk,
+                   unsigned int* counters, int B, int H, int d, int N, int S, int tps, float eps,
+                   int out_dtype, cudaStream_t stream) {
+  const T* q = static_cast<const T*>(qkv);
+  const int nelem = (d + 1) * d;
+  {
+    const int smem = (nelem + 2 * kGenTok * d) * static_cast<int>(sizeof(float));
+    auto kernel = sana_vk_generic<T>;
+    KF_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    kernel<<<dim3(S, H, B), kGenThreads, smem, stream>>>(q, partial, final_vk, counters, H, d, N, S,
+                                                         tps, std::is_same<T, __half>::value);
+    KF_LAUNCH_CHECK();
+  }
+  const int smem = (nelem + kGenTok * d + kGenTok) * static_cast<int>(sizeof(float));
+  const dim3 grid((N + kGenTok - 1) / kGenTok, H, B);
+  auto run = [&](auto kernel, auto* optr) -> int {
+    KF_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    kernel<<<grid, kGenThreads, smem, stream>>>(q, final_vk, optr, H, d, N, eps);
+    KF_LAUNCH_CHECK();
+    return KF_OK;
+  };
+  switch (out_dtype) {
+    case KF_DTYPE_F32: return run(sana_out_generic<T, float>, static_cast<float*>(out));
+    case KF_DTYPE_F16: return run(sana_out_generic<T, __half>, static_cast<__half*>(out));
+    default: return run(sana_out_generic<T, __nv_bfloat16>, static_cast<__nv_bfloat16*>(out));
+  }
+}
+
+bool valid_head_dim(int64_t d) { return d > 0 && d <= 128 && 128 % d == 0; }
+
+}  // namespace
+
+int kf_internal_sana_error(unsigned int* code) {
+  unsigned int v = 0;
+  KF_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_sana_error, sizeof(v)));
+  if (v != 0) {
+    const unsigned int zero = 0;
+    KF_CUDA_TRY(cudaMemcpyToSymbol(g_sana_error, &zero, sizeof(zero)));
+  }
+  *code = v;
+  return KF_OK;
+}
+
+KF_API int kf_sana_default_splits(int64_t batch, int64_t heads, int64_t dim, int64_t seq_len) {
+  if (batch <= 0 || heads <= 0 || seq_len <= 0 || !valid_head_dim(dim)) return 0;
+  return resolve_splits(batch, heads, seq_len, 0);
+}
+
+KF_API size_t kf_sana_linattn_workspace_size(int64_t batch, int64_t heads, int64_t dim,
+                                             int64_t seq_len, int64_t splits) {
+  if (batch <= 0 || heads <= 0 || seq_len <= 0 || !valid_head_dim(dim)) return 0;
+  const int S = resolve_splits(batch, heads, seq_len, splits);
+  return layout_for(batch, heads, dim, S).total;
+}
+
+KF_API int kf_sana_linattn_fwd(const void* qkv, void* out, void* workspace, size_t workspace_bytes,
+                               int64_t batch, int64_t heads, int64_t dim, int64_t seq_len,
+                               int64_t splits, float eps, int in_dtype, int out_dtype,
+                               void* stream) {
+  if (!kf::dtype_valid(in_dtype) || !kf::dtype_valid(out_dtype)) return KF_ERR_UNSUPPORTED;
+  if (batch <= 0 || heads <= 0 || seq_len <= 0) return KF_ERR_INVALID_ARGUMENT;
+  if (!valid_head_dim(dim)) return KF_ERR_UNSUPPORTED;
+  if (qkv == nullptr || out == nullptr || workspace == nullptr) return KF_ERR_INVALID_ARGUMENT;
+  if (!(eps >= 0.f)) return KF_ERR_INVALID_ARGUMENT;
+  // TMA coordinates and kernel indices are 32-bit.
+  if (batch > 65535 || seq_len > (int64_t(1) << 30) || heads * dim > (int64_t(1) << 24) ||
+      batch * seq_len * 3 * heads * dim > (int64_t(1) << 40))
+    return KF_ERR_UNSUPPORTED;
+  const int S = resolve_splits(batch, heads, seq_len, splits);
+  const WorkspaceLayout lay = layout_for(batch, heads, dim, S);
+  if (workspace_bytes < lay.total) return KF_ERR_WORKSPACE;
+  if (!kf::aligned(workspace, 256)) return KF_ERR_MISALIGNED;
+  if (!kf::aligned(qkv, kf::dtype_size(in_dtype)) || !kf::aligned(out, kf::dtype_size(out_dtype)))
+    return KF_ERR_MISALIGNED;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* partial = reinterpret_cast<float*>(ws + lay.partial_off);
+  float* final_vk = reinterpret_cast<float*>(ws + lay.final_off);
+  unsigned int* counters = reinterpret_cast<unsigned int*>(ws + lay.counter_off);
+  const int B = static_cast<int>(batch), H = static_cast<int>(heads), d = static_cast<int>(dim);
+  const int N = static_cast<int>(seq_len);
+  const int tiles = static_cast<int>(ceil_div(N, kTok));
+  const int tps = static_cast<int>(ceil_div(tiles, S));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+  const bool fast = d == kD && (in_dtype == KF_DTYPE_BF16 || in_dtype == KF_DTYPE_F16) &&
+                    H * kD >= 64 && N >= kTok && kf::aligned(qkv, 16) && kf::aligned(out, 16);
+  if (fast) {
+    if (in_dtype == KF_DTYPE_BF16)
+      return launch_fast<__nv_bfloat16, kMaxG>(qkv, out, partial, final_vk, counters, B, H, N, S,
+                                               tiles, tps, eps, out_dtype, s);
+    return launch_fast<__half, kMaxG>(qkv, out, partial, final_vk, counters, B, H, N, S, tiles, tps,
+                                      eps, out_dtype, s);
+  }
+  switch (in_dtype) {
+    case KF_DTYPE_F32:
+      return launch_generic<float>(qkv, out, partial, final_vk, counters, B, H, d, N, S, tps, eps, out_dtype, s);
+    case KF_DTYPE_F16:
+      return launch_generic<__half>(qkv, out, partial, final_vk, counters, B, H, d, N, S, tps, eps, out_dtype, s);
+    default:
+      return launch_generic<__nv_bfloat16>(qkv, out, partial, final_vk, counters, B, H, d, N, S, tps, eps, out_dtype, s);
+  }
+}

@@ -1,0 +1,70 @@
+"""CPU oracle for SANA ReLU linear attention -- TEST INFRASTRUCTURE ONLY.
+
+Restates ``LiteLA.attn_matmul`` (SANA_LinearAttention/original.py:99-117) and the packed-QKV
+views that the reference harness feeds it (SANA_LinearAttention/test.py:52-57, 74-75):
+
+    q, k = ReLU(q), ReLU(k)                      # q, v: [B, h, d, N]; k: [B, h, N, d]
+    v'   = [v ; 1]                               # one padding row of ones  -> [B, h, d+1, N]
+    vk   = v' @ k                                # [B, h, d+1, d], rounded to the input dtype
+    o    = (vk @ q).float()                      # [B, h, d+1, N]
+    out  = o[:, :, :d] / (o[:, :, d:] + eps)     # fp32
+
+``attn_matmul_reference`` keeps the reference's intermediate roundings (low-precision
+matmul outputs); ``attn_exact`` evaluates the same formula in float64 without intermediate
+rounding, which is what the CUDA kernel's fp32 accumulation approximates.
+"""
+
+from __future__ import annotations
+
+import torch
+
+
+def unpack_qkv(qkv: torch.Tensor, heads: int, dim: int):
+    """Packed ``[B, N, 3, C]`` -> the (q, k, v) views of SANA test.py:54-57."""
+    batch, seq_len, three, channels = qkv.shape
+    assert three == 3 and channels == heads * dim
+    q, k, v = qkv.unbind(2)
+    q = q.transpose(-1, -2).reshape(batch, heads, dim, seq_len)
+    k = k.transpose(-1, -2).reshape(batch, heads, dim, seq_len).transpose(-1, -2)
+    v = v.transpose(-1, -2).reshape(batch, heads, dim, seq_len)
+    return q, k, v
+
+
+def heads_to_tokens(out: torch.Tensor) -> torch.Tensor:
+    """``[B, h, d, N]`` -> ``[B, N, h*d]`` (SANA test.py:74-75 / original.py:142)."""
+    batch, heads, dim, seq_len = out.shape
+    return out.reshape(batch, heads * dim, seq_len).permute(0, 2, 1).contiguous()
+
+
+def attn_matmul_reference(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, eps: float = 1e-15):
+    """Reference-semantics ``attn_matmul`` on the CPU; returns fp32 ``[B, h, d, N]``."""
+    q, k, v = (t.detach().cpu() for t in (q, k, v))
+    q = torch.clamp_min(q, 0)
+    k = torch.clamp_min(k, 0)
+    ones = torch.ones(*v.shape[:-2], 1, v.shape[-1], dtype=v.dtype)
+    v_aug = torch.cat([v, ones], dim=-2)
+    vk = torch.matmul(v_aug, k)
+    full = torch.matmul(vk, q)
+    if full.dtype in (torch.float16, torch.bfloat16):
+        full = full.float()
+    numerator, denominator = full[:, :, :-1], full[:, :, -1:]
+    return numerator / (denominator + eps)
+
+
+def qkv_attention_reference(qkv: torch.Tensor, heads: int, dim: int, eps: float = 1e-15):
+    """Packed ``[B, N, 3, C]`` -> fp32 ``[B, N, C]`` with reference roundings."""
+    return heads_to_tokens(attn_matmul_reference(*unpack_qkv(qkv.detach().cpu(), heads, dim), eps))
+
+
+def attn_exact(qkv: torch.Tensor, heads: int, dim: int, eps: float = 1e-15) -> torch.Tensor:
+    """Float64 evaluation of the same formula: packed ``[B, N, 3, C]`` -> ``[B, N, C]``."""
+    x = qkv.detach().to("cpu", torch.float64)
+    batch, seq_len, _, channels = x.shape
+    q = torch.clamp_min(x[:, :, 0].reshape(batch, seq_len, heads, dim), 0)
+    k = torch.clamp_min(x[:, :, 1].reshape(batch, seq_len, heads, dim), 0)
+    v = x[:, :, 2].reshape(batch, seq_len, heads, dim)
+    vk = torch.einsum("bnhr,bnhc->bhrc", v, k)          # sum over tokens: [B, h, d, d]
+    ksum = k.sum(dim=1)                                  # [B, h, d]
+    num = torch.einsum("bhrc,bnhc->bnhr", vk, q)
+    den = torch.einsum("bhc,bnhc->bnh", ksum, q)[..., None]
+    return (num / (den + eps)).reshape(batch, seq_len, channels)

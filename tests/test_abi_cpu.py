@@ -1,0 +1,78 @@
+"""C ABI checks that need no GPU: the library loads and exports every declared symbol, and the
+host-side argument validation rejects bad calls before any launch."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from kernelforge_b200 import _lib
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "kernelforge_b200.h"
+
+
+def declared_functions():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(kf_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    assert "kf_rmsnorm_fwd" in names and "kf_sana_linattn_fwd" in names
+
+
+@pytest.mark.parametrize("name", declared_functions())
+def test_library_exports_declared_symbol(name):
+    lib = ctypes.CDLL(str(_lib.LIB_PATH))
+    assert hasattr(lib, name), f"{name} is declared in {HEADER.name} but not exported"
+    assert name in _lib.SIGNATURES, f"{name} has no ctypes signature in kernelforge_b200/_lib.py"
+
+
+def test_status_strings_and_version():
+    assert _lib.status_string(0) == "ok"
+    assert "workspace" in _lib.status_string(4)
+    assert _lib.lib.kf_abi_version() >= 1
+
+
+def test_rmsnorm_rejects_bad_arguments_without_launching():
+    f = _lib.lib.kf_rmsnorm_fwd
+    # bad dtype / sizes / null pointers are refused before touching the device
+    assert f(1, None, 1, 4, 8, 8, 8, 1e-6, 7, None) == 2
+    assert f(1, None, 1, 4, 0, 8, 8, 1e-6, 2, None) == 1
+    assert f(None, None, 1, 4, 8, 8, 8, 1e-6, 2, None) == 1
+    assert f(16, None, 16, 4, 8, 4, 8, 1e-6, 2, None) == 1  # row stride < dim
+    assert f(17, None, 16, 4, 8, 8, 8, 1e-6, 2, None) == 3  # misaligned bf16 pointer
+    assert f(None, None, None, 0, 8, 8, 8, 1e-6, 2, None) == 0  # empty: no-op
+
+
+def test_sana_workspace_and_validation():
+    ws = _lib.lib.kf_sana_linattn_workspace_size
+    assert ws(4, 36, 32, 4096, 0) > 0
+    assert ws(4, 36, 48, 4096, 0) == 0  # 48 does not divide 128
+    # more splits never shrink the workspace
+    assert ws(2, 70, 32, 16384, 16) >= ws(2, 70, 32, 16384, 1)
+    f = _lib.lib.kf_sana_linattn_fwd
+    need = ws(1, 2, 32, 128, 0)
+    assert f(256, 256, 256, need - 1, 1, 2, 32, 128, 0, 1e-15, 2, 2, None) == 4  # workspace too small
+    assert f(256, 256, 256, need, 1, 2, 24, 128, 0, 1e-15, 2, 2, None) == 2      # head dim
+    assert f(256, 256, None, need, 1, 2, 32, 128, 0, 1e-15, 2, 2, None) == 1     # no workspace
+    assert f(256, 256, 256, need, 1, 2, 32, 128, 0, 1e-15, 5, 2, None) == 2      # dtype
+
+
+def test_python_signature_validation():
+    from kernelforge_b200.SANA_LinearAttention import qkv_attn_matmul
+    from kernelforge_b200.rmsnorm import rms_norm
+
+    with pytest.raises(ValueError, match="dim must divide"):
+        qkv_attn_matmul(1, 2, 48, 128)
+    with pytest.raises(ValueError, match="output_dtype"):
+        qkv_attn_matmul(1, 2, 32, 128, output_dtype="int8")
+    with pytest.raises(ValueError):
+        rms_norm(0, 1, 8)
+    kernel = rms_norm(1, 2, 8, 1e-6, "bfloat16")
+    with pytest.raises(ValueError, match="shape"):
+        kernel(torch.zeros(1, 3, 8, dtype=torch.bfloat16), torch.zeros(8, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="CUDA"):
+        kernel(torch.zeros(1, 2, 8, dtype=torch.bfloat16), torch.zeros(8, dtype=torch.bfloat16))

@@ -1,0 +1,61 @@
+"""Tolerances shared by the parity tests.
+
+The stated bars:
+* integer / index work: bit-exact;
+* bf16 / fp16 outputs: within 1 ulp of the oracle (``assert_within_ulps``), or, where the
+  reference itself rounds intermediates differently from an fp32-accumulating kernel, within
+  ``ulps`` ulp plus ``atol`` = 1e-2 (``assert_close_ulp_atol``);
+* fp32 outputs: rtol 1e-4 (plus a small atol for values near zero).
+"""
+
+from __future__ import annotations
+
+import torch
+
+_MANTISSA_BITS = {torch.bfloat16: 7, torch.float16: 10, torch.float32: 23, torch.float64: 52}
+
+
+def ulp_of(values: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """Spacing of ``dtype`` at |values| (normal range; subnormals use the smallest spacing)."""
+    v = values.detach().to("cpu", torch.float64).abs()
+    finfo = torch.finfo(dtype)
+    exponent = torch.floor(torch.log2(torch.clamp_min(v, finfo.tiny)))
+    return torch.pow(2.0, exponent - _MANTISSA_BITS[dtype])
+
+
+def assert_within_ulps(actual: torch.Tensor, expected: torch.Tensor, ulps: int = 1, dtype=None):
+    dtype = dtype or expected.dtype
+    a = actual.detach().to("cpu", torch.float64)
+    e = expected.detach().to("cpu", torch.float64)
+    assert a.shape == e.shape, (a.shape, e.shape)
+    diff = (a - e).abs()
+    bound = ulps * ulp_of(e, dtype)
+    bad = diff > bound
+    if bad.any():
+        idx = torch.nonzero(bad)[0].tolist()
+        raise AssertionError(
+            f"{int(bad.sum())} of {bad.numel()} elements differ by more than {ulps} ulp "
+            f"(first at {idx}: actual={a[tuple(idx)].item()!r} expected={e[tuple(idx)].item()!r})"
+        )
+
+
+def assert_close_ulp_atol(actual, expected, *, dtype, ulps=1, atol=1e-2):
+    """|actual - expected| <= atol + ulps * ulp_dtype(expected), elementwise."""
+    a = actual.detach().to("cpu", torch.float64)
+    e = expected.detach().to("cpu", torch.float64)
+    assert a.shape == e.shape, (a.shape, e.shape)
+    bound = atol + ulps * ulp_of(e, dtype)
+    diff = (a - e).abs()
+    bad = diff > bound
+    if bad.any():
+        idx = torch.nonzero(bad)[0].tolist()
+        raise AssertionError(
+            f"{int(bad.sum())} of {bad.numel()} elements outside atol={atol} + {ulps} ulp "
+            f"(max diff {diff.max().item():.3g}; first at {idx}: "
+            f"actual={a[tuple(idx)].item()!r} expected={e[tuple(idx)].item()!r})"
+        )
+
+
+def fa_tolerance(dtype):
+    """FlashAttention-JVP tolerances of the reference harness (flash_attention_jvp/test.py:58-59)."""
+    return {torch.float16: dict(atol=3e-3, rtol=1e-2), torch.bfloat16: dict(atol=3e-2, rtol=3e-2)}[dtype]
