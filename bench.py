@@ -10,7 +10,10 @@ achieved HBM GB/s over all ranks with inputs resident in HBM; ``e2e`` is the sam
 the inputs copied from pinned host memory and the outputs copied back inside the timed region.
 
 Secondary workloads in the same line (``workloads``): SANA linear attention configs
-(B=4,H=36,N=4096) and (B=2,H=70,N=16384), bf16 in/out, each step one ``qkv_attn_matmul`` call.
+(B=4,H=36,N=4096) and (B=2,H=70,N=16384), bf16 in/out, each step one ``qkv_attn_matmul`` call
+(replayed from a CUDA graph); FlashAttention JVP (B=4,H=16,N=4096,D in {64,128}, bf16,
+non-causal), each step one standalone ``flash_attention_jvp`` call (TFLOP/s over 5 GEMMs) or
+one ``flash_attention_fwd_jvp`` call (6 GEMMs).
 
 Multi-GPU: one process per GPU (torchrun), weak scaling -- every rank processes its own
 full-size shard, no collective on the data path; NCCL only takes the max of the per-rank
@@ -344,13 +347,20 @@ def bench_sana(args, dist, peaks, peak_kind, cfg):
     copies = max(1, math.ceil(2 * L2_BYTES / one))  # rotate inputs so each step's data is not L2-hot
     qkvs = [torch.randn(B, N, 3, H * D, device=dev, dtype=torch.bfloat16, generator=gen) for _ in range(copies)]
     fn = qkv_attn_matmul(B, H, D, N, dtype="bfloat16", output_dtype="bfloat16")
-    outs = []
+    # One call is ~2 launches of tens of microseconds: replay each call from a CUDA graph so the
+    # device-resident number measures the kernels, not Python (e2e below keeps the plain call).
+    outs = [fn(q) for q in qkvs]
+    torch.cuda.synchronize()
+    graphs = []
+    for i in range(copies):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            outs.append(fn(qkvs[i]))
+        graphs.append(g)
     timer = LaunchTimer()
 
     def step(i):
-        outs.append(timer.around(lambda: fn(qkvs[i % copies])))
-        if len(outs) > copies:
-            outs.pop(0)
+        timer.around(graphs[i % copies].replay)
 
     ms, dom_ms = time_region(step, args.steps, args.warmup, dist, timer)
     nbytes = sana_bytes(cfg)
@@ -360,7 +370,8 @@ def bench_sana(args, dist, peaks, peak_kind, cfg):
         "value": round(value, 1), "unit": "GB/s", "ms_per_step": round(ms, 4),
         "gpu_launches": 2 * args.steps,
         "config": {"B": B, "H": H, "N": N, "D": D, "dtype_in": "bf16", "dtype_out": "bf16",
-                   "input_copies": copies, "l2": f"{copies} rotating qkv copies ({copies * one / 1e6:.0f} MB)"},
+                   "input_copies": copies, "l2": f"{copies} rotating qkv copies ({copies * one / 1e6:.0f} MB)",
+                   "launch": "each step replays a CUDA graph of one qkv_attn_matmul call"},
         "roofline": roofline(nbytes, dom_ms, peaks["hbm_gbs"], "GB/s", "hbm"),
         "roofline_note": f"producer + epilogue launches of one call, {dom_ms * 1e3:.1f} us avg; "
                          f"{flops / (dom_ms / 1e3) / 1e12:.1f} TFLOP/s of algorithmic FMA work; "
@@ -383,7 +394,7 @@ def bench_sana(args, dist, peaks, peak_kind, cfg):
                          "api": "kernelforge_b200.SANA_LinearAttention.qkv_attn_matmul(...)(qkv)"}
     if dist.world == 1 and dist.rank == 0 and not args.no_cpu:
         result["cpu_baseline"] = sana_cpu_baseline(cfg, seconds=args.cpu_seconds / 2)
-    del qkvs, outs
+    del qkvs, outs, graphs
     torch.cuda.empty_cache()
     return result
 
@@ -410,6 +421,120 @@ def sana_cpu_baseline(cfg, seconds=5.0):
     return {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": cores, "kind": "port",
             "sample": f"B=1, N={n} of (B={B},H={H},N={N},D={D}), {reps} passes, oracle/sana.py "
                       f"(reference attn_matmul on torch CPU, {cores} threads)"}
+
+
+# ---------------------------------------------------------------------------------------------
+# FlashAttention JVP (B=4, H=16, N=4096, D in {64, 128}, bf16, non-causal)
+# ---------------------------------------------------------------------------------------------
+FA_CONFIGS = (
+    {"name": "fajvp_d64", "B": 4, "H": 16, "N": 4096, "D": 64},
+    {"name": "fajvp_d128", "B": 4, "H": 16, "N": 4096, "D": 128},
+)
+
+
+def fa_flops(cfg, gemms):
+    return 2 * gemms * cfg["B"] * cfg["H"] * cfg["N"] * cfg["N"] * cfg["D"]
+
+
+def bench_fa(args, dist, peaks, peak_kind, cfg, fused):
+    import kernelforge_b200.flash_attention_jvp as fa
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    B, H, N, D = cfg["B"], cfg["H"], cfg["N"], cfg["D"]
+    gen = torch.Generator(device=dev).manual_seed(2026 + dist.rank)
+    q, k, v, tq, tk, tv = (torch.randn(B, N, H, D, device=dev, dtype=torch.bfloat16, generator=gen) for _ in range(6))
+    out, lse = fa.flash_attention(q, k, v, return_lse=True)
+    if fused:
+        call = lambda: fa.flash_attention_fwd_jvp(q, k, v, tq, tk, tv)  # noqa: E731
+        gemms, what = 6, "one-pass O, LSE and tangent (flash_attention_fwd_jvp)"
+    else:
+        call = lambda: fa.flash_attention_jvp(q, k, v, tq, tk, tv, out, lse)  # noqa: E731
+        gemms, what = 5, "standalone tangent from cached O/LSE (flash_attention_jvp)"
+    timer = LaunchTimer()
+    keep = []
+
+    def step(_):
+        keep.append(timer.around(call))
+        if len(keep) > 2:
+            keep.pop(0)
+
+    ms, dom_ms = time_region(step, args.steps, args.warmup, dist, timer)
+    flops = fa_flops(cfg, gemms)
+    peak = peaks["bf16_tflops"]
+    result = {
+        "value": round(dist.world * flops / (ms / 1e3) / 1e12, 1), "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
+        "gpu_launches": args.steps,
+        "config": {"B": B, "H": H, "N": N, "D": D, "causal": False, "dtype": "bf16", "call": what,
+                   "flops_per_step": flops, "l2": "inputs larger than L2 (6-8 tensors of B*N*H*D bf16)"},
+        "roofline": roofline(flops, dom_ms, peak, "TFLOP/s", "tensor"),
+        "roofline_note": f"{gemms} GEMMs x 2*B*H*N^2*D flop per launch, {dom_ms * 1e3:.1f} us avg; "
+                         f"peak = {peak_kind} cuBLAS bf16 TFLOP/s (burst)",
+    }
+    if not args.no_e2e:
+        host = [torch.empty_like(t, device="cpu").pin_memory() for t in (q, k, v, tq, tk, tv)]
+        for h, t in zip(host, (q, k, v, tq, tk, tv)):
+            h.copy_(t)
+        host_out = torch.empty_like(q, device="cpu").pin_memory()
+        dev_in = [torch.empty_like(t) for t in (q, k, v, tq, tk, tv)]
+        h2d = sum(t.numel() * 2 for t in host)
+        if not fused:
+            host_o = out.cpu().pin_memory()
+            host_lse = lse.cpu().pin_memory()
+            dev_o, dev_lse = torch.empty_like(out), torch.empty_like(lse)
+            h2d += host_o.numel() * 2 + host_lse.numel() * 4
+
+        def e2e_step(_):
+            for d_, h_ in zip(dev_in, host):
+                d_.copy_(h_, non_blocking=True)
+            if fused:
+                _, _, tangent = fa.flash_attention_fwd_jvp(*dev_in)
+            else:
+                dev_o.copy_(host_o, non_blocking=True)
+                dev_lse.copy_(host_lse, non_blocking=True)
+                tangent = fa.flash_attention_jvp(*dev_in, dev_o, dev_lse)
+            host_out.copy_(tangent, non_blocking=True)
+
+        steps = max(3, min(args.steps, args.e2e_steps))
+        ems, _ = time_region(e2e_step, steps, args.warmup, dist)
+        result["e2e"] = {"value": round(dist.world * flops / (ems / 1e3) / 1e12, 2), "unit": "TFLOP/s",
+                         "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": host_out.numel() * 2,
+                         "steps": steps, "ms_per_step": round(ems, 3),
+                         "api": "kernelforge_b200.flash_attention_jvp." +
+                                ("flash_attention_fwd_jvp" if fused else "flash_attention_jvp")}
+    if dist.world == 1 and dist.rank == 0 and not args.no_cpu:
+        result["cpu_baseline"] = fa_cpu_baseline(cfg, fused, seconds=args.cpu_seconds / 2)
+    del q, k, v, tq, tk, tv, out, lse, keep
+    torch.cuda.empty_cache()
+    return result
+
+
+def fa_cpu_baseline(cfg, fused, seconds=5.0):
+    """oracle.fa_jvp on the host cores, one (batch, head) slice of the config at a time."""
+    from oracle.fa_jvp import attention_jvp, attention_jvp_from_forward, attention_lse, attention
+
+    cores = cpu_threads()
+    N, D = cfg["N"], cfg["D"]
+    g = torch.Generator().manual_seed(0)
+    q, k, v, tq, tk, tv = (torch.randn(1, N, 1, D, generator=g).to(torch.bfloat16) for _ in range(6))
+    if not fused:
+        out = attention(q, k, v)
+        lse = attention_lse(q, k)
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        if fused:
+            attention_jvp(q, k, v, tq, tk, tv)
+        else:
+            attention_jvp_from_forward(q, k, v, tq, tk, tv, out, lse)
+        reps += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    flops = fa_flops(dict(cfg, B=1, H=1), 6 if fused else 5)
+    return {"value": round(flops / dt / 1e12, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "sample": f"{reps} (batch, head) slices of N={N}, D={D} (of B={cfg['B']}, H={cfg['H']}), "
+                      f"oracle/fa_jvp.py {'attention_jvp (torch.func)' if fused else 'attention_jvp_from_forward'} "
+                      f"on torch CPU fp32, {cores} threads"}
 
 
 # ---------------------------------------------------------------------------------------------
@@ -458,7 +583,7 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("all", "rmsnorm", "sana"), default="all")
+    ap.add_argument("--workload", choices=("all", "rmsnorm", "sana", "fajvp"), default="all")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-e2e", action="store_true")
@@ -483,6 +608,10 @@ def main():
     if args.workload in ("all", "sana"):
         for cfg in SANA_CONFIGS:
             workloads[cfg["name"]] = bench_sana(args, dist, peaks, peak_kind, cfg)
+    if args.workload in ("all", "fajvp"):
+        for cfg in FA_CONFIGS:
+            workloads[cfg["name"] + "_standalone"] = bench_fa(args, dist, peaks, peak_kind, cfg, fused=False)
+            workloads[cfg["name"] + "_fused"] = bench_fa(args, dist, peaks, peak_kind, cfg, fused=True)
     clocks = sampler.stop()
     if head is None:  # a single secondary workload was requested: promote it
         name, head = next(iter(workloads.items()))

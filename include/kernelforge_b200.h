@@ -75,21 +75,58 @@ int kf_rmsnorm_fwd(const void* x, const void* weight, void* y,
  *   out [batch, seq_len, heads*dim] in out_dtype
  *   VK_h = sum_t v_t relu(k_t)^T,  ksum_h = sum_t relu(k_t)           (fp32 accumulation)
  *   out[t, h*dim + r] = (VK_h relu(q_t))_r / (ksum_h . relu(q_t) + eps)
- * The token axis is split into `splits` chunks whose fp32 partial sums live in `workspace`
- * (size from kf_sana_linattn_workspace_size). The workspace must be zero-filled before its
- * first use on a stream; every call leaves it ready for the next call (the per-head arrival
- * counters are reset by the kernel that consumes them). Calls that share a workspace must be
- * ordered on one stream. splits <= 0 selects the default split count for the shape.
+ * The token axis is split into `splits` chunks (splits <= 0: a default for the shape). On the
+ * bf16/fp16 head_dim-32 path the chunks of a head group form one thread-block cluster (at
+ * most 8) and reduce through distributed shared memory; the workspace then holds only the
+ * reduced fp32 K^T V and ksum. Other shapes keep fp32 partials in the workspace and reduce
+ * them in the last CTA to arrive (per-head arrival counters). Size the workspace with
+ * kf_sana_linattn_workspace_size and zero-fill it once before its first use; every call
+ * leaves it ready for the next one. Calls that share a workspace must be ordered on one stream.
  * dim must divide 128 (the reference's constraint, custom.py:350-351).
  * ---------------------------------------------------------------------------------------- */
 size_t kf_sana_linattn_workspace_size(int64_t batch, int64_t heads, int64_t dim, int64_t seq_len,
                                       int64_t splits);
 
-int kf_sana_default_splits(int64_t batch, int64_t heads, int64_t dim, int64_t seq_len);
-
 int kf_sana_linattn_fwd(const void* qkv, void* out, void* workspace, size_t workspace_bytes,
                         int64_t batch, int64_t heads, int64_t dim, int64_t seq_len, int64_t splits,
                         float eps, int in_dtype, int out_dtype, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * FlashAttention forward and forward-mode JVP.
+ * Layout: q, tq, out, tangent_out [batch, q_len, q_heads, head_dim]; k, v, tk, tv
+ * [batch, k_len, kv_heads, head_dim]; all contiguous, 16-byte aligned, `dtype` fp16 or bf16.
+ * lse: fp32 [batch, q_heads, q_len], natural log; +inf for a row that sees no key.
+ * head_dim: a multiple of 8, at most 256; q_heads a multiple of kv_heads (GQA / MQA).
+ * causal: key j is visible to query i iff j <= i + k_len - q_len (bottom-right aligned).
+ * softmax_scale: finite and positive (the reference default is head_dim^-1/2).
+ * A NULL tangent (tq / tk / tv) is a zero tangent; its GEMM is skipped.
+ * Deterministic: no atomics; the same inputs give bitwise-identical outputs.
+ * ---------------------------------------------------------------------------------------- */
+
+/* O and LSE. Replaces the native forward that FlashAttentionFunction.forward calls
+ * (_flash_attn_forward, flash_attention_jvp/custom.py:230-239). */
+int kf_fa_fwd(const void* q, const void* k, const void* v, void* out, float* lse,
+              int64_t batch, int64_t q_len, int64_t k_len, int64_t q_heads, int64_t kv_heads,
+              int64_t head_dim, float softmax_scale, int causal, int dtype, void* stream);
+
+/* Standalone JVP from a cached O / LSE:
+ *   tO = P tV + H V - rowsum(H) * O,  P = exp(scale * Q K^T - LSE),
+ *   H = P * scale * (tQ K^T + Q tK^T).
+ * Replaces _attention_jvp_kernel(...)(Q, K, V, TQ, TK, TV, O, LSE) -> TO and the
+ * kernelforge::flash_attention_jvp operator (flash_attention_jvp/custom.py:12-157). */
+int kf_fa_jvp(const void* q, const void* k, const void* v, const void* tq, const void* tk,
+              const void* tv, const void* out, const float* lse, void* tangent_out,
+              int64_t batch, int64_t q_len, int64_t k_len, int64_t q_heads, int64_t kv_heads,
+              int64_t head_dim, float softmax_scale, int causal, int dtype, void* stream);
+
+/* One-pass forward + JVP (O, LSE and tO with online recurrences; six GEMMs per key tile).
+ * Replaces the native forward followed by the JVP launch that torch.func.jvp of
+ * flash_attention performs (flash_attention_jvp/custom.py:226-291), fused as
+ * flash-attention-jvp-derivation.md sections 7-8 describe. */
+int kf_fa_fwd_jvp(const void* q, const void* k, const void* v, const void* tq, const void* tk,
+                  const void* tv, void* out, float* lse, void* tangent_out,
+                  int64_t batch, int64_t q_len, int64_t k_len, int64_t q_heads, int64_t kv_heads,
+                  int64_t head_dim, float softmax_scale, int causal, int dtype, void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -33,10 +33,17 @@ SIGNATURES = {
     "kf_rmsnorm_fwd": (ctypes.c_int, [_c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64,
                                       ctypes.c_float, ctypes.c_int, _c_ptr]),
     "kf_sana_linattn_workspace_size": (ctypes.c_size_t, [_c_i64, _c_i64, _c_i64, _c_i64, _c_i64]),
-    "kf_sana_default_splits": (ctypes.c_int, [_c_i64, _c_i64, _c_i64, _c_i64]),
     "kf_sana_linattn_fwd": (ctypes.c_int, [_c_ptr, _c_ptr, _c_ptr, ctypes.c_size_t, _c_i64, _c_i64,
                                            _c_i64, _c_i64, _c_i64, ctypes.c_float, ctypes.c_int,
                                            ctypes.c_int, _c_ptr]),
+    "kf_fa_fwd": (ctypes.c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64,
+                                 _c_i64, _c_i64, ctypes.c_float, ctypes.c_int, ctypes.c_int, _c_ptr]),
+    "kf_fa_jvp": (ctypes.c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr,
+                                 _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_float,
+                                 ctypes.c_int, ctypes.c_int, _c_ptr]),
+    "kf_fa_fwd_jvp": (ctypes.c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr,
+                                     _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_float,
+                                     ctypes.c_int, ctypes.c_int, _c_ptr]),
 }
 
 

@@ -1,0 +1,91 @@
+// C ABI of the FlashAttention forward / forward-mode JVP kernels: validation and dispatch.
+#include "fa_common.cuh"
+
+#include <cmath>
+
+namespace {
+
+using kf::fa::FaArgs;
+
+int validate(const void* q, const void* k, const void* v, int64_t B, int64_t Nq, int64_t Nk,
+             int64_t Hq, int64_t Hkv, int64_t D, float scale, int dtype) {
+  if (dtype != KF_DTYPE_F16 && dtype != KF_DTYPE_BF16) return KF_ERR_UNSUPPORTED;
+  if (q == nullptr || k == nullptr || v == nullptr) return KF_ERR_INVALID_ARGUMENT;
+  if (B <= 0 || Nq <= 0 || Nk <= 0 || Hq <= 0 || Hkv <= 0 || D <= 0) return KF_ERR_INVALID_ARGUMENT;
+  if (Hq % Hkv != 0 || D % 8 != 0 || D > 256) return KF_ERR_UNSUPPORTED;
+  if (!(std::isfinite(scale) && scale > 0.f)) return KF_ERR_INVALID_ARGUMENT;
+  if (B > 65535 || Hq > 65535 || Nq > (int64_t(1) << 30) || Nk > (int64_t(1) << 30))
+    return KF_ERR_UNSUPPORTED;
+  return KF_OK;
+}
+
+bool aligned16(const void* p) { return p == nullptr || kf::aligned(p, 16); }
+
+FaArgs make_args(const void* q, const void* k, const void* v, const void* tq, const void* tk,
+                 const void* tv, int64_t B, int64_t Nq, int64_t Nk, int64_t Hq, int64_t Hkv,
+                 int64_t D, float scale, int causal) {
+  FaArgs a = {};
+  a.q = q; a.k = k; a.v = v; a.tq = tq; a.tk = tk; a.tv = tv;
+  a.B = static_cast<int>(B); a.Nq = static_cast<int>(Nq); a.Nk = static_cast<int>(Nk);
+  a.Hq = static_cast<int>(Hq); a.Hkv = static_cast<int>(Hkv); a.D = static_cast<int>(D);
+  a.scale = scale;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.causal = causal ? 1 : 0;
+  return a;
+}
+
+}  // namespace
+
+KF_API int kf_fa_fwd(const void* q, const void* k, const void* v, void* out, float* lse,
+                     int64_t batch, int64_t q_len, int64_t k_len, int64_t q_heads,
+                     int64_t kv_heads, int64_t head_dim, float softmax_scale, int causal,
+                     int dtype, void* stream) {
+  int st = validate(q, k, v, batch, q_len, k_len, q_heads, kv_heads, head_dim, softmax_scale, dtype);
+  if (st != KF_OK) return st;
+  if (out == nullptr || lse == nullptr) return KF_ERR_INVALID_ARGUMENT;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || !kf::aligned(lse, 4))
+    return KF_ERR_MISALIGNED;
+  FaArgs a = make_args(q, k, v, nullptr, nullptr, nullptr, batch, q_len, k_len, q_heads, kv_heads,
+                       head_dim, softmax_scale, causal);
+  a.o_out = out;
+  a.lse_out = lse;
+  return kf::fa::launch_general(a, kf::fa::kModeFwd, dtype, static_cast<cudaStream_t>(stream));
+}
+
+KF_API int kf_fa_jvp(const void* q, const void* k, const void* v, const void* tq, const void* tk,
+                     const void* tv, const void* out, const float* lse, void* tangent_out,
+                     int64_t batch, int64_t q_len, int64_t k_len, int64_t q_heads,
+                     int64_t kv_heads, int64_t head_dim, float softmax_scale, int causal,
+                     int dtype, void* stream) {
+  int st = validate(q, k, v, batch, q_len, k_len, q_heads, kv_heads, head_dim, softmax_scale, dtype);
+  if (st != KF_OK) return st;
+  if (out == nullptr || lse == nullptr || tangent_out == nullptr) return KF_ERR_INVALID_ARGUMENT;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(tq) || !aligned16(tk) ||
+      !aligned16(tv) || !aligned16(out) || !aligned16(tangent_out) || !kf::aligned(lse, 4))
+    return KF_ERR_MISALIGNED;
+  FaArgs a = make_args(q, k, v, tq, tk, tv, batch, q_len, k_len, q_heads, kv_heads, head_dim,
+                       softmax_scale, causal);
+  a.o_in = out;
+  a.lse_in = lse;
+  a.to_out = tangent_out;
+  return kf::fa::launch_general(a, kf::fa::kModeJvp, dtype, static_cast<cudaStream_t>(stream));
+}
+
+KF_API int kf_fa_fwd_jvp(const void* q, const void* k, const void* v, const void* tq,
+                         const void* tk, const void* tv, void* out, float* lse, void* tangent_out,
+                         int64_t batch, int64_t q_len, int64_t k_len, int64_t q_heads,
+                         int64_t kv_heads, int64_t head_dim, float softmax_scale, int causal,
+                         int dtype, void* stream) {
+  int st = validate(q, k, v, batch, q_len, k_len, q_heads, kv_heads, head_dim, softmax_scale, dtype);
+  if (st != KF_OK) return st;
+  if (out == nullptr || lse == nullptr || tangent_out == nullptr) return KF_ERR_INVALID_ARGUMENT;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(tq) || !aligned16(tk) ||
+      !aligned16(tv) || !aligned16(out) || !aligned16(tangent_out) || !kf::aligned(lse, 4))
+    return KF_ERR_MISALIGNED;
+  FaArgs a = make_args(q, k, v, tq, tk, tv, batch, q_len, k_len, q_heads, kv_heads, head_dim,
+                       softmax_scale, causal);
+  a.o_out = out;
+  a.lse_out = lse;
+  a.to_out = tangent_out;
+  return kf::fa::launch_general(a, kf::fa::kModeFwdJvp, dtype, static_cast<cudaStream_t>(stream));
+}

@@ -8,6 +8,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "kf_common.cuh"
 
 namespace kf {
@@ -66,6 +68,30 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 }
 
 // ------------------------------------------------------------------------------------------
+// Thread-block clusters: hardware cluster barrier and distributed shared memory reads.
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// ------------------------------------------------------------------------------------------
 // TMA (tensor copies through the async proxy). No .multicast::cluster form is used anywhere.
 // ------------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar,
@@ -91,11 +117,32 @@ __device__ __forceinline__ void tma_store_commit() {
 __device__ __forceinline__ void tma_store_wait_read0() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
+__device__ __forceinline__ void tma_store_wait_read1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
 __device__ __forceinline__ void tma_store_wait_all0() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// 1-D bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Programmatic dependent launch: the primary grid lets its dependent grid start launching;
+// the dependent waits for the primary's completion (and memory) before consuming its output.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait_primary() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 // Byte offset of 16-byte chunk `chunk` in row `row` of a tile written by TMA with
@@ -205,6 +252,78 @@ inline CUtensorMapDataType map_type(int dtype) {
     case KF_DTYPE_F16: return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     default: return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   }
+}
+
+// Per-device cache of kernel preparation. The dynamic shared-memory opt-in is a per-function
+// attribute: it is only ever raised (to the largest size requested so far), so launches of the
+// same kernel with different sizes stay valid. Occupancy is cached per (function, size). The
+// runtime queries cost microseconds; each is done once.
+struct KernelPrep {
+  const void* fn = nullptr;
+  int smem = -1;       // occupancy entries: size; attribute entries: largest opt-in so far
+  int occupancy = 0;
+};
+inline int prepare_kernel(const void* fn, int threads, int smem, int* occupancy_out) {
+  constexpr int kSlots = 256;
+  static KernelPrep attr_cache[64][kSlots];
+  static KernelPrep occ_cache[64][kSlots];
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return KF_ERR_CUDA;
+  }
+  const bool cached_dev = dev >= 0 && dev < 64;
+  // 1. shared-memory opt-in
+  KernelPrep* attr = nullptr;
+  if (cached_dev) {
+    for (int i = 0; i < kSlots; ++i) {
+      KernelPrep& c = attr_cache[dev][i];
+      if (c.fn == fn || c.fn == nullptr) {
+        attr = &c;
+        break;
+      }
+    }
+  }
+  if (attr == nullptr || attr->fn == nullptr || attr->smem < smem) {
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return KF_ERR_CUDA;
+    }
+    if (attr != nullptr) {
+      attr->smem = smem;
+      attr->fn = fn;
+    }
+  }
+  // 2. occupancy for this size
+  if (occupancy_out == nullptr) return KF_OK;
+  KernelPrep* occ_slot = nullptr;
+  if (cached_dev) {
+    for (int i = 0; i < kSlots; ++i) {
+      KernelPrep& c = occ_cache[dev][i];
+      if (c.fn == fn && c.smem == smem) {
+        *occupancy_out = c.occupancy;
+        return KF_OK;
+      }
+      if (c.fn == nullptr) {
+        occ_slot = &c;
+        break;
+      }
+    }
+  }
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, threads, smem) != cudaSuccess || occ <= 0) {
+    (void)cudaGetLastError();
+    occ = 1;
+  }
+  if (occ_slot != nullptr) {
+    occ_slot->occupancy = occ;
+    occ_slot->smem = smem;
+    occ_slot->fn = fn;
+  }
+  *occupancy_out = occ;
+  return KF_OK;
 }
 
 inline int current_device_sms() {

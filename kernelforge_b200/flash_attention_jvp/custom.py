@@ -1,0 +1,339 @@
+"""FlashAttention forward and forward-mode JVP on the sm_100a kernels (``kf_fa_*``).
+
+Drop-in for the reference's flash_attention_jvp/custom.py (names, signatures, validation
+messages): ``flash_attention``, ``flash_attention_jvp``, ``get_jvp_config``,
+``FlashAttentionFunction``, ``_attention_jvp_kernel``, ``_default_jvp_config``,
+``_validate_inputs``, ``_prepare_tangent`` and the ``_flash_attn_forward`` /
+``_flash_attn_backward`` module attributes that the reference harness patches.
+
+Differences from the reference, by design:
+
+* the forward (O and the natural-log LSE) is this library's own kernel, not the flash_attn
+  binary, so ``flash_attention`` matches ``flash_attn_func`` within tolerance, not bitwise;
+* ``flash_attention_fwd_jvp`` adds the one-pass forward + JVP (O, LSE and tO from a single
+  scan over the keys, flash-attention-jvp-derivation.md sections 7-8);
+* tile arguments (``block_m``, ``block_n``, ``threads``, ``num_stages``) are validated over the
+  reference's schedule domain (custom.py:215-217) and otherwise ignored: the kernels choose
+  their own tiles. Results are deterministic for a given shape;
+* a ``None`` tangent is passed to the kernel as a null pointer and its GEMM is skipped
+  (the reference materialises zeros, custom.py:180-185): the result is the same.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+from torch.autograd.function import once_differentiable
+
+from .. import _lib
+
+_OP_NAMESPACE = "kernelforge_b200"
+
+
+# ---------------------------------------------------------------------------------------------
+# validation (flash_attention_jvp/custom.py:160-185)
+# ---------------------------------------------------------------------------------------------
+def _validate_inputs(q, k, v, softmax_scale):
+    if any(x.ndim != 4 for x in (q, k, v)):
+        raise ValueError("q, k, v must have shape [batch, sequence, heads, dim]")
+    if q.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError("FlashAttention JVP supports float16 and bfloat16")
+    if not q.is_cuda or any(x.device != q.device or x.dtype != q.dtype for x in (k, v)):
+        raise ValueError("q, k, v must use the same CUDA device and dtype")
+    b, nq, h, d = q.shape
+    if min(b, nq, h, d, k.shape[1], k.shape[2]) <= 0:
+        raise ValueError("batch, sequence lengths, heads, and head dimension must be positive")
+    if k.shape != v.shape or k.shape[0] != b or k.shape[-1] != d:
+        raise ValueError("k and v must match, with the same batch and head dimension as q")
+    if h % k.shape[2] or d % 8 or d > 256:
+        raise ValueError("query heads must be divisible by KV heads; dim must be a multiple of 8 <= 256")
+    scale = d ** -0.5 if softmax_scale is None else float(softmax_scale)
+    if not math.isfinite(scale) or scale <= 0:
+        raise ValueError("softmax_scale must be finite and positive")
+    return scale
+
+
+def _prepare_tangent(tangent, primal, name):
+    """Validate a tangent; ``None`` stays ``None`` (a zero tangent, skipped by the kernel)."""
+    if tangent is None:
+        return None
+    if tangent.shape != primal.shape or tangent.device != primal.device or tangent.dtype != primal.dtype:
+        raise ValueError(f"{name} must have the same shape, device, and dtype as its primal")
+    return tangent.contiguous()
+
+
+def _default_jvp_config(dim, keys, causal):
+    """The reference's recorded schedule defaults (custom.py:123-128), kept for API parity."""
+    block_n, threads = (32, 256) if dim > 128 else (64, 128)
+    stages = 1 if keys <= block_n or (not causal and keys >= 8192) else 2
+    return dict(block_m=64, block_n=block_n, threads=threads, num_stages=stages)
+
+
+def get_jvp_config(q, k, v, *, softmax_scale=None, causal=False):
+    """Return deterministic default settings without compiling or tuning."""
+    _validate_inputs(q, k, v, softmax_scale)
+    return _default_jvp_config(q.shape[-1], k.shape[1], causal)
+
+
+def _check_schedule(block_m, block_n, threads, num_stages):
+    if (block_m not in (16, 32, 64, 128) or block_n not in (32, 64, 128)
+            or threads not in (128, 256) or num_stages not in (1, 2, 3)):
+        raise ValueError("unsupported tile/pipeline configuration")
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _dims(q, k):
+    return (q.shape[0], q.shape[1], k.shape[1], q.shape[2], k.shape[2], q.shape[3])
+
+
+# ---------------------------------------------------------------------------------------------
+# opaque torch operators around the C ABI (unwrap torch.func tensors, provide fake kernels)
+# ---------------------------------------------------------------------------------------------
+@torch.library.custom_op(f"{_OP_NAMESPACE}::flash_attention_forward", mutates_args=(), device_types="cuda")
+def _launch_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, causal: bool
+                ) -> tuple[torch.Tensor, torch.Tensor]:
+    out = torch.empty_like(q)
+    lse = torch.empty((q.shape[0], q.shape[2], q.shape[1]), dtype=torch.float32, device=q.device)
+    with torch.cuda.device(q.device):
+        status = _lib.lib.kf_fa_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(out), _ptr(lse), *_dims(q, k),
+                                    float(scale), int(causal), _lib.dtype_code(q.dtype),
+                                    _lib.stream_handle(q.device))
+    _lib.check(status, "kf_fa_fwd")
+    return out, lse
+
+
+@_launch_fwd.register_fake
+def _launch_fwd_fake(q, k, v, scale, causal):
+    return torch.empty_like(q), q.new_empty((q.shape[0], q.shape[2], q.shape[1]), dtype=torch.float32)
+
+
+@torch.library.custom_op(f"{_OP_NAMESPACE}::flash_attention_jvp", mutates_args=(), device_types="cuda")
+def _launch_jvp(
+    q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+    tq: Optional[torch.Tensor], tk: Optional[torch.Tensor], tv: Optional[torch.Tensor],
+    out: torch.Tensor, lse: torch.Tensor,
+    scale: float, causal: bool, block_m: int, block_n: int, threads: int, num_stages: int,
+) -> torch.Tensor:
+    tangent = torch.empty_like(out)
+    with torch.cuda.device(q.device):
+        status = _lib.lib.kf_fa_jvp(_ptr(q), _ptr(k), _ptr(v), _ptr(tq), _ptr(tk), _ptr(tv), _ptr(out),
+                                    _ptr(lse), _ptr(tangent), *_dims(q, k), float(scale), int(causal),
+                                    _lib.dtype_code(q.dtype), _lib.stream_handle(q.device))
+    _lib.check(status, "kf_fa_jvp")
+    return tangent
+
+
+@_launch_jvp.register_fake
+def _launch_jvp_fake(q, k, v, tq, tk, tv, out, lse, scale, causal, block_m, block_n, threads, num_stages):
+    return torch.empty_like(out)
+
+
+@torch.library.custom_op(f"{_OP_NAMESPACE}::flash_attention_fwd_jvp", mutates_args=(), device_types="cuda")
+def _launch_fwd_jvp(
+    q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+    tq: Optional[torch.Tensor], tk: Optional[torch.Tensor], tv: Optional[torch.Tensor],
+    scale: float, causal: bool,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    out = torch.empty_like(q)
+    tangent = torch.empty_like(q)
+    lse = torch.empty((q.shape[0], q.shape[2], q.shape[1]), dtype=torch.float32, device=q.device)
+    with torch.cuda.device(q.device):
+        status = _lib.lib.kf_fa_fwd_jvp(_ptr(q), _ptr(k), _ptr(v), _ptr(tq), _ptr(tk), _ptr(tv), _ptr(out),
+                                        _ptr(lse), _ptr(tangent), *_dims(q, k), float(scale), int(causal),
+                                        _lib.dtype_code(q.dtype), _lib.stream_handle(q.device))
+    _lib.check(status, "kf_fa_fwd_jvp")
+    return out, lse, tangent
+
+
+@_launch_fwd_jvp.register_fake
+def _launch_fwd_jvp_fake(q, k, v, tq, tk, tv, scale, causal):
+    lse = q.new_empty((q.shape[0], q.shape[2], q.shape[1]), dtype=torch.float32)
+    return torch.empty_like(q), lse, torch.empty_like(q)
+
+
+# ---------------------------------------------------------------------------------------------
+# forward / backward with the flash_attn-style signatures the reference calls
+# ---------------------------------------------------------------------------------------------
+def _flash_attn_forward(q, k, v, dropout_p, softmax_scale, causal, window_size_left=-1,
+                        window_size_right=-1, softcap=0.0, alibi_slopes=None, return_softmax=False):
+    """This library's forward with flash_attn's ``_flash_attn_forward`` signature.
+
+    Returns ``(out, lse, None, None)``: LSE is fp32 ``[B, Hq, Nq]`` in natural-log units with
+    ``+inf`` for rows that see no key. Dropout, windows, softcap and ALiBi are not supported.
+    """
+    if dropout_p != 0.0 or window_size_left != -1 or window_size_right != -1 or softcap != 0.0 \
+            or alibi_slopes is not None or return_softmax:
+        raise NotImplementedError("only dropout_p=0, full windows, no softcap/ALiBi are supported")
+    out, lse = _launch_fwd(q.contiguous(), k.contiguous(), v.contiguous(), float(softmax_scale), bool(causal))
+    return out, lse, None, None
+
+
+def _flash_attn_backward(dout, q, k, v, out, lse, dq, dk, dv, dropout_p, softmax_scale, causal,
+                         window_size_left=-1, window_size_right=-1, softcap=0.0, alibi_slopes=None,
+                         deterministic=False):
+    """VJP of attention from the saved O and LSE (fp32 dense recomputation per batch on the GPU).
+
+    Outside the forward-mode hot path; writes dq, dk, dv in place like flash_attn's function.
+    """
+    if dropout_p != 0.0 or window_size_left != -1 or window_size_right != -1 or softcap != 0.0 \
+            or alibi_slopes is not None:
+        raise NotImplementedError("only dropout_p=0, full windows, no softcap/ALiBi are supported")
+    b_, nq, hq, d = q.shape
+    nk, hkv = k.shape[1], k.shape[2]
+    groups = hq // hkv
+    if causal:
+        rows = torch.arange(nq, device=q.device)[:, None]
+        cols = torch.arange(nk, device=q.device)[None, :]
+        visible = cols <= rows + nk - nq
+    for b in range(b_):
+        qh = q[b].float().transpose(0, 1)
+        kh = k[b].float().transpose(0, 1).repeat_interleave(groups, 0)
+        vh = v[b].float().transpose(0, 1).repeat_interleave(groups, 0)
+        doh = dout[b].float().transpose(0, 1)
+        oh = out[b].float().transpose(0, 1)
+        probs = torch.exp(torch.matmul(qh, kh.transpose(-1, -2)) * softmax_scale - lse[b].float()[..., None])
+        if causal:
+            probs = probs.masked_fill(~visible, 0.0)
+        dprobs = torch.matmul(doh, vh.transpose(-1, -2))
+        dscores = probs * (dprobs - (doh * oh).sum(-1, keepdim=True))
+        dq[b].copy_((torch.matmul(dscores, kh) * softmax_scale).transpose(0, 1))
+        dk_full = torch.matmul(dscores.transpose(-1, -2), qh) * softmax_scale
+        dv_full = torch.matmul(probs.transpose(-1, -2), doh)
+        dk[b].copy_(dk_full.view(hkv, groups, nk, d).sum(1).transpose(0, 1))
+        dv[b].copy_(dv_full.view(hkv, groups, nk, d).sum(1).transpose(0, 1))
+    return dq, dk, dv
+
+
+# ---------------------------------------------------------------------------------------------
+# public API (flash_attention_jvp/custom.py:137-291)
+# ---------------------------------------------------------------------------------------------
+def _attention_jvp_kernel(batch, queries, keys, heads, kv_heads, dim, dtype, scale, causal,
+                          block_m=64, block_n=64, threads=128, num_stages=2):
+    """Shape-specialised JVP callable ``kernel(Q, K, V, TQ, TK, TV, O, LSE) -> TO``."""
+    _check_schedule(block_m, block_n, threads, num_stages)
+    torch_dtype = {"float16": torch.float16, "bfloat16": torch.bfloat16}[dtype]
+    expected_q = (batch, queries, heads, dim)
+    expected_k = (batch, keys, kv_heads, dim)
+
+    def kernel(Q, K, V, TQ, TK, TV, O, LSE):
+        for t, shape in ((Q, expected_q), (TQ, expected_q), (O, expected_q), (K, expected_k),
+                         (V, expected_k), (TK, expected_k), (TV, expected_k)):
+            if tuple(t.shape) != shape or t.dtype != torch_dtype:
+                raise ValueError(f"expected {shape} {torch_dtype}, got {tuple(t.shape)} {t.dtype}")
+        return _launch_jvp(*(t.contiguous() for t in (Q, K, V, TQ, TK, TV, O)), LSE.contiguous(),
+                           float(scale), bool(causal), block_m, block_n, threads, num_stages)
+
+    return kernel
+
+
+@torch.no_grad()
+def flash_attention_jvp(
+    q, k, v, tq, tk, tv, out, lse, *, softmax_scale=None, causal=False,
+    block_m=64, block_n=None, threads=None, num_stages=None,
+):
+    """Standalone JVP using cached forward results, without a forward launch.
+
+    q/tq: [B, Nq, Hq, D]; k/tk/v/tv: [B, Nk, Hkv, D]; out: [B, Nq, Hq, D];
+    lse: [B, Hq, Nq] float32, natural logarithms, from these primals, scale and causal setting.
+    A None tangent denotes zero. The result has q's dtype and out's shape.
+    """
+    scale = _validate_inputs(q, k, v, softmax_scale)
+    if out.shape != q.shape or out.dtype != q.dtype or out.device != q.device:
+        raise ValueError("out must have q's shape, device, and dtype")
+    if lse.shape != (q.shape[0], q.shape[2], q.shape[1]) or lse.dtype != torch.float32 or lse.device != q.device:
+        raise ValueError("lse must be float32 [B, Hq, Nq] on q's device")
+    defaults = _default_jvp_config(q.shape[-1], k.shape[1], causal)
+    block_m = defaults["block_m"] if block_m is None else block_m
+    block_n = defaults["block_n"] if block_n is None else block_n
+    if threads is None:
+        threads = 128 if block_m == 16 else defaults["threads"]
+    if num_stages is None:
+        num_stages = 1 if k.shape[1] <= block_n or (not causal and k.shape[1] >= 8192) else 2
+    _check_schedule(block_m, block_n, threads, num_stages)
+    q, k, v = (x.contiguous() for x in (q, k, v))
+    tq, tk, tv = (_prepare_tangent(t, p, n) for t, p, n in zip((tq, tk, tv), (q, k, v), ("tq", "tk", "tv")))
+    return _launch_jvp(q, k, v, tq, tk, tv, out.contiguous(), lse.contiguous(),
+                       scale, bool(causal), block_m, block_n, threads, num_stages)
+
+
+@torch.no_grad()
+def flash_attention_fwd_jvp(q, k, v, tq, tk, tv, *, softmax_scale=None, causal=False):
+    """One pass over the keys: returns ``(out, lse, tangent)``.
+
+    Computes the forward output, its natural-log LSE and the JVP tangent together with the
+    online recurrences of flash-attention-jvp-derivation.md (sections 7-8): six GEMMs per tile
+    instead of the two-launch forward (2) + standalone JVP (5).
+    """
+    scale = _validate_inputs(q, k, v, softmax_scale)
+    q, k, v = (x.contiguous() for x in (q, k, v))
+    tq, tk, tv = (_prepare_tangent(t, p, n) for t, p, n in zip((tq, tk, tv), (q, k, v), ("tq", "tk", "tv")))
+    return _launch_fwd_jvp(q, k, v, tq, tk, tv, scale, bool(causal))
+
+
+class FlashAttentionFunction(torch.autograd.Function):
+    """Attention with this library's forward and forward-mode JVP, with torch.func support."""
+
+    @staticmethod
+    def forward(q, k, v, softmax_scale, causal):
+        scale = _validate_inputs(q, k, v, softmax_scale)
+        out, lse, _, _ = _flash_attn_forward(
+            q, k, v, dropout_p=0.0, softmax_scale=scale, causal=causal,
+            window_size_left=-1, window_size_right=-1, softcap=0.0,
+            alibi_slopes=None, return_softmax=False,
+        )
+        # LSE is an auxiliary output so setup_context can save it without running forward twice.
+        return out, lse
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        q, k, v, scale, causal = inputs
+        out, lse = output
+        ctx.softmax_scale = q.shape[-1] ** -0.5 if scale is None else float(scale)
+        ctx.causal = causal
+        ctx.set_materialize_grads(False)
+        ctx.mark_non_differentiable(lse)
+        ctx.save_for_backward(q, k, v, out, lse)
+        ctx.save_for_forward(q, k, v, out, lse)
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, dout, dlse):
+        if dout is None:
+            return (None,) * 5
+        q, k, v, out, lse = ctx.saved_tensors
+        dq, dk, dv = (torch.empty_like(x, memory_format=torch.contiguous_format) for x in (q, k, v))
+        _flash_attn_backward(
+            dout.contiguous(), q, k, v, out, lse, dq, dk, dv,
+            dropout_p=0.0, softmax_scale=ctx.softmax_scale, causal=ctx.causal,
+            window_size_left=-1, window_size_right=-1, softcap=0.0,
+            alibi_slopes=None, deterministic=False,
+        )
+        return dq, dk, dv, None, None
+
+    @staticmethod
+    def jvp(ctx, tq, tk, tv, tscale, tcausal):
+        q, k, v, out, lse = ctx.saved_tensors
+        tangent = flash_attention_jvp(
+            q, k, v, tq, tk, tv, out, lse,
+            softmax_scale=ctx.softmax_scale, causal=ctx.causal,
+        )
+        return tangent, None
+
+
+def flash_attention(q, k, v, *, softmax_scale=None, causal=False, return_lse=False):
+    """Attention with this library's forward, a VJP, and the custom forward-mode rule.
+
+    Return out by default, or (out, lse) when return_lse=True. The natural-log LSE is a
+    non-differentiable auxiliary output for standalone JVP calls. Supports torch.func.jvp and
+    torch.autograd.forward_ad. Dropout is fixed at zero; first-order derivatives only.
+    """
+    _validate_inputs(q, k, v, softmax_scale)
+    out, lse = FlashAttentionFunction.apply(
+        q.contiguous(), k.contiguous(), v.contiguous(), softmax_scale, bool(causal)
+    )
+    return (out, lse) if return_lse else out

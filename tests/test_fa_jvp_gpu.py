@@ -1,0 +1,324 @@
+"""FlashAttention forward / JVP parity on the GPU through the C ABI.
+
+Mirrors the reference harness flash_attention_jvp/test.py (cases, seeds, tolerances, known-answer
+properties) and adds the one-pass forward + JVP and the reference-generated golden fixtures.
+Oracle: CPU float64 (``oracle.fa_jvp``). Tolerances (flash_attention_jvp/test.py:58-59):
+fp16 atol 3e-3 / rtol 1e-2, bf16 atol = rtol = 3e-2.
+"""
+
+from pathlib import Path
+from unittest.mock import patch
+
+import pytest
+import torch
+
+from oracle.fa_jvp import attention, attention_jvp, attention_jvp_from_forward, attention_lse
+from tests.tolerances import fa_tolerance as tolerance
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+DTYPES = (torch.float16, torch.bfloat16)
+# B, Nq, Nk, Hq, Hkv, D, causal, scale (flash_attention_jvp/test.py:25-38)
+CASES = (
+    (1, 7, 11, 2, 2, 8, False, None),
+    (2, 33, 65, 4, 4, 24, False, 0.3),
+    (1, 129, 131, 3, 3, 64, False, None),
+    (1, 65, 65, 2, 2, 64, True, None),
+    (1, 19, 71, 4, 2, 96, True, None),
+    (1, 71, 19, 4, 1, 32, True, None),
+    (1, 37, 91, 6, 2, 128, False, 0.2),
+    (1, 9, 13, 2, 1, 256, False, None),
+    (1, 1, 1, 2, 2, 64, True, None),
+    (1, 17, 29, 2, 2, 16, False, 0.05),
+    (1, 23, 37, 2, 2, 80, False, 0.15),
+    (1, 999, 515, 2, 2, 64, False, None),
+)
+
+
+@pytest.fixture(scope="module")
+def fa():
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA is required")
+    import kernelforge_b200.flash_attention_jvp.custom as mod
+
+    return mod
+
+
+def make_inputs(case, dtype, *, noncontiguous=False):
+    b, nq, nk, h, hk, d, _, _ = case
+    torch.manual_seed(2026)
+    shapes = ((b, nq, h, d), (b, nk, hk, d), (b, nk, hk, d))
+    inputs = []
+    for shape in (*shapes, *shapes):
+        if noncontiguous:
+            expanded = (*shape[:-1], shape[-1] * 2)
+            x = torch.randn(expanded, device="cuda", dtype=dtype)[..., ::2]
+        else:
+            x = torch.randn(shape, device="cuda", dtype=dtype)
+        inputs.append(x)
+    return tuple(inputs)
+
+
+def double_reference(inputs):
+    return tuple(x.detach().cpu().double() for x in inputs)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("case", CASES)
+def test_standalone_jvp(fa, case, dtype):
+    q, k, v, tq, tk, tv = make_inputs(case, dtype)
+    kwargs = dict(causal=case[-2], softmax_scale=case[-1])
+    out, lse = fa.flash_attention(q, k, v, return_lse=True, **kwargs)
+    with patch("kernelforge_b200.flash_attention_jvp.custom._flash_attn_forward",
+               side_effect=AssertionError("extra forward")):
+        actual = fa.flash_attention_jvp(q, k, v, tq, tk, tv, out, lse, **kwargs)
+    ref_out, ref_tangent = attention_jvp(*double_reference((q, k, v, tq, tk, tv)), **kwargs)
+    torch.testing.assert_close(out.cpu().double(), ref_out, **tolerance(dtype))
+    torch.testing.assert_close(actual.cpu().double(), ref_tangent, **tolerance(dtype))
+    dense = attention_jvp_from_forward(q, k, v, tq, tk, tv, out, lse, **kwargs)
+    torch.testing.assert_close(actual, dense, **tolerance(dtype))
+    ref_lse = attention_lse(*double_reference((q, k)), **kwargs)
+    finite = torch.isfinite(ref_lse)
+    assert torch.equal(finite, torch.isfinite(lse.cpu()))
+    torch.testing.assert_close(lse.cpu().double()[finite], ref_lse[finite], rtol=1e-3, atol=1e-3)
+    assert actual.shape == out.shape and actual.dtype == dtype and torch.isfinite(actual).all()
+    if kwargs["causal"] and q.shape[1] > k.shape[1]:
+        assert torch.count_nonzero(actual[:, :q.shape[1] - k.shape[1]]) == 0
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("case", CASES)
+def test_one_pass_forward_and_jvp(fa, case, dtype):
+    """The fused scan gives O, LSE and tO within tolerance of the float64 oracle."""
+    q, k, v, tq, tk, tv = make_inputs(case, dtype)
+    kwargs = dict(causal=case[-2], softmax_scale=case[-1])
+    out, lse, tangent = fa.flash_attention_fwd_jvp(q, k, v, tq, tk, tv, **kwargs)
+    ref_out, ref_tangent = attention_jvp(*double_reference((q, k, v, tq, tk, tv)), **kwargs)
+    torch.testing.assert_close(out.cpu().double(), ref_out, **tolerance(dtype))
+    torch.testing.assert_close(tangent.cpu().double(), ref_tangent, **tolerance(dtype))
+    out2, lse2 = fa.flash_attention(q, k, v, return_lse=True, **kwargs)
+    torch.testing.assert_close(lse, lse2, rtol=1e-5, atol=1e-5)
+    if kwargs["causal"] and q.shape[1] > k.shape[1]:
+        empty = q.shape[1] - k.shape[1]
+        assert torch.count_nonzero(tangent[:, :empty]) == 0 and torch.count_nonzero(out[:, :empty]) == 0
+        assert torch.isinf(lse[:, :, :empty]).all()
+
+
+@pytest.mark.parametrize("index", range(7))
+def test_golden_fixtures(fa, index):
+    """Inputs and float64 outputs produced by running the reference's original.py."""
+    case = torch.load(GOLDEN / "fa_jvp_golden.pt", weights_only=False)[index]
+    b, nq, nk, h, hk, d, causal, scale = case["case"]
+    for dtype in DTYPES:
+        q, k, v, tq, tk, tv = (case[n].to(dtype).cuda() for n in ("q", "k", "v", "tq", "tk", "tv"))
+        out, lse = fa.flash_attention(q, k, v, softmax_scale=scale, causal=causal, return_lse=True)
+        tangent = fa.flash_attention_jvp(q, k, v, tq, tk, tv, out, lse, softmax_scale=scale, causal=causal)
+        torch.testing.assert_close(out.cpu().float(), case["out"], **tolerance(dtype))
+        torch.testing.assert_close(tangent.cpu().float(), case["tangent"], **tolerance(dtype))
+        o2, l2, t2 = fa.flash_attention_fwd_jvp(q, k, v, tq, tk, tv, softmax_scale=scale, causal=causal)
+        torch.testing.assert_close(t2.cpu().float(), case["tangent"], **tolerance(dtype))
+        finite = torch.isfinite(case["lse"])
+        torch.testing.assert_close(lse.cpu()[finite], case["lse"][finite], rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("causal", (False, True))
+def test_autograd_interfaces(fa, dtype, causal):
+    case = (1, 67, 41, 4, 2, 64, causal, 0.17)
+    inputs = make_inputs(case, dtype, noncontiguous=True)
+    q, k, v, tq, tk, tv = inputs
+    kwargs = dict(causal=causal, softmax_scale=case[-1])
+
+    def fn(q, k, v):
+        return fa.flash_attention(q, k, v, **kwargs)
+
+    def fn_with_lse(q, k, v):
+        return fa.flash_attention(q, k, v, return_lse=True, **kwargs)
+
+    ref_out, ref_tangent = attention_jvp(*double_reference(inputs), causal=causal, softmax_scale=case[-1])
+    out, tangent = torch.func.jvp(fn, (q, k, v), (tq, tk, tv))
+    torch.testing.assert_close(out.cpu().double(), ref_out, **tolerance(dtype))
+    torch.testing.assert_close(tangent.cpu().double(), ref_tangent, **tolerance(dtype))
+    (stats_out, lse), (stats_tangent, lse_tangent) = torch.func.jvp(fn_with_lse, (q, k, v), (tq, tk, tv))
+    torch.testing.assert_close(stats_out, out, atol=0, rtol=0)
+    torch.testing.assert_close(stats_tangent, tangent, atol=0, rtol=0)
+    assert lse.shape == (q.shape[0], q.shape[2], q.shape[1]) and lse.dtype == torch.float32
+    assert torch.count_nonzero(lse_tangent) == 0
+    with torch.autograd.forward_ad.dual_level():
+        duals = tuple(torch.autograd.forward_ad.make_dual(p, t) for p, t in zip((q, k, v), (tq, tk, tv)))
+        primal, forward_tangent = torch.autograd.forward_ad.unpack_dual(fn(*duals))
+        torch.testing.assert_close(primal, out, atol=0, rtol=0)
+        torch.testing.assert_close(forward_tangent, tangent, atol=0, rtol=0)
+        dual_stats_out, dual_lse = fn_with_lse(*duals)
+        stats_primal, stats_forward_tangent = torch.autograd.forward_ad.unpack_dual(dual_stats_out)
+        lse_primal, lse_forward_tangent = torch.autograd.forward_ad.unpack_dual(dual_lse)
+        torch.testing.assert_close(stats_primal, primal, atol=0, rtol=0)
+        torch.testing.assert_close(stats_forward_tangent, forward_tangent, atol=0, rtol=0)
+        torch.testing.assert_close(lse_primal, lse, atol=0, rtol=0)
+        assert lse_forward_tangent is None
+
+    primals = tuple(x.detach().requires_grad_() for x in (q, k, v))
+    cotangent = torch.randn_like(out)
+    actual_out = fn(*primals)
+    actual_grads = torch.autograd.grad(actual_out, primals, cotangent)
+    stats_out, lse = fn_with_lse(*primals)
+    assert not lse.requires_grad
+    stats_grads = torch.autograd.grad(stats_out, primals, cotangent)
+    torch.testing.assert_close(stats_out, actual_out, atol=0, rtol=0)
+    double_primals = tuple(x.requires_grad_() for x in double_reference(primals))
+    reference_out = attention(*double_primals, causal=causal, softmax_scale=case[-1])
+    reference_grads = torch.autograd.grad(reference_out, double_primals, cotangent.cpu().double())
+    for actual, stats, reference in zip(actual_grads, stats_grads, reference_grads):
+        torch.testing.assert_close(actual, stats, atol=0, rtol=0)
+        torch.testing.assert_close(actual.cpu().double(), reference, **tolerance(dtype))
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_missing_and_value_only_tangents(fa, dtype):
+    case = (1, 35, 49, 2, 2, 64, False, None)
+    q, k, v, tq, tk, tv = make_inputs(case, dtype)
+    out, lse = fa.flash_attention(q, k, v, return_lse=True)
+    for tangents in ((None, None, None), (None, None, tv), (tq, None, None), (None, tk, None)):
+        actual = fa.flash_attention_jvp(q, k, v, *tangents, out, lse)
+        ref_tangents = tuple(None if x is None else x.cpu().double() for x in tangents)
+        _, reference = attention_jvp(*double_reference((q, k, v)), *ref_tangents)
+        torch.testing.assert_close(actual.cpu().double(), reference, **tolerance(dtype))
+    with torch.autograd.forward_ad.dual_level():
+        dual_v = torch.autograd.forward_ad.make_dual(v, tv)
+        _, actual = torch.autograd.forward_ad.unpack_dual(fa.flash_attention(q, k, dual_v))
+    expected = fa.flash_attention_jvp(q, k, v, None, None, tv, out, lse)
+    torch.testing.assert_close(actual, expected, atol=0, rtol=0)
+    # A missing tangent and an explicit zero tangent agree exactly.
+    zeros = fa.flash_attention_jvp(q, k, v, torch.zeros_like(q), torch.zeros_like(k), tv, out, lse)
+    torch.testing.assert_close(zeros, expected, atol=0, rtol=0)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_uniform_score_shift_and_tile_sizes(fa, dtype):
+    case = (1, 39, 73, 2, 2, 64, False, None)
+    q, k, v, tq, tk, tv = make_inputs(case, dtype)
+    tk = torch.ones_like(k) * 0.25  # Q dK^T is constant across keys.
+    out, lse = fa.flash_attention(q, k, v, return_lse=True)
+    shifted = fa.flash_attention_jvp(q, k, v, None, tk, None, out, lse)
+    torch.testing.assert_close(shifted, torch.zeros_like(shifted), **tolerance(dtype))
+    _, reference = attention_jvp(*double_reference((q, k, v, tq, tk, tv)))
+    for bm, bn, threads in ((16, 32, 128), (32, 64, 128), (64, 128, 256)):
+        actual = fa.flash_attention_jvp(q, k, v, tq, tk, tv, out, lse, block_m=bm, block_n=bn, threads=threads)
+        torch.testing.assert_close(actual.cpu().double(), reference, **tolerance(dtype))
+
+
+def test_finite_difference_and_duality(fa):
+    case = (1, 23, 31, 4, 2, 32, True, None)
+    inputs = make_inputs(case, torch.float16)
+    q, k, v, tq, tk, tv = inputs
+    out, lse = fa.flash_attention(q, k, v, causal=True, return_lse=True)
+    actual = fa.flash_attention_jvp(*inputs, out, lse, causal=True)
+    primals, tangents = double_reference(inputs[:3]), double_reference(inputs[3:])
+    epsilon = 1e-4
+    plus = attention(*(p + epsilon * t for p, t in zip(primals, tangents)), causal=True)
+    minus = attention(*(p - epsilon * t for p, t in zip(primals, tangents)), causal=True)
+    torch.testing.assert_close(actual.cpu().double(), (plus - minus) / (2 * epsilon), **tolerance(q.dtype))
+    primals = tuple(x.requires_grad_() for x in inputs[:3])
+    cotangent = torch.randn_like(out)
+    grads = torch.autograd.grad(fa.flash_attention(*primals, causal=True), primals, cotangent)
+    lhs = (actual.float() * cotangent.float()).sum()
+    rhs = sum((g.float() * t.float()).sum() for g, t in zip(grads, inputs[3:]))
+    torch.testing.assert_close(lhs, rhs, atol=2e-2, rtol=1e-2)
+
+
+def test_input_validation(fa):
+    case = (1, 9, 13, 2, 2, 64, False, None)
+    q, k, v, tq, tk, tv = make_inputs(case, torch.float16)
+    out, lse = fa.flash_attention(q, k, v, return_lse=True)
+    with pytest.raises(ValueError, match="lse"):
+        fa.flash_attention_jvp(q, k, v, tq, tk, tv, out, lse.half())
+    with pytest.raises(ValueError, match="tq"):
+        fa.flash_attention_jvp(q, k, v, tq[:, :-1], tk, tv, out, lse)
+    with pytest.raises(ValueError, match="finite"):
+        fa.flash_attention(q, k, v, softmax_scale=float("nan"))
+    with pytest.raises(ValueError, match="positive"):
+        fa.flash_attention(q, k, v, softmax_scale=0.0)
+    with pytest.raises(ValueError, match="float16"):
+        fa.flash_attention(q.float(), k.float(), v.float())
+    with pytest.raises(ValueError, match="pipeline"):
+        fa.flash_attention_jvp(q, k, v, tq, tk, tv, out, lse, num_stages=4)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("causal", (False, True))
+@pytest.mark.parametrize("stages", (2, 3))
+def test_pipeline_tails_and_empty_rows(fa, dtype, causal, stages):
+    inputs = make_inputs((1, 193, 97, 4, 2, 64, causal, None), dtype)
+    out, lse = fa.flash_attention(*inputs[:3], causal=causal, return_lse=True)
+    actual = fa.flash_attention_jvp(*inputs, out, lse, causal=causal, block_m=32, block_n=32, threads=128,
+                                    num_stages=stages)
+    _, reference = attention_jvp(*double_reference(inputs), causal=causal)
+    torch.testing.assert_close(actual.cpu().double(), reference, **tolerance(dtype))
+    if causal:
+        assert torch.count_nonzero(actual[:, :96]) == 0
+
+
+def test_graph_replay_with_updated_tangent(fa):
+    inputs = make_inputs((1, 67, 131, 4, 2, 64, True, None), torch.float16)
+    out, lse = fa.flash_attention(*inputs[:3], causal=True, return_lse=True)
+    config = fa.get_jvp_config(*inputs[:3], causal=True)
+    actual = fa.flash_attention_jvp(*inputs, out, lse, causal=True)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        captured = fa.flash_attention_jvp(*inputs, out, lse, causal=True)
+    graph.replay()
+    torch.cuda.synchronize()
+    torch.testing.assert_close(captured, actual, atol=0, rtol=0)
+    inputs[5].add_(0.03125)
+    graph.replay()
+    torch.cuda.synchronize()
+    expected = fa.flash_attention_jvp(*inputs, out, lse, causal=True)
+    torch.testing.assert_close(captured, expected, atol=0, rtol=0)
+    assert fa.get_jvp_config(*inputs[:3], causal=True) == config
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("causal", (False, True))
+def test_long_key_default_and_explicit_pipeline(fa, dtype, causal):
+    inputs = make_inputs((1, 5, 8192, 2, 1, 64, causal, None), dtype)
+    out, lse = fa.flash_attention(*inputs[:3], causal=causal, return_lse=True)
+    config = fa.get_jvp_config(*inputs[:3], causal=causal)
+    assert config["num_stages"] == (2 if causal else 1)
+    actual = fa.flash_attention_jvp(*inputs, out, lse, causal=causal)
+    explicit = fa.flash_attention_jvp(*inputs, out, lse, causal=causal, num_stages=2)
+    _, reference = attention_jvp(*double_reference(inputs), causal=causal)
+    torch.testing.assert_close(actual.cpu().double(), reference, **tolerance(dtype))
+    torch.testing.assert_close(explicit.cpu().double(), reference, **tolerance(dtype))
+
+
+def test_kernel_factory_signature(fa):
+    """_attention_jvp_kernel(...) returns kernel(*inputs, out, lse), as test.py:340-344 uses it."""
+    b, n, h, d = 1, 96, 2, 64
+    inputs = make_inputs((b, n, n, h, h, d, False, None), torch.bfloat16)
+    out, lse = fa.flash_attention(*inputs[:3], return_lse=True)
+    kernel = fa._attention_jvp_kernel(b, n, n, h, h, d, "bfloat16", d ** -0.5, False, block_m=64,
+                                      block_n=64, threads=128, num_stages=2)
+    reference = attention_jvp_from_forward(*inputs, out, lse)
+    torch.testing.assert_close(kernel(*inputs, out, lse), reference, **tolerance(torch.bfloat16))
+
+
+@pytest.mark.parametrize("d", (64, 128))
+def test_baseline_config_slices(fa, d):
+    """BASELINE FA-JVP config (B=4, H=16, N=4096, bf16, non-causal): the full launch, checked on
+    one (batch, head) slice per batch against the CPU oracle, and deterministic across runs."""
+    torch.manual_seed(2026)
+    shape = (4, 4096, 16, d)
+    q, k, v, tq, tk, tv = (torch.randn(shape, device="cuda", dtype=torch.bfloat16) for _ in range(6))
+    out, lse = fa.flash_attention(q, k, v, return_lse=True)
+    tangent = fa.flash_attention_jvp(q, k, v, tq, tk, tv, out, lse)
+    out2, lse2, tangent2 = fa.flash_attention_fwd_jvp(q, k, v, tq, tk, tv)
+    again = fa.flash_attention_jvp(q, k, v, tq, tk, tv, out, lse)
+    assert torch.equal(again, tangent)
+    for b, h in ((0, 0), (1, 7), (2, 11), (3, 15)):
+        sl = [x[b:b + 1, :, h:h + 1].cpu().double() for x in (q, k, v, tq, tk, tv)]
+        ref_out, ref_tangent = attention_jvp(*sl)
+        torch.testing.assert_close(out[b:b + 1, :, h:h + 1].cpu().double(), ref_out, **tolerance(torch.bfloat16))
+        torch.testing.assert_close(tangent[b:b + 1, :, h:h + 1].cpu().double(), ref_tangent, **tolerance(torch.bfloat16))
+        torch.testing.assert_close(out2[b:b + 1, :, h:h + 1].cpu().double(), ref_out, **tolerance(torch.bfloat16))
+        torch.testing.assert_close(tangent2[b:b + 1, :, h:h + 1].cpu().double(), ref_tangent, **tolerance(torch.bfloat16))
+    torch.testing.assert_close(lse2, lse, rtol=1e-5, atol=1e-5)

@@ -23,19 +23,32 @@ def ulp_of(values: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     return torch.pow(2.0, exponent - _MANTISSA_BITS[dtype])
 
 
+def ulp_distance(actual: torch.Tensor, expected: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """Number of representable ``dtype`` values between actual and expected (both rounded to
+    ``dtype``), from the ordering of their bit patterns."""
+    int_type = {torch.bfloat16: torch.int16, torch.float16: torch.int16, torch.float32: torch.int32}[dtype]
+    sign_mask = {torch.int16: 0x7FFF, torch.int32: 0x7FFFFFFF}[int_type]
+
+    def key(t):
+        i = t.detach().to("cpu").to(dtype).contiguous().view(int_type).to(torch.int64)
+        return torch.where(i < 0, -(i & sign_mask), i)
+
+    return (key(actual) - key(expected)).abs()
+
+
 def assert_within_ulps(actual: torch.Tensor, expected: torch.Tensor, ulps: int = 1, dtype=None):
     dtype = dtype or expected.dtype
-    a = actual.detach().to("cpu", torch.float64)
-    e = expected.detach().to("cpu", torch.float64)
-    assert a.shape == e.shape, (a.shape, e.shape)
-    diff = (a - e).abs()
-    bound = ulps * ulp_of(e, dtype)
-    bad = diff > bound
+    assert actual.shape == expected.shape, (actual.shape, expected.shape)
+    dist = ulp_distance(actual, expected, dtype)
+    bad = dist > ulps
     if bad.any():
+        a = actual.detach().to("cpu", torch.float64)
+        e = expected.detach().to("cpu", torch.float64)
         idx = torch.nonzero(bad)[0].tolist()
         raise AssertionError(
             f"{int(bad.sum())} of {bad.numel()} elements differ by more than {ulps} ulp "
-            f"(first at {idx}: actual={a[tuple(idx)].item()!r} expected={e[tuple(idx)].item()!r})"
+            f"(max {int(dist.max())}; first at {idx}: actual={a[tuple(idx)].item()!r} "
+            f"expected={e[tuple(idx)].item()!r})"
         )
 
 
@@ -59,3 +72,20 @@ def assert_close_ulp_atol(actual, expected, *, dtype, ulps=1, atol=1e-2):
 def fa_tolerance(dtype):
     """FlashAttention-JVP tolerances of the reference harness (flash_attention_jvp/test.py:58-59)."""
     return {torch.float16: dict(atol=3e-3, rtol=1e-2), torch.bfloat16: dict(atol=3e-2, rtol=3e-2)}[dtype]
+
+
+def assert_rmsnorm_close(actual, expected):
+    """RMSNorm bar (rmsnorm/original.py:51-52 double rounding).
+
+    The normalised row is rounded to the 16-bit dtype before the weight multiply. When the
+    kernel's fp32 row scale differs from the oracle's in its last bit (summation order), the
+    intermediate can round one ulp differently, and multiplying by a weight below one can turn
+    that into two ulps of the output. So every element is within 2 ulps (ulp distance counted
+    in representable values) and within the reference harness tolerance rtol = atol = 2e-2
+    (rmsnorm/test.py:62-63). fp32 outputs: rtol 1e-5.
+    """
+    if expected.dtype == torch.float32:
+        torch.testing.assert_close(actual.detach().cpu(), expected.detach().cpu(), rtol=1e-5, atol=1e-6)
+        return
+    assert_within_ulps(actual, expected, ulps=2)
+    torch.testing.assert_close(actual.detach().cpu().float(), expected.detach().cpu().float(), rtol=2e-2, atol=2e-2)
