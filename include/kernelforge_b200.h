@@ -91,6 +91,27 @@ int kf_sana_linattn_fwd(const void* qkv, void* out, void* workspace, size_t work
                         int64_t batch, int64_t heads, int64_t dim, int64_t seq_len, int64_t splits,
                         float eps, int in_dtype, int out_dtype, void* stream);
 
+/*
+ * kf_sana_linattn_fwd without a workspace, for callers that cannot allocate device memory
+ * (code running inside another runtime's memory manager or allocator hook, or under a fixed
+ * memory budget). No counterpart in the reference. It allocates nothing: its scratch is a
+ * file-scope device array of kf_sana_noalloc_scratch_bytes() bytes (16 MiB), which every GPU
+ * that loads the library holds until exit. The caller still passes qkv and out.
+ * - Shapes whose scratch does not fit are rejected with KF_ERR_WORKSPACE before any launch
+ *   (the bf16/fp16 head_dim-32 path needs batch*heads*4224 bytes; other shapes use fewer
+ *   splits until their partials fit).
+ * - The first call on a device looks up the array's device address (cudaGetSymbolAddress);
+ *   make that first call outside any stream capture.
+ * - Every call shares the one array: calls that overlap on the GPU (other streams, other
+ *   threads) race. Order them on one stream. The arrival counters are zeroed by each call.
+ */
+int kf_sana_linattn_fwd_noalloc(const void* qkv, void* out, int64_t batch, int64_t heads,
+                                int64_t dim, int64_t seq_len, int64_t splits, float eps,
+                                int in_dtype, int out_dtype, void* stream);
+
+/* Size in bytes of the fixed scratch array used by kf_sana_linattn_fwd_noalloc. */
+size_t kf_sana_noalloc_scratch_bytes(void);
+
 /* ------------------------------------------------------------------------------------------
  * FlashAttention forward and forward-mode JVP.
  * Layout: q, tq, out, tangent_out [batch, q_len, q_heads, head_dim]; k, v, tk, tv

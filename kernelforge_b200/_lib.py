@@ -36,6 +36,9 @@ SIGNATURES = {
     "kf_sana_linattn_fwd": (ctypes.c_int, [_c_ptr, _c_ptr, _c_ptr, ctypes.c_size_t, _c_i64, _c_i64,
                                            _c_i64, _c_i64, _c_i64, ctypes.c_float, ctypes.c_int,
                                            ctypes.c_int, _c_ptr]),
+    "kf_sana_linattn_fwd_noalloc": (ctypes.c_int, [_c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
+                                                   ctypes.c_float, ctypes.c_int, ctypes.c_int, _c_ptr]),
+    "kf_sana_noalloc_scratch_bytes": (ctypes.c_size_t, []),
     "kf_fa_fwd": (ctypes.c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64,
                                  _c_i64, _c_i64, ctypes.c_float, ctypes.c_int, ctypes.c_int, _c_ptr]),
     "kf_fa_jvp": (ctypes.c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr,

@@ -713,3 +713,99 @@ KF_API int kf_sana_linattn_fwd(const void* qkv, void* out, void* workspace, size
       return launch_generic<__nv_bfloat16>(qkv, out, partial, final_vk, counters, B, H, d, N, S_gen, eps, out_dtype, s);
   }
 }
+
+// ------------------------------------------------------------------------------------------
+// No-allocation variant of kf_sana_linattn_fwd.
+//
+// Some callers cannot allocate device memory at call time: code that runs inside another
+// runtime's memory manager or a custom allocator hook, or that owns a fixed memory budget
+// and may not grow it. For them the scratch (the reduced K^T V / ksum, and for the generic
+// path the split partials and arrival counters) lives in this file-scope device array instead
+// of a caller-provided workspace. Every GPU that loads the library holds it until exit.
+// ------------------------------------------------------------------------------------------
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB
+static __device__ __align__(256) uint8_t g_sana_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+// Device address of the scratch array on the current device. In host code the array's name is
+// only a host-side stand-in, so the address comes from cudaGetSymbolAddress, once per device.
+int noalloc_scratch(uint8_t** out) {
+  static uint8_t* addr[64] = {};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return KF_ERR_CUDA;
+  }
+  if (dev < 0 || dev >= 64) return KF_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_sana_noalloc_scratch) != cudaSuccess || p == nullptr) {
+      (void)cudaGetLastError();
+      return KF_ERR_CUDA;
+    }
+    addr[dev] = static_cast<uint8_t*>(p);
+  }
+  *out = addr[dev];
+  return KF_OK;
+}
+
+}  // namespace
+
+KF_API size_t kf_sana_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
+
+KF_API int kf_sana_linattn_fwd_noalloc(const void* qkv, void* out, int64_t batch, int64_t heads,
+                                       int64_t dim, int64_t seq_len, int64_t splits, float eps,
+                                       int in_dtype, int out_dtype, void* stream) {
+  if (!kf::dtype_valid(in_dtype) || !kf::dtype_valid(out_dtype)) return KF_ERR_UNSUPPORTED;
+  if (batch <= 0 || heads <= 0 || seq_len <= 0) return KF_ERR_INVALID_ARGUMENT;
+  if (!valid_head_dim(dim)) return KF_ERR_UNSUPPORTED;
+  if (qkv == nullptr || out == nullptr) return KF_ERR_INVALID_ARGUMENT;
+  if (!(eps >= 0.f)) return KF_ERR_INVALID_ARGUMENT;
+  if (batch > 65535 || seq_len > (int64_t(1) << 30) || heads * dim > (int64_t(1) << 24) ||
+      batch * seq_len * 3 * heads * dim > (int64_t(1) << 40))
+    return KF_ERR_UNSUPPORTED;
+  if (!kf::aligned(qkv, kf::dtype_size(in_dtype)) || !kf::aligned(out, kf::dtype_size(out_dtype)))
+    return KF_ERR_MISALIGNED;
+  const int B = static_cast<int>(batch), H = static_cast<int>(heads), d = static_cast<int>(dim);
+  const int N = static_cast<int>(seq_len);
+  const size_t per_head = static_cast<size_t>(d + 1) * d * sizeof(float);
+  const bool fast = d == kD && (in_dtype == KF_DTYPE_BF16 || in_dtype == KF_DTYPE_F16) &&
+                    H * kD >= 64 && N >= kTok && kf::aligned(qkv, 16) && kf::aligned(out, 16);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (fast) {
+    // Only the reduced K^T V / ksum (B*H*33*32 floats) is needed.
+    if (static_cast<size_t>(batch) * heads * per_head > kNoAllocScratchBytes) return KF_ERR_WORKSPACE;
+    uint8_t* scratch = nullptr;
+    const int st = noalloc_scratch(&scratch);
+    if (st != KF_OK) return st;
+    float* final_vk = reinterpret_cast<float*>(scratch);
+    const int S = fast_splits(B, H, N, splits);
+    if (in_dtype == KF_DTYPE_BF16)
+      return launch_fast<__nv_bfloat16, kFastHeads>(qkv, out, final_vk, B, H, N, S, eps, out_dtype, s);
+    return launch_fast<__half, kFastHeads>(qkv, out, final_vk, B, H, N, S, eps, out_dtype, s);
+  }
+  // Generic path: as many splits as the default asks for and the scratch holds.
+  int S = generic_splits(batch, heads, seq_len, splits);
+  while (S > 1 && layout_for(batch, heads, dim, S).total > kNoAllocScratchBytes) --S;
+  const WorkspaceLayout lay = layout_for(batch, heads, dim, S);
+  if (lay.total > kNoAllocScratchBytes) return KF_ERR_WORKSPACE;
+  uint8_t* scratch = nullptr;
+  const int st = noalloc_scratch(&scratch);
+  if (st != KF_OK) return st;
+  float* partial = reinterpret_cast<float*>(scratch + lay.partial_off);
+  float* final_vk = reinterpret_cast<float*>(scratch + lay.final_off);
+  unsigned int* counters = reinterpret_cast<unsigned int*>(scratch + lay.counter_off);
+  // The arrival counters must start at zero; the array keeps whatever the last call left.
+  KF_CUDA_TRY(cudaMemsetAsync(counters, 0, static_cast<size_t>(batch) * heads * sizeof(unsigned int), s));
+  switch (in_dtype) {
+    case KF_DTYPE_F32:
+      return launch_generic<float>(qkv, out, partial, final_vk, counters, B, H, d, N, S, eps, out_dtype, s);
+    case KF_DTYPE_F16:
+      return launch_generic<__half>(qkv, out, partial, final_vk, counters, B, H, d, N, S, eps, out_dtype, s);
+    default:
+      return launch_generic<__nv_bfloat16>(qkv, out, partial, final_vk, counters, B, H, d, N, S, eps, out_dtype, s);
+  }
+}
