@@ -68,6 +68,8 @@ KF_API int kf_fa_jvp(const void* q, const void* k, const void* v, const void* tq
   a.o_in = out;
   a.lse_in = lse;
   a.to_out = tangent_out;
+  if (kf::fa::sm100_jvp_supported(a))
+    return kf::fa::launch_sm100_jvp(a, dtype, static_cast<cudaStream_t>(stream));
   return kf::fa::launch_general(a, kf::fa::kModeJvp, dtype, static_cast<cudaStream_t>(stream));
 }
 

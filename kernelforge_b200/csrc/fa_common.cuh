@@ -30,4 +30,8 @@ struct FaArgs {
 // mma.sync path: any D in 8..256 (multiple of 8), fp16 / bf16.
 int launch_general(const FaArgs& a, int mode, int dtype, cudaStream_t stream);
 
+// tcgen05 / TMEM / TMA path of the standalone JVP: D in {64, 128}, at least one tangent.
+bool sm100_jvp_supported(const FaArgs& a);
+int launch_sm100_jvp(const FaArgs& a, int dtype, cudaStream_t stream);
+
 }  // namespace kf::fa

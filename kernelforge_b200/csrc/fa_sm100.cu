@@ -1,0 +1,352 @@
+// FlashAttention forward-mode JVP on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// Standalone JVP from a cached O and LSE (flash_attention_jvp/custom.py:12-120):
+//   P  = exp(gamma * Q K^T - LSE)                     (keys masked to 0)
+//   H  = P * gamma * (tQ K^T + Q tK^T)
+//   tO = P tV + H V - rowsum(H) * O
+//
+// One CTA owns 128 query rows of one (batch, head); one thread of the softmax warpgroup owns
+// one row (= one TMEM lane). Warp roles:
+//   warp 0      TMA producer: Q, tQ once; a ring of {K, tK, V, tV} tiles of 64 keys
+//   warp 1      TMEM owner and single-thread MMA issuer
+//   warps 2..5  scores -> P, H (into TMEM as 16-bit A operands), row sums, epilogue
+// Tensor memory (512 columns x 128 lanes, fp32):
+//   [0, D)                         tO accumulator (D <= 128)
+//   [128 + 128 b, +64)  b = 0, 1   S of key tile j (b = j & 1); P (bf16 pairs) overwrites it
+//   [192 + 128 b, +64)             dS = tQ K^T + Q tK^T;        H (bf16 pairs) overwrites it
+// Double-buffered S / dS let the tensor core compute tile j+1's scores while the softmax
+// warps turn tile j into P and H. Per 64-key tile the MMA warp issues
+//   S  = Q K^T            (D/16 x M128 N64 K16, operands from shared memory)
+//   dS = tQ K^T + Q tK^T  (2 D/16 x M128 N64 K16)
+//   tO += P tV + H V      (2 x 4 x M128 N=D K16, A from tensor memory, B MN-major)
+// All operand tiles arrive by TMA with 128-byte swizzle; every wait is a bounded mbarrier
+// wait that records KF_ERR_DEVICE_TIMEOUT in the module's error word and gives up.
+#include "fa_common.cuh"
+#include "kf_tcgen05.cuh"
+
+namespace {
+
+using kf::fa::FaArgs;
+
+__device__ unsigned int g_fa_error = 0;
+
+constexpr int kBM = 128;       // query rows per CTA (one TMEM lane each)
+constexpr int kBN = 64;        // keys per tile
+constexpr int kThreads = 192;  // 6 warps
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kAccCol = 0;
+constexpr uint32_t kBufCol = 128;  // S of buffer b at kBufCol + 128 b, dS 64 columns further
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <int D> struct JvpCfg {
+  static constexpr int kStages = D == 64 ? 4 : 2;
+  static constexpr int kKB = D / 64;                    // 128-byte boxes along the head dim
+  static constexpr int kQBytes = kKB * kBM * 128;       // Q or tQ
+  static constexpr int kTileBytes = kKB * kBN * 128;    // K, tK, V or tV of one tile
+  static constexpr int kStageBytes = 4 * kTileBytes;
+  static constexpr int kBarOffset = 2 * kQBytes + kStages * kStageBytes;
+  static constexpr int kSmemBytes = kBarOffset + 256 + 1024;  // barriers + alignment slack
+};
+
+__device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
+  return bf16 ? kf::Mma<__nv_bfloat16>::from_f2(a, b) : kf::Mma<__half>::from_f2(a, b);
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads, 1)
+fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_tq,
+                    const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_tk,
+                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_tv,
+                    const FaArgs p) {
+  using C = JvpCfg<D>;
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (kf::smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t* q_s = smem;
+  uint8_t* tq_s = smem + C::kQBytes;
+  uint8_t* kv_s = smem + 2 * C::kQBytes;
+  uint64_t* q_full = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
+  uint64_t* kv_full = q_full + 1;
+  uint64_t* kv_empty = kv_full + C::kStages;
+  uint64_t* s_full = kv_empty + C::kStages;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* pv_done = p_full + 2;
+  uint64_t* acc_full = pv_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qtile = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int q0 = qtile * kBM;
+  const int kvh = h / (p.Hq / p.Hkv);
+  const bool has_tq = p.tq != nullptr, has_tk = p.tk != nullptr, has_tv = p.tv != nullptr;
+  const bool has_h = has_tq || has_tk;
+  int k_end = p.Nk;
+  if (p.causal) k_end = min(p.Nk, max(0, q0 + kBM + p.Nk - p.Nq));
+  const int ntiles = (k_end + kBN - 1) / kBN;
+
+  if (threadIdx.x == 0) {
+    kf::mbar_init(q_full, 1);
+    for (int s = 0; s < C::kStages; ++s) {
+      kf::mbar_init(&kv_full[s], 1);
+      kf::mbar_init(&kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      kf::mbar_init(&s_full[i], 1);
+      kf::mbar_init(&p_full[i], kBM);
+      kf::mbar_init(&pv_done[i], 1);
+    }
+    kf::mbar_init(acc_full, 1);
+    kf::fence_mbar_init();
+  }
+  if (warp == 1) kf::tc::tmem_alloc(tmem_slot, kTmemCols);
+  kf::tc::fence_before_sync();
+  __syncthreads();
+  kf::tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      kf::prefetch_tensormap(&tm_q);
+      kf::prefetch_tensormap(&tm_k);
+      kf::mbar_arrive_expect_tx(q_full, C::kQBytes * (has_tq ? 2 : 1));
+      for (int kb = 0; kb < C::kKB; ++kb) {
+        kf::tma_load_4d(q_s + kb * kBM * 128, &tm_q, q_full, kb * 64, h, q0, b);
+        if (has_tq) kf::tma_load_4d(tq_s + kb * kBM * 128, &tm_tq, q_full, kb * 64, h, q0, b);
+      }
+      const uint32_t kv_bytes = C::kTileBytes * (1 + (has_tk ? 1 : 0) + (has_h ? 1 : 0) + (has_tv ? 1 : 0));
+      for (int j = 0; j < ntiles; ++j) {
+        const int stage = j % C::kStages;
+        if (j >= C::kStages &&
+            !kf::mbar_wait_bounded(&kv_empty[stage], ((j / C::kStages) - 1) & 1, &g_fa_error))
+          break;
+        uint8_t* base = kv_s + stage * C::kStageBytes;
+        kf::mbar_arrive_expect_tx(&kv_full[stage], kv_bytes);
+        for (int kb = 0; kb < C::kKB; ++kb) {
+          const int off = kb * kBN * 128;
+          kf::tma_load_4d(base + off, &tm_k, &kv_full[stage], kb * 64, kvh, j * kBN, b);
+          if (has_tk) kf::tma_load_4d(base + C::kTileBytes + off, &tm_tk, &kv_full[stage], kb * 64, kvh, j * kBN, b);
+          if (has_h) kf::tma_load_4d(base + 2 * C::kTileBytes + off, &tm_v, &kv_full[stage], kb * 64, kvh, j * kBN, b);
+          if (has_tv) kf::tma_load_4d(base + 3 * C::kTileBytes + off, &tm_tv, &kv_full[stage], kb * 64, kvh, j * kBN, b);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idS = kf::tc::idesc_f16(kBf16 ? 1 : 0, kBM, kBN, false, false);
+      constexpr uint32_t idPV = kf::tc::idesc_f16(kBf16 ? 1 : 0, kBM, D, false, true);
+      const uint32_t q_addr = kf::smem_u32(q_s), tq_addr = kf::smem_u32(tq_s);
+      bool ok = kf::mbar_wait_bounded(q_full, 0, &g_fa_error);
+      kf::tc::fence_after_sync();
+      uint32_t acc_started = 0;
+      for (int j = 0; ok && j <= ntiles; ++j) {
+        if (j < ntiles) {
+          const int stage = j % C::kStages, buf = j & 1;
+          if (j >= 2 && !kf::mbar_wait_bounded(&pv_done[buf], ((j >> 1) - 1) & 1, &g_fa_error)) break;
+          if (!kf::mbar_wait_bounded(&kv_full[stage], (j / C::kStages) & 1, &g_fa_error)) break;
+          kf::tc::fence_after_sync();
+          const uint32_t base = kf::smem_u32(kv_s + stage * C::kStageBytes);
+          const uint32_t s_col = tmem + kBufCol + 128 * buf;
+          const uint32_t ts_col = s_col + 64;
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
+            const uint32_t koff = (k >> 2) * kBN * 128 + (k & 3) * 32;
+            kf::tc::mma_ss(s_col, kf::tc::desc_sw128(q_addr + off, 16, 1024),
+                           kf::tc::desc_sw128(base + koff, 16, 1024), idS, k > 0);
+          }
+          uint32_t ts_started = 0;
+          if (has_tq) {
+#pragma unroll
+            for (int k = 0; k < D / 16; ++k) {
+              const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
+              const uint32_t koff = (k >> 2) * kBN * 128 + (k & 3) * 32;
+              kf::tc::mma_ss(ts_col, kf::tc::desc_sw128(tq_addr + off, 16, 1024),
+                             kf::tc::desc_sw128(base + koff, 16, 1024), idS, ts_started);
+              ts_started = 1;
+            }
+          }
+          if (has_tk) {
+#pragma unroll
+            for (int k = 0; k < D / 16; ++k) {
+              const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
+              const uint32_t koff = (k >> 2) * kBN * 128 + (k & 3) * 32;
+              kf::tc::mma_ss(ts_col, kf::tc::desc_sw128(q_addr + off, 16, 1024),
+                             kf::tc::desc_sw128(base + C::kTileBytes + koff, 16, 1024), idS, ts_started);
+              ts_started = 1;
+            }
+          }
+          kf::tc::commit(&s_full[buf]);
+        }
+        if (j >= 1) {
+          const int jj = j - 1, buf = jj & 1, stage = jj % C::kStages;
+          if (!kf::mbar_wait_bounded(&p_full[buf], (jj >> 1) & 1, &g_fa_error)) break;
+          kf::tc::fence_after_sync();
+          const uint32_t base = kf::smem_u32(kv_s + stage * C::kStageBytes);
+          const uint32_t p_col = tmem + kBufCol + 128 * buf;
+          const uint32_t h_col = p_col + 64;
+#pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk) {
+            if (has_tv) {
+              kf::tc::mma_ts(tmem + kAccCol, p_col + kk * 8,
+                             kf::tc::desc_sw128(base + 3 * C::kTileBytes + kk * 2048, kBN * 128, 1024),
+                             idPV, acc_started);
+              acc_started = 1;
+            }
+            if (has_h) {
+              kf::tc::mma_ts(tmem + kAccCol, h_col + kk * 8,
+                             kf::tc::desc_sw128(base + 2 * C::kTileBytes + kk * 2048, kBN * 128, 1024),
+                             idPV, acc_started);
+              acc_started = 1;
+            }
+          }
+          kf::tc::commit(&pv_done[buf]);
+          kf::tc::commit(&kv_empty[stage]);
+        }
+      }
+      kf::tc::commit(acc_full);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax / epilogue
+    const int quarter = warp & 3;  // warps 2, 3, 4, 5 own TMEM lanes 64, 96, 0, 32 + lane
+    const int row = quarter * 32 + lane;
+    const int qrow = q0 + row;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const float lse_l2 = qrow < p.Nq ? p.lse_in[(static_cast<int64_t>(b) * p.Hq + h) * p.Nq + qrow] * kLog2e
+                                     : __int_as_float(0x7f800000);
+    // Keys [0, limit) are visible to this row.
+    const int limit = p.causal ? min(p.Nk, qrow + p.Nk - p.Nq + 1) : p.Nk;
+    float csum = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      const int buf = j & 1;
+      ok = kf::mbar_wait_bounded(&s_full[buf], (j >> 1) & 1, &g_fa_error);
+      if (!ok) break;
+      kf::tc::fence_after_sync();
+      const uint32_t s_col = lane_base + kBufCol + 128 * buf;
+      const uint32_t ts_col = s_col + 64;
+      const int k0 = j * kBN;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t sr[32], tr[32];
+        kf::tc::ld_32x32b_x32(s_col + c * 32, sr);
+        if (has_h) kf::tc::ld_32x32b_x32(ts_col + c * 32, tr);
+        kf::tc::wait_ld();
+        uint32_t pp[16], hh[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int key = k0 + c * 32 + 2 * i;
+          const float p0 = key < limit ? exp2f(fmaf(__uint_as_float(sr[2 * i]), p.scale_log2, -lse_l2)) : 0.f;
+          const float p1 = key + 1 < limit ? exp2f(fmaf(__uint_as_float(sr[2 * i + 1]), p.scale_log2, -lse_l2)) : 0.f;
+          pp[i] = pack2(p0, p1, kBf16);
+          if (has_h) {
+            const float h0 = p0 * __uint_as_float(tr[2 * i]) * p.scale;
+            const float h1 = p1 * __uint_as_float(tr[2 * i + 1]) * p.scale;
+            csum += h0 + h1;
+            hh[i] = pack2(h0, h1, kBf16);
+          }
+        }
+        kf::tc::st_32x32b_x16(s_col + c * 16, pp);
+        if (has_h) kf::tc::st_32x32b_x16(ts_col + c * 16, hh);
+      }
+      kf::tc::wait_st();
+      kf::tc::fence_before_sync();
+      kf::mbar_arrive(&p_full[buf]);
+    }
+    // Epilogue: tO = acc - rowsum(H) * O
+    if (ok) ok = kf::mbar_wait_bounded(acc_full, 0, &g_fa_error);
+    if (ok) {
+      kf::tc::fence_after_sync();
+      const int64_t roff = ((static_cast<int64_t>(b) * p.Nq + qrow) * p.Hq + h) * D;
+      const T* orow = static_cast<const T*>(p.o_in) + roff;
+      T* trow = static_cast<T*>(p.to_out) + roff;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t ar[32];
+        kf::tc::ld_32x32b_x32(lane_base + kAccCol + c * 32, ar);
+        kf::tc::wait_ld();
+        if (qrow < p.Nq) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            const uint4 o = *reinterpret_cast<const uint4*>(orow + c * 32 + v * 8);
+            const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
+            uint32_t tw[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 of = kf::Mma<T>::to_f2(ow[e]);
+              const int i = v * 8 + e * 2;
+              const float a0 = ntiles > 0 ? __uint_as_float(ar[i]) : 0.f;
+              const float a1 = ntiles > 0 ? __uint_as_float(ar[i + 1]) : 0.f;
+              tw[e] = pack2(a0 - csum * of.x, a1 - csum * of.y, kBf16);
+            }
+            *reinterpret_cast<uint4*>(trow + c * 32 + v * 8) = make_uint4(tw[0], tw[1], tw[2], tw[3]);
+          }
+        }
+      }
+    }
+  }
+  kf::tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    kf::tc::fence_after_sync();
+    kf::tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+bool encode_bnhd(CUtensorMap* map, const void* base, int dtype, int B, int N, int H, int D, int rows) {
+  const uint64_t es = 2;
+  const uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(H), static_cast<uint64_t>(N),
+                            static_cast<uint64_t>(B)};
+  const uint64_t strides[3] = {D * es, static_cast<uint64_t>(H) * D * es,
+                               static_cast<uint64_t>(N) * H * D * es};
+  const uint32_t box[4] = {64, 1, static_cast<uint32_t>(rows), 1};
+  return kf_host::encode_tiled(map, kf_host::map_type(dtype), 4, base, dims, strides, box,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <typename T, int D>
+int launch_jvp(const FaArgs& a, int dtype, cudaStream_t stream) {
+  using C = JvpCfg<D>;
+  CUtensorMap mq, mtq, mk, mtk, mv, mtv;
+  if (!encode_bnhd(&mq, a.q, dtype, a.B, a.Nq, a.Hq, D, kBM) ||
+      !encode_bnhd(&mtq, a.tq ? a.tq : a.q, dtype, a.B, a.Nq, a.Hq, D, kBM) ||
+      !encode_bnhd(&mk, a.k, dtype, a.B, a.Nk, a.Hkv, D, kBN) ||
+      !encode_bnhd(&mtk, a.tk ? a.tk : a.k, dtype, a.B, a.Nk, a.Hkv, D, kBN) ||
+      !encode_bnhd(&mv, a.v, dtype, a.B, a.Nk, a.Hkv, D, kBN) ||
+      !encode_bnhd(&mtv, a.tv ? a.tv : a.v, dtype, a.B, a.Nk, a.Hkv, D, kBN))
+    return KF_ERR_CUDA;
+  auto kernel = fa_jvp_sm100_kernel<T, D>;
+  const int prep = kf_host::prepare_kernel(reinterpret_cast<const void*>(kernel), kThreads, C::kSmemBytes, nullptr);
+  if (prep != KF_OK) return prep;
+  const dim3 grid((a.Nq + kBM - 1) / kBM, a.Hq, a.B);
+  kernel<<<grid, kThreads, C::kSmemBytes, stream>>>(mq, mtq, mk, mtk, mv, mtv, a);
+  KF_LAUNCH_CHECK();
+  return KF_OK;
+}
+
+}  // namespace
+
+int kf_internal_fa_error(unsigned int* code) {
+  unsigned int v = 0;
+  KF_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_fa_error, sizeof(v)));
+  if (v != 0) {
+    const unsigned int zero = 0;
+    KF_CUDA_TRY(cudaMemcpyToSymbol(g_fa_error, &zero, sizeof(zero)));
+  }
+  *code = v;
+  return KF_OK;
+}
+
+namespace kf::fa {
+
+bool sm100_jvp_supported(const FaArgs& a) {
+  return (a.D == 64 || a.D == 128) && (a.tq != nullptr || a.tk != nullptr || a.tv != nullptr);
+}
+
+int launch_sm100_jvp(const FaArgs& a, int dtype, cudaStream_t s) {
+  if (dtype == KF_DTYPE_BF16) return a.D == 64 ? launch_jvp<__nv_bfloat16, 64>(a, dtype, s) : launch_jvp<__nv_bfloat16, 128>(a, dtype, s);
+  return a.D == 64 ? launch_jvp<__half, 64>(a, dtype, s) : launch_jvp<__half, 128>(a, dtype, s);
+}
+
+}  // namespace kf::fa

@@ -2,6 +2,7 @@
 #include "kf_common.cuh"
 
 int kf_internal_sana_error(unsigned int* code);
+int kf_internal_fa_error(unsigned int* code);
 
 KF_API const char* kf_status_string(int status) {
   switch (status) {
@@ -26,5 +27,9 @@ KF_API int kf_query_device_error(void* stream, int* code) {
   int st = kf_internal_sana_error(&sana);
   if (st != KF_OK) return st;
   if (sana != 0 && *code == KF_OK) *code = static_cast<int>(sana);
+  unsigned int fa = 0;
+  st = kf_internal_fa_error(&fa);
+  if (st != KF_OK) return st;
+  if (fa != 0 && *code == KF_OK) *code = static_cast<int>(fa);
   return KF_OK;
 }

@@ -1,5 +1,5 @@
-// sm_100a primitives written as inline PTX: mbarriers, TMA (cp.async.bulk.tensor, no
-// multicast anywhere), ldmatrix and legacy-shape mma.sync, plus host-side tensor-map encoding
+// sm_100a primitives written as inline PTX: mbarriers, TMA (cp.async.bulk.tensor, single-CTA
+// copies only), ldmatrix and legacy-shape mma.sync, plus host-side tensor-map encoding
 // through the driver entry point (no link-time dependency on libcuda).
 #pragma once
 
@@ -92,7 +92,7 @@ __device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
 }
 
 // ------------------------------------------------------------------------------------------
-// TMA (tensor copies through the async proxy). No .multicast::cluster form is used anywhere.
+// TMA (tensor copies through the async proxy). Every load here is a plain single-CTA copy.
 // ------------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int c0, int c1, int c2, int c3) {
