@@ -49,6 +49,8 @@ KF_API int kf_fa_fwd(const void* q, const void* k, const void* v, void* out, flo
                        head_dim, softmax_scale, causal);
   a.o_out = out;
   a.lse_out = lse;
+  if (kf::fa::sm100_fused_supported(a, kf::fa::kModeFwd))
+    return kf::fa::launch_sm100_fused(a, kf::fa::kModeFwd, dtype, static_cast<cudaStream_t>(stream));
   return kf::fa::launch_general(a, kf::fa::kModeFwd, dtype, static_cast<cudaStream_t>(stream));
 }
 
@@ -89,5 +91,7 @@ KF_API int kf_fa_fwd_jvp(const void* q, const void* k, const void* v, const void
   a.o_out = out;
   a.lse_out = lse;
   a.to_out = tangent_out;
+  if (kf::fa::sm100_fused_supported(a, kf::fa::kModeFwdJvp))
+    return kf::fa::launch_sm100_fused(a, kf::fa::kModeFwdJvp, dtype, static_cast<cudaStream_t>(stream));
   return kf::fa::launch_general(a, kf::fa::kModeFwdJvp, dtype, static_cast<cudaStream_t>(stream));
 }

@@ -34,4 +34,9 @@ int launch_general(const FaArgs& a, int mode, int dtype, cudaStream_t stream);
 bool sm100_jvp_supported(const FaArgs& a);
 int launch_sm100_jvp(const FaArgs& a, int dtype, cudaStream_t stream);
 
+// tcgen05 / TMEM / TMA path of the forward (kModeFwd) and one-pass forward + JVP
+// (kModeFwdJvp): D in {64, 128}; the one-pass mode needs at least one tangent.
+bool sm100_fused_supported(const FaArgs& a, int mode);
+int launch_sm100_fused(const FaArgs& a, int mode, int dtype, cudaStream_t stream);
+
 }  // namespace kf::fa

@@ -5,11 +5,14 @@
 //   H  = P * gamma * (tQ K^T + Q tK^T)
 //   tO = P tV + H V - rowsum(H) * O
 //
-// One CTA owns 128 query rows of one (batch, head); one thread of the softmax warpgroup owns
+// One CTA owns 128 query rows of one (batch, head); in each softmax warpgroup one thread owns
 // one row (= one TMEM lane). Warp roles:
-//   warp 0      TMA producer: Q, tQ once; a ring of {K, tK, V, tV} tiles of 64 keys
-//   warp 1      TMEM owner and single-thread MMA issuer
-//   warps 2..5  scores -> P, H (into TMEM as 16-bit A operands), row sums, epilogue
+//   warps 0..3  softmax warpgroup 0: even key tiles (score buffer 0)
+//   warps 4..7  softmax warpgroup 1: odd key tiles (score buffer 1)
+//               each turns scores into P, H (16-bit A operands written back to TMEM) and row
+//               sums; at the end both add their row sums and split the epilogue by columns
+//   warp 8      TMA producer: Q, tQ once; a ring of {K, tK, V, tV} tiles of 64 keys
+//   warp 9      TMEM owner and single-thread MMA issuer
 // Tensor memory (512 columns x 128 lanes, fp32):
 //   [0, D)                         tO accumulator (D <= 128)
 //   [128 + 128 b, +64)  b = 0, 1   S of key tile j (b = j & 1); P (bf16 pairs) overwrites it
@@ -32,7 +35,9 @@ __device__ unsigned int g_fa_error = 0;
 
 constexpr int kBM = 128;       // query rows per CTA (one TMEM lane each)
 constexpr int kBN = 64;        // keys per tile
-constexpr int kThreads = 192;  // 6 warps
+constexpr int kThreads = 320;  // 10 warps
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAccCol = 0;
 constexpr uint32_t kBufCol = 128;  // S of buffer b at kBufCol + 128 b, dS 64 columns further
@@ -45,11 +50,23 @@ template <int D> struct JvpCfg {
   static constexpr int kTileBytes = kKB * kBN * 128;    // K, tK, V or tV of one tile
   static constexpr int kStageBytes = 4 * kTileBytes;
   static constexpr int kBarOffset = 2 * kQBytes + kStages * kStageBytes;
-  static constexpr int kSmemBytes = kBarOffset + 256 + 1024;  // barriers + alignment slack
+  static constexpr int kSmemBytes = kBarOffset + 256 + 2 * kBM * 4 + 1024;  // barriers, row sums, slack
 };
 
 __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
   return bf16 ? kf::Mma<__nv_bfloat16>::from_f2(a, b) : kf::Mma<__half>::from_f2(a, b);
+}
+
+// 2^x with the MUFU instruction (flushes subnormal results to zero; exp2(-inf) = 0).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Named barrier over the two softmax warpgroups (256 threads).
+__device__ __forceinline__ void softmax_groups_sync() {
+  asm volatile("bar.sync 1, 256;" ::: "memory");
 }
 
 template <typename T, int D>
@@ -73,6 +90,7 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   uint64_t* pv_done = p_full + 2;
   uint64_t* acc_full = pv_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  float* row_sums = reinterpret_cast<float*>(smem + C::kBarOffset + 256);  // [2][kBM]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qtile = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -98,13 +116,13 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     kf::mbar_init(acc_full, 1);
     kf::fence_mbar_init();
   }
-  if (warp == 1) kf::tc::tmem_alloc(tmem_slot, kTmemCols);
+  if (warp == kMmaWarp) kf::tc::tmem_alloc(tmem_slot, kTmemCols);
   kf::tc::fence_before_sync();
   __syncthreads();
   kf::tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
+  if (warp == kProducerWarp) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       kf::prefetch_tensormap(&tm_q);
@@ -131,7 +149,7 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idS = kf::tc::idesc_f16(kBf16 ? 1 : 0, kBM, kBN, false, false);
@@ -209,7 +227,8 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     }
   } else {
     // ------------------------------------------------------------------ softmax / epilogue
-    const int quarter = warp & 3;  // warps 2, 3, 4, 5 own TMEM lanes 64, 96, 0, 32 + lane
+    const int group = warp >> 2;   // softmax warpgroup: tiles j with (j & 1) == group
+    const int quarter = warp & 3;  // TMEM lanes [32 quarter, 32 quarter + 32)
     const int row = quarter * 32 + lane;
     const int qrow = q0 + row;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
@@ -217,16 +236,16 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                                      : __int_as_float(0x7f800000);
     // Keys [0, limit) are visible to this row.
     const int limit = p.causal ? min(p.Nk, qrow + p.Nk - p.Nq + 1) : p.Nk;
+    const uint32_t s_col = lane_base + kBufCol + 128 * group;
+    const uint32_t ts_col = s_col + 64;
     float csum = 0.f;
     bool ok = true;
-    for (int j = 0; j < ntiles; ++j) {
-      const int buf = j & 1;
-      ok = kf::mbar_wait_bounded(&s_full[buf], (j >> 1) & 1, &g_fa_error);
+    for (int j = group; j < ntiles; j += 2) {
+      ok = kf::mbar_wait_bounded(&s_full[group], (j >> 1) & 1, &g_fa_error);
       if (!ok) break;
       kf::tc::fence_after_sync();
-      const uint32_t s_col = lane_base + kBufCol + 128 * buf;
-      const uint32_t ts_col = s_col + 64;
       const int k0 = j * kBN;
+      const bool full = k0 + kBN <= limit;  // no masking inside this tile for this row
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t sr[32], tr[32];
@@ -234,11 +253,15 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         if (has_h) kf::tc::ld_32x32b_x32(ts_col + c * 32, tr);
         kf::tc::wait_ld();
         uint32_t pp[16], hh[16];
+        const int kc = k0 + c * 32;
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const int key = k0 + c * 32 + 2 * i;
-          const float p0 = key < limit ? exp2f(fmaf(__uint_as_float(sr[2 * i]), p.scale_log2, -lse_l2)) : 0.f;
-          const float p1 = key + 1 < limit ? exp2f(fmaf(__uint_as_float(sr[2 * i + 1]), p.scale_log2, -lse_l2)) : 0.f;
+          float p0 = ex2(fmaf(__uint_as_float(sr[2 * i]), p.scale_log2, -lse_l2));
+          float p1 = ex2(fmaf(__uint_as_float(sr[2 * i + 1]), p.scale_log2, -lse_l2));
+          if (!full) {
+            p0 = kc + 2 * i < limit ? p0 : 0.f;
+            p1 = kc + 2 * i + 1 < limit ? p1 : 0.f;
+          }
           pp[i] = pack2(p0, p1, kBf16);
           if (has_h) {
             const float h0 = p0 * __uint_as_float(tr[2 * i]) * p.scale;
@@ -252,9 +275,13 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       }
       kf::tc::wait_st();
       kf::tc::fence_before_sync();
-      kf::mbar_arrive(&p_full[buf]);
+      kf::mbar_arrive(&p_full[group]);
     }
-    // Epilogue: tO = acc - rowsum(H) * O
+    // Total row sum of H over both warpgroups' tiles.
+    row_sums[group * kBM + row] = csum;
+    softmax_groups_sync();
+    csum = row_sums[row] + row_sums[kBM + row];
+    // Epilogue: tO = acc - rowsum(H) * O; warpgroup g writes columns [g D/2, (g + 1) D/2).
     if (ok) ok = kf::mbar_wait_bounded(acc_full, 0, &g_fa_error);
     if (ok) {
       kf::tc::fence_after_sync();
@@ -262,7 +289,8 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       const T* orow = static_cast<const T*>(p.o_in) + roff;
       T* trow = static_cast<T*>(p.to_out) + roff;
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
+      for (int cc = 0; cc < D / 64; ++cc) {
+        const int c = group * (D / 64) + cc;  // 32-column chunk
         uint32_t ar[32];
         kf::tc::ld_32x32b_x32(lane_base + kAccCol + c * 32, ar);
         kf::tc::wait_ld();
@@ -288,7 +316,334 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   }
   kf::tc::fence_before_sync();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
+    kf::tc::fence_after_sync();
+    kf::tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ============================================================================================
+// One-pass forward (+ JVP): O, LSE (and tO) with online statistics
+// (flash-attention-jvp-derivation.md sections 7-8):
+//   E = exp2(x - m), x = gamma log2(e) S;  l += rowsum(E);  U += E V
+//   H = E * gamma (tQ K^T + Q tK^T);       r += rowsum(H);  G += H V + E tV
+//   O = U / l;  tO = G / l - (r / l) O;  LSE = (m + log2 l) ln 2
+// Both softmax warpgroups work on every 64-key tile, each on 32 of its keys; they exchange the
+// tile row maxima through shared memory. The reference max m only moves when a tile's max
+// exceeds it by more than 8 (a factor 256 in E); then the accumulators U, G of that row are
+// rescaled in TMEM after the previous tile's output MMAs have completed. Tensor memory:
+//   [0, D) G (tO accumulator) | [128, 384) S / dS double buffer | [384, 384 + D) U
+// P and H (16-bit) overwrite the first 16 columns of each warpgroup's 32-column S / dS half.
+// ============================================================================================
+constexpr uint32_t kUCol = 384;
+constexpr float kRescaleThreshold = 8.f;  // log2 units
+
+template <int D> struct FusedCfg : JvpCfg<D> {
+  static constexpr int kSmemBytes = JvpCfg<D>::kBarOffset + 256 + 6 * kBM * 4 + 64 + 1024;
+};
+
+template <typename T, int D, bool kJvp>
+__global__ void __launch_bounds__(kThreads, 1)
+fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_tq,
+                      const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_tk,
+                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_tv,
+                      const FaArgs p) {
+  using C = FusedCfg<D>;
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (kf::smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t* q_s = smem;
+  uint8_t* tq_s = smem + C::kQBytes;
+  uint8_t* kv_s = smem + 2 * C::kQBytes;
+  uint64_t* q_full = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
+  uint64_t* kv_full = q_full + 1;
+  uint64_t* kv_empty = kv_full + C::kStages;
+  uint64_t* s_full = kv_empty + C::kStages;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* pv_done = p_full + 2;
+  uint64_t* acc_full = pv_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  float* tile_max = reinterpret_cast<float*>(smem + C::kBarOffset + 256);  // [2 buffers][2 groups][kBM]
+  float* part_sums = tile_max + 4 * kBM;                                     // [2 groups][kBM] (l, then r)
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(part_sums + 2 * kBM);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qtile = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int q0 = qtile * kBM;
+  const int kvh = h / (p.Hq / p.Hkv);
+  const bool has_tq = kJvp && p.tq != nullptr, has_tk = kJvp && p.tk != nullptr;
+  const bool has_tv = kJvp && p.tv != nullptr;
+  const bool has_h = has_tq || has_tk;
+  int k_end = p.Nk;
+  if (p.causal) k_end = min(p.Nk, max(0, q0 + kBM + p.Nk - p.Nq));
+  const int ntiles = (k_end + kBN - 1) / kBN;
+
+  if (threadIdx.x == 0) {
+    kf::mbar_init(q_full, 1);
+    for (int s = 0; s < C::kStages; ++s) {
+      kf::mbar_init(&kv_full[s], 1);
+      kf::mbar_init(&kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      kf::mbar_init(&s_full[i], 1);
+      kf::mbar_init(&p_full[i], 2 * kBM);
+      kf::mbar_init(&pv_done[i], 1);
+    }
+    kf::mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    kf::fence_mbar_init();
+  }
+  if (warp == kMmaWarp) kf::tc::tmem_alloc(tmem_slot, kTmemCols);
+  kf::tc::fence_before_sync();
+  __syncthreads();
+  kf::tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == kProducerWarp) {
+    if (lane == 0) {
+      kf::prefetch_tensormap(&tm_q);
+      kf::prefetch_tensormap(&tm_k);
+      kf::prefetch_tensormap(&tm_v);
+      kf::mbar_arrive_expect_tx(q_full, C::kQBytes * (has_tq ? 2 : 1));
+      for (int kb = 0; kb < C::kKB; ++kb) {
+        kf::tma_load_4d(q_s + kb * kBM * 128, &tm_q, q_full, kb * 64, h, q0, b);
+        if (has_tq) kf::tma_load_4d(tq_s + kb * kBM * 128, &tm_tq, q_full, kb * 64, h, q0, b);
+      }
+      const uint32_t kv_bytes = C::kTileBytes * (2 + (has_tk ? 1 : 0) + (has_tv ? 1 : 0));
+      for (int j = 0; j < ntiles; ++j) {
+        const int stage = j % C::kStages;
+        if (j >= C::kStages &&
+            !kf::mbar_wait_or_abort(&kv_empty[stage], ((j / C::kStages) - 1) & 1, &g_fa_error, abort_flag))
+          break;
+        uint8_t* base = kv_s + stage * C::kStageBytes;
+        kf::mbar_arrive_expect_tx(&kv_full[stage], kv_bytes);
+        for (int kb = 0; kb < C::kKB; ++kb) {
+          const int off = kb * kBN * 128;
+          kf::tma_load_4d(base + off, &tm_k, &kv_full[stage], kb * 64, kvh, j * kBN, b);
+          if (has_tk) kf::tma_load_4d(base + C::kTileBytes + off, &tm_tk, &kv_full[stage], kb * 64, kvh, j * kBN, b);
+          kf::tma_load_4d(base + 2 * C::kTileBytes + off, &tm_v, &kv_full[stage], kb * 64, kvh, j * kBN, b);
+          if (has_tv) kf::tma_load_4d(base + 3 * C::kTileBytes + off, &tm_tv, &kv_full[stage], kb * 64, kvh, j * kBN, b);
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      constexpr uint32_t idS = kf::tc::idesc_f16(kBf16 ? 1 : 0, kBM, kBN, false, false);
+      constexpr uint32_t idPV = kf::tc::idesc_f16(kBf16 ? 1 : 0, kBM, D, false, true);
+      const uint32_t q_addr = kf::smem_u32(q_s), tq_addr = kf::smem_u32(tq_s);
+      bool ok = kf::mbar_wait_or_abort(q_full, 0, &g_fa_error, abort_flag);
+      kf::tc::fence_after_sync();
+      uint32_t u_started = 0, g_started = 0;
+      for (int j = 0; ok && j <= ntiles; ++j) {
+        if (j < ntiles) {
+          const int stage = j % C::kStages, buf = j & 1;
+          if (j >= 2 && !kf::mbar_wait_or_abort(&pv_done[buf], ((j >> 1) - 1) & 1, &g_fa_error, abort_flag)) break;
+          if (!kf::mbar_wait_or_abort(&kv_full[stage], (j / C::kStages) & 1, &g_fa_error, abort_flag)) break;
+          kf::tc::fence_after_sync();
+          const uint32_t base = kf::smem_u32(kv_s + stage * C::kStageBytes);
+          const uint32_t s_col = tmem + kBufCol + 128 * buf;
+          const uint32_t ts_col = s_col + 64;
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
+            const uint32_t koff = (k >> 2) * kBN * 128 + (k & 3) * 32;
+            kf::tc::mma_ss(s_col, kf::tc::desc_sw128(q_addr + off, 16, 1024),
+                           kf::tc::desc_sw128(base + koff, 16, 1024), idS, k > 0);
+          }
+          uint32_t ts_started = 0;
+          if (has_tq) {
+#pragma unroll
+            for (int k = 0; k < D / 16; ++k) {
+              const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
+              const uint32_t koff = (k >> 2) * kBN * 128 + (k & 3) * 32;
+              kf::tc::mma_ss(ts_col, kf::tc::desc_sw128(tq_addr + off, 16, 1024),
+                             kf::tc::desc_sw128(base + koff, 16, 1024), idS, ts_started);
+              ts_started = 1;
+            }
+          }
+          if (has_tk) {
+#pragma unroll
+            for (int k = 0; k < D / 16; ++k) {
+              const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
+              const uint32_t koff = (k >> 2) * kBN * 128 + (k & 3) * 32;
+              kf::tc::mma_ss(ts_col, kf::tc::desc_sw128(q_addr + off, 16, 1024),
+                             kf::tc::desc_sw128(base + C::kTileBytes + koff, 16, 1024), idS, ts_started);
+              ts_started = 1;
+            }
+          }
+          kf::tc::commit(&s_full[buf]);
+        }
+        if (j >= 1) {
+          const int jj = j - 1, buf = jj & 1, stage = jj % C::kStages;
+          if (!kf::mbar_wait_or_abort(&p_full[buf], (jj >> 1) & 1, &g_fa_error, abort_flag)) break;
+          kf::tc::fence_after_sync();
+          const uint32_t base = kf::smem_u32(kv_s + stage * C::kStageBytes);
+          const uint32_t p_col = tmem + kBufCol + 128 * buf;
+          const uint32_t h_col = p_col + 64;
+#pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk) {
+            // keys [16 kk, 16 kk + 16): warpgroup kk / 2 wrote them at columns 32 (kk / 2) + 8 (kk % 2)
+            const uint32_t acol = (kk >> 1) * 32 + (kk & 1) * 8;
+            const uint64_t vdesc = kf::tc::desc_sw128(base + 2 * C::kTileBytes + kk * 2048, kBN * 128, 1024);
+            kf::tc::mma_ts(tmem + kUCol, p_col + acol, vdesc, idPV, u_started);
+            u_started = 1;
+            if (has_h) {
+              kf::tc::mma_ts(tmem + kAccCol, h_col + acol, vdesc, idPV, g_started);
+              g_started = 1;
+            }
+            if (has_tv) {
+              kf::tc::mma_ts(tmem + kAccCol, p_col + acol,
+                             kf::tc::desc_sw128(base + 3 * C::kTileBytes + kk * 2048, kBN * 128, 1024),
+                             idPV, g_started);
+              g_started = 1;
+            }
+          }
+          kf::tc::commit(&pv_done[buf]);
+          kf::tc::commit(&kv_empty[stage]);
+        }
+      }
+      kf::tc::commit(acc_full);
+    }
+  } else {
+    const int group = warp >> 2;   // which 32 keys of each tile this warpgroup handles
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int qrow = q0 + row;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const int limit = qrow >= p.Nq ? 0 : (p.causal ? min(p.Nk, qrow + p.Nk - p.Nq + 1) : p.Nk);
+    float m_ref = -INFINITY, l_part = 0.f, r_part = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      const int buf = j & 1;
+      if (ok) ok = kf::mbar_wait_or_abort(&s_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag);
+      kf::tc::fence_after_sync();
+      const uint32_t s_col = lane_base + kBufCol + 128 * buf + group * 32;
+      const uint32_t ts_col = s_col + 64;
+      uint32_t sr[32], tr[32];
+      float mx = -INFINITY;
+      const int kc = j * kBN + group * 32;
+      if (ok) {
+        kf::tc::ld_32x32b_x32(s_col, sr);
+        if (has_h) kf::tc::ld_32x32b_x32(ts_col, tr);
+        kf::tc::wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float x = kc + i < limit ? __uint_as_float(sr[i]) * p.scale_log2 : -INFINITY;
+          sr[i] = __float_as_uint(x);
+          mx = fmaxf(mx, x);
+        }
+      }
+      // Exchange the two halves' maxima (every softmax thread reaches this barrier).
+      tile_max[(buf * 2 + group) * kBM + row] = mx;
+      softmax_groups_sync();
+      mx = fmaxf(tile_max[(buf * 2) * kBM + row], tile_max[(buf * 2 + 1) * kBM + row]);
+      if (ok) {
+        if (mx > m_ref + kRescaleThreshold) {
+          if (j > 0 && m_ref != -INFINITY) {
+            // Rescale this row's accumulators once the previous tile's output MMAs are done.
+            const float alpha = ex2(m_ref - mx);
+            ok = kf::mbar_wait_or_abort(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, &g_fa_error, abort_flag);
+            kf::tc::fence_after_sync();
+            if (ok) {
+#pragma unroll
+              for (int c = 0; c < D / 64; ++c) {
+                const uint32_t col = (group * (D / 2)) + c * 32;
+                uint32_t ar[32];
+                kf::tc::ld_32x32b_x32(lane_base + kUCol + col, ar);
+                kf::tc::wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) ar[i] = __float_as_uint(__uint_as_float(ar[i]) * alpha);
+                kf::tc::st_32x32b_x32(lane_base + kUCol + col, ar);
+                if (kJvp) {
+                  kf::tc::ld_32x32b_x32(lane_base + kAccCol + col, ar);
+                  kf::tc::wait_ld();
+#pragma unroll
+                  for (int i = 0; i < 32; ++i) ar[i] = __float_as_uint(__uint_as_float(ar[i]) * alpha);
+                  kf::tc::st_32x32b_x32(lane_base + kAccCol + col, ar);
+                }
+              }
+            }
+            l_part *= alpha;
+            r_part *= alpha;
+          }
+          m_ref = mx;
+        }
+        const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
+        uint32_t pp[16], hh[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float e0 = ex2(__uint_as_float(sr[2 * i]) - m_use);
+          const float e1 = ex2(__uint_as_float(sr[2 * i + 1]) - m_use);
+          l_part += e0 + e1;
+          pp[i] = pack2(e0, e1, kBf16);
+          if (has_h) {
+            const float h0 = e0 * __uint_as_float(tr[2 * i]) * p.scale;
+            const float h1 = e1 * __uint_as_float(tr[2 * i + 1]) * p.scale;
+            r_part += h0 + h1;
+            hh[i] = pack2(h0, h1, kBf16);
+          }
+        }
+        kf::tc::st_32x32b_x16(s_col, pp);
+        if (has_h) kf::tc::st_32x32b_x16(ts_col, hh);
+        kf::tc::wait_st();
+      }
+      kf::tc::fence_before_sync();
+      kf::mbar_arrive(&p_full[buf]);
+    }
+    // Combine the two warpgroups' row sums.
+    part_sums[group * kBM + row] = l_part;
+    softmax_groups_sync();
+    const float l_tot = part_sums[row] + part_sums[kBM + row];
+    softmax_groups_sync();
+    part_sums[group * kBM + row] = r_part;
+    softmax_groups_sync();
+    const float r_tot = part_sums[row] + part_sums[kBM + row];
+    if (ok) ok = kf::mbar_wait_or_abort(acc_full, 0, &g_fa_error, abort_flag);
+    if (ok) {
+      kf::tc::fence_after_sync();
+      const float inv_l = l_tot > 0.f ? 1.f / l_tot : 0.f;
+      const float rl = r_tot * inv_l;
+      const int64_t roff = ((static_cast<int64_t>(b) * p.Nq + qrow) * p.Hq + h) * D;
+      T* orow = static_cast<T*>(p.o_out) + roff;
+      T* trow = kJvp ? static_cast<T*>(p.to_out) + roff : nullptr;
+      if (group == 0 && qrow < p.Nq) {
+        const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
+        p.lse_out[(static_cast<int64_t>(b) * p.Hq + h) * p.Nq + qrow] =
+            l_tot > 0.f ? (m_use + log2f(l_tot)) * 0.6931471805599453f : __int_as_float(0x7f800000);
+      }
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        const int col = group * (D / 2) + c * 32;
+        uint32_t ur[32], gr[32];
+        kf::tc::ld_32x32b_x32(lane_base + kUCol + col, ur);
+        if (kJvp) kf::tc::ld_32x32b_x32(lane_base + kAccCol + col, gr);
+        kf::tc::wait_ld();
+        if (qrow < p.Nq) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint32_t ow[4], tw[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int i = v * 8 + e * 2;
+              const float o0 = ntiles > 0 ? __uint_as_float(ur[i]) * inv_l : 0.f;
+              const float o1 = ntiles > 0 ? __uint_as_float(ur[i + 1]) * inv_l : 0.f;
+              ow[e] = pack2(o0, o1, kBf16);
+              if (kJvp) {
+                const float g0 = ntiles > 0 ? __uint_as_float(gr[i]) * inv_l : 0.f;
+                const float g1 = ntiles > 0 ? __uint_as_float(gr[i + 1]) * inv_l : 0.f;
+                tw[e] = pack2(g0 - rl * o0, g1 - rl * o1, kBf16);
+              }
+            }
+            *reinterpret_cast<uint4*>(orow + col + v * 8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+            if (kJvp) *reinterpret_cast<uint4*>(trow + col + v * 8) = make_uint4(tw[0], tw[1], tw[2], tw[3]);
+          }
+        }
+      }
+    }
+  }
+  kf::tc::fence_before_sync();
+  __syncthreads();
+  if (warp == kMmaWarp) {
     kf::tc::fence_after_sync();
     kf::tc::tmem_dealloc(tmem, kTmemCols);
   }
@@ -325,6 +680,26 @@ int launch_jvp(const FaArgs& a, int dtype, cudaStream_t stream) {
   return KF_OK;
 }
 
+template <typename T, int D, bool kJvp>
+int launch_fused(const FaArgs& a, int dtype, cudaStream_t stream) {
+  using C = FusedCfg<D>;
+  CUtensorMap mq, mtq, mk, mtk, mv, mtv;
+  if (!encode_bnhd(&mq, a.q, dtype, a.B, a.Nq, a.Hq, D, kBM) ||
+      !encode_bnhd(&mtq, a.tq ? a.tq : a.q, dtype, a.B, a.Nq, a.Hq, D, kBM) ||
+      !encode_bnhd(&mk, a.k, dtype, a.B, a.Nk, a.Hkv, D, kBN) ||
+      !encode_bnhd(&mtk, a.tk ? a.tk : a.k, dtype, a.B, a.Nk, a.Hkv, D, kBN) ||
+      !encode_bnhd(&mv, a.v, dtype, a.B, a.Nk, a.Hkv, D, kBN) ||
+      !encode_bnhd(&mtv, a.tv ? a.tv : a.v, dtype, a.B, a.Nk, a.Hkv, D, kBN))
+    return KF_ERR_CUDA;
+  auto kernel = fa_fused_sm100_kernel<T, D, kJvp>;
+  const int prep = kf_host::prepare_kernel(reinterpret_cast<const void*>(kernel), kThreads, C::kSmemBytes, nullptr);
+  if (prep != KF_OK) return prep;
+  const dim3 grid((a.Nq + kBM - 1) / kBM, a.Hq, a.B);
+  kernel<<<grid, kThreads, C::kSmemBytes, stream>>>(mq, mtq, mk, mtk, mv, mtv, a);
+  KF_LAUNCH_CHECK();
+  return KF_OK;
+}
+
 }  // namespace
 
 int kf_internal_fa_error(unsigned int* code) {
@@ -342,6 +717,22 @@ namespace kf::fa {
 
 bool sm100_jvp_supported(const FaArgs& a) {
   return (a.D == 64 || a.D == 128) && (a.tq != nullptr || a.tk != nullptr || a.tv != nullptr);
+}
+
+bool sm100_fused_supported(const FaArgs& a, int mode) {
+  if (a.D != 64 && a.D != 128) return false;
+  if (mode == kModeFwd) return true;
+  return a.tq != nullptr || a.tk != nullptr || a.tv != nullptr;
+}
+
+int launch_sm100_fused(const FaArgs& a, int mode, int dtype, cudaStream_t s) {
+  const bool jvp = mode == kModeFwdJvp;
+  if (dtype == KF_DTYPE_BF16) {
+    if (a.D == 64) return jvp ? launch_fused<__nv_bfloat16, 64, true>(a, dtype, s) : launch_fused<__nv_bfloat16, 64, false>(a, dtype, s);
+    return jvp ? launch_fused<__nv_bfloat16, 128, true>(a, dtype, s) : launch_fused<__nv_bfloat16, 128, false>(a, dtype, s);
+  }
+  if (a.D == 64) return jvp ? launch_fused<__half, 64, true>(a, dtype, s) : launch_fused<__half, 64, false>(a, dtype, s);
+  return jvp ? launch_fused<__half, 128, true>(a, dtype, s) : launch_fused<__half, 128, false>(a, dtype, s);
 }
 
 int launch_sm100_jvp(const FaArgs& a, int dtype, cudaStream_t s) {

@@ -67,6 +67,27 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// Bounded wait that also gives up as soon as another thread of the CTA has set *abort (a
+// shared-memory flag), so a CTA whose roles synchronise with each other never waits out one
+// timeout per remaining step after the first failure. A timeout sets *abort itself.
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, unsigned int* err,
+                                                   volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((++spins & 63u) == 0) {
+      if (*abort) return false;
+      if (globaltimer_ns() - start > kWaitTimeoutNs) {
+        atomicCAS(err, 0u, static_cast<unsigned int>(KF_ERR_DEVICE_TIMEOUT));
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------------------------------
 // Thread-block clusters: hardware cluster barrier and distributed shared memory reads.
 // ------------------------------------------------------------------------------------------
