@@ -11,14 +11,10 @@
 //   warps 4..7  softmax warpgroup 1: odd key tiles (score buffer 1)
 //               each turns scores into P, H (16-bit A operands written back to TMEM) and row
 //               sums; at the end both add their row sums and split the epilogue by columns
-//   warp 8      TMA producer: Q, tQ once; a ring of {K, tK, V, tV} tiles of 64 keys
+//   warp 8      TMA producer: Q, tQ once; rings of {K, tK} and {V, tV} tiles of 64 keys
 //   warp 9      TMEM owner and single-thread MMA issuer
-// Tensor memory (512 columns x 128 lanes, fp32):
-//   [0, D)                         tO accumulator (D <= 128)
-//   [128 + 128 b, +64)  b = 0, 1   S of key tile j (b = j & 1); P (bf16 pairs) overwrites it
-//   [192 + 128 b, +64)             dS = tQ K^T + Q tK^T;        H (bf16 pairs) overwrites it
-// Double-buffered S / dS let the tensor core compute tile j+1's scores while the softmax
-// warps turn tile j into P and H. Per 64-key tile the MMA warp issues
+// Double-buffered S / dS in tensor memory let the tensor core compute tile j+1's scores while
+// the softmax warps turn tile j into P and H. Per 64-key tile the MMA warp issues
 //   S  = Q K^T            (D/16 x M128 N64 K16, operands from shared memory)
 //   dS = tQ K^T + Q tK^T  (2 D/16 x M128 N64 K16)
 //   tO += P tV + H V      (2 x 4 x M128 N=D K16, A from tensor memory, B MN-major)
@@ -43,15 +39,148 @@ constexpr uint32_t kAccCol = 0;
 constexpr uint32_t kBufCol = 128;  // S of buffer b at kBufCol + 128 b, dS 64 columns further
 constexpr float kLog2e = 1.4426950408889634f;
 
-template <int D> struct JvpCfg {
-  static constexpr int kStages = D == 64 ? 4 : 2;
+// Shared-memory plan: Q, tQ once; a ring of {K, tK} stages (freed when a tile's score MMAs
+// complete) and a separate ring of {V, tV} stages (freed when its output MMAs complete), so
+// the next tiles' K can stream in while the current tile's V is still in use.
+template <int D> struct Cfg {
   static constexpr int kKB = D / 64;                    // 128-byte boxes along the head dim
   static constexpr int kQBytes = kKB * kBM * 128;       // Q or tQ
   static constexpr int kTileBytes = kKB * kBN * 128;    // K, tK, V or tV of one tile
-  static constexpr int kStageBytes = 4 * kTileBytes;
-  static constexpr int kBarOffset = 2 * kQBytes + kStages * kStageBytes;
-  static constexpr int kSmemBytes = kBarOffset + 256 + 2 * kBM * 4 + 1024;  // barriers, row sums, slack
+  static constexpr int kKStages = D == 64 ? 4 : 2;
+  static constexpr int kVStages = D == 64 ? 4 : 2;
+  static constexpr int kKOffset = 2 * kQBytes;
+  static constexpr int kVOffset = kKOffset + kKStages * 2 * kTileBytes;
+  static constexpr int kBarOffset = kVOffset + kVStages * 2 * kTileBytes;
+  static constexpr int kScratchOffset = kBarOffset + 512;                 // row statistics
+  static constexpr int kSmemBytes = kScratchOffset + 6 * kBM * 4 + 64 + 1024;  // + abort flag, slack
 };
+
+// Barriers, in shared memory after the operand tiles.
+template <int D> struct Bars {
+  uint64_t* q_full;
+  uint64_t* k_full;   // [kKStages]
+  uint64_t* k_empty;  // [kKStages]
+  uint64_t* v_full;   // [kVStages]
+  uint64_t* v_empty;  // [kVStages]
+  uint64_t* s_full;   // [2]
+  uint64_t* p_full;   // [2]
+  uint64_t* pv_done;  // [2]
+  uint64_t* acc_full;
+  uint32_t* tmem_slot;
+  __device__ explicit Bars(uint8_t* smem) {
+    using C = Cfg<D>;
+    q_full = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
+    k_full = q_full + 1;
+    k_empty = k_full + C::kKStages;
+    v_full = k_empty + C::kKStages;
+    v_empty = v_full + C::kVStages;
+    s_full = v_empty + C::kVStages;
+    p_full = s_full + 2;
+    pv_done = p_full + 2;
+    acc_full = pv_done + 2;
+    tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  }
+  __device__ void init(int p_arrivals) const {
+    using C = Cfg<D>;
+    kf::mbar_init(q_full, 1);
+    for (int s = 0; s < C::kKStages; ++s) {
+      kf::mbar_init(&k_full[s], 1);
+      kf::mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < C::kVStages; ++s) {
+      kf::mbar_init(&v_full[s], 1);
+      kf::mbar_init(&v_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      kf::mbar_init(&s_full[i], 1);
+      kf::mbar_init(&p_full[i], p_arrivals);
+      kf::mbar_init(&pv_done[i], 1);
+    }
+    kf::mbar_init(acc_full, 1);
+  }
+};
+
+// TMA producer (one thread): Q, tQ, then K tiles one ahead of V tiles -- the order in which
+// the MMA warp consumes them -- each behind its ring's "empty" barrier.
+template <int D>
+__device__ void produce(const Bars<D>& bars, uint8_t* smem, const CUtensorMap* tm_q, const CUtensorMap* tm_tq,
+                        const CUtensorMap* tm_k, const CUtensorMap* tm_tk, const CUtensorMap* tm_v,
+                        const CUtensorMap* tm_tv, bool has_tq, bool has_tk, bool need_v, bool has_tv,
+                        int h, int kvh, int q0, int b, int ntiles, volatile int* abort) {
+  using C = Cfg<D>;
+  kf::prefetch_tensormap(tm_q);
+  kf::prefetch_tensormap(tm_k);
+  kf::mbar_arrive_expect_tx(bars.q_full, C::kQBytes * (has_tq ? 2 : 1));
+  for (int kb = 0; kb < C::kKB; ++kb) {
+    kf::tma_load_4d(smem + kb * kBM * 128, tm_q, bars.q_full, kb * 64, h, q0, b);
+    if (has_tq) kf::tma_load_4d(smem + C::kQBytes + kb * kBM * 128, tm_tq, bars.q_full, kb * 64, h, q0, b);
+  }
+  const uint32_t k_bytes = C::kTileBytes * (has_tk ? 2 : 1);
+  const uint32_t v_bytes = C::kTileBytes * ((need_v ? 1 : 0) + (has_tv ? 1 : 0));
+  auto load_k = [&](int j) -> bool {
+    const int st = j % C::kKStages;
+    if (j >= C::kKStages && !kf::mbar_wait_or_abort(&bars.k_empty[st], ((j / C::kKStages) - 1) & 1, &g_fa_error, abort))
+      return false;
+    uint8_t* base = smem + C::kKOffset + st * 2 * C::kTileBytes;
+    kf::mbar_arrive_expect_tx(&bars.k_full[st], k_bytes);
+    for (int kb = 0; kb < C::kKB; ++kb) {
+      kf::tma_load_4d(base + kb * kBN * 128, tm_k, &bars.k_full[st], kb * 64, kvh, j * kBN, b);
+      if (has_tk) kf::tma_load_4d(base + C::kTileBytes + kb * kBN * 128, tm_tk, &bars.k_full[st], kb * 64, kvh, j * kBN, b);
+    }
+    return true;
+  };
+  auto load_v = [&](int j) -> bool {
+    const int st = j % C::kVStages;
+    if (j >= C::kVStages && !kf::mbar_wait_or_abort(&bars.v_empty[st], ((j / C::kVStages) - 1) & 1, &g_fa_error, abort))
+      return false;
+    uint8_t* base = smem + C::kVOffset + st * 2 * C::kTileBytes;
+    kf::mbar_arrive_expect_tx(&bars.v_full[st], v_bytes);
+    for (int kb = 0; kb < C::kKB; ++kb) {
+      if (need_v) kf::tma_load_4d(base + kb * kBN * 128, tm_v, &bars.v_full[st], kb * 64, kvh, j * kBN, b);
+      if (has_tv) kf::tma_load_4d(base + C::kTileBytes + kb * kBN * 128, tm_tv, &bars.v_full[st], kb * 64, kvh, j * kBN, b);
+    }
+    return true;
+  };
+  if (ntiles > 0 && !load_k(0)) return;
+  for (int j = 0; j < ntiles; ++j) {
+    if (j + 1 < ntiles && !load_k(j + 1)) return;
+    if (!load_v(j)) return;
+  }
+}
+
+// Score MMAs of tile j into S / dS columns (s_col, ts_col).
+template <int D>
+__device__ __forceinline__ void issue_scores(uint32_t q_addr, uint32_t tq_addr, uint32_t k_base, int tile_bytes,
+                                             uint32_t s_col, uint32_t ts_col, uint32_t idS, bool has_tq, bool has_tk) {
+#pragma unroll
+  for (int k = 0; k < D / 16; ++k) {
+    const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
+    const uint32_t koff = (k >> 2) * kBN * 128 + (k & 3) * 32;
+    kf::tc::mma_ss(s_col, kf::tc::desc_sw128(q_addr + off, 16, 1024), kf::tc::desc_sw128(k_base + koff, 16, 1024),
+                   idS, k > 0);
+  }
+  uint32_t started = 0;
+  if (has_tq) {
+#pragma unroll
+    for (int k = 0; k < D / 16; ++k) {
+      const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
+      const uint32_t koff = (k >> 2) * kBN * 128 + (k & 3) * 32;
+      kf::tc::mma_ss(ts_col, kf::tc::desc_sw128(tq_addr + off, 16, 1024),
+                     kf::tc::desc_sw128(k_base + koff, 16, 1024), idS, started);
+      started = 1;
+    }
+  }
+  if (has_tk) {
+#pragma unroll
+    for (int k = 0; k < D / 16; ++k) {
+      const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
+      const uint32_t koff = (k >> 2) * kBN * 128 + (k & 3) * 32;
+      kf::tc::mma_ss(ts_col, kf::tc::desc_sw128(q_addr + off, 16, 1024),
+                     kf::tc::desc_sw128(k_base + tile_bytes + koff, 16, 1024), idS, started);
+      started = 1;
+    }
+  }
+}
 
 __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
   return bf16 ? kf::Mma<__nv_bfloat16>::from_f2(a, b) : kf::Mma<__half>::from_f2(a, b);
@@ -69,28 +198,27 @@ __device__ __forceinline__ void softmax_groups_sync() {
   asm volatile("bar.sync 1, 256;" ::: "memory");
 }
 
+// ============================================================================================
+// Standalone JVP. Tensor memory:
+//   [0, D) tO accumulator | S_b at 128 + 128 b, dS_b at 192 + 128 b | P_b at 384 + 64 b, H_b +32
+// P and H have their own columns, so tile j+1's score MMAs never wait for tile j's output MMAs.
+// Softmax warpgroup g handles the tiles j with (j & 1) == g.
+// ============================================================================================
+constexpr uint32_t kPCol = 384;
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, 1)
 fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_tq,
                     const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_tk,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_tv,
                     const FaArgs p) {
-  using C = JvpCfg<D>;
+  using C = Cfg<D>;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (kf::smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint8_t* q_s = smem;
-  uint8_t* tq_s = smem + C::kQBytes;
-  uint8_t* kv_s = smem + 2 * C::kQBytes;
-  uint64_t* q_full = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
-  uint64_t* kv_full = q_full + 1;
-  uint64_t* kv_empty = kv_full + C::kStages;
-  uint64_t* s_full = kv_empty + C::kStages;
-  uint64_t* p_full = s_full + 2;
-  uint64_t* pv_done = p_full + 2;
-  uint64_t* acc_full = pv_done + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
-  float* row_sums = reinterpret_cast<float*>(smem + C::kBarOffset + 256);  // [2][kBM]
+  const Bars<D> bars(smem);
+  float* row_sums = reinterpret_cast<float*>(smem + C::kScratchOffset);  // [2][kBM]
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(row_sums + 6 * kBM);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qtile = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -103,130 +231,69 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   const int ntiles = (k_end + kBN - 1) / kBN;
 
   if (threadIdx.x == 0) {
-    kf::mbar_init(q_full, 1);
-    for (int s = 0; s < C::kStages; ++s) {
-      kf::mbar_init(&kv_full[s], 1);
-      kf::mbar_init(&kv_empty[s], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      kf::mbar_init(&s_full[i], 1);
-      kf::mbar_init(&p_full[i], kBM);
-      kf::mbar_init(&pv_done[i], 1);
-    }
-    kf::mbar_init(acc_full, 1);
+    bars.init(kBM);
+    *abort_flag = 0;
     kf::fence_mbar_init();
   }
-  if (warp == kMmaWarp) kf::tc::tmem_alloc(tmem_slot, kTmemCols);
+  if (warp == kMmaWarp) kf::tc::tmem_alloc(bars.tmem_slot, kTmemCols);
   kf::tc::fence_before_sync();
   __syncthreads();
   kf::tc::fence_after_sync();
-  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem = *bars.tmem_slot;
 
   if (warp == kProducerWarp) {
-    // ------------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      kf::prefetch_tensormap(&tm_q);
-      kf::prefetch_tensormap(&tm_k);
-      kf::mbar_arrive_expect_tx(q_full, C::kQBytes * (has_tq ? 2 : 1));
-      for (int kb = 0; kb < C::kKB; ++kb) {
-        kf::tma_load_4d(q_s + kb * kBM * 128, &tm_q, q_full, kb * 64, h, q0, b);
-        if (has_tq) kf::tma_load_4d(tq_s + kb * kBM * 128, &tm_tq, q_full, kb * 64, h, q0, b);
-      }
-      const uint32_t kv_bytes = C::kTileBytes * (1 + (has_tk ? 1 : 0) + (has_h ? 1 : 0) + (has_tv ? 1 : 0));
-      for (int j = 0; j < ntiles; ++j) {
-        const int stage = j % C::kStages;
-        if (j >= C::kStages &&
-            !kf::mbar_wait_bounded(&kv_empty[stage], ((j / C::kStages) - 1) & 1, &g_fa_error))
-          break;
-        uint8_t* base = kv_s + stage * C::kStageBytes;
-        kf::mbar_arrive_expect_tx(&kv_full[stage], kv_bytes);
-        for (int kb = 0; kb < C::kKB; ++kb) {
-          const int off = kb * kBN * 128;
-          kf::tma_load_4d(base + off, &tm_k, &kv_full[stage], kb * 64, kvh, j * kBN, b);
-          if (has_tk) kf::tma_load_4d(base + C::kTileBytes + off, &tm_tk, &kv_full[stage], kb * 64, kvh, j * kBN, b);
-          if (has_h) kf::tma_load_4d(base + 2 * C::kTileBytes + off, &tm_v, &kv_full[stage], kb * 64, kvh, j * kBN, b);
-          if (has_tv) kf::tma_load_4d(base + 3 * C::kTileBytes + off, &tm_tv, &kv_full[stage], kb * 64, kvh, j * kBN, b);
-        }
-      }
-    }
+    if (lane == 0)
+      produce<D>(bars, smem, &tm_q, &tm_tq, &tm_k, &tm_tk, &tm_v, &tm_tv, has_tq, has_tk, has_h, has_tv, h, kvh,
+                 q0, b, ntiles, abort_flag);
   } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idS = kf::tc::idesc_f16(kBf16 ? 1 : 0, kBM, kBN, false, false);
       constexpr uint32_t idPV = kf::tc::idesc_f16(kBf16 ? 1 : 0, kBM, D, false, true);
-      const uint32_t q_addr = kf::smem_u32(q_s), tq_addr = kf::smem_u32(tq_s);
-      bool ok = kf::mbar_wait_bounded(q_full, 0, &g_fa_error);
+      const uint32_t q_addr = kf::smem_u32(smem), tq_addr = q_addr + C::kQBytes;
+      bool ok = kf::mbar_wait_or_abort(bars.q_full, 0, &g_fa_error, abort_flag);
       kf::tc::fence_after_sync();
+      auto scores = [&](int j) -> bool {
+        const int st = j % C::kKStages, buf = j & 1;
+        if (!kf::mbar_wait_or_abort(&bars.k_full[st], (j / C::kKStages) & 1, &g_fa_error, abort_flag)) return false;
+        kf::tc::fence_after_sync();
+        const uint32_t k_base = kf::smem_u32(smem + C::kKOffset + st * 2 * C::kTileBytes);
+        const uint32_t s_col = tmem + kBufCol + 128 * buf;
+        issue_scores<D>(q_addr, tq_addr, k_base, C::kTileBytes, s_col, s_col + 64, idS, has_tq, has_tk);
+        kf::tc::commit(&bars.s_full[buf]);
+        kf::tc::commit(&bars.k_empty[st]);
+        return true;
+      };
       uint32_t acc_started = 0;
-      for (int j = 0; ok && j <= ntiles; ++j) {
-        if (j < ntiles) {
-          const int stage = j % C::kStages, buf = j & 1;
-          if (j >= 2 && !kf::mbar_wait_bounded(&pv_done[buf], ((j >> 1) - 1) & 1, &g_fa_error)) break;
-          if (!kf::mbar_wait_bounded(&kv_full[stage], (j / C::kStages) & 1, &g_fa_error)) break;
-          kf::tc::fence_after_sync();
-          const uint32_t base = kf::smem_u32(kv_s + stage * C::kStageBytes);
-          const uint32_t s_col = tmem + kBufCol + 128 * buf;
-          const uint32_t ts_col = s_col + 64;
+      if (ok && ntiles > 0) ok = scores(0);
+      for (int j = 0; ok && j < ntiles; ++j) {
+        // Tile j+1's scores go in before tile j's output MMAs: they only need S_{j+1}'s buffer,
+        // which tile j-1's softmax released before tile j-1's output MMAs were issued.
+        if (j + 1 < ntiles && !(ok = scores(j + 1))) break;
+        const int buf = j & 1, st = j % C::kVStages;
+        if (!(ok = kf::mbar_wait_or_abort(&bars.p_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag))) break;
+        if (!(ok = kf::mbar_wait_or_abort(&bars.v_full[st], (j / C::kVStages) & 1, &g_fa_error, abort_flag))) break;
+        kf::tc::fence_after_sync();
+        const uint32_t v_base = kf::smem_u32(smem + C::kVOffset + st * 2 * C::kTileBytes);
+        const uint32_t p_col = tmem + kPCol + 64 * buf;
 #pragma unroll
-          for (int k = 0; k < D / 16; ++k) {
-            const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
-            const uint32_t koff = (k >> 2) * kBN * 128 + (k & 3) * 32;
-            kf::tc::mma_ss(s_col, kf::tc::desc_sw128(q_addr + off, 16, 1024),
-                           kf::tc::desc_sw128(base + koff, 16, 1024), idS, k > 0);
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          if (has_tv) {
+            kf::tc::mma_ts(tmem + kAccCol, p_col + kk * 8,
+                           kf::tc::desc_sw128(v_base + C::kTileBytes + kk * 2048, kBN * 128, 1024), idPV, acc_started);
+            acc_started = 1;
           }
-          uint32_t ts_started = 0;
-          if (has_tq) {
-#pragma unroll
-            for (int k = 0; k < D / 16; ++k) {
-              const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
-              const uint32_t koff = (k >> 2) * kBN * 128 + (k & 3) * 32;
-              kf::tc::mma_ss(ts_col, kf::tc::desc_sw128(tq_addr + off, 16, 1024),
-                             kf::tc::desc_sw128(base + koff, 16, 1024), idS, ts_started);
-              ts_started = 1;
-            }
+          if (has_h) {
+            kf::tc::mma_ts(tmem + kAccCol, p_col + 32 + kk * 8,
+                           kf::tc::desc_sw128(v_base + kk * 2048, kBN * 128, 1024), idPV, acc_started);
+            acc_started = 1;
           }
-          if (has_tk) {
-#pragma unroll
-            for (int k = 0; k < D / 16; ++k) {
-              const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
-              const uint32_t koff = (k >> 2) * kBN * 128 + (k & 3) * 32;
-              kf::tc::mma_ss(ts_col, kf::tc::desc_sw128(q_addr + off, 16, 1024),
-                             kf::tc::desc_sw128(base + C::kTileBytes + koff, 16, 1024), idS, ts_started);
-              ts_started = 1;
-            }
-          }
-          kf::tc::commit(&s_full[buf]);
         }
-        if (j >= 1) {
-          const int jj = j - 1, buf = jj & 1, stage = jj % C::kStages;
-          if (!kf::mbar_wait_bounded(&p_full[buf], (jj >> 1) & 1, &g_fa_error)) break;
-          kf::tc::fence_after_sync();
-          const uint32_t base = kf::smem_u32(kv_s + stage * C::kStageBytes);
-          const uint32_t p_col = tmem + kBufCol + 128 * buf;
-          const uint32_t h_col = p_col + 64;
-#pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk) {
-            if (has_tv) {
-              kf::tc::mma_ts(tmem + kAccCol, p_col + kk * 8,
-                             kf::tc::desc_sw128(base + 3 * C::kTileBytes + kk * 2048, kBN * 128, 1024),
-                             idPV, acc_started);
-              acc_started = 1;
-            }
-            if (has_h) {
-              kf::tc::mma_ts(tmem + kAccCol, h_col + kk * 8,
-                             kf::tc::desc_sw128(base + 2 * C::kTileBytes + kk * 2048, kBN * 128, 1024),
-                             idPV, acc_started);
-              acc_started = 1;
-            }
-          }
-          kf::tc::commit(&pv_done[buf]);
-          kf::tc::commit(&kv_empty[stage]);
-        }
+        kf::tc::commit(&bars.pv_done[buf]);
+        kf::tc::commit(&bars.v_empty[st]);
       }
-      kf::tc::commit(acc_full);
+      kf::tc::commit(bars.acc_full);
     }
   } else {
-    // ------------------------------------------------------------------ softmax / epilogue
     const int group = warp >> 2;   // softmax warpgroup: tiles j with (j & 1) == group
     const int quarter = warp & 3;  // TMEM lanes [32 quarter, 32 quarter + 32)
     const int row = quarter * 32 + lane;
@@ -234,14 +301,17 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const float lse_l2 = qrow < p.Nq ? p.lse_in[(static_cast<int64_t>(b) * p.Hq + h) * p.Nq + qrow] * kLog2e
                                      : __int_as_float(0x7f800000);
-    // Keys [0, limit) are visible to this row.
-    const int limit = p.causal ? min(p.Nk, qrow + p.Nk - p.Nq + 1) : p.Nk;
+    const int limit = p.causal ? min(p.Nk, qrow + p.Nk - p.Nq + 1) : p.Nk;  // keys [0, limit) visible
     const uint32_t s_col = lane_base + kBufCol + 128 * group;
     const uint32_t ts_col = s_col + 64;
+    const uint32_t p_col = lane_base + kPCol + 64 * group;
+    const uint32_t h_col = p_col + 32;
     float csum = 0.f;
     bool ok = true;
     for (int j = group; j < ntiles; j += 2) {
-      ok = kf::mbar_wait_bounded(&s_full[group], (j >> 1) & 1, &g_fa_error);
+      ok = kf::mbar_wait_or_abort(&bars.s_full[group], (j >> 1) & 1, &g_fa_error, abort_flag);
+      // This warpgroup's P / H columns were last read by tile j-2's output MMAs.
+      if (ok && j >= 2) ok = kf::mbar_wait_or_abort(&bars.pv_done[group], ((j >> 1) - 1) & 1, &g_fa_error, abort_flag);
       if (!ok) break;
       kf::tc::fence_after_sync();
       const int k0 = j * kBN;
@@ -270,19 +340,18 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             hh[i] = pack2(h0, h1, kBf16);
           }
         }
-        kf::tc::st_32x32b_x16(s_col + c * 16, pp);
-        if (has_h) kf::tc::st_32x32b_x16(ts_col + c * 16, hh);
+        kf::tc::st_32x32b_x16(p_col + c * 16, pp);
+        if (has_h) kf::tc::st_32x32b_x16(h_col + c * 16, hh);
       }
       kf::tc::wait_st();
       kf::tc::fence_before_sync();
-      kf::mbar_arrive(&p_full[group]);
+      kf::mbar_arrive(&bars.p_full[group]);
     }
-    // Total row sum of H over both warpgroups' tiles.
     row_sums[group * kBM + row] = csum;
     softmax_groups_sync();
     csum = row_sums[row] + row_sums[kBM + row];
     // Epilogue: tO = acc - rowsum(H) * O; warpgroup g writes columns [g D/2, (g + 1) D/2).
-    if (ok) ok = kf::mbar_wait_bounded(acc_full, 0, &g_fa_error);
+    if (ok) ok = kf::mbar_wait_or_abort(bars.acc_full, 0, &g_fa_error, abort_flag);
     if (ok) {
       kf::tc::fence_after_sync();
       const int64_t roff = ((static_cast<int64_t>(b) * p.Nq + qrow) * p.Hq + h) * D;
@@ -333,14 +402,11 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 // exceeds it by more than 8 (a factor 256 in E); then the accumulators U, G of that row are
 // rescaled in TMEM after the previous tile's output MMAs have completed. Tensor memory:
 //   [0, D) G (tO accumulator) | [128, 384) S / dS double buffer | [384, 384 + D) U
-// P and H (16-bit) overwrite the first 16 columns of each warpgroup's 32-column S / dS half.
+// P and H (16-bit) overwrite the first 16 columns of each warpgroup's 32-column S / dS half, so
+// tile j's score MMAs wait for tile j-2's output MMAs (same buffer).
 // ============================================================================================
 constexpr uint32_t kUCol = 384;
 constexpr float kRescaleThreshold = 8.f;  // log2 units
-
-template <int D> struct FusedCfg : JvpCfg<D> {
-  static constexpr int kSmemBytes = JvpCfg<D>::kBarOffset + 256 + 6 * kBM * 4 + 64 + 1024;
-};
 
 template <typename T, int D, bool kJvp>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -348,23 +414,13 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
                       const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_tk,
                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_tv,
                       const FaArgs p) {
-  using C = FusedCfg<D>;
+  using C = Cfg<D>;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (kf::smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint8_t* q_s = smem;
-  uint8_t* tq_s = smem + C::kQBytes;
-  uint8_t* kv_s = smem + 2 * C::kQBytes;
-  uint64_t* q_full = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
-  uint64_t* kv_full = q_full + 1;
-  uint64_t* kv_empty = kv_full + C::kStages;
-  uint64_t* s_full = kv_empty + C::kStages;
-  uint64_t* p_full = s_full + 2;
-  uint64_t* pv_done = p_full + 2;
-  uint64_t* acc_full = pv_done + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
-  float* tile_max = reinterpret_cast<float*>(smem + C::kBarOffset + 256);  // [2 buffers][2 groups][kBM]
-  float* part_sums = tile_max + 4 * kBM;                                     // [2 groups][kBM] (l, then r)
+  const Bars<D> bars(smem);
+  float* tile_max = reinterpret_cast<float*>(smem + C::kScratchOffset);  // [2 buffers][2 groups][kBM]
+  float* part_sums = tile_max + 4 * kBM;                                   // [2 groups][kBM]
   volatile int* abort_flag = reinterpret_cast<volatile int*>(part_sums + 2 * kBM);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -379,112 +435,53 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
   const int ntiles = (k_end + kBN - 1) / kBN;
 
   if (threadIdx.x == 0) {
-    kf::mbar_init(q_full, 1);
-    for (int s = 0; s < C::kStages; ++s) {
-      kf::mbar_init(&kv_full[s], 1);
-      kf::mbar_init(&kv_empty[s], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      kf::mbar_init(&s_full[i], 1);
-      kf::mbar_init(&p_full[i], 2 * kBM);
-      kf::mbar_init(&pv_done[i], 1);
-    }
-    kf::mbar_init(acc_full, 1);
+    bars.init(2 * kBM);
     *abort_flag = 0;
     kf::fence_mbar_init();
   }
-  if (warp == kMmaWarp) kf::tc::tmem_alloc(tmem_slot, kTmemCols);
+  if (warp == kMmaWarp) kf::tc::tmem_alloc(bars.tmem_slot, kTmemCols);
   kf::tc::fence_before_sync();
   __syncthreads();
   kf::tc::fence_after_sync();
-  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem = *bars.tmem_slot;
 
   if (warp == kProducerWarp) {
-    if (lane == 0) {
-      kf::prefetch_tensormap(&tm_q);
-      kf::prefetch_tensormap(&tm_k);
-      kf::prefetch_tensormap(&tm_v);
-      kf::mbar_arrive_expect_tx(q_full, C::kQBytes * (has_tq ? 2 : 1));
-      for (int kb = 0; kb < C::kKB; ++kb) {
-        kf::tma_load_4d(q_s + kb * kBM * 128, &tm_q, q_full, kb * 64, h, q0, b);
-        if (has_tq) kf::tma_load_4d(tq_s + kb * kBM * 128, &tm_tq, q_full, kb * 64, h, q0, b);
-      }
-      const uint32_t kv_bytes = C::kTileBytes * (2 + (has_tk ? 1 : 0) + (has_tv ? 1 : 0));
-      for (int j = 0; j < ntiles; ++j) {
-        const int stage = j % C::kStages;
-        if (j >= C::kStages &&
-            !kf::mbar_wait_or_abort(&kv_empty[stage], ((j / C::kStages) - 1) & 1, &g_fa_error, abort_flag))
-          break;
-        uint8_t* base = kv_s + stage * C::kStageBytes;
-        kf::mbar_arrive_expect_tx(&kv_full[stage], kv_bytes);
-        for (int kb = 0; kb < C::kKB; ++kb) {
-          const int off = kb * kBN * 128;
-          kf::tma_load_4d(base + off, &tm_k, &kv_full[stage], kb * 64, kvh, j * kBN, b);
-          if (has_tk) kf::tma_load_4d(base + C::kTileBytes + off, &tm_tk, &kv_full[stage], kb * 64, kvh, j * kBN, b);
-          kf::tma_load_4d(base + 2 * C::kTileBytes + off, &tm_v, &kv_full[stage], kb * 64, kvh, j * kBN, b);
-          if (has_tv) kf::tma_load_4d(base + 3 * C::kTileBytes + off, &tm_tv, &kv_full[stage], kb * 64, kvh, j * kBN, b);
-        }
-      }
-    }
+    if (lane == 0)
+      produce<D>(bars, smem, &tm_q, &tm_tq, &tm_k, &tm_tk, &tm_v, &tm_tv, has_tq, has_tk, true, has_tv, h, kvh,
+                 q0, b, ntiles, abort_flag);
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
       constexpr uint32_t idS = kf::tc::idesc_f16(kBf16 ? 1 : 0, kBM, kBN, false, false);
       constexpr uint32_t idPV = kf::tc::idesc_f16(kBf16 ? 1 : 0, kBM, D, false, true);
-      const uint32_t q_addr = kf::smem_u32(q_s), tq_addr = kf::smem_u32(tq_s);
-      bool ok = kf::mbar_wait_or_abort(q_full, 0, &g_fa_error, abort_flag);
+      const uint32_t q_addr = kf::smem_u32(smem), tq_addr = q_addr + C::kQBytes;
+      bool ok = kf::mbar_wait_or_abort(bars.q_full, 0, &g_fa_error, abort_flag);
       kf::tc::fence_after_sync();
       uint32_t u_started = 0, g_started = 0;
       for (int j = 0; ok && j <= ntiles; ++j) {
         if (j < ntiles) {
-          const int stage = j % C::kStages, buf = j & 1;
-          if (j >= 2 && !kf::mbar_wait_or_abort(&pv_done[buf], ((j >> 1) - 1) & 1, &g_fa_error, abort_flag)) break;
-          if (!kf::mbar_wait_or_abort(&kv_full[stage], (j / C::kStages) & 1, &g_fa_error, abort_flag)) break;
+          const int st = j % C::kKStages, buf = j & 1;
+          if (j >= 2 && !(ok = kf::mbar_wait_or_abort(&bars.pv_done[buf], ((j >> 1) - 1) & 1, &g_fa_error, abort_flag))) break;
+          if (!(ok = kf::mbar_wait_or_abort(&bars.k_full[st], (j / C::kKStages) & 1, &g_fa_error, abort_flag))) break;
           kf::tc::fence_after_sync();
-          const uint32_t base = kf::smem_u32(kv_s + stage * C::kStageBytes);
+          const uint32_t k_base = kf::smem_u32(smem + C::kKOffset + st * 2 * C::kTileBytes);
           const uint32_t s_col = tmem + kBufCol + 128 * buf;
-          const uint32_t ts_col = s_col + 64;
-#pragma unroll
-          for (int k = 0; k < D / 16; ++k) {
-            const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
-            const uint32_t koff = (k >> 2) * kBN * 128 + (k & 3) * 32;
-            kf::tc::mma_ss(s_col, kf::tc::desc_sw128(q_addr + off, 16, 1024),
-                           kf::tc::desc_sw128(base + koff, 16, 1024), idS, k > 0);
-          }
-          uint32_t ts_started = 0;
-          if (has_tq) {
-#pragma unroll
-            for (int k = 0; k < D / 16; ++k) {
-              const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
-              const uint32_t koff = (k >> 2) * kBN * 128 + (k & 3) * 32;
-              kf::tc::mma_ss(ts_col, kf::tc::desc_sw128(tq_addr + off, 16, 1024),
-                             kf::tc::desc_sw128(base + koff, 16, 1024), idS, ts_started);
-              ts_started = 1;
-            }
-          }
-          if (has_tk) {
-#pragma unroll
-            for (int k = 0; k < D / 16; ++k) {
-              const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
-              const uint32_t koff = (k >> 2) * kBN * 128 + (k & 3) * 32;
-              kf::tc::mma_ss(ts_col, kf::tc::desc_sw128(q_addr + off, 16, 1024),
-                             kf::tc::desc_sw128(base + C::kTileBytes + koff, 16, 1024), idS, ts_started);
-              ts_started = 1;
-            }
-          }
-          kf::tc::commit(&s_full[buf]);
+          issue_scores<D>(q_addr, tq_addr, k_base, C::kTileBytes, s_col, s_col + 64, idS, has_tq, has_tk);
+          kf::tc::commit(&bars.s_full[buf]);
+          kf::tc::commit(&bars.k_empty[st]);
         }
         if (j >= 1) {
-          const int jj = j - 1, buf = jj & 1, stage = jj % C::kStages;
-          if (!kf::mbar_wait_or_abort(&p_full[buf], (jj >> 1) & 1, &g_fa_error, abort_flag)) break;
+          const int jj = j - 1, buf = jj & 1, st = jj % C::kVStages;
+          if (!(ok = kf::mbar_wait_or_abort(&bars.p_full[buf], (jj >> 1) & 1, &g_fa_error, abort_flag))) break;
+          if (!(ok = kf::mbar_wait_or_abort(&bars.v_full[st], (jj / C::kVStages) & 1, &g_fa_error, abort_flag))) break;
           kf::tc::fence_after_sync();
-          const uint32_t base = kf::smem_u32(kv_s + stage * C::kStageBytes);
+          const uint32_t v_base = kf::smem_u32(smem + C::kVOffset + st * 2 * C::kTileBytes);
           const uint32_t p_col = tmem + kBufCol + 128 * buf;
           const uint32_t h_col = p_col + 64;
 #pragma unroll
           for (int kk = 0; kk < kBN / 16; ++kk) {
             // keys [16 kk, 16 kk + 16): warpgroup kk / 2 wrote them at columns 32 (kk / 2) + 8 (kk % 2)
             const uint32_t acol = (kk >> 1) * 32 + (kk & 1) * 8;
-            const uint64_t vdesc = kf::tc::desc_sw128(base + 2 * C::kTileBytes + kk * 2048, kBN * 128, 1024);
+            const uint64_t vdesc = kf::tc::desc_sw128(v_base + kk * 2048, kBN * 128, 1024);
             kf::tc::mma_ts(tmem + kUCol, p_col + acol, vdesc, idPV, u_started);
             u_started = 1;
             if (has_h) {
@@ -493,16 +490,16 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
             }
             if (has_tv) {
               kf::tc::mma_ts(tmem + kAccCol, p_col + acol,
-                             kf::tc::desc_sw128(base + 3 * C::kTileBytes + kk * 2048, kBN * 128, 1024),
-                             idPV, g_started);
+                             kf::tc::desc_sw128(v_base + C::kTileBytes + kk * 2048, kBN * 128, 1024), idPV,
+                             g_started);
               g_started = 1;
             }
           }
-          kf::tc::commit(&pv_done[buf]);
-          kf::tc::commit(&kv_empty[stage]);
+          kf::tc::commit(&bars.pv_done[buf]);
+          kf::tc::commit(&bars.v_empty[st]);
         }
       }
-      kf::tc::commit(acc_full);
+      kf::tc::commit(bars.acc_full);
     }
   } else {
     const int group = warp >> 2;   // which 32 keys of each tile this warpgroup handles
@@ -515,7 +512,7 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
       const int buf = j & 1;
-      if (ok) ok = kf::mbar_wait_or_abort(&s_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag);
+      if (ok) ok = kf::mbar_wait_or_abort(&bars.s_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag);
       kf::tc::fence_after_sync();
       const uint32_t s_col = lane_base + kBufCol + 128 * buf + group * 32;
       const uint32_t ts_col = s_col + 64;
@@ -542,7 +539,7 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
           if (j > 0 && m_ref != -INFINITY) {
             // Rescale this row's accumulators once the previous tile's output MMAs are done.
             const float alpha = ex2(m_ref - mx);
-            ok = kf::mbar_wait_or_abort(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, &g_fa_error, abort_flag);
+            ok = kf::mbar_wait_or_abort(&bars.pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, &g_fa_error, abort_flag);
             kf::tc::fence_after_sync();
             if (ok) {
 #pragma unroll
@@ -588,7 +585,7 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         kf::tc::wait_st();
       }
       kf::tc::fence_before_sync();
-      kf::mbar_arrive(&p_full[buf]);
+      kf::mbar_arrive(&bars.p_full[buf]);
     }
     // Combine the two warpgroups' row sums.
     part_sums[group * kBM + row] = l_part;
@@ -598,7 +595,7 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
     part_sums[group * kBM + row] = r_part;
     softmax_groups_sync();
     const float r_tot = part_sums[row] + part_sums[kBM + row];
-    if (ok) ok = kf::mbar_wait_or_abort(acc_full, 0, &g_fa_error, abort_flag);
+    if (ok) ok = kf::mbar_wait_or_abort(bars.acc_full, 0, &g_fa_error, abort_flag);
     if (ok) {
       kf::tc::fence_after_sync();
       const float inv_l = l_tot > 0.f ? 1.f / l_tot : 0.f;
@@ -662,7 +659,7 @@ bool encode_bnhd(CUtensorMap* map, const void* base, int dtype, int B, int N, in
 
 template <typename T, int D>
 int launch_jvp(const FaArgs& a, int dtype, cudaStream_t stream) {
-  using C = JvpCfg<D>;
+  using C = Cfg<D>;
   CUtensorMap mq, mtq, mk, mtk, mv, mtv;
   if (!encode_bnhd(&mq, a.q, dtype, a.B, a.Nq, a.Hq, D, kBM) ||
       !encode_bnhd(&mtq, a.tq ? a.tq : a.q, dtype, a.B, a.Nq, a.Hq, D, kBM) ||
@@ -682,7 +679,7 @@ int launch_jvp(const FaArgs& a, int dtype, cudaStream_t stream) {
 
 template <typename T, int D, bool kJvp>
 int launch_fused(const FaArgs& a, int dtype, cudaStream_t stream) {
-  using C = FusedCfg<D>;
+  using C = Cfg<D>;
   CUtensorMap mq, mtq, mk, mtk, mv, mtv;
   if (!encode_bnhd(&mq, a.q, dtype, a.B, a.Nq, a.Hq, D, kBM) ||
       !encode_bnhd(&mtq, a.tq ? a.tq : a.q, dtype, a.B, a.Nq, a.Hq, D, kBM) ||
