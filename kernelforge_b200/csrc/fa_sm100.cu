@@ -12,7 +12,10 @@
 //               each turns scores into P, H (16-bit A operands written back to TMEM) and row
 //               sums; at the end both add their row sums and split the epilogue by columns
 //   warp 8      TMA producer: Q, tQ once; rings of {K, tK} and {V, tV} tiles of 64 keys
-//   warp 9      TMEM owner and single-thread MMA issuer
+//   warp 9      TMEM owner; one thread issues the score MMAs (runs ahead while buffers allow)
+//   warp 10     one thread issues the output MMAs as each tile's P / H become ready
+// Two issuing threads keep the tensor core's short instruction queue fed: while one waits on a
+// barrier the other issues.
 // Double-buffered S / dS in tensor memory let the tensor core compute tile j+1's scores while
 // the softmax warps turn tile j into P and H. Per 64-key tile the MMA warp issues
 //   S  = Q K^T            (D/16 x M128 N64 K16, operands from shared memory)
@@ -31,23 +34,27 @@ __device__ unsigned int g_fa_error = 0;
 
 constexpr int kBM = 128;       // query rows per CTA (one TMEM lane each)
 constexpr int kBN = 64;        // keys per tile
-constexpr int kThreads = 320;  // 10 warps
+constexpr int kThreads = 352;  // 11 warps
 constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
+constexpr int kMmaWarp = 9;     // TMEM owner; issues the score MMAs
+constexpr int kPvWarp = 10;     // issues the output MMAs
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAccCol = 0;
 constexpr uint32_t kBufCol = 128;  // S of buffer b at kBufCol + 128 b, dS 64 columns further
 constexpr float kLog2e = 1.4426950408889634f;
 
-// Shared-memory plan: Q, tQ once; a ring of {K, tK} stages (freed when a tile's score MMAs
-// complete) and a separate ring of {V, tV} stages (freed when its output MMAs complete), so
-// the next tiles' K can stream in while the current tile's V is still in use.
+// Shared-memory plan: Q, tQ once; a two-stage ring of {K, tK} (a stage is free again once the
+// tile's score MMAs complete) and a separate two-stage ring of {V, tV} (free once the tile's
+// output MMAs complete), so the next tile's K streams in while the current tile's V is in use.
+// With two stages, stage (j & 1) and score / output buffer (j & 1) coincide: the producer waits
+// on the same completion barriers as the softmax warps (s_full, pv_done) instead of on
+// separate "empty" barriers, which saves the MMA thread two commits per tile.
 template <int D> struct Cfg {
   static constexpr int kKB = D / 64;                    // 128-byte boxes along the head dim
   static constexpr int kQBytes = kKB * kBM * 128;       // Q or tQ
   static constexpr int kTileBytes = kKB * kBN * 128;    // K, tK, V or tV of one tile
-  static constexpr int kKStages = D == 64 ? 4 : 2;
-  static constexpr int kVStages = D == 64 ? 4 : 2;
+  static constexpr int kKStages = 2;
+  static constexpr int kVStages = 2;
   static constexpr int kKOffset = 2 * kQBytes;
   static constexpr int kVOffset = kKOffset + kKStages * 2 * kTileBytes;
   static constexpr int kBarOffset = kVOffset + kVStages * 2 * kTileBytes;
@@ -58,23 +65,19 @@ template <int D> struct Cfg {
 // Barriers, in shared memory after the operand tiles.
 template <int D> struct Bars {
   uint64_t* q_full;
-  uint64_t* k_full;   // [kKStages]
-  uint64_t* k_empty;  // [kKStages]
-  uint64_t* v_full;   // [kVStages]
-  uint64_t* v_empty;  // [kVStages]
-  uint64_t* s_full;   // [2]
-  uint64_t* p_full;   // [2]
-  uint64_t* pv_done;  // [2]
+  uint64_t* k_full;   // [2]
+  uint64_t* v_full;   // [2]
+  uint64_t* s_full;   // [2] scores of tile j complete (also: K stage j & 1 free)
+  uint64_t* p_full;   // [2] P / H of tile j written
+  uint64_t* pv_done;  // [2] output MMAs of tile j complete (also: V stage j & 1 free)
   uint64_t* acc_full;
   uint32_t* tmem_slot;
   __device__ explicit Bars(uint8_t* smem) {
     using C = Cfg<D>;
     q_full = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
     k_full = q_full + 1;
-    k_empty = k_full + C::kKStages;
-    v_full = k_empty + C::kKStages;
-    v_empty = v_full + C::kVStages;
-    s_full = v_empty + C::kVStages;
+    v_full = k_full + C::kKStages;
+    s_full = v_full + C::kVStages;
     p_full = s_full + 2;
     pv_done = p_full + 2;
     acc_full = pv_done + 2;
@@ -83,14 +86,8 @@ template <int D> struct Bars {
   __device__ void init(int p_arrivals) const {
     using C = Cfg<D>;
     kf::mbar_init(q_full, 1);
-    for (int s = 0; s < C::kKStages; ++s) {
-      kf::mbar_init(&k_full[s], 1);
-      kf::mbar_init(&k_empty[s], 1);
-    }
-    for (int s = 0; s < C::kVStages; ++s) {
-      kf::mbar_init(&v_full[s], 1);
-      kf::mbar_init(&v_empty[s], 1);
-    }
+    for (int s = 0; s < C::kKStages; ++s) kf::mbar_init(&k_full[s], 1);
+    for (int s = 0; s < C::kVStages; ++s) kf::mbar_init(&v_full[s], 1);
     for (int i = 0; i < 2; ++i) {
       kf::mbar_init(&s_full[i], 1);
       kf::mbar_init(&p_full[i], p_arrivals);
@@ -118,8 +115,8 @@ __device__ void produce(const Bars<D>& bars, uint8_t* smem, const CUtensorMap* t
   const uint32_t k_bytes = C::kTileBytes * (has_tk ? 2 : 1);
   const uint32_t v_bytes = C::kTileBytes * ((need_v ? 1 : 0) + (has_tv ? 1 : 0));
   auto load_k = [&](int j) -> bool {
-    const int st = j % C::kKStages;
-    if (j >= C::kKStages && !kf::mbar_wait_or_abort(&bars.k_empty[st], ((j / C::kKStages) - 1) & 1, &g_fa_error, abort))
+    const int st = j & 1;  // stage j & 1 was last read by tile j-2's score MMAs
+    if (j >= 2 && !kf::mbar_wait_or_abort<true>(&bars.s_full[st], ((j >> 1) - 1) & 1, &g_fa_error, abort))
       return false;
     uint8_t* base = smem + C::kKOffset + st * 2 * C::kTileBytes;
     kf::mbar_arrive_expect_tx(&bars.k_full[st], k_bytes);
@@ -130,8 +127,8 @@ __device__ void produce(const Bars<D>& bars, uint8_t* smem, const CUtensorMap* t
     return true;
   };
   auto load_v = [&](int j) -> bool {
-    const int st = j % C::kVStages;
-    if (j >= C::kVStages && !kf::mbar_wait_or_abort(&bars.v_empty[st], ((j / C::kVStages) - 1) & 1, &g_fa_error, abort))
+    const int st = j & 1;  // stage j & 1 was last read by tile j-2's output MMAs
+    if (j >= 2 && !kf::mbar_wait_or_abort<true>(&bars.pv_done[st], ((j >> 1) - 1) & 1, &g_fa_error, abort))
       return false;
     uint8_t* base = smem + C::kVOffset + st * 2 * C::kTileBytes;
     kf::mbar_arrive_expect_tx(&bars.v_full[st], v_bytes);
@@ -148,10 +145,9 @@ __device__ void produce(const Bars<D>& bars, uint8_t* smem, const CUtensorMap* t
   }
 }
 
-// Score MMAs of tile j into S / dS columns (s_col, ts_col).
+// Score MMAs of tile j: S = Q K^T into s_col, then dS = tQ K^T + Q tK^T into ts_col.
 template <int D>
-__device__ __forceinline__ void issue_scores(uint32_t q_addr, uint32_t tq_addr, uint32_t k_base, int tile_bytes,
-                                             uint32_t s_col, uint32_t ts_col, uint32_t idS, bool has_tq, bool has_tk) {
+__device__ __forceinline__ void issue_s(uint32_t q_addr, uint32_t k_base, uint32_t s_col, uint32_t idS) {
 #pragma unroll
   for (int k = 0; k < D / 16; ++k) {
     const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
@@ -159,6 +155,10 @@ __device__ __forceinline__ void issue_scores(uint32_t q_addr, uint32_t tq_addr, 
     kf::tc::mma_ss(s_col, kf::tc::desc_sw128(q_addr + off, 16, 1024), kf::tc::desc_sw128(k_base + koff, 16, 1024),
                    idS, k > 0);
   }
+}
+template <int D>
+__device__ __forceinline__ void issue_ds(uint32_t q_addr, uint32_t tq_addr, uint32_t k_base, int tile_bytes,
+                                         uint32_t ts_col, uint32_t idS, bool has_tq, bool has_tk) {
   uint32_t started = 0;
   if (has_tq) {
 #pragma unroll
@@ -247,33 +247,34 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                  q0, b, ntiles, abort_flag);
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
+      // Scores of tile j into buffer j & 1 once tile j-2's softmax has read that buffer.
       constexpr uint32_t idS = kf::tc::idesc_f16(kBf16 ? 1 : 0, kBM, kBN, false, false);
-      constexpr uint32_t idPV = kf::tc::idesc_f16(kBf16 ? 1 : 0, kBM, D, false, true);
       const uint32_t q_addr = kf::smem_u32(smem), tq_addr = q_addr + C::kQBytes;
-      bool ok = kf::mbar_wait_or_abort(bars.q_full, 0, &g_fa_error, abort_flag);
-      kf::tc::fence_after_sync();
-      auto scores = [&](int j) -> bool {
-        const int st = j % C::kKStages, buf = j & 1;
-        if (!kf::mbar_wait_or_abort(&bars.k_full[st], (j / C::kKStages) & 1, &g_fa_error, abort_flag)) return false;
-        kf::tc::fence_after_sync();
-        const uint32_t k_base = kf::smem_u32(smem + C::kKOffset + st * 2 * C::kTileBytes);
-        const uint32_t s_col = tmem + kBufCol + 128 * buf;
-        issue_scores<D>(q_addr, tq_addr, k_base, C::kTileBytes, s_col, s_col + 64, idS, has_tq, has_tk);
-        kf::tc::commit(&bars.s_full[buf]);
-        kf::tc::commit(&bars.k_empty[st]);
-        return true;
-      };
-      uint32_t acc_started = 0;
-      if (ok && ntiles > 0) ok = scores(0);
+      bool ok = kf::mbar_wait_or_abort<true>(bars.q_full, 0, &g_fa_error, abort_flag);
       for (int j = 0; ok && j < ntiles; ++j) {
-        // Tile j+1's scores go in before tile j's output MMAs: they only need S_{j+1}'s buffer,
-        // which tile j-1's softmax released before tile j-1's output MMAs were issued.
-        if (j + 1 < ntiles && !(ok = scores(j + 1))) break;
-        const int buf = j & 1, st = j % C::kVStages;
-        if (!(ok = kf::mbar_wait_or_abort(&bars.p_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag))) break;
-        if (!(ok = kf::mbar_wait_or_abort(&bars.v_full[st], (j / C::kVStages) & 1, &g_fa_error, abort_flag))) break;
+        const int buf = j & 1;
+        if (j >= 2 && !(ok = kf::mbar_wait_or_abort<true>(&bars.p_full[buf], ((j >> 1) - 1) & 1, &g_fa_error, abort_flag))) break;
+        if (!(ok = kf::mbar_wait_or_abort<true>(&bars.k_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag))) break;
         kf::tc::fence_after_sync();
-        const uint32_t v_base = kf::smem_u32(smem + C::kVOffset + st * 2 * C::kTileBytes);
+        const uint32_t k_base = kf::smem_u32(smem + C::kKOffset + buf * 2 * C::kTileBytes);
+        const uint32_t s_col = tmem + kBufCol + 128 * buf;
+        issue_s<D>(q_addr, k_base, s_col, idS);
+        issue_ds<D>(q_addr, tq_addr, k_base, C::kTileBytes, s_col + 64, idS, has_tq, has_tk);
+        kf::tc::commit(&bars.s_full[buf]);
+      }
+    }
+  } else if (warp == kPvWarp) {
+    if (lane == 0) {
+      // tO += P tV + H V for tile j once its P / H are written and its V / tV have arrived.
+      constexpr uint32_t idPV = kf::tc::idesc_f16(kBf16 ? 1 : 0, kBM, D, false, true);
+      uint32_t acc_started = 0;
+      bool ok = true;
+      for (int j = 0; ok && j < ntiles; ++j) {
+        const int buf = j & 1;
+        if (!(ok = kf::mbar_wait_or_abort<true>(&bars.p_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag))) break;
+        if (!(ok = kf::mbar_wait_or_abort<true>(&bars.v_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag))) break;
+        kf::tc::fence_after_sync();
+        const uint32_t v_base = kf::smem_u32(smem + C::kVOffset + buf * 2 * C::kTileBytes);
         const uint32_t p_col = tmem + kPCol + 64 * buf;
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
@@ -289,7 +290,6 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
           }
         }
         kf::tc::commit(&bars.pv_done[buf]);
-        kf::tc::commit(&bars.v_empty[st]);
       }
       kf::tc::commit(bars.acc_full);
     }
@@ -316,12 +316,18 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       kf::tc::fence_after_sync();
       const int k0 = j * kBN;
       const bool full = k0 + kBN <= limit;  // no masking inside this tile for this row
+      uint32_t sv[2][32], tv[2][32];
+      kf::tc::ld_32x32b_x32(s_col, sv[0]);
+      kf::tc::ld_32x32b_x32(s_col + 32, sv[1]);
+      if (has_h) {
+        kf::tc::ld_32x32b_x32(ts_col, tv[0]);
+        kf::tc::ld_32x32b_x32(ts_col + 32, tv[1]);
+      }
+      kf::tc::wait_ld();
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        uint32_t sr[32], tr[32];
-        kf::tc::ld_32x32b_x32(s_col + c * 32, sr);
-        if (has_h) kf::tc::ld_32x32b_x32(ts_col + c * 32, tr);
-        kf::tc::wait_ld();
+        const uint32_t (&sr)[32] = sv[c];
+        const uint32_t (&tr)[32] = tv[c];
         uint32_t pp[16], hh[16];
         const int kc = k0 + c * 32;
 #pragma unroll
@@ -451,53 +457,54 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
                  q0, b, ntiles, abort_flag);
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
+      // Scores of tile j into buffer j & 1 once tile j-2's output MMAs have consumed the P / H
+      // that overwrote that buffer.
       constexpr uint32_t idS = kf::tc::idesc_f16(kBf16 ? 1 : 0, kBM, kBN, false, false);
-      constexpr uint32_t idPV = kf::tc::idesc_f16(kBf16 ? 1 : 0, kBM, D, false, true);
       const uint32_t q_addr = kf::smem_u32(smem), tq_addr = q_addr + C::kQBytes;
-      bool ok = kf::mbar_wait_or_abort(bars.q_full, 0, &g_fa_error, abort_flag);
-      kf::tc::fence_after_sync();
+      bool ok = kf::mbar_wait_or_abort<true>(bars.q_full, 0, &g_fa_error, abort_flag);
+      for (int j = 0; ok && j < ntiles; ++j) {
+        const int buf = j & 1;
+        if (j >= 2 && !(ok = kf::mbar_wait_or_abort<true>(&bars.pv_done[buf], ((j >> 1) - 1) & 1, &g_fa_error, abort_flag))) break;
+        if (!(ok = kf::mbar_wait_or_abort<true>(&bars.k_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag))) break;
+        kf::tc::fence_after_sync();
+        const uint32_t k_base = kf::smem_u32(smem + C::kKOffset + buf * 2 * C::kTileBytes);
+        const uint32_t s_col = tmem + kBufCol + 128 * buf;
+        issue_s<D>(q_addr, k_base, s_col, idS);
+        issue_ds<D>(q_addr, tq_addr, k_base, C::kTileBytes, s_col + 64, idS, has_tq, has_tk);
+        kf::tc::commit(&bars.s_full[buf]);
+      }
+    }
+  } else if (warp == kPvWarp) {
+    if (lane == 0) {
+      constexpr uint32_t idPV = kf::tc::idesc_f16(kBf16 ? 1 : 0, kBM, D, false, true);
       uint32_t u_started = 0, g_started = 0;
-      for (int j = 0; ok && j <= ntiles; ++j) {
-        if (j < ntiles) {
-          const int st = j % C::kKStages, buf = j & 1;
-          if (j >= 2 && !(ok = kf::mbar_wait_or_abort(&bars.pv_done[buf], ((j >> 1) - 1) & 1, &g_fa_error, abort_flag))) break;
-          if (!(ok = kf::mbar_wait_or_abort(&bars.k_full[st], (j / C::kKStages) & 1, &g_fa_error, abort_flag))) break;
-          kf::tc::fence_after_sync();
-          const uint32_t k_base = kf::smem_u32(smem + C::kKOffset + st * 2 * C::kTileBytes);
-          const uint32_t s_col = tmem + kBufCol + 128 * buf;
-          issue_scores<D>(q_addr, tq_addr, k_base, C::kTileBytes, s_col, s_col + 64, idS, has_tq, has_tk);
-          kf::tc::commit(&bars.s_full[buf]);
-          kf::tc::commit(&bars.k_empty[st]);
-        }
-        if (j >= 1) {
-          const int jj = j - 1, buf = jj & 1, st = jj % C::kVStages;
-          if (!(ok = kf::mbar_wait_or_abort(&bars.p_full[buf], (jj >> 1) & 1, &g_fa_error, abort_flag))) break;
-          if (!(ok = kf::mbar_wait_or_abort(&bars.v_full[st], (jj / C::kVStages) & 1, &g_fa_error, abort_flag))) break;
-          kf::tc::fence_after_sync();
-          const uint32_t v_base = kf::smem_u32(smem + C::kVOffset + st * 2 * C::kTileBytes);
-          const uint32_t p_col = tmem + kBufCol + 128 * buf;
-          const uint32_t h_col = p_col + 64;
+      bool ok = true;
+      for (int j = 0; ok && j < ntiles; ++j) {
+        const int buf = j & 1;
+        if (!(ok = kf::mbar_wait_or_abort<true>(&bars.p_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag))) break;
+        if (!(ok = kf::mbar_wait_or_abort<true>(&bars.v_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag))) break;
+        kf::tc::fence_after_sync();
+        const uint32_t v_base = kf::smem_u32(smem + C::kVOffset + buf * 2 * C::kTileBytes);
+        const uint32_t p_col = tmem + kBufCol + 128 * buf;
+        const uint32_t h_col = p_col + 64;
 #pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk) {
-            // keys [16 kk, 16 kk + 16): warpgroup kk / 2 wrote them at columns 32 (kk / 2) + 8 (kk % 2)
-            const uint32_t acol = (kk >> 1) * 32 + (kk & 1) * 8;
-            const uint64_t vdesc = kf::tc::desc_sw128(v_base + kk * 2048, kBN * 128, 1024);
-            kf::tc::mma_ts(tmem + kUCol, p_col + acol, vdesc, idPV, u_started);
-            u_started = 1;
-            if (has_h) {
-              kf::tc::mma_ts(tmem + kAccCol, h_col + acol, vdesc, idPV, g_started);
-              g_started = 1;
-            }
-            if (has_tv) {
-              kf::tc::mma_ts(tmem + kAccCol, p_col + acol,
-                             kf::tc::desc_sw128(v_base + C::kTileBytes + kk * 2048, kBN * 128, 1024), idPV,
-                             g_started);
-              g_started = 1;
-            }
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          // keys [16 kk, 16 kk + 16): warpgroup kk / 2 wrote them at columns 32 (kk / 2) + 8 (kk % 2)
+          const uint32_t acol = (kk >> 1) * 32 + (kk & 1) * 8;
+          const uint64_t vdesc = kf::tc::desc_sw128(v_base + kk * 2048, kBN * 128, 1024);
+          kf::tc::mma_ts(tmem + kUCol, p_col + acol, vdesc, idPV, u_started);
+          u_started = 1;
+          if (has_h) {
+            kf::tc::mma_ts(tmem + kAccCol, h_col + acol, vdesc, idPV, g_started);
+            g_started = 1;
           }
-          kf::tc::commit(&bars.pv_done[buf]);
-          kf::tc::commit(&bars.v_empty[st]);
+          if (has_tv) {
+            kf::tc::mma_ts(tmem + kAccCol, p_col + acol,
+                           kf::tc::desc_sw128(v_base + C::kTileBytes + kk * 2048, kBN * 128, 1024), idPV, g_started);
+            g_started = 1;
+          }
         }
+        kf::tc::commit(&bars.pv_done[buf]);
       }
       kf::tc::commit(bars.acc_full);
     }

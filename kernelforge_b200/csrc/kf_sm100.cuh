@@ -67,16 +67,37 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// Relaxed-semantics probe of a phase. Threads that keep asynchronous tensor-core or TMA work
+// in flight (the MMA issuer, the TMA producer) use it: an acquire-semantics try_wait in such a
+// thread stalls its issue for hundreds of cycles even when the phase has long completed.
+// Ordering for them comes from the producers of each phase: TMA completes a transaction only
+// after its bytes are in shared memory, tcgen05.commit arrives only after the MMAs' reads, and
+// the softmax threads run tcgen05.wait::st + tcgen05.fence::before_thread_sync before arriving
+// (the consumer issues tcgen05.fence::after_thread_sync after the wait).
+__device__ __forceinline__ bool mbar_try_wait_relaxed(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.relaxed.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait that also gives up as soon as another thread of the CTA has set *abort (a
 // shared-memory flag), so a CTA whose roles synchronise with each other never waits out one
 // timeout per remaining step after the first failure. A timeout sets *abort itself.
+template <bool kRelaxed = false>
 __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, unsigned int* err,
                                                    volatile int* abort) {
-  if (mbar_try_wait(bar, parity)) return true;
+  auto probe = [&]() { return kRelaxed ? mbar_try_wait_relaxed(bar, parity) : mbar_try_wait(bar, parity); };
+  if (probe()) return true;
   const uint64_t start = globaltimer_ns();
   uint32_t spins = 0;
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (probe()) return true;
     if ((++spins & 63u) == 0) {
       if (*abort) return false;
       if (globaltimer_ns() - start > kWaitTimeoutNs) {
