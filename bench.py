@@ -51,9 +51,13 @@ SANA_CONFIGS = (
     {"name": "sana_cfg2", "B": 2, "H": 70, "N": 16384, "D": 32},
 )
 
-# DRAM bytes per launch of the dominant RMSNorm launch (262144 x 8192 bf16) from ncu
-# (dram__bytes_read.sum + dram__bytes_write.sum); None until a capture is summarised in profiles/.
-RMSNORM_NCU_TRAFFIC_BYTES = None
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from `ncu --set full`
+# captures of the `--case ncu-small` shapes. RMSNorm: the 32768 x 8192 capture (536,926,976 read +
+# 486,499,328 written) scaled by rows to the dominant 262144 x 8192 launch (x 8; every row is read
+# once and written once, so traffic is linear in rows). SANA cfg1: both kernels of one call at the
+# bench size itself (producer 75,520,256 + 2,361,600; epilogue 38,514,688 + 2,368,768).
+RMSNORM_NCU_TRAFFIC_BYTES = 8 * (536_926_976 + 486_499_328)
+SANA_NCU_TRAFFIC_BYTES = {"sana_cfg1": 75_520_256 + 2_361_600 + 38_514_688 + 2_368_768}
 
 
 # ---------------------------------------------------------------------------------------------
@@ -216,7 +220,15 @@ def cpu_threads():
 # ---------------------------------------------------------------------------------------------
 # RMSNorm sweep
 # ---------------------------------------------------------------------------------------------
+# --case ncu-small: one small configuration per workload for `ncu --set full` captures (inputs
+# still larger than L2, a few GB on the device at most). Not a benchmark line.
+SMALL = {"rows": (32768,), "hidden": (8192,)}
+CASE = "full"
+
+
 def sweep_points():
+    if CASE == "ncu-small":
+        return [(r, h) for r in SMALL["rows"] for h in SMALL["hidden"]]
     return [(r, h) for r in SWEEP_ROWS for h in SWEEP_HIDDEN]
 
 
@@ -234,7 +246,7 @@ def bench_rmsnorm(args, dist, peaks, peak_kind):
         xs.append(torch.randn(rows, hidden, device=dev, dtype=torch.bfloat16, generator=gen))
         ws.append((1 + 0.1 * torch.randn(hidden, device=dev, generator=gen)).to(torch.bfloat16))
         ys.append(torch.empty(rows, hidden, device=dev, dtype=torch.bfloat16))
-    dominant_index = len(xs) - 1  # 262144 x 8192
+    dominant_index = len(xs) - 1  # the largest tensor (262144 x 8192 in the sweep)
     timer = LaunchTimer()
 
     def step(_):
@@ -372,7 +384,8 @@ def bench_sana(args, dist, peaks, peak_kind, cfg):
         "config": {"B": B, "H": H, "N": N, "D": D, "dtype_in": "bf16", "dtype_out": "bf16",
                    "input_copies": copies, "l2": f"{copies} rotating qkv copies ({copies * one / 1e6:.0f} MB)",
                    "launch": "each step replays a CUDA graph of one qkv_attn_matmul call"},
-        "roofline": roofline(nbytes, dom_ms, peaks["hbm_gbs"], "GB/s", "hbm"),
+        "roofline": roofline(nbytes, dom_ms, peaks["hbm_gbs"], "GB/s", "hbm",
+                             SANA_NCU_TRAFFIC_BYTES.get(cfg["name"])),
         "roofline_note": f"producer + epilogue launches of one call, {dom_ms * 1e3:.1f} us avg; "
                          f"{flops / (dom_ms / 1e3) / 1e12:.1f} TFLOP/s of algorithmic FMA work; "
                          f"peak = {peak_kind} HBM copy GB/s",
@@ -429,6 +442,10 @@ def sana_cpu_baseline(cfg, seconds=5.0):
 FA_CONFIGS = (
     {"name": "fajvp_d64", "B": 4, "H": 16, "N": 4096, "D": 64},
     {"name": "fajvp_d128", "B": 4, "H": 16, "N": 4096, "D": 128},
+)
+FA_SMALL = (
+    {"name": "fajvp_d64", "B": 1, "H": 8, "N": 4096, "D": 64},
+    {"name": "fajvp_d128", "B": 1, "H": 8, "N": 4096, "D": 128},
 )
 
 
@@ -588,7 +605,11 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--case", choices=("full", "ncu-small"), default="full",
+                    help="ncu-small: one small configuration per workload, for ncu --set full captures")
     args = ap.parse_args()
+    global CASE
+    CASE = args.case
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
 
@@ -606,10 +627,10 @@ def main():
     if args.workload in ("all", "rmsnorm"):
         head = bench_rmsnorm(args, dist, peaks, peak_kind)
     if args.workload in ("all", "sana"):
-        for cfg in SANA_CONFIGS:
+        for cfg in (SANA_CONFIGS[:1] if CASE == "ncu-small" else SANA_CONFIGS):
             workloads[cfg["name"]] = bench_sana(args, dist, peaks, peak_kind, cfg)
     if args.workload in ("all", "fajvp"):
-        for cfg in FA_CONFIGS:
+        for cfg in (FA_SMALL if CASE == "ncu-small" else FA_CONFIGS):
             workloads[cfg["name"] + "_standalone"] = bench_fa(args, dist, peaks, peak_kind, cfg, fused=False)
             workloads[cfg["name"] + "_fused"] = bench_fa(args, dist, peaks, peak_kind, cfg, fused=True)
     clocks = sampler.stop()
@@ -624,7 +645,9 @@ def main():
             "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) tensors generated on device)",
-            "config": {"workload": workload_name, "rows": list(SWEEP_ROWS), "hidden": list(SWEEP_HIDDEN),
+            "config": {"workload": workload_name if CASE == "full" else workload_name + " (ncu-small case)",
+                       "rows": sorted({r for r, _ in sweep_points()}),
+                       "hidden": sorted({h for _, h in sweep_points()}),
                        "eps": 1e-6, "l2": "inputs larger than L2: one step streams every sweep tensor",
                        "parallelism": f"weak scaling, {dist.world} rank(s) x full sweep, no collective"},
             "roofline": head["roofline"], "gpu_launches": head["gpu_launches"],
