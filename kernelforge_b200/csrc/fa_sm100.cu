@@ -312,6 +312,8 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       ok = kf::mbar_wait_or_abort(&bars.s_full[group], (j >> 1) & 1, &g_fa_error, abort_flag);
       // This warpgroup's P / H columns were last read by tile j-2's output MMAs.
       if (ok && j >= 2) ok = kf::mbar_wait_or_abort(&bars.pv_done[group], ((j >> 1) - 1) & 1, &g_fa_error, abort_flag);
+      // Warp-uniform outcome: the tcgen05 copies below are .sync.aligned.
+      ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       kf::tc::fence_after_sync();
       const int k0 = j * kBN;
@@ -358,6 +360,7 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     csum = row_sums[row] + row_sums[kBM + row];
     // Epilogue: tO = acc - rowsum(H) * O; warpgroup g writes columns [g D/2, (g + 1) D/2).
     if (ok) ok = kf::mbar_wait_or_abort(bars.acc_full, 0, &g_fa_error, abort_flag);
+    ok = __all_sync(0xffffffffu, ok);
     if (ok) {
       kf::tc::fence_after_sync();
       const int64_t roff = ((static_cast<int64_t>(b) * p.Nq + qrow) * p.Hq + h) * D;
@@ -520,6 +523,7 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
     for (int j = 0; j < ntiles; ++j) {
       const int buf = j & 1;
       if (ok) ok = kf::mbar_wait_or_abort(&bars.s_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);  // the tcgen05 copies below are .sync.aligned
       kf::tc::fence_after_sync();
       const uint32_t s_col = lane_base + kBufCol + 128 * buf + group * 32;
       const uint32_t ts_col = s_col + 64;
@@ -542,11 +546,17 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       softmax_groups_sync();
       mx = fmaxf(tile_max[(buf * 2) * kBM + row], tile_max[(buf * 2 + 1) * kBM + row]);
       if (ok) {
-        if (mx > m_ref + kRescaleThreshold) {
-          if (j > 0 && m_ref != -INFINITY) {
-            // Rescale this row's accumulators once the previous tile's output MMAs are done.
-            const float alpha = ex2(m_ref - mx);
-            ok = kf::mbar_wait_or_abort(&bars.pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, &g_fa_error, abort_flag);
+        // A warp moves to new reference maxima when any of its rows grew past the threshold
+        // (warp-uniform, as the tensor-memory copies are .sync.aligned); the other rows move to
+        // their own max as well, with alpha = 1 where it did not change.
+        if (__any_sync(0xffffffffu, mx > m_ref + kRescaleThreshold)) {
+          const float m_new = fmaxf(m_ref, mx);
+          if (j > 0) {
+            // Rescale the accumulators once the previous tile's output MMAs are done (rows
+            // with no key seen yet hold zeros: alpha = 1).
+            const float alpha = m_ref == -INFINITY ? 1.f : ex2(m_ref - m_new);
+            ok = __all_sync(0xffffffffu, kf::mbar_wait_or_abort(&bars.pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1,
+                                                                &g_fa_error, abort_flag));
             kf::tc::fence_after_sync();
             if (ok) {
 #pragma unroll
@@ -570,7 +580,7 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
             l_part *= alpha;
             r_part *= alpha;
           }
-          m_ref = mx;
+          m_ref = m_new;
         }
         const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
         uint32_t pp[16], hh[16];
@@ -603,6 +613,7 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
     softmax_groups_sync();
     const float r_tot = part_sums[row] + part_sums[kBM + row];
     if (ok) ok = kf::mbar_wait_or_abort(bars.acc_full, 0, &g_fa_error, abort_flag);
+    ok = __all_sync(0xffffffffu, ok);
     if (ok) {
       kf::tc::fence_after_sync();
       const float inv_l = l_tot > 0.f ? 1.f / l_tot : 0.f;

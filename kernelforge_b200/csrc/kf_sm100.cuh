@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "kf_common.cuh"
@@ -109,28 +110,10 @@ __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parit
   }
 }
 
-// ------------------------------------------------------------------------------------------
-// Thread-block clusters: hardware cluster barrier and distributed shared memory reads.
-// ------------------------------------------------------------------------------------------
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile(
-      "barrier.cluster.arrive.release.aligned;\n\t"
-      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
+// Named barrier over `nthreads` threads (a multiple of 32) that use barrier `id` (1..15; 0 is
+// __syncthreads).
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 // ------------------------------------------------------------------------------------------
@@ -305,7 +288,33 @@ struct KernelPrep {
   int smem = -1;       // occupancy entries: size; attribute entries: largest opt-in so far
   int occupancy = 0;
 };
-inline int prepare_kernel(const void* fn, int threads, int smem, int* occupancy_out) {
+// CTAs per SM of a kernel that allocates `tmem_cols` tensor-memory columns per CTA. The
+// runtime's occupancy query assumes such a kernel may hold all 512 columns and answers 1; here
+// the limits are shared memory, registers, threads and the columns the kernel allocates.
+inline int tmem_kernel_occupancy(const void* fn, int threads, int smem, int tmem_cols) {
+  cudaFuncAttributes a{};
+  int dev = 0, smem_sm = 0, reserved = 0, regs_sm = 0, threads_sm = 0;
+  if (cudaFuncGetAttributes(&a, fn) != cudaSuccess || cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&threads_sm, cudaDevAttrMaxThreadsPerMultiProcessor, dev) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 1;
+  }
+  const int warps = (threads + 31) / 32;
+  const int regs_per_warp = (a.numRegs * 32 + 255) / 256 * 256;  // allocation unit: 256 registers
+  int occ = 512 / tmem_cols;
+  occ = std::min(occ, smem_sm / (smem + static_cast<int>(a.sharedSizeBytes) + reserved));
+  if (regs_per_warp > 0) occ = std::min(occ, regs_sm / (regs_per_warp * warps));
+  occ = std::min(occ, threads_sm / threads);
+  return std::max(occ, 1);
+}
+
+// Opt the kernel in to `smem` bytes of dynamic shared memory (cached per device) and, when
+// asked, report how many CTAs of it fit on an SM. tmem_cols > 0: the kernel allocates that
+// many tensor-memory columns per CTA.
+inline int prepare_kernel(const void* fn, int threads, int smem, int* occupancy_out, int tmem_cols = 0) {
   constexpr int kSlots = 256;
   static KernelPrep attr_cache[64][kSlots];
   static KernelPrep occ_cache[64][kSlots];
@@ -333,6 +342,14 @@ inline int prepare_kernel(const void* fn, int threads, int smem, int* occupancy_
       (void)cudaGetLastError();
       return KF_ERR_CUDA;
     }
+    // Kernels with large tiles want every CTA slot the shared memory allows: ask for the
+    // largest shared-memory carveout (the default may keep a bigger L1 and fit fewer CTAs).
+    if (smem >= (64 << 10) &&
+        cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             static_cast<int>(cudaSharedmemCarveoutMaxShared)) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return KF_ERR_CUDA;
+    }
     if (attr != nullptr) {
       attr->smem = smem;
       attr->fn = fn;
@@ -355,7 +372,9 @@ inline int prepare_kernel(const void* fn, int threads, int smem, int* occupancy_
     }
   }
   int occ = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, threads, smem) != cudaSuccess || occ <= 0) {
+  if (tmem_cols > 0) {
+    occ = tmem_kernel_occupancy(fn, threads, smem, tmem_cols);
+  } else if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, threads, smem) != cudaSuccess || occ <= 0) {
     (void)cudaGetLastError();
     occ = 1;
   }

@@ -3,26 +3,28 @@
 // Computes LiteLA.attn_matmul (SANA_LinearAttention/original.py:99-117) as the reference's
 // split-sequence kernels do (SANA_LinearAttention/custom.py:98-388), in two launches:
 //
-//  1. sana_vk_producer   grid (splits, head groups, batch)
-//     Each CTA streams its token range of K and V for G heads through a TMA/mbarrier ring
+//  1. sana_vk_producer   grid (splits, head pairs, batch)
+//     Each CTA streams its token range of K and V for a head pair through a TMA/mbarrier ring
 //     (SWIZZLE_128B boxes of 64 tokens x 2 heads) and accumulates, per head (one warp),
 //         VK[r][c] += v[t][r] * relu(k[t][c])      (mma.sync m16n8k16, fp32 accumulators)
 //         ksum[c]  += relu(k[t][c])                (fp32, from the same B fragments)
-//     It writes fp32 partials; the last CTA to finish a (batch, head group) -- an atomic
-//     arrival counter, no waiting -- sums the partials in split order (deterministic) into the
-//     final VK/ksum and resets the counter for the next call.
-//  2. sana_out_epilogue  grid (token tiles, head groups, batch)
-//     out[t][r] = (VK relu(q_t))_r / (ksum . relu(q_t) + eps). VK and ksum are split into
-//     hi + lo 16-bit halves (two MMAs) so the epilogue keeps ~16 mantissa bits of the fp32
-//     sums; ksum is the 33rd row of the B operand, like the reference's ones-row padding.
-//     The output tile is staged in shared memory and written with a TMA store.
+//     and writes this split's fp32 partial [VK ; ksum] (33 x 32 per head) to the workspace.
+//     The per-head product is 32 x 32: below tcgen05's smallest M, so the warp-level MMA does
+//     it; it hides under the K/V stream.
+//  2. sana_out_tc        persistent, one CTA per (SM, slot), programmatic dependent launch
+//     out[t][r] = (VK relu(q_t))_r / (ksum . relu(q_t) + eps) on the tcgen05 tensor cores,
+//     128 tokens x one head pair per item: relu(Q) in tensor memory as operand A, the
+//     split-summed [VK ; ksum] as hi + lo 16-bit halves in shared memory as operand B (so the
+//     fp32 sums keep ~16 mantissa bits), fp32 accumulators in tensor memory; ksum is the 33rd
+//     row of B, like the reference's ones-row padding. The output tile is staged in shared
+//     memory and written with a TMA store.
 //
-// Intensity is ~16 flop/byte: the path is HBM-bound, K/V are read once by (1), Q read once
-// and out written once by (2). d = 32 is below tcgen05's minimum M (64), so the tensor work
-// uses the warp-level MMA; at the measured rates it is far from the bound.
+// Intensity is ~16 flop/byte: the path is HBM-bound. K/V are read once by (1), Q read once
+// and out written once by (2); the partials (S x 4 KB per head) stay in L2.
 // Shapes outside the fast path (fp32 input, head dims other than 32, tiny tensors) run the
-// generic kernels below (same workspace protocol, CUDA-core fp32 arithmetic).
+// generic kernels below (CUDA-core fp32 arithmetic, partials reduced by the last CTA).
 #include "kf_sm100.cuh"
+#include "kf_tcgen05.cuh"
 
 #include <algorithm>
 #include <type_traits>
@@ -35,11 +37,8 @@ constexpr int kD = 32;                 // fast-path head dim
 constexpr int kTok = 64;               // tokens per tile / TMA box
 constexpr int kBoxBytes = kTok * 128;  // 64 tokens x 128 bytes
 constexpr int kRows = kD + 1;          // 32 VK rows + the ksum row
-constexpr int kMaxG = 4;
 
 int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
-
-constexpr int kMaxClusterSplits = 8;  // portable thread-block cluster size
 
 // Split count of the generic path: ~2 CTAs per SM over (batch, head) units.
 int generic_splits(int64_t B, int64_t H, int64_t N, int64_t requested) {
@@ -53,9 +52,9 @@ int generic_splits(int64_t B, int64_t H, int64_t N, int64_t requested) {
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({s, tiles, 1024})));
 }
 
-// Fast path: the splits of a (batch, head pair) form one cluster (<= 8 CTAs). Default: about
-// two producer CTAs per SM.
+// Fast path: the producer's CTAs are (split, batch, head pair); default about two per SM.
 constexpr int kFastHeads = 2;
+constexpr int kMaxFastSplits = 8;  // the epilogue stages all splits of a head pair at once
 int fast_splits(int64_t B, int64_t H, int64_t N, int64_t requested) {
   const int64_t tiles = std::max<int64_t>(1, ceil_div(N, kTok));
   int64_t s = requested;
@@ -64,23 +63,38 @@ int fast_splits(int64_t B, int64_t H, int64_t N, int64_t requested) {
     const int64_t target = static_cast<int64_t>(kf_host::current_device_sms()) * 2;
     s = (target + units / 2) / std::max<int64_t>(units, 1);
   }
-  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({s, tiles, kMaxClusterSplits})));
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({s, tiles, kMaxFastSplits})));
 }
 
-struct WorkspaceLayout {
-  size_t partial_off, final_off, counter_off, total;
-};
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
-// [partials: B*H*S*(d+1)*d fp32 | final: B*H*(d+1)*d fp32 | counters: B*H u32]. The fast path
-// uses only `final`; the generic path uses all three.
+// Both paths start the workspace with the same arrival counters (B*H u32, zero between calls:
+// the last CTA of each unit resets its counter), so a caller may alternate paths on one
+// workspace.
+//   generic: [counters | partials: B*H*S*(d+1)*d fp32 | final: B*H*(d+1)*d fp32]
+//   fast:    [counters (unused) | partials: B*H*S*33*32 fp32]
+struct WorkspaceLayout {
+  size_t counter_off, partial_off, final_off, total;
+};
 WorkspaceLayout layout_for(int64_t B, int64_t H, int64_t d, int64_t S) {
   WorkspaceLayout l;
   const size_t per_head = static_cast<size_t>(d + 1) * d;
-  l.partial_off = 0;
-  l.final_off = align256(static_cast<size_t>(B * H * S) * per_head * sizeof(float));
-  l.counter_off = l.final_off + align256(static_cast<size_t>(B * H) * per_head * sizeof(float));
-  l.total = l.counter_off + align256(static_cast<size_t>(B * H) * sizeof(unsigned int));
+  l.counter_off = 0;
+  l.partial_off = align256(static_cast<size_t>(B * H) * sizeof(unsigned int));
+  l.final_off = l.partial_off + align256(static_cast<size_t>(B * H * S) * per_head * sizeof(float));
+  l.total = l.final_off + align256(static_cast<size_t>(B * H) * per_head * sizeof(float));
+  return l;
+}
+
+constexpr int kBHalfRows = 48;                     // B rows of one head: 32 VK rows, ksum, 15 zero
+constexpr int kBImageBytes = kBHalfRows * 128;     // one head's B: 48 rows x (32 hi + 32 lo) 16-bit
+struct FastLayout {
+  size_t partial_off, total;
+};
+FastLayout fast_layout(int64_t B, int64_t H, int64_t S) {
+  FastLayout l;
+  l.partial_off = align256(static_cast<size_t>(B * H) * sizeof(unsigned int));
+  l.total = l.partial_off + align256(static_cast<size_t>(B * H * S) * kRows * kD * sizeof(float));
   return l;
 }
 
@@ -93,24 +107,21 @@ __device__ __forceinline__ float operand_scale(float max_abs, bool fp16) {
 }
 
 // ------------------------------------------------------------------------------------------
-// Fast path, kernel 1: K^T V and ksum per split; the S splits of a (batch, head group) are one
-// thread-block cluster and reduce their partials through distributed shared memory.
+// Fast path, kernel 1: K^T V and ksum per split; each split writes its fp32 partial.
 // ------------------------------------------------------------------------------------------
 template <typename T, int G, int STAGES>
 __global__ void __launch_bounds__(G * 32)
-sana_vk_producer(const __grid_constant__ CUtensorMap qkv_map, float* __restrict__ final_vk, int H,
+sana_vk_producer(const __grid_constant__ CUtensorMap qkv_map, float* __restrict__ partial, int H,
                  int tiles, int tiles_per_split) {
-  constexpr int kThreads = G * 32;
   constexpr int kPairs = G / 2;
   constexpr int kStageBytes = 2 * kPairs * kBoxBytes;  // K boxes, then V boxes
   constexpr int kHeadElems = kRows * kD;
-  static_assert(STAGES * kStageBytes >= G * kHeadElems * 4, "reduction buffer must fit the stages");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (kf::smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
 
   const int split = blockIdx.x, hg = blockIdx.y, b = blockIdx.z;
-  const int S = gridDim.x;  // == cluster size
+  const int S = gridDim.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, tig = lane & 3;
   const int h0 = hg * G;
@@ -201,16 +212,16 @@ sana_vk_producer(const __grid_constant__ CUtensorMap qkv_map, float* __restrict_
 
   // The epilogue grid may start its prologue (its Q loads do not depend on this kernel).
   kf::pdl_launch_dependents();
-  // Partials of this split -> own shared memory (the stage ring is idle: every issued load
-  // was waited for). After a timeout the ring may still be written by TMA: leave it alone.
-  float* red = reinterpret_cast<float*>(smem);
-  if (!aborted) {
+  // This split's partial [VK ; ksum] of each head -> partial[b][h][split] (33 x 32 fp32). After a
+  // timeout nothing is written (the error word is set and the results are not used).
+  const int h = h0 + warp;
+  if (!aborted && h < H) {
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt) {
       ksum[nt] += __shfl_xor_sync(0xffffffffu, ksum[nt], 1);
       ksum[nt] += __shfl_xor_sync(0xffffffffu, ksum[nt], 2);
     }
-    float* dst = red + warp * kHeadElems;
+    float* dst = partial + ((static_cast<size_t>(b) * H + h) * S + split) * kHeadElems;
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
@@ -224,209 +235,387 @@ sana_vk_producer(const __grid_constant__ CUtensorMap qkv_map, float* __restrict_
       for (int nt = 0; nt < 4; ++nt) dst[kD * kD + nt * 8 + gid] = ksum[nt];
     }
   }
-  // Every CTA of the cluster reaches both cluster barriers, also after a timeout, so no CTA can
-  // wait for one that has left.
-  __syncthreads();
-  kf::cluster_sync_all();
-  if (!aborted) {
-    // CTA `rank` sums its slice of the G heads' elements over the S splits, in split order.
-    constexpr int kTotal = G * kHeadElems;
-    const int per = (kTotal + S - 1) / S;
-    const int rank = static_cast<int>(kf::cluster_ctarank());
-    const int e_end = min(kTotal, (rank + 1) * per);
-    const uint32_t red_addr = kf::smem_u32(red);
-    for (int e = rank * per + threadIdx.x; e < e_end; e += kThreads) {
-      // Issue all remote loads first, then add in split order (deterministic).
-      float part[kMaxClusterSplits];
-#pragma unroll
-      for (int r = 0; r < kMaxClusterSplits; ++r)
-        part[r] = r < S ? kf::ld_shared_cluster_f32(kf::mapa_shared(red_addr + e * 4, r)) : 0.f;
-      float sum = 0.f;
-#pragma unroll
-      for (int r = 0; r < kMaxClusterSplits; ++r) sum += part[r];
-      const int h = h0 + e / kHeadElems;
-      if (h < H) final_vk[(static_cast<size_t>(b) * H + h) * kHeadElems + e % kHeadElems] = sum;
-    }
-  }
-  kf::cluster_sync_all();  // shared memory stays alive until every remote read is done
 }
 
 // ------------------------------------------------------------------------------------------
-// Fast path, kernel 2: normalised output. Persistent CTAs walk a contiguous range of
-// (batch, head group, 64-token tile) items with a two-deep TMA load / store ring.
+// Fast path, kernel 2: normalised output on the 5th-generation tensor cores.
+//
+// One persistent CTA per SM walks a contiguous range of items (batch, head pair, 128-token
+// tile), with warp-specialised roles:
+//   * workers, warps 0-15, in two groups taking alternate items. Worker warp (group g, head hd,
+//     quarter q) handles tokens 32 q .. 32 q + 31 of the tile -- its tensor-memory lanes -- for
+//     head hd: it writes A = relu(Q) (M = 128 tokens, K = 32 q channels, packed 16-bit pairs)
+//     into tensor memory, and after the MMAs reads D = A.B (128 x 48 fp32) and writes
+//     out[r][c] = D[r][c] / (D[r][32] + eps) with its own TMA store (32 tokens x 32 channels);
+//   * two MMA warps (16, 17), one per group: for each of the group's items and each head, once
+//     the head's four workers have prepared A, four K = 16 MMAs D = A.B_hi + A.B_lo; each also
+//     keeps its group's Q stages full with TMA;
+//   * B = [VK ; ksum ; 0] of a head pair, as hi + lo 16-bit halves side by side along K (so the
+//     fp32 split sums keep ~16 mantissa bits), swizzled like a 128-byte TMA tile: built from the
+//     producer's split partials, summed in split order (deterministic). The first two head pairs
+//     of the CTA are built at the start by every non-MMA thread; later ones by the B warp (18)
+//     while the workers run. fp16 inputs scale B by a power of two that keeps max|VK| below
+//     2^14 (eps is scaled with it); bf16 needs no scaling.
+// A and D are double-buffered per group in tensor memory (2 groups x 2 buffers x 2 heads x 64
+// columns), B per head pair in shared memory. Every wait is on an mbarrier; inside the loop the
+// CTA never synchronises as a whole.
 // ------------------------------------------------------------------------------------------
-template <typename T, typename O, int G>
-__global__ void __launch_bounds__(G * 32)
-sana_out_epilogue(const __grid_constant__ CUtensorMap qkv_map,
-                  const __grid_constant__ CUtensorMap out_map, const float* __restrict__ final_vk,
-                  int H, int C, int head_groups, int tiles_out, int total_items, int items_per_cta,
-                  float eps) {
-  constexpr int kPairs = G / 2;
-  constexpr int kQBytes = kPairs * kBoxBytes;
-  constexpr int kOutBoxes = (G * kD * static_cast<int>(sizeof(O))) / 128;
-  constexpr int kOutBytes = kOutBoxes * kBoxBytes;
-  constexpr int kChPerBox = 128 / static_cast<int>(sizeof(O));
+constexpr int kOutTok = 128;                    // tokens per item
+constexpr int kWorkerWarps = 16;
+constexpr int kMmaWarp0 = 16;                   // MMA warps 16 (group 0) and 17 (group 1)
+constexpr int kBWarp = 18;
+constexpr int kEpiThreads = 32 * 19;
+constexpr int kBuildThreads = 32 * (kWorkerWarps + 1);  // workers + B warp build the first B tiles
+constexpr int kQTileBytes = kOutTok * 128;      // 128 tokens x one head pair (64 channels)
+constexpr uint32_t kEpiTmemCols = 512;
+constexpr uint32_t kBuildBar = 1;               // named barrier of the first B build
+// Tensor memory of (group g, buffer j, head hd): D at 64 (4 g + 2 j + hd) + [0, 48), A at + 48 + [0, 16).
+__device__ __forceinline__ uint32_t tm_slot(int g, int j, int hd) { return 64u * (4 * g + 2 * j + hd); }
+
+template <typename O>
+struct EpiCfg {
+  static constexpr int kStages = sizeof(O) == 4 ? 8 : 10;                 // Q ring depth (even)
+  static constexpr int kWarpOutBytes = 32 * kD * int(sizeof(O));          // 32 tokens x 32 channels
+  static constexpr int kQOff = 0;
+  static constexpr int kOutOff = kStages * kQTileBytes;
+  static constexpr int kBOff = kOutOff + kWorkerWarps * kWarpOutBytes;    // [buffer][head] x kBImageBytes
+  static constexpr int kSmemBytes = kBOff + 4 * kBImageBytes + 1024;
+};
+static_assert(EpiCfg<__nv_bfloat16>::kStages % 2 == 0 && EpiCfg<float>::kStages % 2 == 0,
+              "each MMA warp refills its own group's stages");
+
+// Sum of the S split partials of (head h of the pair, row n, k values 8 kg .. 8 kg + 7), in split
+// order, straight from the workspace (L2).
+__device__ __forceinline__ void sum_splits(const float* __restrict__ partial, int b, int h, int H, int S, int n,
+                                           int kg, float (&v)[8]) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) v[e] = 0.f;
+  if (h >= H) return;
+  const float* src = partial + (static_cast<size_t>(b) * H + h) * S * (kRows * kD) + n * kD + kg * 8;
+  constexpr int kBatch = 4;  // splits whose loads are in flight together
+  for (int sp0 = 0; sp0 < S; sp0 += kBatch) {
+    float4 x[kBatch][2];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u)
+      if (sp0 + u < S) {
+        x[u][0] = __ldcg(reinterpret_cast<const float4*>(src + (sp0 + u) * (kRows * kD)));
+        x[u][1] = __ldcg(reinterpret_cast<const float4*>(src + (sp0 + u) * (kRows * kD) + 4));
+      }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u)
+      if (sp0 + u < S) {
+        v[0] += x[u][0].x; v[1] += x[u][0].y; v[2] += x[u][0].z; v[3] += x[u][0].w;
+        v[4] += x[u][1].x; v[5] += x[u][1].y; v[6] += x[u][1].z; v[7] += x[u][1].w;
+      }
+  }
+}
+
+__device__ __forceinline__ float max_abs8(const float (&v)[8]) {
+  float m = 0.f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(v[e]));
+  return m;
+}
+
+// One B row chunk: 8 k values of row n as hi and lo halves, into tile `tile` (one head).
+template <typename T>
+__device__ __forceinline__ void store_b_chunk(uint8_t* tile, int n, int kg, const float (&v)[8], float scale) {
+  uint32_t hi[4], lo[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float x0 = v[2 * e] * scale, x1 = v[2 * e + 1] * scale;
+    hi[e] = kf::Mma<T>::from_f2(x0, x1);
+    const float2 hf = kf::Mma<T>::to_f2(hi[e]);
+    lo[e] = kf::Mma<T>::from_f2(x0 - hf.x, x1 - hf.y);
+  }
+  uint8_t* row = tile + n * 128;
+  *reinterpret_cast<uint4*>(row + ((kg ^ (n & 7)) << 4)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+  *reinterpret_cast<uint4*>(row + (((4 + kg) ^ (n & 7)) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+}
+
+template <typename T, typename O>
+__global__ void __maxnreg__(96)
+sana_out_tc(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap out_map,
+            const float* __restrict__ partial, int H, int S, int head_pairs, int tiles_out, int total_items,
+            int items_per_cta, float eps) {
+  using Cfg = EpiCfg<O>;
+  constexpr int kStages = Cfg::kStages;
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr bool kFp16 = std::is_same<T, __half>::value;
+  constexpr int kTasks = 2 * kRows * 4;  // B chunks of a head pair: (head, row, group of 8 k values)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (kf::smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint8_t* qbuf[2] = {smem, smem + kQBytes};
-  uint8_t* obuf[2] = {smem + 2 * kQBytes, smem + 2 * kQBytes + kOutBytes};
-  float* vk_s = reinterpret_cast<float*>(smem + 2 * kQBytes + 2 * kOutBytes);  // G heads x 33 x 32
-  __shared__ uint64_t bars[2];
-  __shared__ uint64_t vk_bar;
+  __shared__ uint64_t q_full[kStages];
+  __shared__ uint64_t ready[2][2][2];   // [group][head][buffer]: the head's 4 workers prepared A
+  __shared__ uint64_t d_full[2][2][2];  // [group][head][buffer]: D computed
+  __shared__ uint64_t b_ready[2];       // [B buffer]: B of a head pair built
+  __shared__ uint64_t unit_done[2];     // [B buffer]: all 16 workers are past a head pair
+  __shared__ float eps_s[2][2];         // [B buffer][head]
+  __shared__ uint32_t max_bits[2][2];   // [B buffer][head]: max |VK| of the first two head pairs (fp16)
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
 
   const int first = blockIdx.x * items_per_cta;
-  const int last = min(total_items, first + items_per_cta);
-  if (first >= last) return;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int gid = lane >> 2, tig = lane & 3;
-  const int pair = warp >> 1, g = warp & 1;
+  const int n_items = min(total_items, first + items_per_cta) - first;
+  if (n_items <= 0) return;  // uniform for the whole CTA
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int first_unit = first / tiles_out;
+  const int n_units = (first + n_items - 1) / tiles_out - first_unit + 1;
+  uint8_t* const btiles = smem + Cfg::kBOff;
 
-  auto issue = [&](int item, int buf) {
-    const int unit = item / tiles_out, tt = item % tiles_out;
-    const int b = unit / head_groups, hg = unit % head_groups;
-    kf::mbar_arrive_expect_tx(&bars[buf], kQBytes);
-#pragma unroll
-    for (int p = 0; p < kPairs; ++p)
-      kf::tma_load_4d(qbuf[buf] + p * kBoxBytes, &qkv_map, &bars[buf], (hg * G + 2 * p) * kD, 0,
-                      tt * kTok, b);
-  };
-  if (threadIdx.x == 0) {
-    kf::prefetch_tensormap(&qkv_map);
+  if (t == 0) {
+    kf::prefetch_tensormap(&q_map);
     kf::prefetch_tensormap(&out_map);
-    kf::mbar_init(&bars[0], 1);
-    kf::mbar_init(&bars[1], 1);
-    kf::mbar_init(&vk_bar, 1);
+    for (int st = 0; st < kStages; ++st) kf::mbar_init(&q_full[st], 1);
+    for (int g = 0; g < 2; ++g)
+      for (int h = 0; h < 2; ++h)
+        for (int j = 0; j < 2; ++j) {
+          kf::mbar_init(&ready[g][h][j], 4);
+          kf::mbar_init(&d_full[g][h][j], 1);
+        }
+    for (int j = 0; j < 2; ++j) {
+      kf::mbar_init(&b_ready[j], 1);
+      kf::mbar_init(&unit_done[j], kWorkerWarps);
+      max_bits[j][0] = max_bits[j][1] = 0u;
+    }
+    abort_flag = 0;
     kf::fence_mbar_init();
-    issue(first, 0);
-    if (first + 1 < last) issue(first + 1, 1);
   }
+  if (warp == kMmaWarp0) kf::tc::tmem_alloc(&tmem_slot, kEpiTmemCols);
+  for (int e = t; e < 4 * (kBHalfRows - kRows) * 8; e += kEpiThreads) {  // B rows 33..47 stay zero
+    const int tile = e / ((kBHalfRows - kRows) * 8), row = kRows + (e / 8) % (kBHalfRows - kRows);
+    *reinterpret_cast<uint4*>(btiles + tile * kBImageBytes + row * 128 + (e % 8) * 16) = make_uint4(0, 0, 0, 0);
+  }
+  kf::tc::fence_before_sync();
   __syncthreads();
-  // Q does not depend on the producer; K^T V does: wait for the producer grid from here on.
-  kf::pdl_wait_primary();
-  uint32_t vk_phase = 0;
+  kf::tc::fence_after_sync();
+  const uint32_t tmem = tmem_slot;
+  auto unit_of = [&](int k) { return (first + k) / tiles_out; };
 
-  // B operand: VK^T (K = q channel, N = output row) as hi/lo halves; n-tile 4 row 0 = ksum.
-  uint32_t bhi[2][5][2], blo[2][5][2];
-  float eps_scaled = eps;
-  int cur_unit = -1;
-  for (int it = first, i = 0; it < last; ++it, ++i) {
-    const int unit = it / tiles_out, tt = it % tiles_out;
-    const int b = unit / head_groups, hg = unit % head_groups;
-    const int h0 = hg * G;
-    if (unit != cur_unit) {
-      cur_unit = unit;
-      const int nheads = min(G, H - h0);
-      if (threadIdx.x == 0) {
-        const uint32_t bytes = static_cast<uint32_t>(nheads * kRows * kD * sizeof(float));
-        kf::mbar_arrive_expect_tx(&vk_bar, bytes);
-        kf::bulk_load(vk_s, final_vk + (static_cast<size_t>(b) * H + h0) * kRows * kD, bytes, &vk_bar);
-      }
-      const bool vk_ok = kf::mbar_wait_bounded(&vk_bar, vk_phase, &g_sana_error);
-      vk_phase ^= 1u;
-      if (!__syncthreads_and(vk_ok)) break;
-      const int h = h0 + warp;
-      const bool valid = h < H;
-      const float* src = vk_s + min(warp, nheads - 1) * kRows * kD;
-      float v[2][5][2][2];
-      float vmax = 0.f;
-#pragma unroll
-      for (int ks = 0; ks < 2; ++ks)
-#pragma unroll
-        for (int nt = 0; nt < 5; ++nt)
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            const int r = nt * 8 + gid;
-            const int c = ks * 16 + half * 8 + tig * 2;
-            float2 x = make_float2(0.f, 0.f);
-            if (valid && r <= kD) x = *reinterpret_cast<const float2*>(src + r * kD + c);
-            v[ks][nt][half][0] = x.x;
-            v[ks][nt][half][1] = x.y;
-            vmax = fmaxf(vmax, fmaxf(fabsf(x.x), fabsf(x.y)));
-          }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, o));
-      const float scale = operand_scale(vmax, std::is_same<T, __half>::value);
-      eps_scaled = eps * scale;
-#pragma unroll
-      for (int ks = 0; ks < 2; ++ks)
-#pragma unroll
-        for (int nt = 0; nt < 5; ++nt)
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            const float x0 = v[ks][nt][half][0] * scale, x1 = v[ks][nt][half][1] * scale;
-            const uint32_t hi = kf::Mma<T>::from_f2(x0, x1);
-            const float2 hf = kf::Mma<T>::to_f2(hi);
-            bhi[ks][nt][half] = hi;
-            blo[ks][nt][half] = kf::Mma<T>::from_f2(x0 - hf.x, x1 - hf.y);
-          }
-      __syncthreads();  // vk_s is free for the next unit's copy
-    }
-    const int buf = i & 1;
-    if (threadIdx.x == 0 && i >= 2) kf::tma_store_wait_read1();  // store of item i-2 has read obuf[buf]
-    const bool ok = kf::mbar_wait_bounded(&bars[buf], (i >> 1) & 1, &g_sana_error);
-    if (!__syncthreads_and(ok)) break;
-
-    const uint32_t qbase = kf::smem_u32(qbuf[buf] + pair * kBoxBytes);
-    uint8_t* otile = obuf[buf];
-#pragma unroll
-    for (int mt = 0; mt < kTok / 16; ++mt) {
-      uint32_t a[2][4];
-#pragma unroll
-      for (int ks = 0; ks < 2; ++ks) {
-        const int row = mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-        const int chunk = g * 4 + ks * 2 + (lane >> 4);
-        kf::ldsm_x4(qbase + kf::swz128(row, chunk), a[ks][0], a[ks][1], a[ks][2], a[ks][3]);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) a[ks][j] = kf::Mma<T>::relu2(a[ks][j]);
-      }
-      float acc[5][4];
-#pragma unroll
-      for (int nt = 0; nt < 5; ++nt)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[nt][j] = 0.f;
-#pragma unroll
-      for (int ks = 0; ks < 2; ++ks)
-#pragma unroll
-        for (int nt = 0; nt < 5; ++nt) {
-          kf::Mma<T>::run(acc[nt], a[ks], bhi[ks][nt]);
-          kf::Mma<T>::run(acc[nt], a[ks], blo[ks][nt]);
+  if (warp == kMmaWarp0 || warp == kMmaWarp0 + 1) {
+    // ---- MMA issue and Q loads of group g (one thread) ----
+    const int g = warp - kMmaWarp0;
+    if (lane == 0) {
+      uint32_t commits[2][2] = {};  // [head][buffer]
+      int loaded = -1;
+      auto load = [&](int k) {
+        const int it = first + k;
+        const int unit = it / tiles_out, tt = it % tiles_out;
+        const int b = unit / head_pairs, hp = unit % head_pairs;
+        const int st = k % kStages;
+        kf::mbar_arrive_expect_tx(&q_full[st], kQTileBytes);
+        kf::tma_load_4d(smem + Cfg::kQOff + st * kQTileBytes, &q_map, &q_full[st], hp * 2 * kD, 0, tt * kOutTok, b);
+        loaded = k;
+      };
+      for (int k = g; k < kStages && k < n_items; k += 2) load(k);
+      constexpr uint32_t idesc = kf::tc::idesc_f16(kBf16 ? 1 : 0, kOutTok, kBHalfRows, false, false);
+      int b_unit = -1;
+      for (int k = g, i = 0; k < n_items; k += 2, ++i) {
+        const int j = i & 1;
+        const int u = unit_of(k) - first_unit;
+        // A new head pair's B was written by ordinary stores: observe it with acquire.
+        if (u != b_unit) {
+          if (!kf::mbar_wait_or_abort(&b_ready[u & 1], (u >> 1) & 1, &g_sana_error, &abort_flag)) break;
+          b_unit = u;
         }
-      // Column 32 (n-tile 4, tig 0, first element) holds the denominators of rows gid, gid + 8.
-      const float inv0 = __frcp_rn(__shfl_sync(0xffffffffu, acc[4][0], lane & ~3) + eps_scaled);
-      const float inv1 = __frcp_rn(__shfl_sync(0xffffffffu, acc[4][2], lane & ~3) + eps_scaled);
+        bool ok = true;
+        for (int h = 0; h < 2 && ok; ++h) {
+          // A arrives through tensor memory (ordered by the workers' tcgen05 fences).
+          ok = kf::mbar_wait_or_abort<true>(&ready[g][h][j], (i >> 1) & 1, &g_sana_error, &abort_flag);
+          if (!ok) break;
+          kf::tc::fence_after_sync();
+          const uint32_t slot = tm_slot(g, j, h);
+          const uint32_t b_addr = kf::smem_u32(btiles + ((u & 1) * 2 + h) * kBImageBytes);
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
-        const int cc = warp * kD + nt * 8 + tig * 2;  // channel within the CTA's G heads
+          for (int ks = 0; ks < 4; ++ks)  // hi k 0-15, hi k 16-31, lo k 0-15, lo k 16-31
+            kf::tc::mma_ts(tmem + slot, tmem + slot + 48 + (ks & 1) * 8, kf::tc::desc_sw128(b_addr + ks * 32, 16, 1024),
+                           idesc, ks > 0 ? 1u : 0u);
+          kf::tc::commit(&d_full[g][h][j]);
+          ++commits[h][j];
+        }
+        if (!ok) break;
+        // Both heads' workers have read Q(k): its stage takes item k + kStages (same group).
+        if (k + kStages < n_items) load(k + kStages);
+      }
+      // Leave nothing in flight on exit (after a timeout): MMA groups and Q loads.
+      for (int h = 0; h < 2; ++h)
+        for (int j = 0; j < 2; ++j)
+          if (commits[h][j] > 0) kf::mbar_wait_bounded(&d_full[g][h][j], (commits[h][j] - 1) & 1, &g_sana_error);
+      for (int k = loaded; k >= 0 && k > loaded - kStages; k -= 2)
+        kf::mbar_wait_bounded(&q_full[k % kStages], (k / kStages) & 1, &g_sana_error);
+    }
+  } else {
+    // ---- B tiles of the first two head pairs: every worker and the B warp, one chunk each ----
+    kf::pdl_wait_primary();  // the partials come from the producer grid
+    const int n_first = min(n_units, 2);
+    const int task = warp == kBWarp ? 32 * kWorkerWarps + lane : t;  // < kBuildThreads
+    const int bu = task / kTasks, bt = task % kTasks;
+    const int bh = bt / (kRows * 4), bn = (bt / 4) % kRows, bkg = bt % 4;
+    const bool has_task = bu < n_first;
+    float v[8];
+    int bb = 0, bhp = 0;
+    if (has_task) {
+      const int unit = first_unit + bu;
+      bb = unit / head_pairs;
+      bhp = unit % head_pairs;
+      sum_splits(partial, bb, 2 * bhp + bh, H, S, bn, bkg, v);
+      if (kFp16) atomicMax(&max_bits[bu][bh], __float_as_uint(max_abs8(v)));
+    }
+    if (kFp16) kf::named_bar_sync(kBuildBar, kBuildThreads);
+    auto scale_of = [&](int bu_, int h) {
+      return kFp16 ? operand_scale(__uint_as_float(max_bits[bu_][h]), true) : 1.f;
+    };
+    if (has_task) store_b_chunk<T>(btiles + (bu * 2 + bh) * kBImageBytes, bn, bkg, v, scale_of(bu, bh));
+    kf::fence_proxy_async_smem();  // the tensor cores read B through the async proxy
+    kf::named_bar_sync(kBuildBar, kBuildThreads);
+    if (warp == kBWarp && lane == 0)
+      for (int u = 0; u < n_first; ++u) {
+        eps_s[u][0] = eps * scale_of(u, 0);
+        eps_s[u][1] = eps * scale_of(u, 1);
+        kf::mbar_arrive(&b_ready[u]);
+      }
+
+    if (warp == kBWarp) {
+      // ---- B tiles of later head pairs (only ranges crossing more than two head pairs) ----
+      for (int u = 2; u < n_units; ++u) {
+        // Buffer u & 1 was last used by head pair u - 2: every worker must be past it.
+        if (!__all_sync(0xffffffffu, kf::mbar_wait_or_abort(&unit_done[u & 1], ((u >> 1) - 1) & 1,
+                                                            &g_sana_error, &abort_flag)))
+          break;
+        const int unit = first_unit + u;
+        const int b = unit / head_pairs, hp = unit % head_pairs;
+        float mx0 = 0.f, mx1 = 0.f;
+        if (kFp16) {  // first pass: the scale
+          for (int tk = lane; tk < kTasks; tk += 32) {
+            float w[8];
+            sum_splits(partial, b, 2 * hp + tk / (kRows * 4), H, S, (tk / 4) % kRows, tk % 4, w);
+            if (tk < kRows * 4) mx0 = fmaxf(mx0, max_abs8(w)); else mx1 = fmaxf(mx1, max_abs8(w));
+          }
 #pragma unroll
-        for (int rh = 0; rh < 2; ++rh) {
-          const int row = mt * 16 + gid + rh * 8;
-          const float inv = rh ? inv1 : inv0;
-          const float v0 = acc[nt][rh * 2] * inv;
-          const float v1 = acc[nt][rh * 2 + 1] * inv;
-          const int box = cc / kChPerBox;
-          const int colb = (cc % kChPerBox) * static_cast<int>(sizeof(O));
-          uint8_t* p = otile + box * kBoxBytes + kf::swz128(row, colb >> 4) + (colb & 15);
-          if constexpr (sizeof(O) == 4) {
-            *reinterpret_cast<float2*>(p) = make_float2(v0, v1);
-          } else {
-            *reinterpret_cast<uint32_t*>(p) = kf::Mma<O>::from_f2(v0, v1);
+          for (int o = 16; o > 0; o >>= 1) {
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
           }
         }
+        const float sc0 = kFp16 ? operand_scale(mx0, true) : 1.f, sc1 = kFp16 ? operand_scale(mx1, true) : 1.f;
+        for (int tk = lane; tk < kTasks; tk += 32) {
+          const int h = tk / (kRows * 4);
+          float w[8];
+          sum_splits(partial, b, 2 * hp + h, H, S, (tk / 4) % kRows, tk % 4, w);
+          store_b_chunk<T>(btiles + ((u & 1) * 2 + h) * kBImageBytes, (tk / 4) % kRows, tk % 4, w, h ? sc1 : sc0);
+        }
+        kf::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          eps_s[u & 1][0] = eps * sc0;
+          eps_s[u & 1][1] = eps * sc1;
+          kf::mbar_arrive(&b_ready[u & 1]);
+        }
+        __syncwarp();
       }
-    }
-    kf::fence_proxy_async_smem();
-    __syncthreads();
-    if (threadIdx.x == 0) {
+    } else {
+      // ---- workers ----
+      const int g = warp >> 3, hd = (warp >> 2) & 1, quarter = warp & 3;
+      const uint32_t lanes = static_cast<uint32_t>(quarter * 32) << 16;
+      const int r = quarter * 32 + lane;  // token within the tile
+      const int n_g = (n_items - g + 1) / 2;
+      uint8_t* stage_out = smem + Cfg::kOutOff + warp * Cfg::kWarpOutBytes;
+      // relu(Q) of local item i (item 2 i + g), this warp's tokens and head, into A buffer i & 1;
+      // then tell the MMA warp (this warp has also finished reading D of local item i - 2).
+      auto prep = [&](int i) -> bool {
+        const int k = 2 * i + g;
+        const int st = k % kStages;
+        const bool got = kf::mbar_wait_or_abort(&q_full[st], (k / kStages) & 1, &g_sana_error, &abort_flag);
+        if (!__all_sync(0xffffffffu, got)) return false;  // warp-uniform: the tcgen05 copy is .sync.aligned
+        const uint8_t* row = smem + Cfg::kQOff + st * kQTileBytes + r * 128;
+        uint32_t w[16];
 #pragma unroll
-      for (int box = 0; box < kOutBoxes; ++box) {
-        const int c0 = h0 * kD + box * kChPerBox;
-        if (c0 < C) kf::tma_store_3d(&out_map, otile + box * kBoxBytes, c0, tt * kTok, b);
+        for (int j = 0; j < 4; ++j) {
+          const uint4 x = *reinterpret_cast<const uint4*>(row + (((hd * 4 + j) ^ (r & 7)) << 4));
+          w[4 * j + 0] = kf::Mma<T>::relu2(x.x);
+          w[4 * j + 1] = kf::Mma<T>::relu2(x.y);
+          w[4 * j + 2] = kf::Mma<T>::relu2(x.z);
+          w[4 * j + 3] = kf::Mma<T>::relu2(x.w);
+        }
+        kf::tc::st_32x32b_x16(tmem + lanes + tm_slot(g, i & 1, hd) + 48, w);
+        kf::tc::wait_st();
+        kf::tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) kf::mbar_arrive(&ready[g][hd][i & 1]);
+        return true;
+      };
+      int units_done = 0;  // head pairs this warp has announced as finished
+      auto finish_units = [&](int upto) {
+        for (; units_done < upto; ++units_done)
+          if (lane == 0) kf::mbar_arrive(&unit_done[units_done & 1]);
+      };
+      bool ok = n_g > 0 && prep(0);
+      if (ok && n_g > 1) ok = prep(1);
+      int eps_unit = -1;
+      float eps_h = 0.f;
+      for (int i = 0; ok && i < n_g; ++i) {
+        const int k = 2 * i + g;
+        const int unit = unit_of(k), tt = (first + k) % tiles_out;
+        const int b = unit / head_pairs, hp = unit % head_pairs;
+        const int u = unit - first_unit;
+        finish_units(u);  // every earlier head pair is done for this warp
+        if (u != eps_unit) {
+          // Head pairs 0 and 1 were built before the loop (named barrier); later ones by the B warp.
+          if (u >= 2 && !__all_sync(0xffffffffu, kf::mbar_wait_or_abort(&b_ready[u & 1], (u >> 1) & 1,
+                                                                        &g_sana_error, &abort_flag)))
+            break;
+          eps_unit = u;
+          eps_h = u < 2 ? eps * scale_of(u, hd) : eps_s[u & 1][hd];
+        }
+        if (!__all_sync(0xffffffffu,
+                        kf::mbar_wait_or_abort(&d_full[g][hd][i & 1], (i >> 1) & 1, &g_sana_error, &abort_flag)))
+          break;
+        kf::tc::fence_after_sync();
+        uint32_t num[32], den[2];
+        kf::tc::ld_32x32b_x32(tmem + lanes + tm_slot(g, i & 1, hd), num);
+        kf::tc::ld_32x32b_x2(tmem + lanes + tm_slot(g, i & 1, hd) + kD, den);
+        kf::tc::wait_ld();
+        const float inv = __frcp_rn(__uint_as_float(den[0]) + eps_h);
+        // Stage this warp's 32 tokens x 32 channels (rows of 64 bytes, 64-byte swizzle, for 16-bit
+        // out; rows of 128 bytes, 128-byte swizzle, for fp32) once its previous store has read it.
+        if (lane == 0) kf::tma_store_wait_read0();
+        __syncwarp();
+        if constexpr (sizeof(O) == 4) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<float4*>(stage_out + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                make_float4(__uint_as_float(num[4 * j]) * inv, __uint_as_float(num[4 * j + 1]) * inv,
+                            __uint_as_float(num[4 * j + 2]) * inv, __uint_as_float(num[4 * j + 3]) * inv);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t pk[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              pk[e] = kf::Mma<O>::from_f2(__uint_as_float(num[8 * j + 2 * e]) * inv,
+                                          __uint_as_float(num[8 * j + 2 * e + 1]) * inv);
+            *reinterpret_cast<uint4*>(stage_out + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
+                make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          }
+        }
+        kf::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && 2 * hp + hd < H) {
+          kf::tma_store_3d(&out_map, stage_out, hp * 2 * kD + hd * kD, tt * kOutTok + quarter * 32, b);
+          kf::tma_store_commit();
+        }
+        if (i + 2 < n_g) ok = prep(i + 2);
       }
-      kf::tma_store_commit();
-      if (it + 2 < last) issue(it + 2, buf);
+      finish_units(n_units);
+      if (lane == 0) kf::tma_store_wait_read0();  // shared memory outlives the stores' reads
     }
   }
-  if (threadIdx.x == 0) kf::tma_store_wait_read0();  // smem outlives the stores' reads
+  kf::tc::fence_before_sync();
+  __syncthreads();
+  if (warp == kMmaWarp0) {
+    kf::tc::fence_after_sync();
+    kf::tc::tmem_dealloc(tmem, kEpiTmemCols);
+  }
 }
 
 // ------------------------------------------------------------------------------------------
@@ -536,28 +725,38 @@ sana_out_generic(const T* __restrict__ qkv, const float* __restrict__ final_vk, 
 // ------------------------------------------------------------------------------------------
 constexpr int kFastStages = 3;
 
+// ws: the workspace laid out by fast_layout(B, H, S); its counters are zero between calls.
 template <typename T, int G>
-int launch_fast(const void* qkv, void* out, float* final_vk, int B, int H, int N, int S, float eps,
-                int out_dtype, cudaStream_t stream) {
+int launch_fast(const void* qkv, void* out, uint8_t* ws, int B, int H, int N, int S, float eps, int out_dtype,
+                cudaStream_t stream) {
+  static_assert(G == 2, "the epilogue works on head pairs");
   const int C = H * kD;
   const int in_dtype = std::is_same<T, __half>::value ? KF_DTYPE_F16 : KF_DTYPE_BF16;
   const size_t es = 2;
-  CUtensorMap qkv_map, out_map;
+  float* partial = reinterpret_cast<float*>(ws + fast_layout(B, H, S).partial_off);
+  // qkv [B, N, 3, C] seen as 4-D (channel, q/k/v, token, batch); boxes of 64 channels (one
+  // head pair, 128 bytes) x 64 tokens for the producer and x 128 tokens for the epilogue.
+  CUtensorMap kv_map, q_map, out_map;
   {
     const uint64_t dims[4] = {static_cast<uint64_t>(C), 3, static_cast<uint64_t>(N), static_cast<uint64_t>(B)};
     const uint64_t strides[3] = {C * es, 3 * C * es, static_cast<uint64_t>(N) * 3 * C * es};
     const uint32_t box[4] = {64, 1, kTok, 1};
-    if (!kf_host::encode_tiled(&qkv_map, kf_host::map_type(in_dtype), 4, qkv, dims, strides, box,
+    if (!kf_host::encode_tiled(&kv_map, kf_host::map_type(in_dtype), 4, qkv, dims, strides, box,
+                               CU_TENSOR_MAP_SWIZZLE_128B))
+      return KF_ERR_CUDA;
+    const uint32_t qbox[4] = {64, 1, kOutTok, 1};
+    if (!kf_host::encode_tiled(&q_map, kf_host::map_type(in_dtype), 4, qkv, dims, strides, qbox,
                                CU_TENSOR_MAP_SWIZZLE_128B))
       return KF_ERR_CUDA;
   }
   {
+    // out [B, N, C]: boxes of one head (32 channels) x 32 tokens, one per epilogue worker warp.
     const size_t os = kf::dtype_size(out_dtype);
     const uint64_t dims[3] = {static_cast<uint64_t>(C), static_cast<uint64_t>(N), static_cast<uint64_t>(B)};
     const uint64_t strides[2] = {C * os, static_cast<uint64_t>(N) * C * os};
-    const uint32_t box[3] = {static_cast<uint32_t>(128 / os), kTok, 1};
+    const uint32_t box[3] = {static_cast<uint32_t>(kD), 32, 1};
     if (!kf_host::encode_tiled(&out_map, kf_host::map_type(out_dtype), 3, out, dims, strides, box,
-                               CU_TENSOR_MAP_SWIZZLE_128B))
+                               os == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
       return KF_ERR_CUDA;
   }
   const int HG = (H + G - 1) / G;
@@ -568,34 +767,24 @@ int launch_fast(const void* qkv, void* out, float* final_vk, int B, int H, int N
     const int smem = kFastStages * 2 * (G / 2) * kBoxBytes + kFastStages * 8 + 1024;
     const int prep = kf_host::prepare_kernel(reinterpret_cast<const void*>(kernel), G * 32, smem, nullptr);
     if (prep != KF_OK) return prep;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(S, HG, B);
-    cfg.blockDim = dim3(G * 32);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = S;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    KF_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, qkv_map, final_vk, H, tiles, tps));
+    kernel<<<dim3(S, HG, B), G * 32, smem, stream>>>(kv_map, partial, H, tiles, tps);
+    KF_LAUNCH_CHECK();
   }
-  auto run = [&](auto kernel, int obytes) -> int {
-    const int smem = 2 * (G / 2) * kBoxBytes + 2 * (G * kD * obytes / 128) * kBoxBytes +
-                     G * kRows * kD * 4 + 1024;
+  auto run = [&](auto kernel, int smem) -> int {
     int occ = 1;
-    const int prep = kf_host::prepare_kernel(reinterpret_cast<const void*>(kernel), G * 32, smem, &occ);
+    const int prep = kf_host::prepare_kernel(reinterpret_cast<const void*>(kernel), kEpiThreads, smem, &occ,
+                                             static_cast<int>(kEpiTmemCols));
     if (prep != KF_OK) return prep;
-    const int total = B * HG * tiles;
+    const int tiles_out = (N + kOutTok - 1) / kOutTok;
+    const int total = B * HG * tiles_out;
     const int grid_cap = kf_host::current_device_sms() * occ;
     const int per = (total + grid_cap - 1) / grid_cap;
     const int grid = (total + per - 1) / per;
-    // Programmatic dependent launch: overlaps this grid's prologue with the producer's tail.
+    // Programmatic dependent launch: overlaps this grid's prologue (its Q loads) with the
+    // producer's tail; the partials are read after griddepcontrol.wait.
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(G * 32);
+    cfg.blockDim = dim3(kEpiThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -603,14 +792,14 @@ int launch_fast(const void* qkv, void* out, float* final_vk, int B, int H, int N
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    KF_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, qkv_map, out_map, static_cast<const float*>(final_vk), H, C,
-                                   HG, tiles, total, per, eps));
+    KF_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, q_map, out_map, static_cast<const float*>(partial), H, S, HG,
+                                   tiles_out, total, per, eps));
     return KF_OK;
   };
   switch (out_dtype) {
-    case KF_DTYPE_F32: return run(sana_out_epilogue<T, float, G>, 4);
-    case KF_DTYPE_F16: return run(sana_out_epilogue<T, __half, G>, 2);
-    default: return run(sana_out_epilogue<T, __nv_bfloat16, G>, 2);
+    case KF_DTYPE_F32: return run(sana_out_tc<T, float>, EpiCfg<float>::kSmemBytes);
+    case KF_DTYPE_F16: return run(sana_out_tc<T, __half>, EpiCfg<__half>::kSmemBytes);
+    default: return run(sana_out_tc<T, __nv_bfloat16>, EpiCfg<__nv_bfloat16>::kSmemBytes);
   }
 }
 
@@ -648,6 +837,12 @@ int launch_generic(const void* qkv, void* out, float* partial, float* final_vk,
 
 bool valid_head_dim(int64_t d) { return d > 0 && d <= 128 && 128 % d == 0; }
 
+// Workspace bytes: either path may run for head dim 32 (the input dtype decides).
+size_t workspace_bytes_for(int64_t B, int64_t H, int64_t d, int64_t N, int64_t requested) {
+  const size_t g = layout_for(B, H, d, generic_splits(B, H, N, requested)).total;
+  return d == kD ? std::max(g, fast_layout(B, H, fast_splits(B, H, N, requested)).total) : g;
+}
+
 }  // namespace
 
 int kf_internal_sana_error(unsigned int* code) {
@@ -664,7 +859,7 @@ int kf_internal_sana_error(unsigned int* code) {
 KF_API size_t kf_sana_linattn_workspace_size(int64_t batch, int64_t heads, int64_t dim,
                                              int64_t seq_len, int64_t splits) {
   if (batch <= 0 || heads <= 0 || seq_len <= 0 || !valid_head_dim(dim)) return 0;
-  return layout_for(batch, heads, dim, generic_splits(batch, heads, seq_len, splits)).total;
+  return workspace_bytes_for(batch, heads, dim, seq_len, splits);
 }
 
 KF_API int kf_sana_linattn_fwd(const void* qkv, void* out, void* workspace, size_t workspace_bytes,
@@ -682,7 +877,7 @@ KF_API int kf_sana_linattn_fwd(const void* qkv, void* out, void* workspace, size
     return KF_ERR_UNSUPPORTED;
   const int S_gen = generic_splits(batch, heads, seq_len, splits);
   const WorkspaceLayout lay = layout_for(batch, heads, dim, S_gen);
-  if (workspace_bytes < lay.total) return KF_ERR_WORKSPACE;
+  if (workspace_bytes < workspace_bytes_for(batch, heads, dim, seq_len, splits)) return KF_ERR_WORKSPACE;
   if (!kf::aligned(workspace, 256)) return KF_ERR_MISALIGNED;
   if (!kf::aligned(qkv, kf::dtype_size(in_dtype)) || !kf::aligned(out, kf::dtype_size(out_dtype)))
     return KF_ERR_MISALIGNED;
@@ -701,8 +896,8 @@ KF_API int kf_sana_linattn_fwd(const void* qkv, void* out, void* workspace, size
     // benchmark shape.
     const int S = fast_splits(B, H, N, splits);
     if (in_dtype == KF_DTYPE_BF16)
-      return launch_fast<__nv_bfloat16, kFastHeads>(qkv, out, final_vk, B, H, N, S, eps, out_dtype, s);
-    return launch_fast<__half, kFastHeads>(qkv, out, final_vk, B, H, N, S, eps, out_dtype, s);
+      return launch_fast<__nv_bfloat16, kFastHeads>(qkv, out, ws, B, H, N, S, eps, out_dtype, s);
+    return launch_fast<__half, kFastHeads>(qkv, out, ws, B, H, N, S, eps, out_dtype, s);
   }
   switch (in_dtype) {
     case KF_DTYPE_F32:
@@ -771,21 +966,20 @@ KF_API int kf_sana_linattn_fwd_noalloc(const void* qkv, void* out, int64_t batch
     return KF_ERR_MISALIGNED;
   const int B = static_cast<int>(batch), H = static_cast<int>(heads), d = static_cast<int>(dim);
   const int N = static_cast<int>(seq_len);
-  const size_t per_head = static_cast<size_t>(d + 1) * d * sizeof(float);
   const bool fast = d == kD && (in_dtype == KF_DTYPE_BF16 || in_dtype == KF_DTYPE_F16) &&
                     H * kD >= 64 && N >= kTok && kf::aligned(qkv, 16) && kf::aligned(out, 16);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (fast) {
-    // Only the reduced K^T V / ksum (B*H*33*32 floats) is needed.
-    if (static_cast<size_t>(batch) * heads * per_head > kNoAllocScratchBytes) return KF_ERR_WORKSPACE;
+    // As many splits as the default asks for and the scratch holds.
+    int S = fast_splits(B, H, N, splits);
+    while (S > 1 && fast_layout(B, H, S).total > kNoAllocScratchBytes) --S;
+    if (fast_layout(B, H, S).total > kNoAllocScratchBytes) return KF_ERR_WORKSPACE;
     uint8_t* scratch = nullptr;
     const int st = noalloc_scratch(&scratch);
     if (st != KF_OK) return st;
-    float* final_vk = reinterpret_cast<float*>(scratch);
-    const int S = fast_splits(B, H, N, splits);
     if (in_dtype == KF_DTYPE_BF16)
-      return launch_fast<__nv_bfloat16, kFastHeads>(qkv, out, final_vk, B, H, N, S, eps, out_dtype, s);
-    return launch_fast<__half, kFastHeads>(qkv, out, final_vk, B, H, N, S, eps, out_dtype, s);
+      return launch_fast<__nv_bfloat16, kFastHeads>(qkv, out, scratch, B, H, N, S, eps, out_dtype, s);
+    return launch_fast<__half, kFastHeads>(qkv, out, scratch, B, H, N, S, eps, out_dtype, s);
   }
   // Generic path: as many splits as the default asks for and the scratch holds.
   int S = generic_splits(batch, heads, seq_len, splits);
