@@ -87,13 +87,30 @@ __device__ __forceinline__ bool mbar_try_wait_relaxed(uint64_t* bar, uint32_t pa
   return ok != 0;
 }
 
+// Non-blocking probe of a phase (never suspends the thread).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait that also gives up as soon as another thread of the CTA has set *abort (a
 // shared-memory flag), so a CTA whose roles synchronise with each other never waits out one
 // timeout per remaining step after the first failure. A timeout sets *abort itself.
-template <bool kRelaxed = false>
+// kPoll: probe with test_wait (no suspension) instead of try_wait.
+template <bool kRelaxed = false, bool kPoll = false>
 __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, unsigned int* err,
                                                    volatile int* abort) {
-  auto probe = [&]() { return kRelaxed ? mbar_try_wait_relaxed(bar, parity) : mbar_try_wait(bar, parity); };
+  auto probe = [&]() {
+    return kPoll ? mbar_test_wait(bar, parity)
+                 : (kRelaxed ? mbar_try_wait_relaxed(bar, parity) : mbar_try_wait(bar, parity));
+  };
   if (probe()) return true;
   const uint64_t start = globaltimer_ns();
   uint32_t spins = 0;

@@ -397,7 +397,7 @@ sana_out_tc(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ C
     const int g = warp - kMmaWarp0;
     if (lane == 0) {
       uint32_t commits[2][2] = {};  // [head][buffer]
-      int loaded = -1;
+      int loaded = -1, next_load = g;
       auto load = [&](int k) {
         const int it = first + k;
         const int unit = it / tiles_out, tt = it % tiles_out;
@@ -407,7 +407,12 @@ sana_out_tc(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ C
         kf::tma_load_4d(smem + Cfg::kQOff + st * kQTileBytes, &q_map, &q_full[st], hp * 2 * kD, 0, tt * kOutTok, b);
         loaded = k;
       };
-      for (int k = g; k < kStages && k < n_items; k += 2) load(k);
+      // Q loads: at most kStages items ahead, and only two per group before the first B is ready,
+      // so that B's reads of the split partials do not queue behind the whole ring's loads.
+      auto top_up = [&](int limit) {
+        for (; next_load < n_items && next_load < limit; next_load += 2) load(next_load);
+      };
+      top_up(g + 4);
       constexpr uint32_t idesc = kf::tc::idesc_f16(kBf16 ? 1 : 0, kOutTok, kBHalfRows, false, false);
       int b_unit = -1;
       for (int k = g, i = 0; k < n_items; k += 2, ++i) {
@@ -434,8 +439,10 @@ sana_out_tc(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ C
           ++commits[h][j];
         }
         if (!ok) break;
-        // Both heads' workers have read Q(k): its stage takes item k + kStages (same group).
-        if (k + kStages < n_items) load(k + kStages);
+        // Both heads' workers have read Q(k): the stages of this group's items up to k can take
+        // items up to k + kStages (a TMA issue may block: after the MMAs). The ring fills at
+        // two loads per item, not in one burst.
+        top_up(min(k + kStages + 1, next_load + 4));
       }
       // Leave nothing in flight on exit (after a timeout): MMA groups and Q loads.
       for (int h = 0; h < 2; ++h)
@@ -567,8 +574,8 @@ sana_out_tc(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ C
           eps_unit = u;
           eps_h = u < 2 ? eps * scale_of(u, hd) : eps_s[u & 1][hd];
         }
-        if (!__all_sync(0xffffffffu,
-                        kf::mbar_wait_or_abort(&d_full[g][hd][i & 1], (i >> 1) & 1, &g_sana_error, &abort_flag)))
+        if (!__all_sync(0xffffffffu, kf::mbar_wait_or_abort<false, true>(&d_full[g][hd][i & 1], (i >> 1) & 1,
+                                                                          &g_sana_error, &abort_flag)))
           break;
         kf::tc::fence_after_sync();
         uint32_t num[32], den[2];
