@@ -182,6 +182,31 @@ __device__ __forceinline__ void issue_ds(uint32_t q_addr, uint32_t tq_addr, uint
   }
 }
 
+// S into s_col and dS into s_col + 64 for one key tile. For D = 64 the N = 64 MMAs use the
+// tensor core at 2/3 of its N = 128 rate, so [S | Q tK^T] = Q [K ; tK]^T is one N = 128 MMA
+// (K and tK are adjacent in the stage) and tQ K^T is added to its second half.
+template <int D>
+__device__ __forceinline__ void issue_scores(uint32_t q_addr, uint32_t tq_addr, uint32_t k_base, int tile_bytes,
+                                             uint32_t s_col, bool has_tq, bool has_tk, bool bf16) {
+  const uint32_t idS = kf::tc::idesc_f16(bf16 ? 1 : 0, kBM, kBN, false, false);
+  if (D == 64 && has_tk) {
+    const uint32_t idS2 = kf::tc::idesc_f16(bf16 ? 1 : 0, kBM, 2 * kBN, false, false);
+#pragma unroll
+    for (int k = 0; k < D / 16; ++k)
+      kf::tc::mma_ss(s_col, kf::tc::desc_sw128(q_addr + k * 32, 16, 1024), kf::tc::desc_sw128(k_base + k * 32, 16, 1024),
+                     idS2, k > 0);
+    if (has_tq) {
+#pragma unroll
+      for (int k = 0; k < D / 16; ++k)
+        kf::tc::mma_ss(s_col + 64, kf::tc::desc_sw128(tq_addr + k * 32, 16, 1024),
+                       kf::tc::desc_sw128(k_base + k * 32, 16, 1024), idS, 1);
+    }
+    return;
+  }
+  issue_s<D>(q_addr, k_base, s_col, idS);
+  issue_ds<D>(q_addr, tq_addr, k_base, tile_bytes, s_col + 64, idS, has_tq, has_tk);
+}
+
 __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
   return bf16 ? kf::Mma<__nv_bfloat16>::from_f2(a, b) : kf::Mma<__half>::from_f2(a, b);
 }
@@ -248,7 +273,6 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
       // Scores of tile j into buffer j & 1 once tile j-2's softmax has read that buffer.
-      constexpr uint32_t idS = kf::tc::idesc_f16(kBf16 ? 1 : 0, kBM, kBN, false, false);
       const uint32_t q_addr = kf::smem_u32(smem), tq_addr = q_addr + C::kQBytes;
       bool ok = kf::mbar_wait_or_abort<true>(bars.q_full, 0, &g_fa_error, abort_flag);
       for (int j = 0; ok && j < ntiles; ++j) {
@@ -258,8 +282,7 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         kf::tc::fence_after_sync();
         const uint32_t k_base = kf::smem_u32(smem + C::kKOffset + buf * 2 * C::kTileBytes);
         const uint32_t s_col = tmem + kBufCol + 128 * buf;
-        issue_s<D>(q_addr, k_base, s_col, idS);
-        issue_ds<D>(q_addr, tq_addr, k_base, C::kTileBytes, s_col + 64, idS, has_tq, has_tk);
+        issue_scores<D>(q_addr, tq_addr, k_base, C::kTileBytes, s_col, has_tq, has_tk, kBf16);
         kf::tc::commit(&bars.s_full[buf]);
       }
     }
@@ -410,11 +433,21 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 // tile row maxima through shared memory. The reference max m only moves when a tile's max
 // exceeds it by more than 8 (a factor 256 in E); then the accumulators U, G of that row are
 // rescaled in TMEM after the previous tile's output MMAs have completed. Tensor memory:
-//   [0, D) G (tO accumulator) | [128, 384) S / dS double buffer | [384, 384 + D) U
+//   D = 128: [0, 128) G (tO accumulator) | [128, 384) S / dS double buffer | [384, 512) U
+//   D = 64:  [0, 64) U | [64, 128) G | [128, 384) S / dS double buffer
 // P and H (16-bit) overwrite the first 16 columns of each warpgroup's 32-column S / dS half, so
 // tile j's score MMAs wait for tile j-2's output MMAs (same buffer).
+// For D = 64 the N = 64 MMAs use the tensor core at 2/3 of its N = 128 rate, so pairs are
+// merged into N = 128 MMAs: [S | Q tK^T] = Q [K ; tK]^T (K and tK are adjacent in the stage)
+// then dS += tQ K^T; and [U | G] += E [V | tV] (V, tV adjacent: two 64-wide MN blocks) then
+// G += H V. That takes U at [0, 64) and G at [64, 128), next to each other.
 // ============================================================================================
-constexpr uint32_t kUCol = 384;
+template <int D>
+struct FusedCols {
+  static constexpr bool kMerge = D == 64;
+  static constexpr uint32_t kU = kMerge ? 0 : 384;  // U: E V
+  static constexpr uint32_t kG = kMerge ? 64 : 0;   // G: H V + E tV (the tO accumulator)
+};
 constexpr float kRescaleThreshold = 8.f;  // log2 units
 
 template <typename T, int D, bool kJvp>
@@ -462,7 +495,6 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
     if (lane == 0) {
       // Scores of tile j into buffer j & 1 once tile j-2's output MMAs have consumed the P / H
       // that overwrote that buffer.
-      constexpr uint32_t idS = kf::tc::idesc_f16(kBf16 ? 1 : 0, kBM, kBN, false, false);
       const uint32_t q_addr = kf::smem_u32(smem), tq_addr = q_addr + C::kQBytes;
       bool ok = kf::mbar_wait_or_abort<true>(bars.q_full, 0, &g_fa_error, abort_flag);
       for (int j = 0; ok && j < ntiles; ++j) {
@@ -472,14 +504,15 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         kf::tc::fence_after_sync();
         const uint32_t k_base = kf::smem_u32(smem + C::kKOffset + buf * 2 * C::kTileBytes);
         const uint32_t s_col = tmem + kBufCol + 128 * buf;
-        issue_s<D>(q_addr, k_base, s_col, idS);
-        issue_ds<D>(q_addr, tq_addr, k_base, C::kTileBytes, s_col + 64, idS, has_tq, has_tk);
+        issue_scores<D>(q_addr, tq_addr, k_base, C::kTileBytes, s_col, has_tq, has_tk, kBf16);
         kf::tc::commit(&bars.s_full[buf]);
       }
     }
   } else if (warp == kPvWarp) {
     if (lane == 0) {
       constexpr uint32_t idPV = kf::tc::idesc_f16(kBf16 ? 1 : 0, kBM, D, false, true);
+      constexpr uint32_t idPV2 = kf::tc::idesc_f16(kBf16 ? 1 : 0, kBM, 2 * D, false, true);
+      constexpr uint32_t kU = FusedCols<D>::kU, kG = FusedCols<D>::kG;
       uint32_t u_started = 0, g_started = 0;
       bool ok = true;
       for (int j = 0; ok && j < ntiles; ++j) {
@@ -495,14 +528,22 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
           // keys [16 kk, 16 kk + 16): warpgroup kk / 2 wrote them at columns 32 (kk / 2) + 8 (kk % 2)
           const uint32_t acol = (kk >> 1) * 32 + (kk & 1) * 8;
           const uint64_t vdesc = kf::tc::desc_sw128(v_base + kk * 2048, kBN * 128, 1024);
-          kf::tc::mma_ts(tmem + kUCol, p_col + acol, vdesc, idPV, u_started);
+          if (FusedCols<D>::kMerge && has_tv) {
+            // [U | G] += E [V | tV]: V and tV are the two 64-wide MN blocks of one operand
+            kf::tc::mma_ts(tmem + kU, p_col + acol, kf::tc::desc_sw128(v_base + kk * 2048, C::kTileBytes, 1024),
+                           idPV2, u_started);
+            u_started = g_started = 1;
+            if (has_h) kf::tc::mma_ts(tmem + kG, h_col + acol, vdesc, idPV, 1);
+            continue;
+          }
+          kf::tc::mma_ts(tmem + kU, p_col + acol, vdesc, idPV, u_started);
           u_started = 1;
           if (has_h) {
-            kf::tc::mma_ts(tmem + kAccCol, h_col + acol, vdesc, idPV, g_started);
+            kf::tc::mma_ts(tmem + kG, h_col + acol, vdesc, idPV, g_started);
             g_started = 1;
           }
           if (has_tv) {
-            kf::tc::mma_ts(tmem + kAccCol, p_col + acol,
+            kf::tc::mma_ts(tmem + kG, p_col + acol,
                            kf::tc::desc_sw128(v_base + C::kTileBytes + kk * 2048, kBN * 128, 1024), idPV, g_started);
             g_started = 1;
           }
@@ -563,17 +604,17 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
               for (int c = 0; c < D / 64; ++c) {
                 const uint32_t col = (group * (D / 2)) + c * 32;
                 uint32_t ar[32];
-                kf::tc::ld_32x32b_x32(lane_base + kUCol + col, ar);
+                kf::tc::ld_32x32b_x32(lane_base + FusedCols<D>::kU + col, ar);
                 kf::tc::wait_ld();
 #pragma unroll
                 for (int i = 0; i < 32; ++i) ar[i] = __float_as_uint(__uint_as_float(ar[i]) * alpha);
-                kf::tc::st_32x32b_x32(lane_base + kUCol + col, ar);
+                kf::tc::st_32x32b_x32(lane_base + FusedCols<D>::kU + col, ar);
                 if (kJvp) {
-                  kf::tc::ld_32x32b_x32(lane_base + kAccCol + col, ar);
+                  kf::tc::ld_32x32b_x32(lane_base + FusedCols<D>::kG + col, ar);
                   kf::tc::wait_ld();
 #pragma unroll
                   for (int i = 0; i < 32; ++i) ar[i] = __float_as_uint(__uint_as_float(ar[i]) * alpha);
-                  kf::tc::st_32x32b_x32(lane_base + kAccCol + col, ar);
+                  kf::tc::st_32x32b_x32(lane_base + FusedCols<D>::kG + col, ar);
                 }
               }
             }
@@ -630,8 +671,8 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       for (int c = 0; c < D / 64; ++c) {
         const int col = group * (D / 2) + c * 32;
         uint32_t ur[32], gr[32];
-        kf::tc::ld_32x32b_x32(lane_base + kUCol + col, ur);
-        if (kJvp) kf::tc::ld_32x32b_x32(lane_base + kAccCol + col, gr);
+        kf::tc::ld_32x32b_x32(lane_base + FusedCols<D>::kU + col, ur);
+        if (kJvp) kf::tc::ld_32x32b_x32(lane_base + FusedCols<D>::kG + col, gr);
         kf::tc::wait_ld();
         if (qrow < p.Nq) {
 #pragma unroll
