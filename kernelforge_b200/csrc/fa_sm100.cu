@@ -329,7 +329,10 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     const uint32_t ts_col = s_col + 64;
     const uint32_t p_col = lane_base + kPCol + 64 * group;
     const uint32_t h_col = p_col + 32;
-    float csum = 0.f;
+    // Pairs of keys go through the f32x2 units: exponent argument, H and its row sum.
+    const uint64_t c2 = kf::f2_pack(p.scale_log2, p.scale_log2), nl2 = kf::f2_pack(-lse_l2, -lse_l2);
+    const uint64_t g2 = kf::f2_pack(p.scale, p.scale);
+    uint64_t csum2 = kf::f2_pack(0.f, 0.f);
     bool ok = true;
     for (int j = group; j < ntiles; j += 2) {
       ok = kf::mbar_wait_or_abort(&bars.s_full[group], (j >> 1) & 1, &g_fa_error, abort_flag);
@@ -357,18 +360,20 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         const int kc = k0 + c * 32;
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          float p0 = ex2(fmaf(__uint_as_float(sr[2 * i]), p.scale_log2, -lse_l2));
-          float p1 = ex2(fmaf(__uint_as_float(sr[2 * i + 1]), p.scale_log2, -lse_l2));
+          const float2 a = kf::f2_unpack(kf::f2_fma(kf::f2_pack(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])),
+                                                    c2, nl2));
+          float p0 = ex2(a.x), p1 = ex2(a.y);
           if (!full) {
             p0 = kc + 2 * i < limit ? p0 : 0.f;
             p1 = kc + 2 * i + 1 < limit ? p1 : 0.f;
           }
           pp[i] = pack2(p0, p1, kBf16);
           if (has_h) {
-            const float h0 = p0 * __uint_as_float(tr[2 * i]) * p.scale;
-            const float h1 = p1 * __uint_as_float(tr[2 * i + 1]) * p.scale;
-            csum += h0 + h1;
-            hh[i] = pack2(h0, h1, kBf16);
+            const uint64_t hv = kf::f2_mul(
+                kf::f2_mul(kf::f2_pack(p0, p1), kf::f2_pack(__uint_as_float(tr[2 * i]), __uint_as_float(tr[2 * i + 1]))), g2);
+            csum2 = kf::f2_add(csum2, hv);
+            const float2 hf = kf::f2_unpack(hv);
+            hh[i] = pack2(hf.x, hf.y, kBf16);
           }
         }
         kf::tc::st_32x32b_x16(p_col + c * 16, pp);
@@ -378,9 +383,10 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       kf::tc::fence_before_sync();
       kf::mbar_arrive(&bars.p_full[group]);
     }
-    row_sums[group * kBM + row] = csum;
+    const float2 cs = kf::f2_unpack(csum2);
+    row_sums[group * kBM + row] = cs.x + cs.y;
     softmax_groups_sync();
-    csum = row_sums[row] + row_sums[kBM + row];
+    const float csum = row_sums[row] + row_sums[kBM + row];
     // Epilogue: tO = acc - rowsum(H) * O; warpgroup g writes columns [g D/2, (g + 1) D/2).
     if (ok) ok = kf::mbar_wait_or_abort(bars.acc_full, 0, &g_fa_error, abort_flag);
     ok = __all_sync(0xffffffffu, ok);
@@ -559,7 +565,10 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
     const int qrow = q0 + row;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const int limit = qrow >= p.Nq ? 0 : (p.causal ? min(p.Nk, qrow + p.Nk - p.Nq + 1) : p.Nk);
-    float m_ref = -INFINITY, l_part = 0.f, r_part = 0.f;
+    float m_ref = -INFINITY;
+    // Row sums of E and H as f32x2 pairs; pairs of keys share the f32x2 instructions.
+    uint64_t l2 = kf::f2_pack(0.f, 0.f), r2 = l2;
+    const uint64_t c2 = kf::f2_pack(p.scale_log2, p.scale_log2), g2 = kf::f2_pack(p.scale, p.scale);
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
       const int buf = j & 1;
@@ -575,12 +584,19 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         kf::tc::ld_32x32b_x32(s_col, sr);
         if (has_h) kf::tc::ld_32x32b_x32(ts_col, tr);
         kf::tc::wait_ld();
+        // Row max of the raw scores (masked keys -inf), then scaled: the scale is positive.
+        if (kc + 32 <= limit) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float x = kc + i < limit ? __uint_as_float(sr[i]) * p.scale_log2 : -INFINITY;
-          sr[i] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
+          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(sr[i]));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float x = kc + i < limit ? __uint_as_float(sr[i]) : -INFINITY;
+            sr[i] = __float_as_uint(x);
+            mx = fmaxf(mx, x);
+          }
         }
+        mx *= p.scale_log2;
       }
       // Exchange the two halves' maxima (every softmax thread reaches this barrier).
       tile_max[(buf * 2 + group) * kBM + row] = mx;
@@ -618,24 +634,30 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
                 }
               }
             }
-            l_part *= alpha;
-            r_part *= alpha;
+            const uint64_t alpha2 = kf::f2_pack(alpha, alpha);
+            l2 = kf::f2_mul(l2, alpha2);
+            r2 = kf::f2_mul(r2, alpha2);
           }
           m_ref = m_new;
         }
         const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
+        const uint64_t nm2 = kf::f2_pack(-m_use, -m_use);
         uint32_t pp[16], hh[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float e0 = ex2(__uint_as_float(sr[2 * i]) - m_use);
-          const float e1 = ex2(__uint_as_float(sr[2 * i + 1]) - m_use);
-          l_part += e0 + e1;
+          // E = 2^(S gamma log2(e) - m): one f32x2 FMA per key pair, masked keys give 2^-inf = 0
+          const float2 a = kf::f2_unpack(
+              kf::f2_fma(kf::f2_pack(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])), c2, nm2));
+          const float e0 = ex2(a.x), e1 = ex2(a.y);
+          const uint64_t e2 = kf::f2_pack(e0, e1);
+          l2 = kf::f2_add(l2, e2);
           pp[i] = pack2(e0, e1, kBf16);
           if (has_h) {
-            const float h0 = e0 * __uint_as_float(tr[2 * i]) * p.scale;
-            const float h1 = e1 * __uint_as_float(tr[2 * i + 1]) * p.scale;
-            r_part += h0 + h1;
-            hh[i] = pack2(h0, h1, kBf16);
+            const uint64_t hv =
+                kf::f2_mul(kf::f2_mul(e2, kf::f2_pack(__uint_as_float(tr[2 * i]), __uint_as_float(tr[2 * i + 1]))), g2);
+            r2 = kf::f2_add(r2, hv);
+            const float2 hf = kf::f2_unpack(hv);
+            hh[i] = pack2(hf.x, hf.y, kBf16);
           }
         }
         kf::tc::st_32x32b_x16(s_col, pp);
@@ -646,6 +668,8 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       kf::mbar_arrive(&bars.p_full[buf]);
     }
     // Combine the two warpgroups' row sums.
+    const float2 lf = kf::f2_unpack(l2), rf = kf::f2_unpack(r2);
+    const float l_part = lf.x + lf.y, r_part = rf.x + rf.y;
     part_sums[group * kBM + row] = l_part;
     softmax_groups_sync();
     const float l_tot = part_sums[row] + part_sums[kBM + row];
