@@ -149,6 +149,19 @@ int kf_fa_fwd_jvp(const void* q, const void* k, const void* v, const void* tq, c
                   int64_t batch, int64_t q_len, int64_t k_len, int64_t q_heads, int64_t kv_heads,
                   int64_t head_dim, float softmax_scale, int causal, int dtype, void* stream);
 
+/* Backward (reverse-mode VJP) from the saved O and LSE:
+ *   P = exp(scale * Q K^T - LSE), dP = dO V^T, dS = P * (dP - rowsum(dO * O)),
+ *   dQ = scale * dS K, dK = scale * dS^T Q, dV = P^T dO   (GQA: summed over the group).
+ * Replaces flash_attn's _flash_attn_backward called by FlashAttentionFunction.backward
+ * (flash_attention_jvp/custom.py:255-266). dq / dk / dv are written in full. The workspace
+ * (kf_fa_bwd_workspace_size bytes, 4-byte aligned, contents ignored) holds rowsum(dO * O).
+ * Deterministic: no atomics. */
+size_t kf_fa_bwd_workspace_size(int64_t batch, int64_t q_heads, int64_t q_len);
+int kf_fa_bwd(const void* q, const void* k, const void* v, const void* out, const void* dout,
+              const float* lse, void* dq, void* dk, void* dv, void* workspace, size_t workspace_bytes,
+              int64_t batch, int64_t q_len, int64_t k_len, int64_t q_heads, int64_t kv_heads,
+              int64_t head_dim, float softmax_scale, int causal, int dtype, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

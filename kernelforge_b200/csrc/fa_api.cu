@@ -95,3 +95,33 @@ KF_API int kf_fa_fwd_jvp(const void* q, const void* k, const void* v, const void
     return kf::fa::launch_sm100_fused(a, kf::fa::kModeFwdJvp, dtype, static_cast<cudaStream_t>(stream));
   return kf::fa::launch_general(a, kf::fa::kModeFwdJvp, dtype, static_cast<cudaStream_t>(stream));
 }
+
+KF_API size_t kf_fa_bwd_workspace_size(int64_t batch, int64_t q_heads, int64_t q_len) {
+  if (batch <= 0 || q_heads <= 0 || q_len <= 0) return 0;
+  return static_cast<size_t>(batch) * q_heads * q_len * sizeof(float);
+}
+
+KF_API int kf_fa_bwd(const void* q, const void* k, const void* v, const void* out, const void* dout,
+                     const float* lse, void* dq, void* dk, void* dv, void* workspace, size_t workspace_bytes,
+                     int64_t batch, int64_t q_len, int64_t k_len, int64_t q_heads, int64_t kv_heads,
+                     int64_t head_dim, float softmax_scale, int causal, int dtype, void* stream) {
+  int st = validate(q, k, v, batch, q_len, k_len, q_heads, kv_heads, head_dim, softmax_scale, dtype);
+  if (st != KF_OK) return st;
+  if (out == nullptr || dout == nullptr || lse == nullptr || dq == nullptr || dk == nullptr || dv == nullptr ||
+      workspace == nullptr)
+    return KF_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < kf_fa_bwd_workspace_size(batch, q_heads, q_len)) return KF_ERR_WORKSPACE;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || !aligned16(dout) ||
+      !aligned16(dq) || !aligned16(dk) || !aligned16(dv) || !kf::aligned(lse, 4) || !kf::aligned(workspace, 4))
+    return KF_ERR_MISALIGNED;
+  kf::fa::BwdArgs a = {};
+  a.q = q; a.k = k; a.v = v; a.o = out; a.dout = dout; a.lse = lse;
+  a.delta = static_cast<float*>(workspace);
+  a.dq = dq; a.dk = dk; a.dv = dv;
+  a.B = static_cast<int>(batch); a.Nq = static_cast<int>(q_len); a.Nk = static_cast<int>(k_len);
+  a.Hq = static_cast<int>(q_heads); a.Hkv = static_cast<int>(kv_heads); a.D = static_cast<int>(head_dim);
+  a.scale = softmax_scale;
+  a.scale_log2 = softmax_scale * 1.4426950408889634f;
+  a.causal = causal ? 1 : 0;
+  return kf::fa::launch_bwd(a, dtype, static_cast<cudaStream_t>(stream));
+}

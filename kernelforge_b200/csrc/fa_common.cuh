@@ -27,6 +27,69 @@ struct FaArgs {
   int causal;
 };
 
+// Inputs and outputs of the backward (reverse-mode VJP) from the saved O and LSE. Tensors are
+// contiguous [B, N, H, D]; LSE is fp32 [B, Hq, Nq] (natural log); `delta` is an fp32 workspace
+// [B, Hq, Nq] that the first kernel fills with rowsum(dO * O).
+struct BwdArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* o;
+  const void* dout;
+  const float* lse;
+  float* delta;
+  void* dq;
+  void* dk;
+  void* dv;
+  int B, Nq, Nk, Hq, Hkv, D;
+  float scale;
+  float scale_log2;
+  int causal;
+};
+
+// dQ, dK, dV (mma.sync; any D in 8..256, multiple of 8; deterministic).
+int launch_bwd(const BwdArgs& a, int dtype, cudaStream_t stream);
+
+// cp.async tiles in shared memory for the mma.sync kernels: rows of DP elements at a pitch of a
+// multiple of 64 elements, 16-byte chunk c of row r stored at chunk (c ^ (r & 7)) so that
+// ldmatrix reads are free of bank conflicts.
+namespace tile {
+
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Row pitch (elements) of a shared tile: >= 64 and a multiple of 64 so that 16-byte chunk c of
+// row r can be stored at chunk (c ^ (r & 7)) without bank conflicts for ldmatrix.
+template <int DP> struct Pitch { static constexpr int value = DP <= 64 ? 64 : (DP + 63) / 64 * 64; };
+
+template <int PITCH>
+__device__ __forceinline__ uint32_t tile_off(int row, int chunk) {  // bytes
+  return static_cast<uint32_t>(row * PITCH * 2 + ((chunk ^ (row & 7)) << 4));
+}
+
+// cp.async a [nrows x DP] tile (rows `row0..`, stride `stride` elements) into swizzled smem;
+// rows >= rows_valid and columns >= D are zero-filled.
+template <typename T, int DP, int NT>
+__device__ __forceinline__ void load_tile(uint32_t smem, const T* __restrict__ base, int64_t stride,
+                                          int nrows, int rows_valid, int D) {
+  constexpr int kChunks = DP / 8;
+  constexpr int kPitch = Pitch<DP>::value;
+  for (int i = threadIdx.x; i < nrows * kChunks; i += NT) {
+    const int r = i / kChunks, c = i % kChunks;
+    const bool valid = r < rows_valid && c * 8 < D;
+    const T* src = valid ? base + r * stride + c * 8 : base;
+    cp_async_16(smem + tile_off<kPitch>(r, c), src, valid);
+  }
+}
+
+}  // namespace tile
+
 // mma.sync path: any D in 8..256 (multiple of 8), fp16 / bf16.
 int launch_general(const FaArgs& a, int mode, int dtype, cudaStream_t stream);
 

@@ -31,38 +31,7 @@ constexpr int kBM = 64;  // query rows per CTA (16 per warp)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
-__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
-               "r"(valid ? 16 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
-// Row pitch (elements) of a shared tile: >= 64 and a multiple of 64 so that 16-byte chunk c of
-// row r can be stored at chunk (c ^ (r & 7)) without bank conflicts for ldmatrix.
-template <int DP> struct Pitch { static constexpr int value = DP <= 64 ? 64 : (DP + 63) / 64 * 64; };
-
-template <int PITCH>
-__device__ __forceinline__ uint32_t tile_off(int row, int chunk) {  // bytes
-  return static_cast<uint32_t>(row * PITCH * 2 + ((chunk ^ (row & 7)) << 4));
-}
-
-// cp.async a [nrows x DP] tile (rows `row0..`, stride `stride` elements) into swizzled smem;
-// rows >= rows_valid and columns >= D are zero-filled.
-template <typename T, int DP, int NT>
-__device__ __forceinline__ void load_tile(uint32_t smem, const T* __restrict__ base, int64_t stride,
-                                          int nrows, int rows_valid, int D) {
-  constexpr int kChunks = DP / 8;
-  constexpr int kPitch = Pitch<DP>::value;
-  for (int i = threadIdx.x; i < nrows * kChunks; i += NT) {
-    const int r = i / kChunks, c = i % kChunks;
-    const bool valid = r < rows_valid && c * 8 < D;
-    const T* src = valid ? base + r * stride + c * 8 : base;
-    cp_async_16(smem + tile_off<kPitch>(r, c), src, valid);
-  }
-}
+using namespace kf::fa::tile;
 
 template <typename T, int DP, int BN, int DSPLIT, int MODE>
 __global__ void __launch_bounds__(128 * DSPLIT)

@@ -176,36 +176,35 @@ def _flash_attn_forward(q, k, v, dropout_p, softmax_scale, causal, window_size_l
 def _flash_attn_backward(dout, q, k, v, out, lse, dq, dk, dv, dropout_p, softmax_scale, causal,
                          window_size_left=-1, window_size_right=-1, softcap=0.0, alibi_slopes=None,
                          deterministic=False):
-    """VJP of attention from the saved O and LSE (fp32 dense recomputation per batch on the GPU).
+    """VJP of attention from the saved O and LSE (this library's kernels; always deterministic).
 
-    Outside the forward-mode hot path; writes dq, dk, dv in place like flash_attn's function.
+    Writes dq, dk, dv in place like flash_attn's function (custom.py:261-266 call site).
     """
     if dropout_p != 0.0 or window_size_left != -1 or window_size_right != -1 or softcap != 0.0 \
             or alibi_slopes is not None:
         raise NotImplementedError("only dropout_p=0, full windows, no softcap/ALiBi are supported")
     b_, nq, hq, d = q.shape
     nk, hkv = k.shape[1], k.shape[2]
-    groups = hq // hkv
-    if causal:
-        rows = torch.arange(nq, device=q.device)[:, None]
-        cols = torch.arange(nk, device=q.device)[None, :]
-        visible = cols <= rows + nk - nq
-    for b in range(b_):
-        qh = q[b].float().transpose(0, 1)
-        kh = k[b].float().transpose(0, 1).repeat_interleave(groups, 0)
-        vh = v[b].float().transpose(0, 1).repeat_interleave(groups, 0)
-        doh = dout[b].float().transpose(0, 1)
-        oh = out[b].float().transpose(0, 1)
-        probs = torch.exp(torch.matmul(qh, kh.transpose(-1, -2)) * softmax_scale - lse[b].float()[..., None])
-        if causal:
-            probs = probs.masked_fill(~visible, 0.0)
-        dprobs = torch.matmul(doh, vh.transpose(-1, -2))
-        dscores = probs * (dprobs - (doh * oh).sum(-1, keepdim=True))
-        dq[b].copy_((torch.matmul(dscores, kh) * softmax_scale).transpose(0, 1))
-        dk_full = torch.matmul(dscores.transpose(-1, -2), qh) * softmax_scale
-        dv_full = torch.matmul(probs.transpose(-1, -2), doh)
-        dk[b].copy_(dk_full.view(hkv, groups, nk, d).sum(1).transpose(0, 1))
-        dv[b].copy_(dv_full.view(hkv, groups, nk, d).sum(1).transpose(0, 1))
+    dout, q, k, v, out = (t.contiguous() for t in (dout, q, k, v, out))
+    lse = lse.float().contiguous()
+    # The kernels write dense [B, N, H, D] gradients; strided destinations receive a copy.
+    grads = tuple(g if g.is_contiguous() else torch.empty_like(g, memory_format=torch.contiguous_format)
+                  for g in (dq, dk, dv))
+    workspace = torch.empty(b_ * hq * nq, device=q.device, dtype=torch.float32)
+    with torch.cuda.device(q.device):
+        _lib.check(
+            _lib.lib.kf_fa_bwd(
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), dout.data_ptr(),
+                lse.data_ptr(), grads[0].data_ptr(), grads[1].data_ptr(), grads[2].data_ptr(),
+                workspace.data_ptr(), workspace.numel() * 4, b_, nq, nk, hq, hkv, d,
+                float(softmax_scale), int(bool(causal)), _lib.dtype_code(q.dtype),
+                _lib.stream_handle(q.device),
+            ),
+            "kf_fa_bwd",
+        )
+    for dst, src in zip((dq, dk, dv), grads):
+        if dst is not src:
+            dst.copy_(src)
     return dq, dk, dv
 
 

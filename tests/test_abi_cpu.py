@@ -61,6 +61,24 @@ def test_sana_workspace_and_validation():
     assert f(256, 256, 256, need, 1, 2, 32, 128, 0, 1e-15, 5, 2, None) == 2      # dtype
 
 
+def test_fa_bwd_workspace_and_validation():
+    ws = _lib.lib.kf_fa_bwd_workspace_size
+    assert ws(2, 4, 100) == 2 * 4 * 100 * 4  # fp32 delta per (batch, head, query)
+    assert ws(0, 4, 100) == 0
+    f = _lib.lib.kf_fa_bwd
+    need = ws(1, 2, 16)
+    ptrs = [256] * 9  # q, k, v, out, dout, lse, dq, dk, dv
+    args = (1, 16, 16, 2, 2, 64, 0.125, 0, 2, None)
+    assert f(*ptrs, 256, need - 1, *args) == 4                                       # workspace too small
+    assert f(*ptrs, None, need, *args) == 1                                          # no workspace
+    assert f(*ptrs[:6], None, *ptrs[7:], 256, need, *args) == 1                      # no dq
+    assert f(*ptrs[:4], 264, *ptrs[5:], 256, need, *args) == 3                       # misaligned dout
+    assert f(*ptrs, 256, need, 1, 16, 16, 2, 2, 72 * 4, 0.125, 0, 2, None) == 2      # head dim > 256
+    assert f(*ptrs, 256, need, 1, 16, 16, 3, 2, 64, 0.125, 0, 2, None) == 2         # Hq % Hkv
+    assert f(*ptrs, 256, need, 1, 16, 16, 2, 2, 64, -1.0, 0, 2, None) == 1          # scale
+    assert f(*ptrs, 256, need, 1, 16, 16, 2, 2, 64, 0.125, 0, 7, None) == 2         # dtype
+
+
 def test_python_signature_validation():
     from kernelforge_b200.SANA_LinearAttention import qkv_attn_matmul
     from kernelforge_b200.rmsnorm import rms_norm
