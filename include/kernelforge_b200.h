@@ -154,7 +154,9 @@ int kf_fa_fwd_jvp(const void* q, const void* k, const void* v, const void* tq, c
  *   dQ = scale * dS K, dK = scale * dS^T Q, dV = P^T dO   (GQA: summed over the group).
  * Replaces flash_attn's _flash_attn_backward called by FlashAttentionFunction.backward
  * (flash_attention_jvp/custom.py:255-266). dq / dk / dv are written in full. The workspace
- * (kf_fa_bwd_workspace_size bytes, 4-byte aligned, contents ignored) holds rowsum(dO * O).
+ * (kf_fa_bwd_workspace_size bytes, 16-byte aligned, contents ignored) holds two fp32 row
+ * statistics per (batch, head, query), padded to a multiple of 128 queries: -LSE log2(e) and
+ * -rowsum(dO * O).
  * Deterministic: no atomics. */
 size_t kf_fa_bwd_workspace_size(int64_t batch, int64_t q_heads, int64_t q_len);
 int kf_fa_bwd(const void* q, const void* k, const void* v, const void* out, const void* dout,

@@ -98,7 +98,8 @@ KF_API int kf_fa_fwd_jvp(const void* q, const void* k, const void* v, const void
 
 KF_API size_t kf_fa_bwd_workspace_size(int64_t batch, int64_t q_heads, int64_t q_len) {
   if (batch <= 0 || q_heads <= 0 || q_len <= 0) return 0;
-  return static_cast<size_t>(batch) * q_heads * q_len * sizeof(float);
+  const int64_t padded = (q_len + kf::fa::kBwdRowPad - 1) / kf::fa::kBwdRowPad * kf::fa::kBwdRowPad;
+  return 2 * static_cast<size_t>(batch) * q_heads * padded * sizeof(float);
 }
 
 KF_API int kf_fa_bwd(const void* q, const void* k, const void* v, const void* out, const void* dout,
@@ -112,14 +113,16 @@ KF_API int kf_fa_bwd(const void* q, const void* k, const void* v, const void* ou
     return KF_ERR_INVALID_ARGUMENT;
   if (workspace_bytes < kf_fa_bwd_workspace_size(batch, q_heads, q_len)) return KF_ERR_WORKSPACE;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || !aligned16(dout) ||
-      !aligned16(dq) || !aligned16(dk) || !aligned16(dv) || !kf::aligned(lse, 4) || !kf::aligned(workspace, 4))
+      !aligned16(dq) || !aligned16(dk) || !aligned16(dv) || !kf::aligned(lse, 4) || !aligned16(workspace))
     return KF_ERR_MISALIGNED;
   kf::fa::BwdArgs a = {};
   a.q = q; a.k = k; a.v = v; a.o = out; a.dout = dout; a.lse = lse;
-  a.delta = static_cast<float*>(workspace);
   a.dq = dq; a.dk = dk; a.dv = dv;
   a.B = static_cast<int>(batch); a.Nq = static_cast<int>(q_len); a.Nk = static_cast<int>(k_len);
   a.Hq = static_cast<int>(q_heads); a.Hkv = static_cast<int>(kv_heads); a.D = static_cast<int>(head_dim);
+  a.NqP = (a.Nq + kf::fa::kBwdRowPad - 1) / kf::fa::kBwdRowPad * kf::fa::kBwdRowPad;
+  a.row_nlse = static_cast<float*>(workspace);
+  a.row_ndelta = a.row_nlse + static_cast<int64_t>(a.B) * a.Hq * a.NqP;
   a.scale = softmax_scale;
   a.scale_log2 = softmax_scale * 1.4426950408889634f;
   a.causal = causal ? 1 : 0;

@@ -9,8 +9,10 @@
 //   dP = dO V^T,  dS = P * (dP - delta)
 //   dQ = gamma dS K,  dK = gamma dS^T Q,  dV = P^T dO
 //
-// Three kernels, deterministic (no atomics):
-//   fa_bwd_delta_kernel  one warp per (token, head) row: delta
+// Three kernels, deterministic (no atomics). The first is shared with the tcgen05 kernels of
+// fa_bwd_sm100.cu (head dims 64 and 128); the other two serve every other head dim:
+//   fa_bwd_rowstat_kernel one warp per (batch, head, query) row: -LSE log2(e) and -delta into
+//                        the padded row-statistics arrays
 //   fa_bwd_dq_kernel     query-stationary: 64 query rows per CTA, key tiles streamed through a
 //                        two-stage cp.async ring; S and dP by mma.sync, then dQ += dS K
 //   fa_bwd_dkdv_kernel   key-stationary: 64 keys per CTA, the query tiles of every query head
@@ -31,16 +33,28 @@ constexpr int kBM = 64;  // query rows per dQ CTA, keys per dK/dV CTA
 constexpr float kLog2e = 1.4426950408889634f;
 
 // ------------------------------------------------------------------------------------------
-// delta = rowsum(dO * O), fp32 [B, Hq, Nq]
+// Row statistics, fp32 [B, Hq, NqP]: row_nlse = -LSE log2(e), row_ndelta = -rowsum(dO * O);
+// padding rows (query >= Nq) get -inf and 0.
 // ------------------------------------------------------------------------------------------
 template <typename T>
-__global__ void __launch_bounds__(256) fa_bwd_delta_kernel(const BwdArgs p) {
-  const int64_t rows = static_cast<int64_t>(p.B) * p.Nq * p.Hq;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+__global__ void __launch_bounds__(256) fa_bwd_rowstat_kernel(const BwdArgs p) {
+  const int64_t rows = static_cast<int64_t>(p.B) * p.Hq * p.NqP;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);  // (b, h, i)
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
-  const T* o = static_cast<const T*>(p.o) + row * p.D;
-  const T* d = static_cast<const T*>(p.dout) + row * p.D;
+  const int i = static_cast<int>(row % p.NqP);
+  const int64_t bh = row / p.NqP;
+  if (i >= p.Nq) {
+    if (lane == 0) {
+      p.row_nlse[row] = -__int_as_float(0x7f800000);
+      p.row_ndelta[row] = 0.f;
+    }
+    return;
+  }
+  const int h = static_cast<int>(bh % p.Hq), b = static_cast<int>(bh / p.Hq);
+  const int64_t off = ((static_cast<int64_t>(b) * p.Nq + i) * p.Hq + h) * p.D;
+  const T* o = static_cast<const T*>(p.o) + off;
+  const T* d = static_cast<const T*>(p.dout) + off;
   float sum = 0.f;
   for (int c = lane * 8; c < p.D; c += 256) {
     const uint4 a = *reinterpret_cast<const uint4*>(o + c);
@@ -54,10 +68,8 @@ __global__ void __launch_bounds__(256) fa_bwd_delta_kernel(const BwdArgs p) {
   }
   sum = kf::warp_sum(sum);
   if (lane == 0) {
-    const int h = static_cast<int>(row % p.Hq);
-    const int64_t bi = row / p.Hq;  // b * Nq + i
-    const int i = static_cast<int>(bi % p.Nq), b = static_cast<int>(bi / p.Nq);
-    p.delta[(static_cast<int64_t>(b) * p.Hq + h) * p.Nq + i] = sum;
+    p.row_nlse[row] = -p.lse[bh * p.Nq + i] * kLog2e;
+    p.row_ndelta[row] = -sum;
   }
 }
 
@@ -123,14 +135,14 @@ __global__ void __launch_bounds__(128 * DSPLIT) fa_bwd_dq_kernel(const BwdArgs p
   if (ntiles > 0) load_kv(0, 0);
   cp_async_commit();
 
+  // Rows past Nq read the padding (-inf: P = 0); row_g < q0 + 64 <= NqP.
   const int row_g[2] = {q0 + wrow + gid, q0 + wrow + gid + 8};
-  float lse_l2[2], delta[2];
+  float nlse[2], ndelta[2];
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
-    const bool in = row_g[i] < p.Nq;
-    const int64_t idx = (static_cast<int64_t>(b) * p.Hq + h) * p.Nq + row_g[i];
-    lse_l2[i] = in ? p.lse[idx] * kLog2e : __int_as_float(0x7f800000);  // +inf: P = 0
-    delta[i] = in ? p.delta[idx] : 0.f;
+    const int64_t idx = (static_cast<int64_t>(b) * p.Hq + h) * p.NqP + row_g[i];
+    nlse[i] = p.row_nlse[idx];
+    ndelta[i] = p.row_ndelta[idx];
   }
   float acc[kDT][4];
 #pragma unroll
@@ -180,8 +192,8 @@ __global__ void __launch_bounds__(128 * DSPLIT) fa_bwd_dq_kernel(const BwdArgs p
         const int key = k0 + nt * 8 + tig * 2 + (e & 1);
         const int ri = e >> 1;
         const bool valid = key < p.Nk && (!p.causal || key <= row_g[ri] + p.Nk - p.Nq);
-        const float pr = valid ? exp2f(s[nt][e] * p.scale_log2 - lse_l2[ri]) : 0.f;
-        s[nt][e] = pr * (dp[nt][e] - delta[ri]);
+        const float pr = valid ? exp2f(fmaf(s[nt][e], p.scale_log2, nlse[ri])) : 0.f;
+        s[nt][e] = pr * (dp[nt][e] + ndelta[ri]);
       }
     // dQ += dS K (K as the B operand: keys along k, head dim along n)
 #pragma unroll
@@ -271,13 +283,12 @@ __global__ void __launch_bounds__(128 * DSPLIT) fa_bwd_dkdv_kernel(const BwdArgs
     load_tile<T, DP, kThreads>(s_q, static_cast<const T*>(p.q) + q_off + q0 * q_stride, q_stride, BQ, valid, D);
     load_tile<T, DP, kThreads>(s_q + kQTile, static_cast<const T*>(p.dout) + q_off + q0 * q_stride, q_stride, BQ,
                                valid, D);
-    float* lse_s = reinterpret_cast<float*>(st + 2 * kQTile);
-    float* delta_s = lse_s + BQ;
+    float* nlse_s = reinterpret_cast<float*>(st + 2 * kQTile);
+    float* ndelta_s = nlse_s + BQ;
     for (int i = threadIdx.x; i < BQ; i += kThreads) {
-      const int q = q0 + i;
-      const int64_t idx = (static_cast<int64_t>(b) * p.Hq + h) * p.Nq + q;
-      lse_s[i] = q < p.Nq ? p.lse[idx] * kLog2e : __int_as_float(0x7f800000);
-      delta_s[i] = q < p.Nq ? p.delta[idx] : 0.f;
+      const int64_t idx = (static_cast<int64_t>(b) * p.Hq + h) * p.NqP + q0 + i;  // q0 + i < NqP
+      nlse_s[i] = p.row_nlse[idx];
+      ndelta_s[i] = p.row_ndelta[idx];
     }
   };
   if (n_it > 0) load_stage(0, 0);
@@ -297,8 +308,8 @@ __global__ void __launch_bounds__(128 * DSPLIT) fa_bwd_dkdv_kernel(const BwdArgs
     __syncthreads();
     uint8_t* st = stages + (it & 1) * kStageBytes;
     const uint32_t s_q = kf::smem_u32(st), s_do = s_q + kQTile;
-    const float* lse_s = reinterpret_cast<const float*>(st + 2 * kQTile);
-    const float* delta_s = lse_s + BQ;
+    const float* nlse_s = reinterpret_cast<const float*>(st + 2 * kQTile);
+    const float* ndelta_s = nlse_s + BQ;
     const int q0 = (qt_first + it % qt_count) * BQ;
 
     // S^T = K Q^T and dP^T = V dO^T for this warp's 16 keys
@@ -336,9 +347,9 @@ __global__ void __launch_bounds__(128 * DSPLIT) fa_bwd_dkdv_kernel(const BwdArgs
         const int q = q0 + qi;
         const int key = key_g[e >> 1];
         const bool valid = q < p.Nq && key < p.Nk && (!p.causal || key <= q + p.Nk - p.Nq);
-        const float pr = valid ? exp2f(sT[nt][e] * p.scale_log2 - lse_s[qi]) : 0.f;
+        const float pr = valid ? exp2f(fmaf(sT[nt][e], p.scale_log2, nlse_s[qi])) : 0.f;
         sT[nt][e] = pr;
-        dpT[nt][e] = pr * (dpT[nt][e] - delta_s[qi]);
+        dpT[nt][e] = pr * (dpT[nt][e] + ndelta_s[qi]);
       }
     // dV += P^T dO and dK += dS^T Q (dO, Q as B operands: queries along k, head dim along n)
 #pragma unroll
@@ -408,12 +419,13 @@ int launch_dp(const BwdArgs& a, cudaStream_t stream) {
 }
 
 template <typename T>
-int launch_t(const BwdArgs& a, cudaStream_t s) {
+int launch_t(const BwdArgs& a, int dtype, cudaStream_t s) {
   {
-    const int64_t rows = static_cast<int64_t>(a.B) * a.Nq * a.Hq;
-    fa_bwd_delta_kernel<T><<<static_cast<unsigned int>((rows + 7) / 8), 256, 0, s>>>(a);
+    const int64_t rows = static_cast<int64_t>(a.B) * a.Hq * a.NqP;
+    fa_bwd_rowstat_kernel<T><<<static_cast<unsigned int>((rows + 7) / 8), 256, 0, s>>>(a);
     KF_LAUNCH_CHECK();
   }
+  if (kf::fa::sm100_bwd_supported(a)) return kf::fa::launch_sm100_bwd(a, dtype, s);
   const int d = a.D;
   if (d <= 32) return launch_dp<T, 32>(a, s);
   if (d <= 64) return launch_dp<T, 64>(a, s);
@@ -428,7 +440,7 @@ int launch_t(const BwdArgs& a, cudaStream_t s) {
 namespace kf::fa {
 
 int launch_bwd(const BwdArgs& a, int dtype, cudaStream_t s) {
-  return dtype == KF_DTYPE_F16 ? launch_t<__half>(a, s) : launch_t<__nv_bfloat16>(a, s);
+  return dtype == KF_DTYPE_F16 ? launch_t<__half>(a, dtype, s) : launch_t<__nv_bfloat16>(a, dtype, s);
 }
 
 }  // namespace kf::fa

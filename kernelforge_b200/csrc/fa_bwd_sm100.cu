@@ -1,0 +1,563 @@
+// FlashAttention backward (reverse-mode VJP) on the 5th-generation tensor cores
+// (tcgen05 + TMEM + TMA), head dims 64 and 128, fp16 / bf16, causal (bottom-right), GQA.
+//
+// Replaces the flash_attn binary's _flash_attn_backward that FlashAttentionFunction.backward
+// calls (flash_attention_jvp/custom.py:255-266). After the row-statistics pass of fa_bwd.cu
+// (row_nlse = -LSE log2 e, row_ndelta = -rowsum(dO O), padded), two kernels, no atomics:
+//
+//   dq kernel    query-stationary: 128 query rows of one (batch, head) per CTA, 64-key tiles
+//                  S  = Q K^T,  dP = dO V^T           score MMAs, double-buffered in TMEM
+//                  P  = 2^(S gamma log2 e - LSE log2 e),  dS = P (dP - delta)
+//                  dQ += dS K                          A = dS (16-bit, TMEM), B = K (MN-major)
+//   dkdv kernel  key-stationary: 128 keys of one (batch, KV head) per CTA; the 64-query tiles of
+//                every query head of the group, in order (the group sum is sequential)
+//                  S^T = K Q^T,  dP^T = V dO^T
+//                  P^T, dS^T (16-bit) written over the first 32 columns of their fp32 tiles
+//                  dV += P^T dO,  dK += dS^T Q         B = dO, Q (MN-major)
+// Output scaling: dQ and dK by gamma at the end.
+//
+// Warp roles (352 threads), as in the forward-mode kernels of fa_sm100.cu:
+//   warps 0..3, 4..7  two softmax warpgroups; warpgroup g takes the tiles t with (t & 1) == g,
+//                     one thread per stationary row (= one TMEM lane)
+//   warp 8            TMA producer: the stationary pair once, then a ring of streamed pairs
+//   warp 9            TMEM owner; one thread issues the score MMAs
+//   warp 10           one thread issues the accumulating MMAs
+// Every wait is a bounded mbarrier wait that records KF_ERR_DEVICE_TIMEOUT and gives up.
+#include <climits>
+
+#include "fa_common.cuh"
+#include "kf_tcgen05.cuh"
+
+namespace {
+
+using kf::fa::BwdArgs;
+using kf::fa::encode_bnhd;
+
+__device__ unsigned int g_fa_bwd_error = 0;
+
+constexpr int kRows = 128;     // stationary rows per CTA
+constexpr int kTile = 64;      // streamed rows per tile
+constexpr int kThreads = 352;  // 11 warps
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kOutWarp = 10;
+constexpr uint32_t kTmemCols = 512;
+
+// Shared memory: the stationary pair (Q, dO or K, V), a ring of streamed pairs (K, V or Q, dO)
+// with, per stage, 64 row statistics of each kind (dkdv only), then the barriers.
+template <int D> struct Cfg {
+  static constexpr int kKB = D / 64;                     // 128-byte boxes along the head dim
+  static constexpr int kStatBytes = kKB * kRows * 128;   // one stationary operand
+  static constexpr int kTileBytes = kKB * kTile * 128;   // one streamed operand tile
+  static constexpr int kStages = D == 64 ? 4 : 3;
+  static constexpr int kRingOffset = 2 * kStatBytes;
+  static constexpr int kRowStatOffset = kRingOffset + kStages * 2 * kTileBytes;
+  static constexpr int kBarOffset = kRowStatOffset + kStages * 2 * kTile * 4;
+  static constexpr int kSmemBytes = kBarOffset + 256 + 1024;  // + alignment slack
+};
+
+template <int D> struct Bars {
+  uint64_t* stat_full;
+  uint64_t* ring_full;   // [kStages]
+  uint64_t* ring_empty;  // [kStages] the accumulating MMAs of the stage's tile completed
+  uint64_t* s_full;      // [2] score MMAs of tile t complete
+  uint64_t* p_full;      // [2] softmax of tile t done (scores read, 16-bit operands written)
+  uint64_t* acc_done;    // [2] accumulating MMAs of tile t complete
+  uint64_t* acc_full;
+  uint32_t* tmem_slot;
+  int* abort_flag;
+  __device__ explicit Bars(uint8_t* smem) {
+    using C = Cfg<D>;
+    stat_full = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
+    ring_full = stat_full + 1;
+    ring_empty = ring_full + C::kStages;
+    s_full = ring_empty + C::kStages;
+    p_full = s_full + 2;
+    acc_done = p_full + 2;
+    acc_full = acc_done + 2;
+    tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+    abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  }
+  __device__ void init() const {
+    using C = Cfg<D>;
+    kf::mbar_init(stat_full, 1);
+    for (int s = 0; s < C::kStages; ++s) {
+      kf::mbar_init(&ring_full[s], 1);
+      kf::mbar_init(&ring_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      kf::mbar_init(&s_full[i], 1);
+      kf::mbar_init(&p_full[i], kRows);  // the 128 threads of one softmax warpgroup
+      kf::mbar_init(&acc_done[i], 1);
+    }
+    kf::mbar_init(acc_full, 1);
+    *abort_flag = 0;
+  }
+};
+
+// Streamed tile t of a CTA: head h_base + t / count, rows (first + t % count) * kTile.
+struct TileWalk {
+  int h_base, first, count;
+  __device__ int head(int t) const { return h_base + t / count; }
+  __device__ int row0(int t) const { return (first + t % count) * kTile; }
+};
+
+// TMA producer (one thread). kRowStats: each stage also carries the tile's 64 row statistics.
+template <int D, bool kRowStats>
+__device__ void produce(const Bars<D>& bars, uint8_t* smem, const CUtensorMap* tm_s0, const CUtensorMap* tm_s1,
+                        const CUtensorMap* tm_t0, const CUtensorMap* tm_t1, int stat_head, int stat_row0, int b,
+                        const TileWalk& walk, int ntiles, const BwdArgs& p) {
+  using C = Cfg<D>;
+  volatile int* abort = bars.abort_flag;
+  kf::prefetch_tensormap(tm_s0);
+  kf::prefetch_tensormap(tm_t0);
+  kf::mbar_arrive_expect_tx(bars.stat_full, 2 * C::kStatBytes);
+  for (int kb = 0; kb < C::kKB; ++kb) {
+    kf::tma_load_4d(smem + kb * kRows * 128, tm_s0, bars.stat_full, kb * 64, stat_head, stat_row0, b);
+    kf::tma_load_4d(smem + C::kStatBytes + kb * kRows * 128, tm_s1, bars.stat_full, kb * 64, stat_head, stat_row0, b);
+  }
+  constexpr uint32_t kStageTx = 2 * C::kTileBytes + (kRowStats ? 2 * kTile * 4 : 0);
+  for (int t = 0; t < ntiles; ++t) {
+    const int st = t % C::kStages;
+    if (t >= C::kStages &&
+        !kf::mbar_wait_or_abort<true>(&bars.ring_empty[st], ((t / C::kStages) - 1) & 1, &g_fa_bwd_error, abort))
+      return;
+    uint8_t* base = smem + C::kRingOffset + st * 2 * C::kTileBytes;
+    const int h = walk.head(t), r0 = walk.row0(t);
+    kf::mbar_arrive_expect_tx(&bars.ring_full[st], kStageTx);
+    for (int kb = 0; kb < C::kKB; ++kb) {
+      kf::tma_load_4d(base + kb * kTile * 128, tm_t0, &bars.ring_full[st], kb * 64, h, r0, b);
+      kf::tma_load_4d(base + C::kTileBytes + kb * kTile * 128, tm_t1, &bars.ring_full[st], kb * 64, h, r0, b);
+    }
+    if (kRowStats) {
+      // r0 + 64 <= NqP and NqP is a multiple of 128: 16-byte aligned, in bounds.
+      const int64_t off = (static_cast<int64_t>(b) * p.Hq + h) * p.NqP + r0;
+      float* rs = reinterpret_cast<float*>(smem + C::kRowStatOffset + st * 2 * kTile * 4);
+      kf::bulk_load(rs, p.row_nlse + off, kTile * 4, &bars.ring_full[st]);
+      kf::bulk_load(rs + kTile, p.row_ndelta + off, kTile * 4, &bars.ring_full[st]);
+    }
+  }
+}
+
+// D[128 x 64] = A[128 x D] B[64 x D]^T; A, B K-major 128-byte-swizzled tiles.
+template <int D>
+__device__ __forceinline__ void issue_scores(uint32_t a_addr, uint32_t b_addr, uint32_t d_col, uint32_t idesc) {
+#pragma unroll
+  for (int k = 0; k < D / 16; ++k) {
+    const uint32_t aoff = (k >> 2) * kRows * 128 + (k & 3) * 32;
+    const uint32_t boff = (k >> 2) * kTile * 128 + (k & 3) * 32;
+    kf::tc::mma_ss(d_col, kf::tc::desc_sw128(a_addr + aoff, 16, 1024), kf::tc::desc_sw128(b_addr + boff, 16, 1024),
+                   idesc, k > 0);
+  }
+}
+
+// D[128 x D] += A[128 x 64] B[64 x D]; A 16-bit in TMEM (8 columns per 16 of K), B an MN-major
+// 128-byte-swizzled tile (64-element blocks kTile * 128 bytes apart).
+template <int D>
+__device__ __forceinline__ void issue_accumulate(uint32_t d_col, uint32_t a_col, uint32_t b_addr, uint32_t idesc,
+                                                 uint32_t& started) {
+#pragma unroll
+  for (int kk = 0; kk < kTile / 16; ++kk) {
+    kf::tc::mma_ts(d_col, a_col + kk * 8, kf::tc::desc_sw128(b_addr + kk * 2048, kTile * 128, 1024), idesc, started);
+    started = 1;
+  }
+}
+
+__device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
+  return bf16 ? kf::Mma<__nv_bfloat16>::from_f2(a, b) : kf::Mma<__half>::from_f2(a, b);
+}
+
+// 2^x with the MUFU instruction (flushes subnormal results to zero; exp2(-inf) = 0).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity, const int* abort) {
+  return kf::mbar_wait_or_abort(bar, parity, &g_fa_bwd_error, const_cast<volatile int*>(abort));
+}
+__device__ __forceinline__ bool wait_relaxed(uint64_t* bar, uint32_t parity, const int* abort) {
+  return kf::mbar_wait_or_abort<true>(bar, parity, &g_fa_bwd_error, const_cast<volatile int*>(abort));
+}
+
+// Epilogue store of 32 accumulator columns of one row: out = acc * mul (zeros when nothing was
+// accumulated).
+template <typename T>
+__device__ __forceinline__ void store_row32(T* dst, const uint32_t (&acc)[32], float mul, bool any) {
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+#pragma unroll
+  for (int v = 0; v < 4; ++v) {
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = v * 8 + e * 2;
+      w[e] = any ? pack2(__uint_as_float(acc[i]) * mul, __uint_as_float(acc[i + 1]) * mul, kBf16) : 0u;
+    }
+    *reinterpret_cast<uint4*>(dst + v * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// ============================================================================================
+// dQ. Tensor memory: [0, D) dQ accumulator | S_b at 128 + 128 b, dP_b 64 further |
+// dS_b (16-bit) at 384 + 32 b. dS has its own columns, so tile t+2's score MMAs only wait for
+// tile t's softmax to have read its scores.
+// ============================================================================================
+constexpr uint32_t kDqAcc = 0, kDqBuf = 128, kDqDs = 384;
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads, 1)
+fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
+                       const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                       const BwdArgs p) {
+  using C = Cfg<D>;
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (kf::smem_u32(smem_raw) & 1023u)) & 1023u);
+  const Bars<D> bars(smem);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int q0 = blockIdx.x * kRows;
+  const int kvh = h / (p.Hq / p.Hkv);
+  int k_end = p.Nk;
+  if (p.causal) k_end = min(p.Nk, max(0, q0 + kRows + p.Nk - p.Nq));
+  const int ntiles = (k_end + kTile - 1) / kTile;
+
+  if (threadIdx.x == 0) {
+    bars.init();
+    kf::fence_mbar_init();
+  }
+  if (warp == kMmaWarp) kf::tc::tmem_alloc(bars.tmem_slot, kTmemCols);
+  kf::tc::fence_before_sync();
+  __syncthreads();
+  kf::tc::fence_after_sync();
+  const uint32_t tmem = *bars.tmem_slot;
+  const int* abort = bars.abort_flag;
+
+  if (warp == kProducerWarp) {
+    if (lane == 0)
+      produce<D, false>(bars, smem, &tm_q, &tm_do, &tm_k, &tm_v, h, q0, b, TileWalk{kvh, 0, max(ntiles, 1)}, ntiles, p);
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      constexpr uint32_t idS = kf::tc::idesc_f16(kBf16 ? 1 : 0, kRows, kTile, false, false);
+      const uint32_t q_addr = kf::smem_u32(smem), do_addr = q_addr + C::kStatBytes;
+      bool ok = wait_relaxed(bars.stat_full, 0, abort);
+      for (int t = 0; ok && t < ntiles; ++t) {
+        const int buf = t & 1, st = t % C::kStages;
+        if (t >= 2 && !(ok = wait_relaxed(&bars.p_full[buf], ((t >> 1) - 1) & 1, abort))) break;
+        if (!(ok = wait_relaxed(&bars.ring_full[st], (t / C::kStages) & 1, abort))) break;
+        kf::tc::fence_after_sync();
+        const uint32_t k_addr = kf::smem_u32(smem + C::kRingOffset + st * 2 * C::kTileBytes);
+        const uint32_t s_col = tmem + kDqBuf + 128 * buf;
+        issue_scores<D>(q_addr, k_addr, s_col, idS);                        // S  = Q K^T
+        issue_scores<D>(do_addr, k_addr + C::kTileBytes, s_col + 64, idS);  // dP = dO V^T
+        kf::tc::commit(&bars.s_full[buf]);
+      }
+    }
+  } else if (warp == kOutWarp) {
+    if (lane == 0) {
+      constexpr uint32_t idA = kf::tc::idesc_f16(kBf16 ? 1 : 0, kRows, D, false, true);
+      uint32_t started = 0;
+      bool ok = true;
+      for (int t = 0; ok && t < ntiles; ++t) {
+        const int buf = t & 1, st = t % C::kStages;
+        if (!(ok = wait_relaxed(&bars.p_full[buf], (t >> 1) & 1, abort))) break;
+        kf::tc::fence_after_sync();
+        const uint32_t k_addr = kf::smem_u32(smem + C::kRingOffset + st * 2 * C::kTileBytes);
+        issue_accumulate<D>(tmem + kDqAcc, tmem + kDqDs + 32 * buf, k_addr, idA, started);  // dQ += dS K
+        kf::tc::commit(&bars.acc_done[buf]);
+        kf::tc::commit(&bars.ring_empty[st]);
+      }
+      kf::tc::commit(bars.acc_full);
+    }
+  } else {
+    const int group = warp >> 2, quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int qrow = q0 + row;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const int64_t stat = (static_cast<int64_t>(b) * p.Hq + h) * p.NqP + qrow;  // qrow < NqP
+    const float nlse = p.row_nlse[stat], ndelta = p.row_ndelta[stat];
+    const int limit = p.causal ? min(p.Nk, qrow + p.Nk - p.Nq + 1) : p.Nk;  // keys [0, limit) visible
+    const uint32_t s_col = lane_base + kDqBuf + 128 * group;
+    const uint32_t dp_col = s_col + 64;
+    const uint32_t ds_col = lane_base + kDqDs + 32 * group;
+    const uint64_t c2 = kf::f2_pack(p.scale_log2, p.scale_log2), nl2 = kf::f2_pack(nlse, nlse);
+    const uint64_t nd2 = kf::f2_pack(ndelta, ndelta);
+    bool ok = true;
+    for (int t = group; t < ntiles; t += 2) {
+      ok = wait(&bars.s_full[group], (t >> 1) & 1, abort);
+      // This warpgroup's dS columns were last read by tile t-2's accumulating MMAs.
+      if (ok && t >= 2) ok = wait(&bars.acc_done[group], ((t >> 1) - 1) & 1, abort);
+      ok = __all_sync(0xffffffffu, ok);  // the tcgen05 copies below are .sync.aligned
+      if (!ok) break;
+      kf::tc::fence_after_sync();
+      const int k0 = t * kTile;
+      const bool full = k0 + kTile <= limit;
+      uint32_t sv[2][32], dv[2][32];
+      kf::tc::ld_32x32b_x32(s_col, sv[0]);
+      kf::tc::ld_32x32b_x32(s_col + 32, sv[1]);
+      kf::tc::ld_32x32b_x32(dp_col, dv[0]);
+      kf::tc::ld_32x32b_x32(dp_col + 32, dv[1]);
+      kf::tc::wait_ld();
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t dd[16];
+        const int kc = k0 + c * 32;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 a = kf::f2_unpack(
+              kf::f2_fma(kf::f2_pack(__uint_as_float(sv[c][2 * i]), __uint_as_float(sv[c][2 * i + 1])), c2, nl2));
+          float p0 = ex2(a.x), p1 = ex2(a.y);
+          if (!full) {
+            p0 = kc + 2 * i < limit ? p0 : 0.f;
+            p1 = kc + 2 * i + 1 < limit ? p1 : 0.f;
+          }
+          const uint64_t ds = kf::f2_mul(
+              kf::f2_pack(p0, p1),
+              kf::f2_add(kf::f2_pack(__uint_as_float(dv[c][2 * i]), __uint_as_float(dv[c][2 * i + 1])), nd2));
+          const float2 df = kf::f2_unpack(ds);
+          dd[i] = pack2(df.x, df.y, kBf16);
+        }
+        kf::tc::st_32x32b_x16(ds_col + c * 16, dd);
+      }
+      kf::tc::wait_st();
+      kf::tc::fence_before_sync();
+      kf::mbar_arrive(&bars.p_full[group]);
+    }
+    // Epilogue: dQ = gamma acc; warpgroup g writes columns [g D/2, (g + 1) D/2).
+    if (ok) ok = wait(bars.acc_full, 0, abort);
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok) {
+      kf::tc::fence_after_sync();
+      T* dst = static_cast<T*>(p.dq) + ((static_cast<int64_t>(b) * p.Nq + qrow) * p.Hq + h) * D;
+#pragma unroll
+      for (int cc = 0; cc < D / 64; ++cc) {
+        const int c = group * (D / 64) + cc;  // 32-column chunk
+        uint32_t ar[32];
+        kf::tc::ld_32x32b_x32(lane_base + kDqAcc + c * 32, ar);
+        kf::tc::wait_ld();
+        if (qrow < p.Nq) store_row32<T>(dst + c * 32, ar, p.scale, ntiles > 0);
+      }
+    }
+  }
+  kf::tc::fence_before_sync();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    kf::tc::fence_after_sync();
+    kf::tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ============================================================================================
+// dK, dV. Tensor memory: [0, D) dV | [D, 2D) dK | S^T_b at 2D + 128 b, dP^T_b 64 further.
+// The softmax warps write P^T over the first 32 columns of S^T_b and dS^T over those of dP^T_b
+// (queries [32 c, 32 c + 32) of half c go to columns [16 c, 16 c + 16) after that half is read),
+// so tile t+2's score MMAs wait for tile t's accumulating MMAs.
+// ============================================================================================
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads, 1)
+fa_bwd_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                         const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
+                         const BwdArgs p) {
+  using C = Cfg<D>;
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t kDv = 0, kDk = D, kBuf = 2 * D;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (kf::smem_u32(smem_raw) & 1023u)) & 1023u);
+  const Bars<D> bars(smem);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kvh = blockIdx.y, b = blockIdx.z;
+  const int k0 = blockIdx.x * kRows;
+  const int group = p.Hq / p.Hkv;
+  // Key k is visible to query q iff q >= k + Nq - Nk (causal): queries below k0 + Nq - Nk see
+  // none of these keys.
+  const int q_first = p.causal ? max(0, k0 + p.Nq - p.Nk) : 0;
+  const int qt_first = q_first / kTile;
+  const int qt_count = max(0, (p.Nq + kTile - 1) / kTile - qt_first);
+  const int ntiles = group * qt_count;
+  const TileWalk walk{kvh * group, qt_first, max(qt_count, 1)};
+
+  if (threadIdx.x == 0) {
+    bars.init();
+    kf::fence_mbar_init();
+  }
+  if (warp == kMmaWarp) kf::tc::tmem_alloc(bars.tmem_slot, kTmemCols);
+  kf::tc::fence_before_sync();
+  __syncthreads();
+  kf::tc::fence_after_sync();
+  const uint32_t tmem = *bars.tmem_slot;
+  const int* abort = bars.abort_flag;
+
+  if (warp == kProducerWarp) {
+    if (lane == 0) produce<D, true>(bars, smem, &tm_k, &tm_v, &tm_q, &tm_do, kvh, k0, b, walk, ntiles, p);
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      constexpr uint32_t idS = kf::tc::idesc_f16(kBf16 ? 1 : 0, kRows, kTile, false, false);
+      const uint32_t k_addr = kf::smem_u32(smem), v_addr = k_addr + C::kStatBytes;
+      bool ok = wait_relaxed(bars.stat_full, 0, abort);
+      for (int t = 0; ok && t < ntiles; ++t) {
+        const int buf = t & 1, st = t % C::kStages;
+        if (t >= 2 && !(ok = wait_relaxed(&bars.acc_done[buf], ((t >> 1) - 1) & 1, abort))) break;
+        if (!(ok = wait_relaxed(&bars.ring_full[st], (t / C::kStages) & 1, abort))) break;
+        kf::tc::fence_after_sync();
+        const uint32_t q_addr = kf::smem_u32(smem + C::kRingOffset + st * 2 * C::kTileBytes);
+        const uint32_t s_col = tmem + kBuf + 128 * buf;
+        issue_scores<D>(k_addr, q_addr, s_col, idS);                        // S^T  = K Q^T
+        issue_scores<D>(v_addr, q_addr + C::kTileBytes, s_col + 64, idS);   // dP^T = V dO^T
+        kf::tc::commit(&bars.s_full[buf]);
+      }
+    }
+  } else if (warp == kOutWarp) {
+    if (lane == 0) {
+      constexpr uint32_t idA = kf::tc::idesc_f16(kBf16 ? 1 : 0, kRows, D, false, true);
+      uint32_t v_started = 0, k_started = 0;
+      bool ok = true;
+      for (int t = 0; ok && t < ntiles; ++t) {
+        const int buf = t & 1, st = t % C::kStages;
+        if (!(ok = wait_relaxed(&bars.p_full[buf], (t >> 1) & 1, abort))) break;
+        kf::tc::fence_after_sync();
+        const uint32_t q_addr = kf::smem_u32(smem + C::kRingOffset + st * 2 * C::kTileBytes);
+        const uint32_t s_col = tmem + kBuf + 128 * buf;
+        issue_accumulate<D>(tmem + kDv, s_col, q_addr + C::kTileBytes, idA, v_started);  // dV += P^T dO
+        issue_accumulate<D>(tmem + kDk, s_col + 64, q_addr, idA, k_started);             // dK += dS^T Q
+        kf::tc::commit(&bars.acc_done[buf]);
+        kf::tc::commit(&bars.ring_empty[st]);
+      }
+      kf::tc::commit(bars.acc_full);
+    }
+  } else {
+    const int wg = warp >> 2, quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int key = k0 + row;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const int q_min = p.causal ? key + p.Nq - p.Nk : INT_MIN;  // queries [q_min, Nq) see this key
+    const uint32_t s_col = lane_base + kBuf + 128 * wg;
+    const uint32_t dp_col = s_col + 64;
+    const uint64_t c2 = kf::f2_pack(p.scale_log2, p.scale_log2);
+    bool ok = true;
+    for (int t = wg; t < ntiles; t += 2) {
+      ok = __all_sync(0xffffffffu, wait(&bars.s_full[wg], (t >> 1) & 1, abort));
+      if (!ok) break;
+      kf::tc::fence_after_sync();
+      const int r0 = walk.row0(t);
+      const bool full = r0 >= q_min;
+      const float* rs = reinterpret_cast<const float*>(smem + C::kRowStatOffset + (t % C::kStages) * 2 * kTile * 4);
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t sv[32], dv[32], pp[16], dd[16];
+        kf::tc::ld_32x32b_x32(s_col + c * 32, sv);
+        kf::tc::ld_32x32b_x32(dp_col + c * 32, dv);
+        kf::tc::wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int qi = c * 32 + 2 * i;
+          const float2 nl = *reinterpret_cast<const float2*>(rs + qi);
+          const float2 nd = *reinterpret_cast<const float2*>(rs + kTile + qi);
+          const float2 a = kf::f2_unpack(kf::f2_fma(kf::f2_pack(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1])),
+                                                    c2, kf::f2_pack(nl.x, nl.y)));
+          float p0 = ex2(a.x), p1 = ex2(a.y);
+          if (!full) {
+            p0 = r0 + qi >= q_min ? p0 : 0.f;
+            p1 = r0 + qi + 1 >= q_min ? p1 : 0.f;
+          }
+          const uint64_t ds = kf::f2_mul(
+              kf::f2_pack(p0, p1),
+              kf::f2_add(kf::f2_pack(__uint_as_float(dv[2 * i]), __uint_as_float(dv[2 * i + 1])), kf::f2_pack(nd.x, nd.y)));
+          const float2 df = kf::f2_unpack(ds);
+          pp[i] = pack2(p0, p1, kBf16);
+          dd[i] = pack2(df.x, df.y, kBf16);
+        }
+        kf::tc::st_32x32b_x16(s_col + c * 16, pp);
+        kf::tc::st_32x32b_x16(dp_col + c * 16, dd);
+      }
+      kf::tc::wait_st();
+      kf::tc::fence_before_sync();
+      kf::mbar_arrive(&bars.p_full[wg]);
+    }
+    // Epilogue: dV = acc, dK = gamma acc; warpgroup g writes columns [g D/2, (g + 1) D/2).
+    if (ok) ok = wait(bars.acc_full, 0, abort);
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok) {
+      kf::tc::fence_after_sync();
+      const int64_t off = ((static_cast<int64_t>(b) * p.Nk + key) * p.Hkv + kvh) * D;
+      T* dk = static_cast<T*>(p.dk) + off;
+      T* dv = static_cast<T*>(p.dv) + off;
+#pragma unroll
+      for (int cc = 0; cc < D / 64; ++cc) {
+        const int c = wg * (D / 64) + cc;
+        uint32_t ar[32], br[32];
+        kf::tc::ld_32x32b_x32(lane_base + kDv + c * 32, ar);
+        kf::tc::ld_32x32b_x32(lane_base + kDk + c * 32, br);
+        kf::tc::wait_ld();
+        if (key < p.Nk) {
+          store_row32<T>(dv + c * 32, ar, 1.f, ntiles > 0);
+          store_row32<T>(dk + c * 32, br, p.scale, ntiles > 0);
+        }
+      }
+    }
+  }
+  kf::tc::fence_before_sync();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    kf::tc::fence_after_sync();
+    kf::tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <typename T, int D>
+int launch(const BwdArgs& a, int dtype, cudaStream_t stream) {
+  using C = Cfg<D>;
+  {
+    CUtensorMap mq, mdo, mk, mv;
+    if (!encode_bnhd(&mq, a.q, dtype, a.B, a.Nq, a.Hq, D, kRows) ||
+        !encode_bnhd(&mdo, a.dout, dtype, a.B, a.Nq, a.Hq, D, kRows) ||
+        !encode_bnhd(&mk, a.k, dtype, a.B, a.Nk, a.Hkv, D, kTile) ||
+        !encode_bnhd(&mv, a.v, dtype, a.B, a.Nk, a.Hkv, D, kTile))
+      return KF_ERR_CUDA;
+    auto kernel = fa_bwd_dq_sm100_kernel<T, D>;
+    const int prep = kf_host::prepare_kernel(reinterpret_cast<const void*>(kernel), kThreads, C::kSmemBytes, nullptr);
+    if (prep != KF_OK) return prep;
+    kernel<<<dim3((a.Nq + kRows - 1) / kRows, a.Hq, a.B), kThreads, C::kSmemBytes, stream>>>(mq, mdo, mk, mv, a);
+    KF_LAUNCH_CHECK();
+  }
+  {
+    CUtensorMap mk, mv, mq, mdo;
+    if (!encode_bnhd(&mk, a.k, dtype, a.B, a.Nk, a.Hkv, D, kRows) ||
+        !encode_bnhd(&mv, a.v, dtype, a.B, a.Nk, a.Hkv, D, kRows) ||
+        !encode_bnhd(&mq, a.q, dtype, a.B, a.Nq, a.Hq, D, kTile) ||
+        !encode_bnhd(&mdo, a.dout, dtype, a.B, a.Nq, a.Hq, D, kTile))
+      return KF_ERR_CUDA;
+    auto kernel = fa_bwd_dkdv_sm100_kernel<T, D>;
+    const int prep = kf_host::prepare_kernel(reinterpret_cast<const void*>(kernel), kThreads, C::kSmemBytes, nullptr);
+    if (prep != KF_OK) return prep;
+    kernel<<<dim3((a.Nk + kRows - 1) / kRows, a.Hkv, a.B), kThreads, C::kSmemBytes, stream>>>(mk, mv, mq, mdo, a);
+    KF_LAUNCH_CHECK();
+  }
+  return KF_OK;
+}
+
+}  // namespace
+
+int kf_internal_fa_bwd_error(unsigned int* code) {
+  unsigned int v = 0;
+  KF_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_fa_bwd_error, sizeof(v)));
+  if (v != 0) {
+    const unsigned int zero = 0;
+    KF_CUDA_TRY(cudaMemcpyToSymbol(g_fa_bwd_error, &zero, sizeof(zero)));
+  }
+  *code = v;
+  return KF_OK;
+}
+
+namespace kf::fa {
+
+bool sm100_bwd_supported(const BwdArgs& a) { return a.D == 64 || a.D == 128; }
+
+int launch_sm100_bwd(const BwdArgs& a, int dtype, cudaStream_t s) {
+  if (dtype == KF_DTYPE_BF16) return a.D == 64 ? launch<__nv_bfloat16, 64>(a, dtype, s) : launch<__nv_bfloat16, 128>(a, dtype, s);
+  return a.D == 64 ? launch<__half, 64>(a, dtype, s) : launch<__half, 128>(a, dtype, s);
+}
+
+}  // namespace kf::fa

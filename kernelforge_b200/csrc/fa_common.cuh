@@ -28,8 +28,11 @@ struct FaArgs {
 };
 
 // Inputs and outputs of the backward (reverse-mode VJP) from the saved O and LSE. Tensors are
-// contiguous [B, N, H, D]; LSE is fp32 [B, Hq, Nq] (natural log); `delta` is an fp32 workspace
-// [B, Hq, Nq] that the first kernel fills with rowsum(dO * O).
+// contiguous [B, N, H, D]; LSE is fp32 [B, Hq, Nq] (natural log). The first kernel fills two fp32
+// row-statistics arrays of the workspace, each [B, Hq, NqP] with NqP = Nq rounded up to
+// kBwdRowPad: row_nlse = -LSE log2(e) and row_ndelta = -rowsum(dO * O); padding rows hold -inf
+// and 0, so that they contribute P = 0 and dS = 0 wherever a tile reads past Nq.
+constexpr int kBwdRowPad = 128;
 struct BwdArgs {
   const void* q;
   const void* k;
@@ -37,18 +40,36 @@ struct BwdArgs {
   const void* o;
   const void* dout;
   const float* lse;
-  float* delta;
+  float* row_nlse;
+  float* row_ndelta;
   void* dq;
   void* dk;
   void* dv;
   int B, Nq, Nk, Hq, Hkv, D;
+  int NqP;
   float scale;
   float scale_log2;
   int causal;
 };
 
-// dQ, dK, dV (mma.sync; any D in 8..256, multiple of 8; deterministic).
+// Row statistics, then dQ, dK, dV (deterministic; no atomics). D in {64, 128} runs on the
+// tcgen05 kernels, every other D (8..256, multiple of 8) on the mma.sync ones.
 int launch_bwd(const BwdArgs& a, int dtype, cudaStream_t stream);
+bool sm100_bwd_supported(const BwdArgs& a);
+int launch_sm100_bwd(const BwdArgs& a, int dtype, cudaStream_t stream);
+
+// 4-D TMA map of a contiguous [B, N, H, D] 16-bit tensor with 128-byte swizzle: boxes of 64
+// head-dim elements x 1 head x `rows` tokens x 1 batch.
+inline bool encode_bnhd(CUtensorMap* map, const void* base, int dtype, int B, int N, int H, int D, int rows) {
+  const uint64_t es = 2;
+  const uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(H), static_cast<uint64_t>(N),
+                            static_cast<uint64_t>(B)};
+  const uint64_t strides[3] = {D * es, static_cast<uint64_t>(H) * D * es,
+                               static_cast<uint64_t>(N) * H * D * es};
+  const uint32_t box[4] = {64, 1, static_cast<uint32_t>(rows), 1};
+  return kf_host::encode_tiled(map, kf_host::map_type(dtype), 4, base, dims, strides, box,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+}
 
 // cp.async tiles in shared memory for the mma.sync kernels: rows of DP elements at a pitch of a
 // multiple of 64 elements, 16-byte chunk c of row r stored at chunk (c ^ (r & 7)) so that

@@ -29,6 +29,7 @@
 namespace {
 
 using kf::fa::FaArgs;
+using kf::fa::encode_bnhd;
 
 __device__ unsigned int g_fa_error = 0;
 
@@ -727,17 +728,6 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
     kf::tc::fence_after_sync();
     kf::tc::tmem_dealloc(tmem, kTmemCols);
   }
-}
-
-bool encode_bnhd(CUtensorMap* map, const void* base, int dtype, int B, int N, int H, int D, int rows) {
-  const uint64_t es = 2;
-  const uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(H), static_cast<uint64_t>(N),
-                            static_cast<uint64_t>(B)};
-  const uint64_t strides[3] = {D * es, static_cast<uint64_t>(H) * D * es,
-                               static_cast<uint64_t>(N) * H * D * es};
-  const uint32_t box[4] = {64, 1, static_cast<uint32_t>(rows), 1};
-  return kf_host::encode_tiled(map, kf_host::map_type(dtype), 4, base, dims, strides, box,
-                               CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 template <typename T, int D>

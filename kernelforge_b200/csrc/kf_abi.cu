@@ -3,6 +3,7 @@
 
 int kf_internal_sana_error(unsigned int* code);
 int kf_internal_fa_error(unsigned int* code);
+int kf_internal_fa_bwd_error(unsigned int* code);
 
 KF_API const char* kf_status_string(int status) {
   switch (status) {
@@ -31,5 +32,9 @@ KF_API int kf_query_device_error(void* stream, int* code) {
   st = kf_internal_fa_error(&fa);
   if (st != KF_OK) return st;
   if (fa != 0 && *code == KF_OK) *code = static_cast<int>(fa);
+  unsigned int fa_bwd = 0;
+  st = kf_internal_fa_bwd_error(&fa_bwd);
+  if (st != KF_OK) return st;
+  if (fa_bwd != 0 && *code == KF_OK) *code = static_cast<int>(fa_bwd);
   return KF_OK;
 }

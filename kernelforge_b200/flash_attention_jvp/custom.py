@@ -190,13 +190,14 @@ def _flash_attn_backward(dout, q, k, v, out, lse, dq, dk, dv, dropout_p, softmax
     # The kernels write dense [B, N, H, D] gradients; strided destinations receive a copy.
     grads = tuple(g if g.is_contiguous() else torch.empty_like(g, memory_format=torch.contiguous_format)
                   for g in (dq, dk, dv))
-    workspace = torch.empty(b_ * hq * nq, device=q.device, dtype=torch.float32)
+    workspace_bytes = _lib.lib.kf_fa_bwd_workspace_size(b_, hq, nq)
+    workspace = torch.empty(workspace_bytes // 4, device=q.device, dtype=torch.float32)
     with torch.cuda.device(q.device):
         _lib.check(
             _lib.lib.kf_fa_bwd(
                 q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), dout.data_ptr(),
                 lse.data_ptr(), grads[0].data_ptr(), grads[1].data_ptr(), grads[2].data_ptr(),
-                workspace.data_ptr(), workspace.numel() * 4, b_, nq, nk, hq, hkv, d,
+                workspace.data_ptr(), workspace_bytes, b_, nq, nk, hq, hkv, d,
                 float(softmax_scale), int(bool(causal)), _lib.dtype_code(q.dtype),
                 _lib.stream_handle(q.device),
             ),

@@ -63,7 +63,7 @@ def test_sana_workspace_and_validation():
 
 def test_fa_bwd_workspace_and_validation():
     ws = _lib.lib.kf_fa_bwd_workspace_size
-    assert ws(2, 4, 100) == 2 * 4 * 100 * 4  # fp32 delta per (batch, head, query)
+    assert ws(2, 4, 100) == 2 * 2 * 4 * 128 * 4  # two fp32 statistics per (batch, head, query), padded to 128
     assert ws(0, 4, 100) == 0
     f = _lib.lib.kf_fa_bwd
     need = ws(1, 2, 16)

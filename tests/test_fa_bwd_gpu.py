@@ -2,8 +2,8 @@
 
 FlashAttentionFunction.backward hands dout and the saved (q, k, v, out, lse) to
 ``_flash_attn_backward`` (flash_attention_jvp/custom.py:255-266), which this library serves with
-its own kernels. Oracle: float64 autograd through the CPU attention restatement
-(``oracle.fa_jvp.attention``). Tolerances: the reference harness's gradient bar
+its own kernels (tcgen05 for head dims 64 and 128, mma.sync for the rest). Oracle: float64
+autograd through the CPU attention restatement (``oracle.fa_jvp.attention``). Tolerances: the reference harness's gradient bar
 (flash_attention_jvp/test.py:58-59; fp16 atol 3e-3 / rtol 1e-2, bf16 atol = rtol = 3e-2) with
 atol scaled by the largest reference gradient, since dK / dV sum over every query of a KV group.
 """
@@ -33,6 +33,10 @@ CASES = (
     (2, 256, 384, 8, 2, 128, True, None),
     (1, 200, 333, 2, 2, 256, True, 0.1),
     (1, 999, 515, 2, 2, 64, False, None),
+    (2, 300, 200, 4, 2, 64, True, None),
+    (1, 200, 450, 4, 1, 128, True, None),
+    (1, 1000, 1000, 2, 2, 128, False, None),
+    (3, 130, 70, 6, 3, 64, True, 0.3),
 )
 
 
