@@ -17,8 +17,8 @@
 // Output scaling: dQ and dK by gamma at the end.
 //
 // Warp roles (352 threads), as in the forward-mode kernels of fa_sm100.cu:
-//   warps 0..3, 4..7  two softmax warpgroups; warpgroup g takes the tiles t with (t & 1) == g,
-//                     one thread per stationary row (= one TMEM lane)
+//   warps 0..3, 4..7  two softmax warpgroups; both work on every tile, warpgroup g on streamed
+//                     columns [32 g, 32 g + 32), one thread per stationary row (= one TMEM lane)
 //   warp 8            TMA producer: the stationary pair once, then a ring of streamed pairs
 //   warp 9            TMEM owner; one thread issues the score MMAs
 //   warp 10           one thread issues the accumulating MMAs
@@ -54,15 +54,18 @@ template <int D> struct Cfg {
   static constexpr int kRowStatOffset = kRingOffset + kStages * 2 * kTileBytes;
   static constexpr int kBarOffset = kRowStatOffset + kStages * 2 * kTile * 4;
   static constexpr int kSmemBytes = kBarOffset + 256 + 1024;  // + alignment slack
+  // Score buffers in TMEM (128 columns each) of the dK/dV kernel: dV and dK take 2 D columns.
+  static constexpr int kDkdvBufs = (512 - 2 * D) / 128;
 };
+constexpr int kMaxBufs = 3;
 
 template <int D> struct Bars {
   uint64_t* stat_full;
   uint64_t* ring_full;   // [kStages]
   uint64_t* ring_empty;  // [kStages] the accumulating MMAs of the stage's tile completed
-  uint64_t* s_full;      // [2] score MMAs of tile t complete
-  uint64_t* p_full;      // [2] softmax of tile t done (scores read, 16-bit operands written)
-  uint64_t* acc_done;    // [2] accumulating MMAs of tile t complete
+  uint64_t* s_full;      // [kMaxBufs] score MMAs of tile t complete
+  uint64_t* p_full;      // [kMaxBufs] softmax of tile t done (scores read, 16-bit operands written)
+  uint64_t* acc_done;    // [kMaxBufs] accumulating MMAs of tile t complete
   uint64_t* acc_full;
   uint32_t* tmem_slot;
   int* abort_flag;
@@ -72,9 +75,9 @@ template <int D> struct Bars {
     ring_full = stat_full + 1;
     ring_empty = ring_full + C::kStages;
     s_full = ring_empty + C::kStages;
-    p_full = s_full + 2;
-    acc_done = p_full + 2;
-    acc_full = acc_done + 2;
+    p_full = s_full + kMaxBufs;
+    acc_done = p_full + kMaxBufs;
+    acc_full = acc_done + kMaxBufs;
     tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
     abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
   }
@@ -85,9 +88,9 @@ template <int D> struct Bars {
       kf::mbar_init(&ring_full[s], 1);
       kf::mbar_init(&ring_empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kMaxBufs; ++i) {
       kf::mbar_init(&s_full[i], 1);
-      kf::mbar_init(&p_full[i], kRows);  // the 128 threads of one softmax warpgroup
+      kf::mbar_init(&p_full[i], 2 * kRows);  // both softmax warpgroups
       kf::mbar_init(&acc_done[i], 1);
     }
     kf::mbar_init(acc_full, 1);
@@ -152,13 +155,16 @@ __device__ __forceinline__ void issue_scores(uint32_t a_addr, uint32_t b_addr, u
 }
 
 // D[128 x D] += A[128 x 64] B[64 x D]; A 16-bit in TMEM (8 columns per 16 of K), B an MN-major
-// 128-byte-swizzled tile (64-element blocks kTile * 128 bytes apart).
-template <int D>
+// 128-byte-swizzled tile (64-element blocks kTile * 128 bytes apart). kSplitA: K rows
+// [32 g, 32 g + 32) of A start at column 32 g (each softmax warpgroup packed its 32 values into
+// the first 16 of its own 32 columns); otherwise A is packed contiguously.
+template <int D, bool kSplitA>
 __device__ __forceinline__ void issue_accumulate(uint32_t d_col, uint32_t a_col, uint32_t b_addr, uint32_t idesc,
                                                  uint32_t& started) {
 #pragma unroll
   for (int kk = 0; kk < kTile / 16; ++kk) {
-    kf::tc::mma_ts(d_col, a_col + kk * 8, kf::tc::desc_sw128(b_addr + kk * 2048, kTile * 128, 1024), idesc, started);
+    const uint32_t acol = kSplitA ? (kk >> 1) * 32 + (kk & 1) * 8 : kk * 8;
+    kf::tc::mma_ts(d_col, a_col + acol, kf::tc::desc_sw128(b_addr + kk * 2048, kTile * 128, 1024), idesc, started);
     started = 1;
   }
 }
@@ -200,8 +206,9 @@ __device__ __forceinline__ void store_row32(T* dst, const uint32_t (&acc)[32], f
 
 // ============================================================================================
 // dQ. Tensor memory: [0, D) dQ accumulator | S_b at 128 + 128 b, dP_b 64 further |
-// dS_b (16-bit) at 384 + 32 b. dS has its own columns, so tile t+2's score MMAs only wait for
-// tile t's softmax to have read its scores.
+// dS_b (16-bit) at 384 + 32 b, keys [32 g, 32 g + 32) from warpgroup g at 384 + 32 b + 16 g.
+// dS has its own columns, so tile t+2's score MMAs only wait for tile t's softmax to have read
+// its scores.
 // ============================================================================================
 constexpr uint32_t kDqAcc = 0, kDqBuf = 128, kDqDs = 384;
 
@@ -265,7 +272,7 @@ fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
         if (!(ok = wait_relaxed(&bars.p_full[buf], (t >> 1) & 1, abort))) break;
         kf::tc::fence_after_sync();
         const uint32_t k_addr = kf::smem_u32(smem + C::kRingOffset + st * 2 * C::kTileBytes);
-        issue_accumulate<D>(tmem + kDqAcc, tmem + kDqDs + 32 * buf, k_addr, idA, started);  // dQ += dS K
+        issue_accumulate<D, false>(tmem + kDqAcc, tmem + kDqDs + 32 * buf, k_addr, idA, started);  // dQ += dS K
         kf::tc::commit(&bars.acc_done[buf]);
         kf::tc::commit(&bars.ring_empty[st]);
       }
@@ -279,51 +286,42 @@ fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
     const int64_t stat = (static_cast<int64_t>(b) * p.Hq + h) * p.NqP + qrow;  // qrow < NqP
     const float nlse = p.row_nlse[stat], ndelta = p.row_ndelta[stat];
     const int limit = p.causal ? min(p.Nk, qrow + p.Nk - p.Nq + 1) : p.Nk;  // keys [0, limit) visible
-    const uint32_t s_col = lane_base + kDqBuf + 128 * group;
-    const uint32_t dp_col = s_col + 64;
-    const uint32_t ds_col = lane_base + kDqDs + 32 * group;
     const uint64_t c2 = kf::f2_pack(p.scale_log2, p.scale_log2), nl2 = kf::f2_pack(nlse, nlse);
     const uint64_t nd2 = kf::f2_pack(ndelta, ndelta);
     bool ok = true;
-    for (int t = group; t < ntiles; t += 2) {
-      ok = wait(&bars.s_full[group], (t >> 1) & 1, abort);
-      // This warpgroup's dS columns were last read by tile t-2's accumulating MMAs.
-      if (ok && t >= 2) ok = wait(&bars.acc_done[group], ((t >> 1) - 1) & 1, abort);
+    for (int t = 0; t < ntiles; ++t) {
+      const int buf = t & 1;
+      ok = wait(&bars.s_full[buf], (t >> 1) & 1, abort);
+      // The dS columns of this buffer were last read by tile t-2's accumulating MMAs.
+      if (ok && t >= 2) ok = wait(&bars.acc_done[buf], ((t >> 1) - 1) & 1, abort);
       ok = __all_sync(0xffffffffu, ok);  // the tcgen05 copies below are .sync.aligned
       if (!ok) break;
       kf::tc::fence_after_sync();
-      const int k0 = t * kTile;
-      const bool full = k0 + kTile <= limit;
-      uint32_t sv[2][32], dv[2][32];
-      kf::tc::ld_32x32b_x32(s_col, sv[0]);
-      kf::tc::ld_32x32b_x32(s_col + 32, sv[1]);
-      kf::tc::ld_32x32b_x32(dp_col, dv[0]);
-      kf::tc::ld_32x32b_x32(dp_col + 32, dv[1]);
+      const uint32_t s_col = lane_base + kDqBuf + 128 * buf + 32 * group;  // this warpgroup's 32 keys
+      const int kc = t * kTile + 32 * group;
+      const bool full = kc + 32 <= limit;
+      uint32_t sv[32], dv[32], dd[16];
+      kf::tc::ld_32x32b_x32(s_col, sv);
+      kf::tc::ld_32x32b_x32(s_col + 64, dv);
       kf::tc::wait_ld();
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t dd[16];
-        const int kc = k0 + c * 32;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float2 a = kf::f2_unpack(
-              kf::f2_fma(kf::f2_pack(__uint_as_float(sv[c][2 * i]), __uint_as_float(sv[c][2 * i + 1])), c2, nl2));
-          float p0 = ex2(a.x), p1 = ex2(a.y);
-          if (!full) {
-            p0 = kc + 2 * i < limit ? p0 : 0.f;
-            p1 = kc + 2 * i + 1 < limit ? p1 : 0.f;
-          }
-          const uint64_t ds = kf::f2_mul(
-              kf::f2_pack(p0, p1),
-              kf::f2_add(kf::f2_pack(__uint_as_float(dv[c][2 * i]), __uint_as_float(dv[c][2 * i + 1])), nd2));
-          const float2 df = kf::f2_unpack(ds);
-          dd[i] = pack2(df.x, df.y, kBf16);
+      for (int i = 0; i < 16; ++i) {
+        const float2 a = kf::f2_unpack(
+            kf::f2_fma(kf::f2_pack(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1])), c2, nl2));
+        float p0 = ex2(a.x), p1 = ex2(a.y);
+        if (!full) {
+          p0 = kc + 2 * i < limit ? p0 : 0.f;
+          p1 = kc + 2 * i + 1 < limit ? p1 : 0.f;
         }
-        kf::tc::st_32x32b_x16(ds_col + c * 16, dd);
+        const uint64_t ds = kf::f2_mul(
+            kf::f2_pack(p0, p1), kf::f2_add(kf::f2_pack(__uint_as_float(dv[2 * i]), __uint_as_float(dv[2 * i + 1])), nd2));
+        const float2 df = kf::f2_unpack(ds);
+        dd[i] = pack2(df.x, df.y, kBf16);
       }
+      kf::tc::st_32x32b_x16(lane_base + kDqDs + 32 * buf + 16 * group, dd);
       kf::tc::wait_st();
       kf::tc::fence_before_sync();
-      kf::mbar_arrive(&bars.p_full[group]);
+      kf::mbar_arrive(&bars.p_full[buf]);
     }
     // Epilogue: dQ = gamma acc; warpgroup g writes columns [g D/2, (g + 1) D/2).
     if (ok) ok = wait(bars.acc_full, 0, abort);
@@ -350,10 +348,10 @@ fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
 }
 
 // ============================================================================================
-// dK, dV. Tensor memory: [0, D) dV | [D, 2D) dK | S^T_b at 2D + 128 b, dP^T_b 64 further.
-// The softmax warps write P^T over the first 32 columns of S^T_b and dS^T over those of dP^T_b
-// (queries [32 c, 32 c + 32) of half c go to columns [16 c, 16 c + 16) after that half is read),
-// so tile t+2's score MMAs wait for tile t's accumulating MMAs.
+// dK, dV. Tensor memory: [0, D) dV | [D, 2D) dK | kBufs score buffers: S^T_b at 2D + 128 b,
+// dP^T_b 64 further (3 buffers for D = 64, 2 for D = 128). Warpgroup g reads queries
+// [32 g, 32 g + 32) of S^T_b and dP^T_b and writes P^T and dS^T (16-bit) over the first 16 of
+// those 32 columns, so tile t+kBufs's score MMAs wait for tile t's accumulating MMAs.
 // ============================================================================================
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -363,6 +361,7 @@ fa_bwd_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_
   using C = Cfg<D>;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kDv = 0, kDk = D, kBuf = 2 * D;
+  constexpr int kBufs = C::kDkdvBufs;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (kf::smem_u32(smem_raw) & 1023u)) & 1023u);
   const Bars<D> bars(smem);
@@ -398,8 +397,8 @@ fa_bwd_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_
       const uint32_t k_addr = kf::smem_u32(smem), v_addr = k_addr + C::kStatBytes;
       bool ok = wait_relaxed(bars.stat_full, 0, abort);
       for (int t = 0; ok && t < ntiles; ++t) {
-        const int buf = t & 1, st = t % C::kStages;
-        if (t >= 2 && !(ok = wait_relaxed(&bars.acc_done[buf], ((t >> 1) - 1) & 1, abort))) break;
+        const int buf = t % kBufs, st = t % C::kStages;
+        if (t >= kBufs && !(ok = wait_relaxed(&bars.acc_done[buf], ((t / kBufs) - 1) & 1, abort))) break;
         if (!(ok = wait_relaxed(&bars.ring_full[st], (t / C::kStages) & 1, abort))) break;
         kf::tc::fence_after_sync();
         const uint32_t q_addr = kf::smem_u32(smem + C::kRingOffset + st * 2 * C::kTileBytes);
@@ -415,13 +414,13 @@ fa_bwd_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_
       uint32_t v_started = 0, k_started = 0;
       bool ok = true;
       for (int t = 0; ok && t < ntiles; ++t) {
-        const int buf = t & 1, st = t % C::kStages;
-        if (!(ok = wait_relaxed(&bars.p_full[buf], (t >> 1) & 1, abort))) break;
+        const int buf = t % kBufs, st = t % C::kStages;
+        if (!(ok = wait_relaxed(&bars.p_full[buf], (t / kBufs) & 1, abort))) break;
         kf::tc::fence_after_sync();
         const uint32_t q_addr = kf::smem_u32(smem + C::kRingOffset + st * 2 * C::kTileBytes);
         const uint32_t s_col = tmem + kBuf + 128 * buf;
-        issue_accumulate<D>(tmem + kDv, s_col, q_addr + C::kTileBytes, idA, v_started);  // dV += P^T dO
-        issue_accumulate<D>(tmem + kDk, s_col + 64, q_addr, idA, k_started);             // dK += dS^T Q
+        issue_accumulate<D, true>(tmem + kDv, s_col, q_addr + C::kTileBytes, idA, v_started);  // dV += P^T dO
+        issue_accumulate<D, true>(tmem + kDk, s_col + 64, q_addr, idA, k_started);             // dK += dS^T Q
         kf::tc::commit(&bars.acc_done[buf]);
         kf::tc::commit(&bars.ring_empty[st]);
       }
@@ -433,48 +432,44 @@ fa_bwd_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_
     const int key = k0 + row;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const int q_min = p.causal ? key + p.Nq - p.Nk : INT_MIN;  // queries [q_min, Nq) see this key
-    const uint32_t s_col = lane_base + kBuf + 128 * wg;
-    const uint32_t dp_col = s_col + 64;
     const uint64_t c2 = kf::f2_pack(p.scale_log2, p.scale_log2);
     bool ok = true;
-    for (int t = wg; t < ntiles; t += 2) {
-      ok = __all_sync(0xffffffffu, wait(&bars.s_full[wg], (t >> 1) & 1, abort));
+    for (int t = 0; t < ntiles; ++t) {
+      const int buf = t % kBufs;
+      ok = __all_sync(0xffffffffu, wait(&bars.s_full[buf], (t / kBufs) & 1, abort));
       if (!ok) break;
       kf::tc::fence_after_sync();
-      const int r0 = walk.row0(t);
+      const uint32_t s_col = lane_base + kBuf + 128 * buf + 32 * wg;  // this warpgroup's 32 queries
+      const int r0 = walk.row0(t) + 32 * wg;
       const bool full = r0 >= q_min;
-      const float* rs = reinterpret_cast<const float*>(smem + C::kRowStatOffset + (t % C::kStages) * 2 * kTile * 4);
+      const float* rs = reinterpret_cast<const float*>(smem + C::kRowStatOffset + (t % C::kStages) * 2 * kTile * 4) + 32 * wg;
+      uint32_t sv[32], dv[32], pp[16], dd[16];
+      kf::tc::ld_32x32b_x32(s_col, sv);
+      kf::tc::ld_32x32b_x32(s_col + 64, dv);
+      kf::tc::wait_ld();
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t sv[32], dv[32], pp[16], dd[16];
-        kf::tc::ld_32x32b_x32(s_col + c * 32, sv);
-        kf::tc::ld_32x32b_x32(dp_col + c * 32, dv);
-        kf::tc::wait_ld();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int qi = c * 32 + 2 * i;
-          const float2 nl = *reinterpret_cast<const float2*>(rs + qi);
-          const float2 nd = *reinterpret_cast<const float2*>(rs + kTile + qi);
-          const float2 a = kf::f2_unpack(kf::f2_fma(kf::f2_pack(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1])),
-                                                    c2, kf::f2_pack(nl.x, nl.y)));
-          float p0 = ex2(a.x), p1 = ex2(a.y);
-          if (!full) {
-            p0 = r0 + qi >= q_min ? p0 : 0.f;
-            p1 = r0 + qi + 1 >= q_min ? p1 : 0.f;
-          }
-          const uint64_t ds = kf::f2_mul(
-              kf::f2_pack(p0, p1),
-              kf::f2_add(kf::f2_pack(__uint_as_float(dv[2 * i]), __uint_as_float(dv[2 * i + 1])), kf::f2_pack(nd.x, nd.y)));
-          const float2 df = kf::f2_unpack(ds);
-          pp[i] = pack2(p0, p1, kBf16);
-          dd[i] = pack2(df.x, df.y, kBf16);
+      for (int i = 0; i < 16; ++i) {
+        const float2 nl = *reinterpret_cast<const float2*>(rs + 2 * i);
+        const float2 nd = *reinterpret_cast<const float2*>(rs + kTile + 2 * i);
+        const float2 a = kf::f2_unpack(
+            kf::f2_fma(kf::f2_pack(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1])), c2, kf::f2_pack(nl.x, nl.y)));
+        float p0 = ex2(a.x), p1 = ex2(a.y);
+        if (!full) {
+          p0 = r0 + 2 * i >= q_min ? p0 : 0.f;
+          p1 = r0 + 2 * i + 1 >= q_min ? p1 : 0.f;
         }
-        kf::tc::st_32x32b_x16(s_col + c * 16, pp);
-        kf::tc::st_32x32b_x16(dp_col + c * 16, dd);
+        const uint64_t ds = kf::f2_mul(
+            kf::f2_pack(p0, p1),
+            kf::f2_add(kf::f2_pack(__uint_as_float(dv[2 * i]), __uint_as_float(dv[2 * i + 1])), kf::f2_pack(nd.x, nd.y)));
+        const float2 df = kf::f2_unpack(ds);
+        pp[i] = pack2(p0, p1, kBf16);
+        dd[i] = pack2(df.x, df.y, kBf16);
       }
+      kf::tc::st_32x32b_x16(s_col, pp);
+      kf::tc::st_32x32b_x16(s_col + 64, dd);
       kf::tc::wait_st();
       kf::tc::fence_before_sync();
-      kf::mbar_arrive(&bars.p_full[wg]);
+      kf::mbar_arrive(&bars.p_full[buf]);
     }
     // Epilogue: dV = acc, dK = gamma acc; warpgroup g writes columns [g D/2, (g + 1) D/2).
     if (ok) ok = wait(bars.acc_full, 0, abort);
