@@ -13,7 +13,8 @@ Secondary workloads in the same line (``workloads``): SANA linear attention conf
 (B=4,H=36,N=4096) and (B=2,H=70,N=16384), bf16 in/out, each step one ``qkv_attn_matmul`` call
 (replayed from a CUDA graph); FlashAttention JVP (B=4,H=16,N=4096,D in {64,128}, bf16,
 non-causal), each step one standalone ``flash_attention_jvp`` call (TFLOP/s over 5 GEMMs) or
-one ``flash_attention_fwd_jvp`` call (6 GEMMs).
+one ``flash_attention_fwd_jvp`` call (6 GEMMs); FlashAttention backward on the same configs, each
+step one ``_flash_attn_backward`` call (5 GEMMs), with flash_attn's own backward timed beside it.
 
 Multi-GPU: one process per GPU (torchrun), weak scaling -- every rank processes its own
 full-size shard, no collective on the data path; NCCL only takes the max of the per-rank
@@ -561,6 +562,122 @@ def fa_cpu_baseline(cfg, fused, seconds=5.0):
 
 
 # ---------------------------------------------------------------------------------------------
+# FlashAttention backward (FlashAttentionFunction.backward -> _flash_attn_backward), same configs
+# ---------------------------------------------------------------------------------------------
+FA_BWD_CONFIGS = tuple(dict(c, name=c["name"].replace("fajvp", "fabwd")) for c in FA_CONFIGS)
+FA_BWD_SMALL = tuple(dict(c, name=c["name"].replace("fajvp", "fabwd")) for c in FA_SMALL)
+
+
+def flash_attn_backward_tflops(q, k, v, out, lse, dout, scale, flops, steps=10):
+    """The flash_attn binary's backward on the same tensors (what the reference's
+    FlashAttentionFunction.backward calls); context only, None when it cannot run."""
+    try:
+        from flash_attn.flash_attn_interface import _flash_attn_backward as fa_bwd
+    except Exception:
+        return None
+    dq, dk, dv = (torch.empty_like(x) for x in (q, k, v))
+
+    def call():
+        fa_bwd(dout, q, k, v, out, lse, dq, dk, dv, 0.0, scale, False, -1, -1, 0.0, None, False)
+
+    try:
+        for _ in range(3):
+            call()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            call()
+        b.record()
+        b.synchronize()
+    except Exception:
+        return None
+    return round(flops / (a.elapsed_time(b) / steps / 1e3) / 1e12, 1)
+
+
+def bench_fa_bwd(args, dist, peaks, peak_kind, cfg):
+    from kernelforge_b200.flash_attention_jvp import custom as fa
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    B, H, N, D = cfg["B"], cfg["H"], cfg["N"], cfg["D"]
+    scale = D ** -0.5
+    gen = torch.Generator(device=dev).manual_seed(2026 + dist.rank)
+    q, k, v, dout = (torch.randn(B, N, H, D, device=dev, dtype=torch.bfloat16, generator=gen) for _ in range(4))
+    out, lse = fa.flash_attention(q, k, v, return_lse=True)
+    dq, dk, dv = (torch.empty_like(x) for x in (q, k, v))
+    call = lambda: fa._flash_attn_backward(dout, q, k, v, out, lse, dq, dk, dv, 0.0, scale, False)  # noqa: E731
+    timer = LaunchTimer()
+    ms, dom_ms = time_region(lambda _: timer.around(call), args.steps, args.warmup, dist, timer)
+    flops = fa_flops(cfg, 5)
+    peak = peaks["bf16_tflops"]
+    result = {
+        "value": round(dist.world * flops / (ms / 1e3) / 1e12, 1), "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
+        "gpu_launches": 3 * args.steps,
+        "config": {"B": B, "H": H, "N": N, "D": D, "causal": False, "dtype": "bf16",
+                   "call": "_flash_attn_backward (dq, dk, dv from dout and the saved O, LSE)",
+                   "flops_per_step": flops, "l2": "inputs larger than L2 (8 tensors of B*N*H*D bf16)"},
+        "roofline": roofline(flops, dom_ms, peak, "TFLOP/s", "tensor"),
+        "roofline_note": f"5 GEMMs x 2*B*H*N^2*D algorithmic flop per call (the kernels recompute S and dP in "
+                         f"both the dQ and the dK/dV kernel: 7 GEMMs executed); one call = 3 launches "
+                         f"(row statistics, dQ, dK/dV), {dom_ms * 1e3:.1f} us avg per call; "
+                         f"peak = {peak_kind} cuBLAS bf16 TFLOP/s (burst)",
+    }
+    if dist.rank == 0:
+        result["flash_attn_backward_tflops"] = flash_attn_backward_tflops(q, k, v, out, lse, dout, scale, flops)
+    if not args.no_e2e:
+        host = [t.cpu().pin_memory() for t in (dout, q, k, v, out)]
+        host_lse = lse.cpu().pin_memory()
+        dev_in = [torch.empty_like(t) for t in (dout, q, k, v, out)]
+        dev_lse = torch.empty_like(lse)
+        host_grads = [torch.empty_like(t, device="cpu").pin_memory() for t in (dq, dk, dv)]
+        h2d = sum(t.numel() * 2 for t in host) + host_lse.numel() * 4
+
+        def e2e_step(_):
+            for d_, h_ in zip(dev_in, host):
+                d_.copy_(h_, non_blocking=True)
+            dev_lse.copy_(host_lse, non_blocking=True)
+            fa._flash_attn_backward(*dev_in, dev_lse, dq, dk, dv, 0.0, scale, False)
+            for h_, g_ in zip(host_grads, (dq, dk, dv)):
+                h_.copy_(g_, non_blocking=True)
+
+        steps = max(3, min(args.steps, args.e2e_steps))
+        ems, _ = time_region(e2e_step, steps, args.warmup, dist)
+        result["e2e"] = {"value": round(dist.world * flops / (ems / 1e3) / 1e12, 2), "unit": "TFLOP/s",
+                         "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": sum(t.numel() * 2 for t in host_grads),
+                         "steps": steps, "ms_per_step": round(ems, 3),
+                         "api": "kernelforge_b200.flash_attention_jvp.custom._flash_attn_backward"}
+    if dist.world == 1 and dist.rank == 0 and not args.no_cpu:
+        result["cpu_baseline"] = fa_bwd_cpu_baseline(cfg, seconds=args.cpu_seconds / 2)
+    del q, k, v, dout, out, lse, dq, dk, dv
+    torch.cuda.empty_cache()
+    return result
+
+
+def fa_bwd_cpu_baseline(cfg, seconds=5.0):
+    """Float32 autograd through oracle.fa_jvp.attention on the host cores, one (batch, head) slice
+    of the config at a time."""
+    from oracle.fa_jvp import attention
+
+    cores = cpu_threads()
+    N, D = cfg["N"], cfg["D"]
+    g = torch.Generator().manual_seed(0)
+    q, k, v, dout = (torch.randn(1, N, 1, D, generator=g) for _ in range(4))
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        primals = tuple(x.clone().requires_grad_() for x in (q, k, v))
+        torch.autograd.grad(attention(*primals), primals, dout)
+        reps += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    flops = fa_flops(dict(cfg, B=1, H=1), 5)
+    return {"value": round(flops / dt / 1e12, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "sample": f"{reps} (batch, head) slices of N={N}, D={D} (of B={cfg['B']}, H={cfg['H']}), "
+                      f"torch.autograd through oracle/fa_jvp.py attention on torch CPU fp32, {cores} threads"}
+
+
+# ---------------------------------------------------------------------------------------------
 # reference arm: the reference algorithm on the host cores (oracle restatement)
 # ---------------------------------------------------------------------------------------------
 def run_reference(args):
@@ -606,7 +723,7 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("all", "rmsnorm", "sana", "fajvp"), default="all")
+    ap.add_argument("--workload", choices=("all", "rmsnorm", "sana", "fajvp", "fabwd"), default="all")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-e2e", action="store_true")
@@ -639,6 +756,9 @@ def main():
         for cfg in (FA_SMALL if CASE == "ncu-small" else FA_CONFIGS):
             workloads[cfg["name"] + "_standalone"] = bench_fa(args, dist, peaks, peak_kind, cfg, fused=False)
             workloads[cfg["name"] + "_fused"] = bench_fa(args, dist, peaks, peak_kind, cfg, fused=True)
+    if args.workload in ("all", "fabwd"):
+        for cfg in (FA_BWD_SMALL if CASE == "ncu-small" else FA_BWD_CONFIGS):
+            workloads[cfg["name"]] = bench_fa_bwd(args, dist, peaks, peak_kind, cfg)
     clocks = sampler.stop()
     if head is None:  # a single secondary workload was requested: promote it
         name, head = next(iter(workloads.items()))

@@ -143,14 +143,16 @@ __device__ void produce(const Bars<D>& bars, uint8_t* smem, const CUtensorMap* t
 }
 
 // D[128 x 64] = A[128 x D] B[64 x D]^T; A, B K-major 128-byte-swizzled tiles.
+// The descriptors are built once; each K step only adds a constant offset, which keeps the
+// issuing thread's instruction count per MMA small.
 template <int D>
 __device__ __forceinline__ void issue_scores(uint32_t a_addr, uint32_t b_addr, uint32_t d_col, uint32_t idesc) {
+  const uint64_t a_desc = kf::tc::desc_sw128(a_addr, 16, 1024), b_desc = kf::tc::desc_sw128(b_addr, 16, 1024);
 #pragma unroll
   for (int k = 0; k < D / 16; ++k) {
     const uint32_t aoff = (k >> 2) * kRows * 128 + (k & 3) * 32;
     const uint32_t boff = (k >> 2) * kTile * 128 + (k & 3) * 32;
-    kf::tc::mma_ss(d_col, kf::tc::desc_sw128(a_addr + aoff, 16, 1024), kf::tc::desc_sw128(b_addr + boff, 16, 1024),
-                   idesc, k > 0);
+    kf::tc::mma_ss(d_col, kf::tc::desc_advance(a_desc, aoff), kf::tc::desc_advance(b_desc, boff), idesc, k > 0);
   }
 }
 
@@ -161,10 +163,11 @@ __device__ __forceinline__ void issue_scores(uint32_t a_addr, uint32_t b_addr, u
 template <int D, bool kSplitA>
 __device__ __forceinline__ void issue_accumulate(uint32_t d_col, uint32_t a_col, uint32_t b_addr, uint32_t idesc,
                                                  uint32_t& started) {
+  const uint64_t b_desc = kf::tc::desc_sw128(b_addr, kTile * 128, 1024);
 #pragma unroll
   for (int kk = 0; kk < kTile / 16; ++kk) {
     const uint32_t acol = kSplitA ? (kk >> 1) * 32 + (kk & 1) * 8 : kk * 8;
-    kf::tc::mma_ts(d_col, a_col + acol, kf::tc::desc_sw128(b_addr + kk * 2048, kTile * 128, 1024), idesc, started);
+    kf::tc::mma_ts(d_col, a_col + acol, kf::tc::desc_advance(b_desc, kk * 2048), idesc, started);
     started = 1;
   }
 }

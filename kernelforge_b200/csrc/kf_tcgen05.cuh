@@ -43,6 +43,12 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr, uint32_t lbo_byte
   return d;
 }
 
+// The same descriptor for a matrix `bytes` further on (a multiple of 16; the start address field
+// never carries: shared-memory addresses stay below 2^18 bytes).
+__device__ __forceinline__ uint64_t desc_advance(uint64_t desc, uint32_t bytes) {
+  return desc + static_cast<uint64_t>(bytes >> 4);
+}
+
 // Instruction descriptor of kind::f16 with fp32 accumulation. ab_format: 0 = f16, 1 = bf16.
 __host__ __device__ constexpr uint32_t idesc_f16(int ab_format, int m, int n, bool a_mn_major,
                                                  bool b_mn_major) {

@@ -3,9 +3,10 @@
 FlashAttentionFunction.backward hands dout and the saved (q, k, v, out, lse) to
 ``_flash_attn_backward`` (flash_attention_jvp/custom.py:255-266), which this library serves with
 its own kernels (tcgen05 for head dims 64 and 128, mma.sync for the rest). Oracle: float64
-autograd through the CPU attention restatement (``oracle.fa_jvp.attention``). Tolerances: the reference harness's gradient bar
-(flash_attention_jvp/test.py:58-59; fp16 atol 3e-3 / rtol 1e-2, bf16 atol = rtol = 3e-2) with
-atol scaled by the largest reference gradient, since dK / dV sum over every query of a KV group.
+autograd through the CPU attention restatement (``oracle.fa_jvp.attention``). Tolerances: the
+reference harness's gradient bar (flash_attention_jvp/test.py:58-59; fp16 atol 3e-3 / rtol 1e-2,
+bf16 atol = rtol = 3e-2) with atol scaled by the largest reference gradient, since dK / dV sum
+over every query of a KV group.
 """
 
 import pytest
