@@ -6,7 +6,7 @@
 // (row_nlse = -LSE log2 e, row_ndelta = -rowsum(dO O), padded), two kernels, no atomics:
 //
 //   dq kernel    query-stationary: 128 query rows of one (batch, head) per CTA, 64-key tiles
-//                  S  = Q K^T,  dP = dO V^T           score MMAs, double-buffered in TMEM
+//                  S  = Q K^T,  dP = dO V^T           score MMAs into three TMEM buffers
 //                  P  = 2^(S gamma log2 e - LSE log2 e),  dS = P (dP - delta)
 //                  dQ += dS K                          A = dS (16-bit, TMEM), B = K (MN-major)
 //   dkdv kernel  key-stationary: 128 keys of one (batch, KV head) per CTA; the 64-query tiles of
@@ -208,12 +208,13 @@ __device__ __forceinline__ void store_row32(T* dst, const uint32_t (&acc)[32], f
 }
 
 // ============================================================================================
-// dQ. Tensor memory: [0, D) dQ accumulator | S_b at 128 + 128 b, dP_b 64 further |
-// dS_b (16-bit) at 384 + 32 b, keys [32 g, 32 g + 32) from warpgroup g at 384 + 32 b + 16 g.
-// dS has its own columns, so tile t+2's score MMAs only wait for tile t's softmax to have read
-// its scores.
+// dQ. Tensor memory: [0, D) dQ accumulator | three score buffers, S_b at 128 + 128 b and dP_b
+// 64 further. Warpgroup g reads keys [32 g, 32 g + 32) of S_b and dP_b and writes dS (16-bit)
+// over the first 16 of its 32 S_b columns, so tile t+3's score MMAs wait for tile t's
+// accumulating MMAs.
 // ============================================================================================
-constexpr uint32_t kDqAcc = 0, kDqBuf = 128, kDqDs = 384;
+constexpr uint32_t kDqAcc = 0, kDqBuf = 128;
+constexpr int kDqBufs = 3;
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -254,8 +255,8 @@ fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
       const uint32_t q_addr = kf::smem_u32(smem), do_addr = q_addr + C::kStatBytes;
       bool ok = wait_relaxed(bars.stat_full, 0, abort);
       for (int t = 0; ok && t < ntiles; ++t) {
-        const int buf = t & 1, st = t % C::kStages;
-        if (t >= 2 && !(ok = wait_relaxed(&bars.p_full[buf], ((t >> 1) - 1) & 1, abort))) break;
+        const int buf = t % kDqBufs, st = t % C::kStages;
+        if (t >= kDqBufs && !(ok = wait_relaxed(&bars.acc_done[buf], ((t / kDqBufs) - 1) & 1, abort))) break;
         if (!(ok = wait_relaxed(&bars.ring_full[st], (t / C::kStages) & 1, abort))) break;
         kf::tc::fence_after_sync();
         const uint32_t k_addr = kf::smem_u32(smem + C::kRingOffset + st * 2 * C::kTileBytes);
@@ -271,11 +272,11 @@ fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
       uint32_t started = 0;
       bool ok = true;
       for (int t = 0; ok && t < ntiles; ++t) {
-        const int buf = t & 1, st = t % C::kStages;
-        if (!(ok = wait_relaxed(&bars.p_full[buf], (t >> 1) & 1, abort))) break;
+        const int buf = t % kDqBufs, st = t % C::kStages;
+        if (!(ok = wait_relaxed(&bars.p_full[buf], (t / kDqBufs) & 1, abort))) break;
         kf::tc::fence_after_sync();
         const uint32_t k_addr = kf::smem_u32(smem + C::kRingOffset + st * 2 * C::kTileBytes);
-        issue_accumulate<D, false>(tmem + kDqAcc, tmem + kDqDs + 32 * buf, k_addr, idA, started);  // dQ += dS K
+        issue_accumulate<D, true>(tmem + kDqAcc, tmem + kDqBuf + 128 * buf, k_addr, idA, started);  // dQ += dS K
         kf::tc::commit(&bars.acc_done[buf]);
         kf::tc::commit(&bars.ring_empty[st]);
       }
@@ -293,11 +294,8 @@ fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
     const uint64_t nd2 = kf::f2_pack(ndelta, ndelta);
     bool ok = true;
     for (int t = 0; t < ntiles; ++t) {
-      const int buf = t & 1;
-      ok = wait(&bars.s_full[buf], (t >> 1) & 1, abort);
-      // The dS columns of this buffer were last read by tile t-2's accumulating MMAs.
-      if (ok && t >= 2) ok = wait(&bars.acc_done[buf], ((t >> 1) - 1) & 1, abort);
-      ok = __all_sync(0xffffffffu, ok);  // the tcgen05 copies below are .sync.aligned
+      const int buf = t % kDqBufs;
+      ok = __all_sync(0xffffffffu, wait(&bars.s_full[buf], (t / kDqBufs) & 1, abort));  // .sync.aligned copies follow
       if (!ok) break;
       kf::tc::fence_after_sync();
       const uint32_t s_col = lane_base + kDqBuf + 128 * buf + 32 * group;  // this warpgroup's 32 keys
@@ -321,7 +319,7 @@ fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
         const float2 df = kf::f2_unpack(ds);
         dd[i] = pack2(df.x, df.y, kBf16);
       }
-      kf::tc::st_32x32b_x16(lane_base + kDqDs + 32 * buf + 16 * group, dd);
+      kf::tc::st_32x32b_x16(s_col, dd);
       kf::tc::wait_st();
       kf::tc::fence_before_sync();
       kf::mbar_arrive(&bars.p_full[buf]);
