@@ -7,10 +7,10 @@
 //
 // One CTA owns 128 query rows of one (batch, head); in each softmax warpgroup one thread owns
 // one row (= one TMEM lane). Warp roles:
-//   warps 0..3  softmax warpgroup 0: even key tiles (score buffer 0)
-//   warps 4..7  softmax warpgroup 1: odd key tiles (score buffer 1)
-//               each turns scores into P, H (16-bit A operands written back to TMEM) and row
-//               sums; at the end both add their row sums and split the epilogue by columns
+//   warps 0..7  two softmax warpgroups; in the standalone JVP both work on every 64-key tile,
+//               warpgroup g on keys [32 g, 32 g + 32): they turn scores into P, H (16-bit A
+//               operands written back to TMEM) and row sums; at the end both add their row sums
+//               and split the epilogue by columns
 //   warp 8      TMA producer: Q, tQ once; rings of {K, tK} and {V, tV} tiles of 64 keys
 //   warp 9      TMEM owner; one thread issues the score MMAs (runs ahead while buffers allow)
 //   warp 10     one thread issues the output MMAs as each tile's P / H become ready
@@ -227,8 +227,8 @@ __device__ __forceinline__ void softmax_groups_sync() {
 // ============================================================================================
 // Standalone JVP. Tensor memory:
 //   [0, D) tO accumulator | S_b at 128 + 128 b, dS_b at 192 + 128 b | P_b at 384 + 64 b, H_b +32
-// P and H have their own columns, so tile j+1's score MMAs never wait for tile j's output MMAs.
-// Softmax warpgroup g handles the tiles j with (j & 1) == g.
+// P and H have their own columns, so tile j+2's score MMAs never wait for tile j's output MMAs.
+// Softmax warpgroup g handles keys [32 g, 32 g + 32) of every tile (P and H at +16 g).
 // ============================================================================================
 constexpr uint32_t kPCol = 384;
 
@@ -257,7 +257,7 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   const int ntiles = (k_end + kBN - 1) / kBN;
 
   if (threadIdx.x == 0) {
-    bars.init(kBM);
+    bars.init(2 * kBM);  // p_full: both softmax warpgroups work on every tile
     *abort_flag = 0;
     kf::fence_mbar_init();
   }
@@ -318,7 +318,7 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       kf::tc::commit(bars.acc_full);
     }
   } else {
-    const int group = warp >> 2;   // softmax warpgroup: tiles j with (j & 1) == group
+    const int group = warp >> 2;   // softmax warpgroup: keys [32 group, 32 group + 32) of every tile
     const int quarter = warp & 3;  // TMEM lanes [32 quarter, 32 quarter + 32)
     const int row = quarter * 32 + lane;
     const int qrow = q0 + row;
@@ -326,63 +326,51 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     const float lse_l2 = qrow < p.Nq ? p.lse_in[(static_cast<int64_t>(b) * p.Hq + h) * p.Nq + qrow] * kLog2e
                                      : __int_as_float(0x7f800000);
     const int limit = p.causal ? min(p.Nk, qrow + p.Nk - p.Nq + 1) : p.Nk;  // keys [0, limit) visible
-    const uint32_t s_col = lane_base + kBufCol + 128 * group;
-    const uint32_t ts_col = s_col + 64;
-    const uint32_t p_col = lane_base + kPCol + 64 * group;
-    const uint32_t h_col = p_col + 32;
     // Pairs of keys go through the f32x2 units: exponent argument, H and its row sum.
     const uint64_t c2 = kf::f2_pack(p.scale_log2, p.scale_log2), nl2 = kf::f2_pack(-lse_l2, -lse_l2);
     const uint64_t g2 = kf::f2_pack(p.scale, p.scale);
     uint64_t csum2 = kf::f2_pack(0.f, 0.f);
     bool ok = true;
-    for (int j = group; j < ntiles; j += 2) {
-      ok = kf::mbar_wait_or_abort(&bars.s_full[group], (j >> 1) & 1, &g_fa_error, abort_flag);
-      // This warpgroup's P / H columns were last read by tile j-2's output MMAs.
-      if (ok && j >= 2) ok = kf::mbar_wait_or_abort(&bars.pv_done[group], ((j >> 1) - 1) & 1, &g_fa_error, abort_flag);
+    for (int j = 0; j < ntiles; ++j) {
+      const int buf = j & 1;
+      ok = kf::mbar_wait_or_abort(&bars.s_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag);
+      // The P / H columns of this buffer were last read by tile j-2's output MMAs.
+      if (ok && j >= 2) ok = kf::mbar_wait_or_abort(&bars.pv_done[buf], ((j >> 1) - 1) & 1, &g_fa_error, abort_flag);
       // Warp-uniform outcome: the tcgen05 copies below are .sync.aligned.
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       kf::tc::fence_after_sync();
-      const int k0 = j * kBN;
-      const bool full = k0 + kBN <= limit;  // no masking inside this tile for this row
-      uint32_t sv[2][32], tv[2][32];
-      kf::tc::ld_32x32b_x32(s_col, sv[0]);
-      kf::tc::ld_32x32b_x32(s_col + 32, sv[1]);
-      if (has_h) {
-        kf::tc::ld_32x32b_x32(ts_col, tv[0]);
-        kf::tc::ld_32x32b_x32(ts_col + 32, tv[1]);
-      }
+      const uint32_t s_col = lane_base + kBufCol + 128 * buf + 32 * group;
+      const uint32_t p_col = lane_base + kPCol + 64 * buf + 16 * group;  // 16-bit: 16 columns per 32 keys
+      const int kc = j * kBN + 32 * group;
+      const bool full = kc + 32 <= limit;  // no masking inside these 32 keys for this row
+      uint32_t sr[32], tr[32], pp[16], hh[16];
+      kf::tc::ld_32x32b_x32(s_col, sr);
+      if (has_h) kf::tc::ld_32x32b_x32(s_col + 64, tr);
       kf::tc::wait_ld();
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const uint32_t (&sr)[32] = sv[c];
-        const uint32_t (&tr)[32] = tv[c];
-        uint32_t pp[16], hh[16];
-        const int kc = k0 + c * 32;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float2 a = kf::f2_unpack(kf::f2_fma(kf::f2_pack(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])),
-                                                    c2, nl2));
-          float p0 = ex2(a.x), p1 = ex2(a.y);
-          if (!full) {
-            p0 = kc + 2 * i < limit ? p0 : 0.f;
-            p1 = kc + 2 * i + 1 < limit ? p1 : 0.f;
-          }
-          pp[i] = pack2(p0, p1, kBf16);
-          if (has_h) {
-            const uint64_t hv = kf::f2_mul(
-                kf::f2_mul(kf::f2_pack(p0, p1), kf::f2_pack(__uint_as_float(tr[2 * i]), __uint_as_float(tr[2 * i + 1]))), g2);
-            csum2 = kf::f2_add(csum2, hv);
-            const float2 hf = kf::f2_unpack(hv);
-            hh[i] = pack2(hf.x, hf.y, kBf16);
-          }
+      for (int i = 0; i < 16; ++i) {
+        const float2 a = kf::f2_unpack(kf::f2_fma(kf::f2_pack(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])),
+                                                  c2, nl2));
+        float p0 = ex2(a.x), p1 = ex2(a.y);
+        if (!full) {
+          p0 = kc + 2 * i < limit ? p0 : 0.f;
+          p1 = kc + 2 * i + 1 < limit ? p1 : 0.f;
         }
-        kf::tc::st_32x32b_x16(p_col + c * 16, pp);
-        if (has_h) kf::tc::st_32x32b_x16(h_col + c * 16, hh);
+        pp[i] = pack2(p0, p1, kBf16);
+        if (has_h) {
+          const uint64_t hv = kf::f2_mul(
+              kf::f2_mul(kf::f2_pack(p0, p1), kf::f2_pack(__uint_as_float(tr[2 * i]), __uint_as_float(tr[2 * i + 1]))), g2);
+          csum2 = kf::f2_add(csum2, hv);
+          const float2 hf = kf::f2_unpack(hv);
+          hh[i] = pack2(hf.x, hf.y, kBf16);
+        }
       }
+      kf::tc::st_32x32b_x16(p_col, pp);
+      if (has_h) kf::tc::st_32x32b_x16(p_col + 32, hh);
       kf::tc::wait_st();
       kf::tc::fence_before_sync();
-      kf::mbar_arrive(&bars.p_full[group]);
+      kf::mbar_arrive(&bars.p_full[buf]);
     }
     const float2 cs = kf::f2_unpack(csum2);
     row_sums[group * kBM + row] = cs.x + cs.y;
