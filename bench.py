@@ -14,7 +14,8 @@ Secondary workloads in the same line (``workloads``): SANA linear attention conf
 (replayed from a CUDA graph); FlashAttention JVP (B=4,H=16,N=4096,D in {64,128}, bf16,
 non-causal), each step one standalone ``flash_attention_jvp`` call (TFLOP/s over 5 GEMMs) or
 one ``flash_attention_fwd_jvp`` call (6 GEMMs); FlashAttention backward on the same configs, each
-step one ``_flash_attn_backward`` call (5 GEMMs), with flash_attn's own backward timed beside it.
+step one ``_flash_attn_backward`` call (5 GEMMs); ``--flash-attn-comparator`` also times
+flash_attn's own backward on the same tensors.
 
 Multi-GPU: one process per GPU (torchrun), weak scaling -- every rank processes its own
 full-size shard, no collective on the data path; NCCL only takes the max of the per-rank
@@ -622,7 +623,7 @@ def bench_fa_bwd(args, dist, peaks, peak_kind, cfg):
                          f"(row statistics, dQ, dK/dV), {dom_ms * 1e3:.1f} us avg per call; "
                          f"peak = {peak_kind} cuBLAS bf16 TFLOP/s (burst)",
     }
-    if dist.rank == 0:
+    if dist.rank == 0 and args.flash_attn_comparator:
         result["flash_attn_backward_tflops"] = flash_attn_backward_tflops(q, k, v, out, lse, dout, scale, flops)
     if not args.no_e2e:
         host = [t.cpu().pin_memory() for t in (dout, q, k, v, out)]
@@ -728,6 +729,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--flash-attn-comparator", action="store_true",
+                    help="also time the flash_attn binary's backward on the fabwd tensors (context only; "
+                         "off by default so that the default run loads no attention library)")
     ap.add_argument("--case", choices=("full", "ncu-small"), default="full",
                     help="ncu-small: one small configuration per workload, for ncu --set full captures")
     args = ap.parse_args()
