@@ -728,9 +728,359 @@ sana_out_generic(const T* __restrict__ qkv, const float* __restrict__ final_vk, 
 }
 
 // ------------------------------------------------------------------------------------------
+// Fused path: one launch, one (batch, head) unit per CTA at a time, no workspace.
+//
+// When the batch x head units fill the SMs (or when the caller asks for it with splits = -1),
+// every CTA owns whole heads, so the K^T V reduction never leaves the CTA and no second launch
+// waits for it. Per unit, one TMA producer warp streams through a 16-stage ring of 8 KB stages
+//   phase 1: K and V boxes of 64 tokens x 32 channels (64-byte rows, 64-byte swizzle);
+//   phase 2: Q boxes of 128 tokens x 32 channels;
+// and 16 compute warps consume them in turn: stage number x of the CTA's whole sequence goes to
+// warp x mod 16, so the warp that waits for a ring slot's next fill is the one that released its
+// previous fill (that keeps every parity wait within one phase of the barrier):
+//   phase 1: VK += V^T relu(K) and ksum += relu(K) per warp (mma.sync m16n8k16, fp32), then the
+//            16 warp partials are summed in warp order in shared memory (deterministic);
+//   phase 2: every warp holds B = [VK ; ksum] as hi + lo 16-bit halves in registers (so the
+//            fp32 sums keep ~16 mantissa bits, as on the tcgen05 path) and, per 16 tokens,
+//            D = relu(Q) B_hi + relu(Q) B_lo, out = D[:, :32] / (D[:, 32] + eps), staged in
+//            shared memory and written with a TMA store.
+// The producer runs ahead into the next unit, so the next K/V tiles and the first Q tiles are
+// in flight while the warps reduce. fp16 inputs scale B by a power of two that keeps max|B|
+// below 2^14, with eps scaled alike.
+// ------------------------------------------------------------------------------------------
+constexpr int kFusedWarps = 16;                          // compute warps
+constexpr int kFusedThreads = 32 * (kFusedWarps + 1);    // + the TMA producer warp
+constexpr int kFusedStages = 16;
+constexpr int kFusedStageBytes = 8192;                   // K + V boxes (64 tokens), or a Q box (128 tokens)
+constexpr int kFusedKTok = 64;
+constexpr int kFusedQTok = 128;
+constexpr int kFusedSub = 16;                            // tokens per output store
+constexpr int kFusedPartBytes = kRows * kD * 4;          // one warp's [VK ; ksum] partial, fp32
+constexpr int kFusedSlotBytes = 5 * 1024;                // per-warp slot, 1024-byte aligned
+constexpr uint32_t kFusedBar = 2;                        // named barrier of the compute warps
+struct FusedSmem {
+  static constexpr int kRingOff = 0;
+  // Warp w's slot: its phase-1 partial, then (reused) its phase-2 output staging, two 16-token
+  // buffers at 1024-byte aligned offsets (the swizzled TMA store tiles need that alignment).
+  static constexpr int kPartOff = kFusedStages * kFusedStageBytes;
+  static constexpr int kRedOff = kPartOff + kFusedWarps * kFusedSlotBytes;  // reduced [VK ; ksum]
+  static constexpr int kBarOff = kRedOff + kFusedPartBytes + 16;            // + two max|B| words
+  static constexpr int kBytes = kBarOff + 2 * kFusedStages * 8 + 16 + 1024;
+};
+static_assert(kFusedPartBytes <= kFusedSlotBytes && 2 * 2048 <= kFusedSlotBytes, "slot sizes");
+
+// Byte offset of 16-byte chunk c of row r in a tile of 64-byte rows written with 64-byte swizzle.
+__device__ __forceinline__ uint32_t swz64(uint32_t row, uint32_t chunk) {
+  return row * 64 + ((chunk ^ ((row >> 1) & 3)) << 4);
+}
+
+template <typename T, typename O>
+__global__ void __launch_bounds__(kFusedThreads, 1)
+sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constant__ CUtensorMap q_map,
+                const __grid_constant__ CUtensorMap out_map, int B, int H, int N, float eps) {
+  constexpr bool kFp16 = std::is_same<T, __half>::value;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (kf::smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + FusedSmem::kBarOff);
+  uint64_t* empty = full + kFusedStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kFusedStages);
+  float* red = reinterpret_cast<float*>(smem + FusedSmem::kRedOff);
+  unsigned int* max_bits = reinterpret_cast<unsigned int*>(red + kRows * kD);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gid = lane >> 2, tig = lane & 3, sub = lane >> 3;
+  const int units = B * H;
+  const int kv_tiles = (N + kFusedKTok - 1) / kFusedKTok;
+  const int q_tiles = (N + kFusedQTok - 1) / kFusedQTok;
+  const int per_unit = kv_tiles + q_tiles;  // ring stages per unit
+
+  if (threadIdx.x == 0) {
+    kf::prefetch_tensormap(&kv_map);
+    kf::prefetch_tensormap(&q_map);
+    kf::prefetch_tensormap(&out_map);
+    for (int s = 0; s < kFusedStages; ++s) {
+      kf::mbar_init(&full[s], 1);
+      kf::mbar_init(&empty[s], 1);
+    }
+    *abort_flag = 0;
+    max_bits[0] = max_bits[1] = 0u;
+    kf::fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kFusedWarps) {
+    // ---- TMA producer (one thread): every unit's K/V tiles, then its Q tiles ----
+    if (lane == 0) {
+      int seq = 0;
+      for (int u = blockIdx.x; u < units; u += gridDim.x) {
+        const int b = u / H, h = u % H;
+        for (int i = 0; i < per_unit; ++i, ++seq) {
+          const int st = seq % kFusedStages;
+          if (seq >= kFusedStages &&
+              !kf::mbar_wait_or_abort<true>(&empty[st], ((seq / kFusedStages) - 1) & 1, &g_sana_error, abort_flag))
+            return;
+          uint8_t* base = smem + FusedSmem::kRingOff + st * kFusedStageBytes;
+          kf::mbar_arrive_expect_tx(&full[st], kFusedStageBytes);
+          if (i < kv_tiles) {
+            kf::tma_load_4d(base, &kv_map, &full[st], h * kD, 1, i * kFusedKTok, b);
+            kf::tma_load_4d(base + kFusedStageBytes / 2, &kv_map, &full[st], h * kD, 2, i * kFusedKTok, b);
+          } else {
+            kf::tma_load_4d(base, &q_map, &full[st], h * kD, 0, (i - kv_tiles) * kFusedQTok, b);
+          }
+        }
+      }
+    }
+    return;
+  }
+
+  // ---- compute warps ----
+  uint8_t* part = smem + FusedSmem::kPartOff + warp * kFusedSlotBytes;  // this warp's slot
+  int seq0 = 0;  // ring sequence number of the unit's first stage
+  bool ok = true;
+  int parity = 0;  // max|B| word of this unit (two words: one is reset while the other is in use)
+  for (int u = blockIdx.x; u < units; u += gridDim.x, seq0 += per_unit, parity ^= 1) {
+    const int b = u / H, h = u % H;
+    // Phase 1: this warp's K/V tiles.
+    float acc[2][4][4];
+    float ksum[4];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      ksum[nt] = 0.f;
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[mt][nt][j] = 0.f;
+    }
+    for (int i = (warp - seq0 % kFusedWarps + kFusedWarps) % kFusedWarps; i < kv_tiles; i += kFusedWarps) {
+      const int seq = seq0 + i, st = seq % kFusedStages;
+      if (ok) ok = __all_sync(0xffffffffu, kf::mbar_wait_or_abort(&full[st], (seq / kFusedStages) & 1,
+                                                                  &g_sana_error, abort_flag));
+      if (!ok) break;
+      const uint32_t kbase = kf::smem_u32(smem + FusedSmem::kRingOff + st * kFusedStageBytes);
+      const uint32_t vbase = kbase + kFusedStageBytes / 2;
+#pragma unroll
+      for (int ks = 0; ks < kFusedKTok / 16; ++ks) {
+        uint32_t a[2][4];
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          // A = V^T (M = v channel, K = token): transposed 8x8 loads of token-major rows.
+          const int row = ks * 16 + (lane & 7) + (sub >> 1) * 8;
+          kf::ldsm_x4_t(vbase + swz64(row, mt * 2 + (sub & 1)), a[mt][0], a[mt][1], a[mt][2], a[mt][3]);
+        }
+        uint32_t bf[4][2];
+#pragma unroll
+        for (int np = 0; np < 2; ++np) {
+          // B = relu(K) (K = token, N = k channel), two n-tiles per x4 load.
+          const int row = ks * 16 + (lane & 7) + (sub & 1) * 8;
+          kf::ldsm_x4_t(kbase + swz64(row, np * 2 + (sub >> 1)), bf[2 * np][0], bf[2 * np][1], bf[2 * np + 1][0],
+                        bf[2 * np + 1][1]);
+        }
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          bf[nt][0] = kf::Mma<T>::relu2(bf[nt][0]);
+          bf[nt][1] = kf::Mma<T>::relu2(bf[nt][1]);
+          const float2 x = kf::Mma<T>::to_f2(bf[nt][0]);
+          const float2 y = kf::Mma<T>::to_f2(bf[nt][1]);
+          ksum[nt] += (x.x + x.y) + (y.x + y.y);
+        }
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+          for (int nt = 0; nt < 4; ++nt) kf::Mma<T>::run(acc[mt][nt], a[mt], bf[nt]);
+      }
+      __syncwarp();
+      if (lane == 0) kf::mbar_arrive(&empty[st]);
+    }
+    // This warp's partial [VK ; ksum] into its slot (its previous output stores must have read it).
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      ksum[nt] += __shfl_xor_sync(0xffffffffu, ksum[nt], 1);
+      ksum[nt] += __shfl_xor_sync(0xffffffffu, ksum[nt], 2);
+    }
+    if (lane == 0) kf::tma_store_wait_read0();
+    __syncwarp();
+    float* pw = reinterpret_cast<float*>(part);
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const int r = mt * 16 + gid, c = nt * 8 + tig * 2;
+        *reinterpret_cast<float2*>(pw + r * kD + c) = make_float2(acc[mt][nt][0], acc[mt][nt][1]);
+        *reinterpret_cast<float2*>(pw + (r + 8) * kD + c) = make_float2(acc[mt][nt][2], acc[mt][nt][3]);
+      }
+    if (tig == 0) {
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) pw[kD * kD + nt * 8 + gid] = ksum[nt];
+    }
+    kf::named_bar_sync(kFusedBar, 32 * kFusedWarps);
+    // Every compute thread is past the previous unit's read of the other word.
+    if (threadIdx.x == 0) max_bits[parity ^ 1] = 0u;
+    // Sum of the 16 partials in warp order, and max|B| for the fp16 scale.
+    float m = 0.f;
+    for (int e = threadIdx.x; e < kRows * kD; e += 32 * kFusedWarps) {
+      float s = 0.f;
+#pragma unroll
+      for (int w = 0; w < kFusedWarps; ++w)
+        s += reinterpret_cast<const float*>(smem + FusedSmem::kPartOff + w * kFusedSlotBytes)[e];
+      red[e] = s;
+      m = fmaxf(m, fabsf(s));
+    }
+    if (kFp16) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (lane == 0) atomicMax(&max_bits[parity], __float_as_uint(m));  // non-negative floats order as integers
+    }
+    kf::named_bar_sync(kFusedBar, 32 * kFusedWarps);
+    const float scale = operand_scale(__uint_as_float(max_bits[parity]), kFp16);
+    const float eps_s = eps * scale;
+    // B fragments (K = q channel c, N = output row r: VK[r][c], r = 32 is ksum[c], rows 33..39 zero)
+    // as hi and lo halves.
+    uint32_t bhi[2][5][2], blo[2][5][2];
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks)
+#pragma unroll
+      for (int nt = 0; nt < 5; ++nt) {
+        const int r = nt * 8 + gid;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int c = ks * 16 + tig * 2 + half * 8;
+          float x0 = 0.f, x1 = 0.f;
+          if (r <= kD) {
+            x0 = red[r * kD + c] * scale;
+            x1 = red[r * kD + c + 1] * scale;
+          }
+          bhi[ks][nt][half] = kf::Mma<T>::from_f2(x0, x1);
+          const float2 hf = kf::Mma<T>::to_f2(bhi[ks][nt][half]);
+          blo[ks][nt][half] = kf::Mma<T>::from_f2(x0 - hf.x, x1 - hf.y);
+        }
+      }
+    // Phase 2: this warp's Q tiles, 16 tokens at a time.
+    int nstore = 0;
+    for (int j = (warp - (seq0 + kv_tiles) % kFusedWarps + kFusedWarps) % kFusedWarps; j < q_tiles;
+         j += kFusedWarps) {
+      const int seq = seq0 + kv_tiles + j, st = seq % kFusedStages;
+      if (ok) ok = __all_sync(0xffffffffu, kf::mbar_wait_or_abort(&full[st], (seq / kFusedStages) & 1,
+                                                                  &g_sana_error, abort_flag));
+      if (!ok) break;
+      const uint32_t qbase = kf::smem_u32(smem + FusedSmem::kRingOff + st * kFusedStageBytes);
+#pragma unroll 1
+      for (int m16 = 0; m16 < kFusedQTok / kFusedSub; ++m16) {
+        uint32_t a[2][4];
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+          const int row = m16 * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          kf::ldsm_x4(qbase + swz64(row, ks * 2 + (lane >> 4)), a[ks][0], a[ks][1], a[ks][2], a[ks][3]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) a[ks][e] = kf::Mma<T>::relu2(a[ks][e]);
+        }
+        if (m16 == kFusedQTok / kFusedSub - 1) {  // the stage is no longer read
+          __syncwarp();
+          if (lane == 0) kf::mbar_arrive(&empty[st]);
+        }
+        float d[5][4];
+#pragma unroll
+        for (int nt = 0; nt < 5; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) d[nt][e] = 0.f;
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks)
+#pragma unroll
+          for (int nt = 0; nt < 5; ++nt) {
+            kf::Mma<T>::run(d[nt], a[ks], bhi[ks][nt]);
+            kf::Mma<T>::run(d[nt], a[ks], blo[ks][nt]);
+          }
+        // Denominator D[row][32]: column 0 of n-tile 4, held by the quad's first thread.
+        const float den0 = __shfl_sync(0xffffffffu, d[4][0], lane & ~3);
+        const float den1 = __shfl_sync(0xffffffffu, d[4][2], lane & ~3);
+        const float inv0 = __frcp_rn(den0 + eps_s), inv1 = __frcp_rn(den1 + eps_s);
+        // Stage 16 tokens x 32 channels in buffer (nstore & 1) once its previous store has read it.
+        uint8_t* stage = part + (nstore & 1) * (kFusedSub * kD * int(sizeof(O)));
+        if (lane == 0) kf::tma_store_wait_read1();
+        __syncwarp();
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          const int c = nt * 8 + tig * 2;
+          if constexpr (sizeof(O) == 4) {
+            // rows of 128 bytes, 128-byte swizzle
+            const uint32_t off = (c & 3) * 4;
+            *reinterpret_cast<float2*>(stage + gid * 128 + (((c >> 2) ^ (gid & 7)) << 4) + off) =
+                make_float2(d[nt][0] * inv0, d[nt][1] * inv0);
+            *reinterpret_cast<float2*>(stage + (gid + 8) * 128 + (((c >> 2) ^ ((gid + 8) & 7)) << 4) + off) =
+                make_float2(d[nt][2] * inv1, d[nt][3] * inv1);
+          } else {
+            // rows of 64 bytes, 64-byte swizzle
+            const uint32_t off = (c & 7) * 2;
+            *reinterpret_cast<uint32_t*>(stage + swz64(gid, c >> 3) + off) =
+                kf::Mma<O>::from_f2(d[nt][0] * inv0, d[nt][1] * inv0);
+            *reinterpret_cast<uint32_t*>(stage + swz64(gid + 8, c >> 3) + off) =
+                kf::Mma<O>::from_f2(d[nt][2] * inv1, d[nt][3] * inv1);
+          }
+        }
+        kf::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          kf::tma_store_3d(&out_map, stage, h * kD, j * kFusedQTok + m16 * kFusedSub, b);
+          kf::tma_store_commit();
+        }
+        ++nstore;
+      }
+    }
+  }
+  if (lane == 0) kf::tma_store_wait_read0();  // shared memory outlives the stores' reads
+}
+
+// ------------------------------------------------------------------------------------------
 // Host side
 // ------------------------------------------------------------------------------------------
 constexpr int kFastStages = 3;
+
+// Fused path (no workspace): one CTA per SM over the batch x head units.
+bool fused_fills_device(int64_t B, int64_t H) {
+  const int64_t units = B * H, sms = kf_host::current_device_sms();
+  const int64_t waves = (units + sms - 1) / sms;
+  return units * 10 >= waves * sms * 9;  // at least 90% of the CTA slots of the last wave busy
+}
+
+template <typename T>
+int launch_fused(const void* qkv, void* out, int B, int H, int N, float eps, int out_dtype, cudaStream_t stream) {
+  const int C = H * kD;
+  const int in_dtype = std::is_same<T, __half>::value ? KF_DTYPE_F16 : KF_DTYPE_BF16;
+  const size_t es = 2;
+  // qkv [B, N, 3, C] as (channel, q/k/v, token, batch); boxes of one head (32 channels,
+  // 64 bytes) x 64 tokens (K, V) or x 128 tokens (Q).
+  CUtensorMap kv_map, q_map, out_map;
+  const uint64_t dims[4] = {static_cast<uint64_t>(C), 3, static_cast<uint64_t>(N), static_cast<uint64_t>(B)};
+  const uint64_t strides[3] = {C * es, 3 * C * es, static_cast<uint64_t>(N) * 3 * C * es};
+  const uint32_t kv_box[4] = {static_cast<uint32_t>(kD), 1, kFusedKTok, 1};
+  const uint32_t q_box[4] = {static_cast<uint32_t>(kD), 1, kFusedQTok, 1};
+  if (!kf_host::encode_tiled(&kv_map, kf_host::map_type(in_dtype), 4, qkv, dims, strides, kv_box,
+                             CU_TENSOR_MAP_SWIZZLE_64B) ||
+      !kf_host::encode_tiled(&q_map, kf_host::map_type(in_dtype), 4, qkv, dims, strides, q_box,
+                             CU_TENSOR_MAP_SWIZZLE_64B))
+    return KF_ERR_CUDA;
+  // out [B, N, C]: boxes of one head x 16 tokens, one per compute warp and 16 tokens.
+  const size_t os = kf::dtype_size(out_dtype);
+  const uint64_t odims[3] = {static_cast<uint64_t>(C), static_cast<uint64_t>(N), static_cast<uint64_t>(B)};
+  const uint64_t ostrides[2] = {C * os, static_cast<uint64_t>(N) * C * os};
+  const uint32_t obox[3] = {static_cast<uint32_t>(kD), kFusedSub, 1};
+  if (!kf_host::encode_tiled(&out_map, kf_host::map_type(out_dtype), 3, out, odims, ostrides, obox,
+                             os == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
+    return KF_ERR_CUDA;
+  const int grid = static_cast<int>(std::min<int64_t>(static_cast<int64_t>(B) * H, kf_host::current_device_sms()));
+  auto run = [&](auto kernel) -> int {
+    const int prep = kf_host::prepare_kernel(reinterpret_cast<const void*>(kernel), kFusedThreads, FusedSmem::kBytes,
+                                             nullptr);
+    if (prep != KF_OK) return prep;
+    kernel<<<grid, kFusedThreads, FusedSmem::kBytes, stream>>>(kv_map, q_map, out_map, B, H, N, eps);
+    KF_LAUNCH_CHECK();
+    return KF_OK;
+  };
+  switch (out_dtype) {
+    case KF_DTYPE_F32: return run(sana_head_fused<T, float>);
+    case KF_DTYPE_F16: return run(sana_head_fused<T, __half>);
+    default: return run(sana_head_fused<T, __nv_bfloat16>);
+  }
+}
 
 // ws: the workspace laid out by fast_layout(B, H, S); its counters are zero between calls.
 template <typename T, int G>
@@ -898,6 +1248,11 @@ KF_API int kf_sana_linattn_fwd(const void* qkv, void* out, void* workspace, size
 
   const bool fast = d == kD && (in_dtype == KF_DTYPE_BF16 || in_dtype == KF_DTYPE_F16) &&
                     H * kD >= 64 && N >= kTok && kf::aligned(qkv, 16) && kf::aligned(out, 16);
+  if (fast && (splits == -1 || (splits == 0 && fused_fills_device(B, H)))) {
+    // Whole heads per CTA, one launch, no workspace traffic.
+    if (in_dtype == KF_DTYPE_BF16) return launch_fused<__nv_bfloat16>(qkv, out, B, H, N, eps, out_dtype, s);
+    return launch_fused<__half>(qkv, out, B, H, N, eps, out_dtype, s);
+  }
   if (fast) {
     // Two heads (one 128-byte TMA box) per CTA measured at or above four heads on every
     // benchmark shape.

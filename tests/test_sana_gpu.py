@@ -95,6 +95,32 @@ def test_explicit_splits_repeat_calls_and_determinism(kf, splits):
     check_exact(first, qkv, 8, 32)
 
 
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32, torch.float16])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("b,n,h", [(1, 1024, 36), (2, 1000, 3), (1, 64, 2), (1, 65, 2), (3, 333, 5),
+                                   (2, 1500, 100)])
+def test_fused_path_shapes(kf, b, n, h, dtype, out_dtype):
+    """splits = -1 selects the one-launch path (whole heads per CTA) on any fast-path shape; with
+    200 (batch, head) units the CTAs walk several units each."""
+    g = torch.Generator().manual_seed(b * 7000 + n + h)
+    qkv = torch.randn(b, n, 3, h * 32, generator=g).to(dtype)
+    fn = kf.QKVAttnMatmul(b, h, 32, n, 1e-15, NAMES[dtype], NAMES[out_dtype], splits=-1)
+    q = qkv.cuda()
+    first = fn(q).clone()
+    second = fn(q).clone()
+    assert first.shape == (b, n, h * 32) and first.dtype == out_dtype
+    assert torch.equal(first, second)  # deterministic: fixed warp order in the reduction
+    check_exact(first, qkv, h, 32)
+
+
+def test_fused_and_split_paths_agree(kf):
+    g = torch.Generator().manual_seed(13)
+    qkv = torch.randn(2, 2048, 3, 6 * 32, generator=g).to(torch.bfloat16).cuda()
+    fused = kf.QKVAttnMatmul(2, 6, 32, 2048, 1e-15, "bfloat16", "float", splits=-1)(qkv)
+    split = kf.QKVAttnMatmul(2, 6, 32, 2048, 1e-15, "bfloat16", "float", splits=4)(qkv)
+    torch.testing.assert_close(fused, split, rtol=1e-5, atol=1e-6)
+
+
 def test_reference_harness_form(kf):
     """SANA test.py:50-82 at N=4096, C=1152, B=1, bf16 in / bf16 out."""
     torch.manual_seed(0)
