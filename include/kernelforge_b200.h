@@ -75,13 +75,17 @@ int kf_rmsnorm_fwd(const void* x, const void* weight, void* y,
  *   out [batch, seq_len, heads*dim] in out_dtype
  *   VK_h = sum_t v_t relu(k_t)^T,  ksum_h = sum_t relu(k_t)           (fp32 accumulation)
  *   out[t, h*dim + r] = (VK_h relu(q_t))_r / (ksum_h . relu(q_t) + eps)
- * The token axis is split into `splits` chunks (splits <= 0: a default for the shape). On the
- * bf16/fp16 head_dim-32 path the chunks of a head group form one thread-block cluster (at
- * most 8) and reduce through distributed shared memory; the workspace then holds only the
- * reduced fp32 K^T V and ksum. Other shapes keep fp32 partials in the workspace and reduce
- * them in the last CTA to arrive (per-head arrival counters). Size the workspace with
- * kf_sana_linattn_workspace_size and zero-fill it once before its first use; every call
- * leaves it ready for the next one. Calls that share a workspace must be ordered on one stream.
+ * `splits` picks the schedule of the bf16/fp16 head_dim-32 path:
+ *   0       automatic: the one-launch path when batch*heads fills the GPU's SMs (at least 90%
+ *           of the CTA slots of the last wave), else the split path with a default split count;
+ *   -1      the one-launch path: each CTA owns whole (batch, head) units, reduces K^T V and
+ *           ksum in shared memory and writes the output (the workspace is not touched);
+ *   s > 0   the split path: the token axis in s chunks whose fp32 partials go through the
+ *           workspace to a tcgen05 epilogue launch.
+ * Other shapes (fp32 input, other head dims) keep fp32 partials in the workspace and reduce them
+ * in the last CTA to arrive (per-head arrival counters). Size the workspace with
+ * kf_sana_linattn_workspace_size and zero-fill it once before its first use; every call leaves
+ * it ready for the next one. Calls that share a workspace must be ordered on one stream.
  * dim must divide 128 (the reference's constraint, custom.py:350-351).
  * ---------------------------------------------------------------------------------------- */
 size_t kf_sana_linattn_workspace_size(int64_t batch, int64_t heads, int64_t dim, int64_t seq_len,

@@ -27,6 +27,9 @@ class QKVAttnMatmul:
     arrival counter per head group), allocated zero-filled on first use per device and reused
     by every later call, so the callable is CUDA-graph capturable after its first call.
     Calls through one callable must be ordered on one stream (they share the workspace).
+    ``splits``: None or 0 picks the schedule automatically, -1 forces the one-launch path
+    (whole heads per CTA, no workspace traffic), a positive count the split path with that many
+    token chunks (``kf_sana_linattn_fwd`` in include/kernelforge_b200.h).
     """
 
     def __init__(self, batch, heads, dim, seq_len, eps, dtype, output_dtype, splits=None):

@@ -768,6 +768,10 @@ struct FusedSmem {
   static constexpr int kBytes = kBarOff + 2 * kFusedStages * 8 + 16 + 1024;
 };
 static_assert(kFusedPartBytes <= kFusedSlotBytes && 2 * 2048 <= kFusedSlotBytes, "slot sizes");
+// Ring slot x % kFusedStages is consumed by warp x % kFusedWarps: with equal counts the warp that
+// waits for a slot's next fill is the one that released the previous fill, so no parity wait on
+// `full` can see a phase two fills old and no extra arrival can reach `empty`.
+static_assert(kFusedStages == kFusedWarps, "ring depth must equal the number of compute warps");
 
 // Byte offset of 16-byte chunk c of row r in a tile of 64-byte rows written with 64-byte swizzle.
 __device__ __forceinline__ uint32_t swz64(uint32_t row, uint32_t chunk) {
