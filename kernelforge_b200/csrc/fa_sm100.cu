@@ -84,11 +84,14 @@ template <int D> struct Bars {
     acc_full = pv_done + 2;
     tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
   }
-  __device__ void init(int p_arrivals) const {
+  // k_extra / v_extra: arrivals besides the producer's that complete a K or V stage. The kernels
+  // fold "score buffer j & 1 free" into k_full and "P / H of tile j written" into v_full, so each
+  // MMA thread waits on one barrier per tile.
+  __device__ void init(int p_arrivals, int k_extra, int v_extra) const {
     using C = Cfg<D>;
     kf::mbar_init(q_full, 1);
-    for (int s = 0; s < C::kKStages; ++s) kf::mbar_init(&k_full[s], 1);
-    for (int s = 0; s < C::kVStages; ++s) kf::mbar_init(&v_full[s], 1);
+    for (int s = 0; s < C::kKStages; ++s) kf::mbar_init(&k_full[s], 1 + k_extra);
+    for (int s = 0; s < C::kVStages; ++s) kf::mbar_init(&v_full[s], 1 + v_extra);
     for (int i = 0; i < 2; ++i) {
       kf::mbar_init(&s_full[i], 1);
       kf::mbar_init(&p_full[i], p_arrivals);
@@ -257,7 +260,12 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   const int ntiles = (k_end + kBN - 1) / kBN;
 
   if (threadIdx.x == 0) {
-    bars.init(2 * kBM);  // p_full: both softmax warpgroups work on every tile
+    // Each MMA thread waits on one barrier per tile (a probe costs ~200 cycles while the tensor
+    // cores read shared memory): k_full[j & 1] completes when K / tK of tile j have landed AND
+    // every softmax thread has read tile j-2's scores out of buffer j & 1; v_full[j & 1] when
+    // V / tV of tile j have landed AND every softmax thread has written tile j's P and H.
+    bars.init(1, 2 * kBM, 2 * kBM);  // p_full is not used here
+    // Buffers 0 and 1 start free: the softmax threads' share of tiles 0 and 1's k_full phases.
     *abort_flag = 0;
     kf::fence_mbar_init();
   }
@@ -266,6 +274,10 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   __syncthreads();
   kf::tc::fence_after_sync();
   const uint32_t tmem = *bars.tmem_slot;
+  if (warp < 8) {
+    kf::mbar_arrive(&bars.k_full[0]);
+    kf::mbar_arrive(&bars.k_full[1]);
+  }
 
   if (warp == kProducerWarp) {
     if (lane == 0)
@@ -273,12 +285,12 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                  q0, b, ntiles, abort_flag);
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
-      // Scores of tile j into buffer j & 1 once tile j-2's softmax has read that buffer.
+      // Scores of tile j into buffer j & 1 once K of tile j has landed and tile j-2's softmax has
+      // read that buffer (one barrier).
       const uint32_t q_addr = kf::smem_u32(smem), tq_addr = q_addr + C::kQBytes;
       bool ok = kf::mbar_wait_or_abort<true>(bars.q_full, 0, &g_fa_error, abort_flag);
       for (int j = 0; ok && j < ntiles; ++j) {
         const int buf = j & 1;
-        if (j >= 2 && !(ok = kf::mbar_wait_or_abort<true>(&bars.p_full[buf], ((j >> 1) - 1) & 1, &g_fa_error, abort_flag))) break;
         if (!(ok = kf::mbar_wait_or_abort<true>(&bars.k_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag))) break;
         kf::tc::fence_after_sync();
         const uint32_t k_base = kf::smem_u32(smem + C::kKOffset + buf * 2 * C::kTileBytes);
@@ -289,13 +301,13 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     }
   } else if (warp == kPvWarp) {
     if (lane == 0) {
-      // tO += P tV + H V for tile j once its P / H are written and its V / tV have arrived.
+      // tO += P tV + H V for tile j once its V / tV have arrived and its P / H are written (one
+      // barrier).
       constexpr uint32_t idPV = kf::tc::idesc_f16(kBf16 ? 1 : 0, kBM, D, false, true);
       uint32_t acc_started = 0;
       bool ok = true;
       for (int j = 0; ok && j < ntiles; ++j) {
         const int buf = j & 1;
-        if (!(ok = kf::mbar_wait_or_abort<true>(&bars.p_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag))) break;
         if (!(ok = kf::mbar_wait_or_abort<true>(&bars.v_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag))) break;
         kf::tc::fence_after_sync();
         const uint32_t v_base = kf::smem_u32(smem + C::kVOffset + buf * 2 * C::kTileBytes);
@@ -348,6 +360,9 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       kf::tc::ld_32x32b_x32(s_col, sr);
       if (has_h) kf::tc::ld_32x32b_x32(s_col + 64, tr);
       kf::tc::wait_ld();
+      // This thread's share of buffer j & 1 is read: tile j+2's scores may go there.
+      kf::tc::fence_before_sync();
+      kf::mbar_arrive(&bars.k_full[buf]);
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const float2 a = kf::f2_unpack(kf::f2_fma(kf::f2_pack(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])),
@@ -370,7 +385,7 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       if (has_h) kf::tc::st_32x32b_x16(p_col + 32, hh);
       kf::tc::wait_st();
       kf::tc::fence_before_sync();
-      kf::mbar_arrive(&bars.p_full[buf]);
+      kf::mbar_arrive(&bars.v_full[buf]);
     }
     const float2 cs = kf::f2_unpack(csum2);
     row_sums[group * kBM + row] = cs.x + cs.y;
@@ -472,7 +487,11 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
   const int ntiles = (k_end + kBN - 1) / kBN;
 
   if (threadIdx.x == 0) {
-    bars.init(2 * kBM);
+    // k_full[j & 1] completes when K / tK of tile j have landed AND tile j-2's output MMAs (which
+    // read the P / H written over score buffer j & 1) are done: the output thread commits to it.
+    // v_full[j & 1] completes when V / tV of tile j have landed AND every softmax thread has
+    // written tile j's P and H. p_full is not used here.
+    bars.init(1, 1, 2 * kBM);
     *abort_flag = 0;
     kf::fence_mbar_init();
   }
@@ -488,13 +507,12 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
                  q0, b, ntiles, abort_flag);
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
-      // Scores of tile j into buffer j & 1 once tile j-2's output MMAs have consumed the P / H
-      // that overwrote that buffer.
+      // Scores of tile j into buffer j & 1 once K of tile j has landed and tile j-2's output MMAs
+      // have consumed the P / H that overwrote that buffer (one barrier).
       const uint32_t q_addr = kf::smem_u32(smem), tq_addr = q_addr + C::kQBytes;
       bool ok = kf::mbar_wait_or_abort<true>(bars.q_full, 0, &g_fa_error, abort_flag);
       for (int j = 0; ok && j < ntiles; ++j) {
         const int buf = j & 1;
-        if (j >= 2 && !(ok = kf::mbar_wait_or_abort<true>(&bars.pv_done[buf], ((j >> 1) - 1) & 1, &g_fa_error, abort_flag))) break;
         if (!(ok = kf::mbar_wait_or_abort<true>(&bars.k_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag))) break;
         kf::tc::fence_after_sync();
         const uint32_t k_base = kf::smem_u32(smem + C::kKOffset + buf * 2 * C::kTileBytes);
@@ -510,9 +528,11 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       constexpr uint32_t kU = FusedCols<D>::kU, kG = FusedCols<D>::kG;
       uint32_t u_started = 0, g_started = 0;
       bool ok = true;
+      // Score buffers 0 and 1 start free: this thread's share of tiles 0 and 1's k_full phases.
+      kf::mbar_arrive(&bars.k_full[0]);
+      kf::mbar_arrive(&bars.k_full[1]);
       for (int j = 0; ok && j < ntiles; ++j) {
         const int buf = j & 1;
-        if (!(ok = kf::mbar_wait_or_abort<true>(&bars.p_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag))) break;
         if (!(ok = kf::mbar_wait_or_abort<true>(&bars.v_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag))) break;
         kf::tc::fence_after_sync();
         const uint32_t v_base = kf::smem_u32(smem + C::kVOffset + buf * 2 * C::kTileBytes);
@@ -544,6 +564,7 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
           }
         }
         kf::tc::commit(&bars.pv_done[buf]);
+        kf::tc::commit(&bars.k_full[buf]);  // score buffer j & 1 is free for tile j+2
       }
       kf::tc::commit(bars.acc_full);
     }
@@ -654,7 +675,7 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         kf::tc::wait_st();
       }
       kf::tc::fence_before_sync();
-      kf::mbar_arrive(&bars.p_full[buf]);
+      kf::mbar_arrive(&bars.v_full[buf]);
     }
     // Combine the two warpgroups' row sums.
     const float2 lf = kf::f2_unpack(l2), rf = kf::f2_unpack(r2);
