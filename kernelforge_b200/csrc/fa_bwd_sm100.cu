@@ -61,11 +61,10 @@ constexpr int kMaxBufs = 3;
 
 template <int D> struct Bars {
   uint64_t* stat_full;
-  uint64_t* ring_full;   // [kStages]
+  uint64_t* ring_full;   // [kStages] the tile's operands landed AND its score buffer is free
   uint64_t* ring_empty;  // [kStages] the accumulating MMAs of the stage's tile completed
   uint64_t* s_full;      // [kMaxBufs] score MMAs of tile t complete
   uint64_t* p_full;      // [kMaxBufs] softmax of tile t done (scores read, 16-bit operands written)
-  uint64_t* acc_done;    // [kMaxBufs] accumulating MMAs of tile t complete
   uint64_t* acc_full;
   uint32_t* tmem_slot;
   int* abort_flag;
@@ -76,8 +75,7 @@ template <int D> struct Bars {
     ring_empty = ring_full + C::kStages;
     s_full = ring_empty + C::kStages;
     p_full = s_full + kMaxBufs;
-    acc_done = p_full + kMaxBufs;
-    acc_full = acc_done + kMaxBufs;
+    acc_full = p_full + kMaxBufs;
     tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
     abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
   }
@@ -85,13 +83,14 @@ template <int D> struct Bars {
     using C = Cfg<D>;
     kf::mbar_init(stat_full, 1);
     for (int s = 0; s < C::kStages; ++s) {
-      kf::mbar_init(&ring_full[s], 1);
+      // Two arrivals: the producer's (with the TMA bytes) and the accumulating thread's commit
+      // that frees the tile's score buffer, so the score thread waits on one barrier per tile.
+      kf::mbar_init(&ring_full[s], 2);
       kf::mbar_init(&ring_empty[s], 1);
     }
     for (int i = 0; i < kMaxBufs; ++i) {
       kf::mbar_init(&s_full[i], 1);
       kf::mbar_init(&p_full[i], 2 * kRows);  // both softmax warpgroups
-      kf::mbar_init(&acc_done[i], 1);
     }
     kf::mbar_init(acc_full, 1);
     *abort_flag = 0;
@@ -256,7 +255,6 @@ fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
       bool ok = wait_relaxed(bars.stat_full, 0, abort);
       for (int t = 0; ok && t < ntiles; ++t) {
         const int buf = t % kDqBufs, st = t % C::kStages;
-        if (t >= kDqBufs && !(ok = wait_relaxed(&bars.acc_done[buf], ((t / kDqBufs) - 1) & 1, abort))) break;
         if (!(ok = wait_relaxed(&bars.ring_full[st], (t / C::kStages) & 1, abort))) break;
         kf::tc::fence_after_sync();
         const uint32_t k_addr = kf::smem_u32(smem + C::kRingOffset + st * 2 * C::kTileBytes);
@@ -271,14 +269,18 @@ fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
       constexpr uint32_t idA = kf::tc::idesc_f16(kBf16 ? 1 : 0, kRows, D, false, true);
       uint32_t started = 0;
       bool ok = true;
+      // Score buffers start free: the first kDqBufs tiles' buffer arrivals.
+      for (int t = 0; t < kDqBufs; ++t) kf::mbar_arrive(&bars.ring_full[t % C::kStages]);
       for (int t = 0; ok && t < ntiles; ++t) {
         const int buf = t % kDqBufs, st = t % C::kStages;
         if (!(ok = wait_relaxed(&bars.p_full[buf], (t / kDqBufs) & 1, abort))) break;
         kf::tc::fence_after_sync();
         const uint32_t k_addr = kf::smem_u32(smem + C::kRingOffset + st * 2 * C::kTileBytes);
         issue_accumulate<D, true>(tmem + kDqAcc, tmem + kDqBuf + 128 * buf, k_addr, idA, started);  // dQ += dS K
-        kf::tc::commit(&bars.acc_done[buf]);
         kf::tc::commit(&bars.ring_empty[st]);
+        // Buffer `buf` is free for tile t + kDqBufs (that tile's ring stage: its phase is the
+        // next one to complete there, as the score thread already waited for tile t).
+        kf::tc::commit(&bars.ring_full[(t + kDqBufs) % C::kStages]);
       }
       kf::tc::commit(bars.acc_full);
     }
@@ -399,7 +401,6 @@ fa_bwd_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_
       bool ok = wait_relaxed(bars.stat_full, 0, abort);
       for (int t = 0; ok && t < ntiles; ++t) {
         const int buf = t % kBufs, st = t % C::kStages;
-        if (t >= kBufs && !(ok = wait_relaxed(&bars.acc_done[buf], ((t / kBufs) - 1) & 1, abort))) break;
         if (!(ok = wait_relaxed(&bars.ring_full[st], (t / C::kStages) & 1, abort))) break;
         kf::tc::fence_after_sync();
         const uint32_t q_addr = kf::smem_u32(smem + C::kRingOffset + st * 2 * C::kTileBytes);
@@ -414,6 +415,8 @@ fa_bwd_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_
       constexpr uint32_t idA = kf::tc::idesc_f16(kBf16 ? 1 : 0, kRows, D, false, true);
       uint32_t v_started = 0, k_started = 0;
       bool ok = true;
+      // Score buffers start free: the first kBufs tiles' buffer arrivals.
+      for (int t = 0; t < kBufs; ++t) kf::mbar_arrive(&bars.ring_full[t % C::kStages]);
       for (int t = 0; ok && t < ntiles; ++t) {
         const int buf = t % kBufs, st = t % C::kStages;
         if (!(ok = wait_relaxed(&bars.p_full[buf], (t / kBufs) & 1, abort))) break;
@@ -422,8 +425,8 @@ fa_bwd_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_
         const uint32_t s_col = tmem + kBuf + 128 * buf;
         issue_accumulate<D, true>(tmem + kDv, s_col, q_addr + C::kTileBytes, idA, v_started);  // dV += P^T dO
         issue_accumulate<D, true>(tmem + kDk, s_col + 64, q_addr, idA, k_started);             // dK += dS^T Q
-        kf::tc::commit(&bars.acc_done[buf]);
         kf::tc::commit(&bars.ring_empty[st]);
+        kf::tc::commit(&bars.ring_full[(t + kBufs) % C::kStages]);  // buffer free for tile t + kBufs
       }
       kf::tc::commit(bars.acc_full);
     }
