@@ -56,11 +56,21 @@ SANA_CONFIGS = (
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from `ncu --set full`
 # captures of the `--case ncu-small` shapes. RMSNorm: the 32768 x 8192 capture (536,926,976 read +
 # 486,499,328 written) scaled by rows to the dominant 262144 x 8192 launch (x 8; every row is read
-# once and written once, so traffic is linear in rows). SANA cfg1: both kernels of one call at the
-# bench size itself (producer 75,511,552 + 2,177,024; epilogue 40,378,368 + 3,662,848; most of
-# the 37.7 MB output is still in L2 when the epilogue ends).
+# once and written once, so traffic is linear in rows). SANA cfg1: the one-launch kernel of a call
+# at the bench size itself (113,272,832 read + 7,127,808 written; most of the 37.7 MB output is
+# still in L2 when the kernel ends).
 RMSNORM_NCU_TRAFFIC_BYTES = 8 * (536_926_976 + 486_499_328)
-SANA_NCU_TRAFFIC_BYTES = {"sana_cfg1": 75_511_552 + 2_177_024 + 40_378_368 + 3_662_848}
+SANA_NCU_TRAFFIC_BYTES = {"sana_cfg1": 113_272_832 + 7_127_808}
+
+
+def sana_launches_per_call(B, H):
+    """Kernel launches of one default-schedule qkv_attn_matmul call (bf16, head dim 32): the
+    library picks its one-launch path when batch x heads fills at least 90% of the CTA slots of
+    the last wave of SMs (kf_sana_linattn_fwd, splits = 0), else producer + epilogue."""
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    units = B * H
+    waves = -(-units // sms)
+    return 1 if units * 10 >= waves * sms * 9 else 2
 
 
 # ---------------------------------------------------------------------------------------------
@@ -362,7 +372,7 @@ def bench_sana(args, dist, peaks, peak_kind, cfg):
     copies = max(1, math.ceil(2 * L2_BYTES / one))  # rotate inputs so each step's data is not L2-hot
     qkvs = [torch.randn(B, N, 3, H * D, device=dev, dtype=torch.bfloat16, generator=gen) for _ in range(copies)]
     fn = qkv_attn_matmul(B, H, D, N, dtype="bfloat16", output_dtype="bfloat16")
-    # One call is two launches of tens of microseconds: the device-resident number replays
+    # One call is one or two launches of tens of microseconds: the device-resident number replays
     # calls from CUDA graphs so that it measures the kernels, not Python or graph launches. A
     # replay runs `cpg` consecutive calls (one call = one step) on rotating inputs; the timed
     # region is exactly args.steps calls. e2e below keeps the plain per-call API.
@@ -386,15 +396,17 @@ def bench_sana(args, dist, peaks, peak_kind, cfg):
     nbytes = sana_bytes(cfg)
     value = dist.world * nbytes / (ms / 1e3) / 1e9
     flops = 4 * B * H * N * D * (D + 1)
+    launches = sana_launches_per_call(B, H)
     result = {
         "value": round(value, 1), "unit": "GB/s", "ms_per_step": round(ms, 4),
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": launches * args.steps,
         "config": {"B": B, "H": H, "N": N, "D": D, "dtype_in": "bf16", "dtype_out": "bf16",
                    "input_copies": copies, "l2": f"{copies} rotating qkv copies ({copies * one / 1e6:.0f} MB)",
                    "launch": f"CUDA graphs of {cpg} consecutive qkv_attn_matmul calls (one call = one step)"},
         "roofline": roofline(nbytes, dom_ms, peaks["hbm_gbs"], "GB/s", "hbm",
                              SANA_NCU_TRAFFIC_BYTES.get(cfg["name"])),
-        "roofline_note": f"producer + epilogue launches of one call, {dom_ms * 1e3:.1f} us avg over graph replays; "
+        "roofline_note": f"{'the one-launch kernel' if launches == 1 else 'producer + epilogue launches'} of one "
+                         f"call, {dom_ms * 1e3:.1f} us avg over graph replays; "
                          f"{flops / (dom_ms / 1e3) / 1e12:.1f} TFLOP/s of algorithmic FMA work; "
                          f"peak = {peak_kind} HBM copy GB/s",
     }
