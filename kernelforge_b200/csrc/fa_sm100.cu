@@ -149,6 +149,12 @@ __device__ void produce(const Bars<D>& bars, uint8_t* smem, const CUtensorMap* t
   }
 }
 
+// 128-byte-swizzle descriptor of the matrix `off` bytes past `base`: the descriptor of `base`
+// (loop-invariant, built once per tile) plus the offset, so each K step costs one add.
+__device__ __forceinline__ uint64_t dsw(uint32_t base, uint32_t off, uint32_t lbo) {
+  return kf::tc::desc_advance(kf::tc::desc_sw128(base, lbo, 1024), off);
+}
+
 // Score MMAs of tile j: S = Q K^T into s_col, then dS = tQ K^T + Q tK^T into ts_col.
 template <int D>
 __device__ __forceinline__ void issue_s(uint32_t q_addr, uint32_t k_base, uint32_t s_col, uint32_t idS) {
@@ -156,7 +162,7 @@ __device__ __forceinline__ void issue_s(uint32_t q_addr, uint32_t k_base, uint32
   for (int k = 0; k < D / 16; ++k) {
     const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
     const uint32_t koff = (k >> 2) * kBN * 128 + (k & 3) * 32;
-    kf::tc::mma_ss(s_col, kf::tc::desc_sw128(q_addr + off, 16, 1024), kf::tc::desc_sw128(k_base + koff, 16, 1024),
+    kf::tc::mma_ss(s_col, dsw(q_addr, off, 16), dsw(k_base, koff, 16),
                    idS, k > 0);
   }
 }
@@ -169,8 +175,8 @@ __device__ __forceinline__ void issue_ds(uint32_t q_addr, uint32_t tq_addr, uint
     for (int k = 0; k < D / 16; ++k) {
       const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
       const uint32_t koff = (k >> 2) * kBN * 128 + (k & 3) * 32;
-      kf::tc::mma_ss(ts_col, kf::tc::desc_sw128(tq_addr + off, 16, 1024),
-                     kf::tc::desc_sw128(k_base + koff, 16, 1024), idS, started);
+      kf::tc::mma_ss(ts_col, dsw(tq_addr, off, 16),
+                     dsw(k_base, koff, 16), idS, started);
       started = 1;
     }
   }
@@ -179,8 +185,8 @@ __device__ __forceinline__ void issue_ds(uint32_t q_addr, uint32_t tq_addr, uint
     for (int k = 0; k < D / 16; ++k) {
       const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
       const uint32_t koff = (k >> 2) * kBN * 128 + (k & 3) * 32;
-      kf::tc::mma_ss(ts_col, kf::tc::desc_sw128(q_addr + off, 16, 1024),
-                     kf::tc::desc_sw128(k_base + tile_bytes + koff, 16, 1024), idS, started);
+      kf::tc::mma_ss(ts_col, dsw(q_addr, off, 16),
+                     dsw(k_base + tile_bytes, koff, 16), idS, started);
       started = 1;
     }
   }
@@ -197,13 +203,13 @@ __device__ __forceinline__ void issue_scores(uint32_t q_addr, uint32_t tq_addr, 
     const uint32_t idS2 = kf::tc::idesc_f16(bf16 ? 1 : 0, kBM, 2 * kBN, false, false);
 #pragma unroll
     for (int k = 0; k < D / 16; ++k)
-      kf::tc::mma_ss(s_col, kf::tc::desc_sw128(q_addr + k * 32, 16, 1024), kf::tc::desc_sw128(k_base + k * 32, 16, 1024),
+      kf::tc::mma_ss(s_col, dsw(q_addr, k * 32, 16), dsw(k_base, k * 32, 16),
                      idS2, k > 0);
     if (has_tq) {
 #pragma unroll
       for (int k = 0; k < D / 16; ++k)
-        kf::tc::mma_ss(s_col + 64, kf::tc::desc_sw128(tq_addr + k * 32, 16, 1024),
-                       kf::tc::desc_sw128(k_base + k * 32, 16, 1024), idS, 1);
+        kf::tc::mma_ss(s_col + 64, dsw(tq_addr, k * 32, 16),
+                       dsw(k_base, k * 32, 16), idS, 1);
     }
     return;
   }
@@ -316,12 +322,12 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         for (int kk = 0; kk < kBN / 16; ++kk) {
           if (has_tv) {
             kf::tc::mma_ts(tmem + kAccCol, p_col + kk * 8,
-                           kf::tc::desc_sw128(v_base + C::kTileBytes + kk * 2048, kBN * 128, 1024), idPV, acc_started);
+                           dsw(v_base + C::kTileBytes, kk * 2048, kBN * 128), idPV, acc_started);
             acc_started = 1;
           }
           if (has_h) {
             kf::tc::mma_ts(tmem + kAccCol, p_col + 32 + kk * 8,
-                           kf::tc::desc_sw128(v_base + kk * 2048, kBN * 128, 1024), idPV, acc_started);
+                           dsw(v_base, kk * 2048, kBN * 128), idPV, acc_started);
             acc_started = 1;
           }
         }
@@ -542,10 +548,10 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         for (int kk = 0; kk < kBN / 16; ++kk) {
           // keys [16 kk, 16 kk + 16): warpgroup kk / 2 wrote them at columns 32 (kk / 2) + 8 (kk % 2)
           const uint32_t acol = (kk >> 1) * 32 + (kk & 1) * 8;
-          const uint64_t vdesc = kf::tc::desc_sw128(v_base + kk * 2048, kBN * 128, 1024);
+          const uint64_t vdesc = dsw(v_base, kk * 2048, kBN * 128);
           if (FusedCols<D>::kMerge && has_tv) {
             // [U | G] += E [V | tV]: V and tV are the two 64-wide MN blocks of one operand
-            kf::tc::mma_ts(tmem + kU, p_col + acol, kf::tc::desc_sw128(v_base + kk * 2048, C::kTileBytes, 1024),
+            kf::tc::mma_ts(tmem + kU, p_col + acol, dsw(v_base, kk * 2048, C::kTileBytes),
                            idPV2, u_started);
             u_started = g_started = 1;
             if (has_h) kf::tc::mma_ts(tmem + kG, h_col + acol, vdesc, idPV, 1);
@@ -559,7 +565,7 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
           }
           if (has_tv) {
             kf::tc::mma_ts(tmem + kG, p_col + acol,
-                           kf::tc::desc_sw128(v_base + C::kTileBytes + kk * 2048, kBN * 128, 1024), idPV, g_started);
+                           dsw(v_base + C::kTileBytes, kk * 2048, kBN * 128), idPV, g_started);
             g_started = 1;
           }
         }
