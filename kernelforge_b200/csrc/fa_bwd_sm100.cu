@@ -1,5 +1,6 @@
 // FlashAttention backward (reverse-mode VJP) on the 5th-generation tensor cores
-// (tcgen05 + TMEM + TMA), head dims 64 and 128, fp16 / bf16, causal (bottom-right), GQA.
+// (tcgen05 + TMEM + TMA), head dims 64 and 72..128 (the latter on zero-padded D = 128 tiles),
+// fp16 / bf16, causal (bottom-right), GQA.
 //
 // Replaces the flash_attn binary's _flash_attn_backward that FlashAttentionFunction.backward
 // calls (flash_attention_jvp/custom.py:255-266). After the row-statistics pass of fa_bwd.cu
@@ -190,12 +191,13 @@ __device__ __forceinline__ bool wait_relaxed(uint64_t* bar, uint32_t parity, con
 }
 
 // Epilogue store of 32 accumulator columns of one row: out = acc * mul (zeros when nothing was
-// accumulated).
+// accumulated); only the first `valid` columns exist (head dims below the kernel's padded one).
 template <typename T>
-__device__ __forceinline__ void store_row32(T* dst, const uint32_t (&acc)[32], float mul, bool any) {
+__device__ __forceinline__ void store_row32(T* dst, const uint32_t (&acc)[32], float mul, bool any, int valid) {
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
 #pragma unroll
   for (int v = 0; v < 4; ++v) {
+    if (v * 8 >= valid) break;
     uint32_t w[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -331,14 +333,14 @@ fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
     ok = __all_sync(0xffffffffu, ok);
     if (ok) {
       kf::tc::fence_after_sync();
-      T* dst = static_cast<T*>(p.dq) + ((static_cast<int64_t>(b) * p.Nq + qrow) * p.Hq + h) * D;
+      T* dst = static_cast<T*>(p.dq) + ((static_cast<int64_t>(b) * p.Nq + qrow) * p.Hq + h) * p.D;  // real head dim
 #pragma unroll
       for (int cc = 0; cc < D / 64; ++cc) {
         const int c = group * (D / 64) + cc;  // 32-column chunk
         uint32_t ar[32];
         kf::tc::ld_32x32b_x32(lane_base + kDqAcc + c * 32, ar);
         kf::tc::wait_ld();
-        if (qrow < p.Nq) store_row32<T>(dst + c * 32, ar, p.scale, ntiles > 0);
+        if (qrow < p.Nq) store_row32<T>(dst + c * 32, ar, p.scale, ntiles > 0, p.D - c * 32);
       }
     }
   }
@@ -480,7 +482,7 @@ fa_bwd_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_
     ok = __all_sync(0xffffffffu, ok);
     if (ok) {
       kf::tc::fence_after_sync();
-      const int64_t off = ((static_cast<int64_t>(b) * p.Nk + key) * p.Hkv + kvh) * D;
+      const int64_t off = ((static_cast<int64_t>(b) * p.Nk + key) * p.Hkv + kvh) * p.D;  // real head dim
       T* dk = static_cast<T*>(p.dk) + off;
       T* dv = static_cast<T*>(p.dv) + off;
 #pragma unroll
@@ -491,8 +493,8 @@ fa_bwd_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_
         kf::tc::ld_32x32b_x32(lane_base + kDk + c * 32, br);
         kf::tc::wait_ld();
         if (key < p.Nk) {
-          store_row32<T>(dv + c * 32, ar, 1.f, ntiles > 0);
-          store_row32<T>(dk + c * 32, br, p.scale, ntiles > 0);
+          store_row32<T>(dv + c * 32, ar, 1.f, ntiles > 0, p.D - c * 32);
+          store_row32<T>(dk + c * 32, br, p.scale, ntiles > 0, p.D - c * 32);
         }
       }
     }
@@ -510,10 +512,11 @@ int launch(const BwdArgs& a, int dtype, cudaStream_t stream) {
   using C = Cfg<D>;
   {
     CUtensorMap mq, mdo, mk, mv;
-    if (!encode_bnhd(&mq, a.q, dtype, a.B, a.Nq, a.Hq, D, kRows) ||
-        !encode_bnhd(&mdo, a.dout, dtype, a.B, a.Nq, a.Hq, D, kRows) ||
-        !encode_bnhd(&mk, a.k, dtype, a.B, a.Nk, a.Hkv, D, kTile) ||
-        !encode_bnhd(&mv, a.v, dtype, a.B, a.Nk, a.Hkv, D, kTile))
+    // The maps carry the real head dim: boxes past it (D < 128) read as zeros.
+    if (!encode_bnhd(&mq, a.q, dtype, a.B, a.Nq, a.Hq, a.D, kRows) ||
+        !encode_bnhd(&mdo, a.dout, dtype, a.B, a.Nq, a.Hq, a.D, kRows) ||
+        !encode_bnhd(&mk, a.k, dtype, a.B, a.Nk, a.Hkv, a.D, kTile) ||
+        !encode_bnhd(&mv, a.v, dtype, a.B, a.Nk, a.Hkv, a.D, kTile))
       return KF_ERR_CUDA;
     auto kernel = fa_bwd_dq_sm100_kernel<T, D>;
     const int prep = kf_host::prepare_kernel(reinterpret_cast<const void*>(kernel), kThreads, C::kSmemBytes, nullptr);
@@ -523,10 +526,10 @@ int launch(const BwdArgs& a, int dtype, cudaStream_t stream) {
   }
   {
     CUtensorMap mk, mv, mq, mdo;
-    if (!encode_bnhd(&mk, a.k, dtype, a.B, a.Nk, a.Hkv, D, kRows) ||
-        !encode_bnhd(&mv, a.v, dtype, a.B, a.Nk, a.Hkv, D, kRows) ||
-        !encode_bnhd(&mq, a.q, dtype, a.B, a.Nq, a.Hq, D, kTile) ||
-        !encode_bnhd(&mdo, a.dout, dtype, a.B, a.Nq, a.Hq, D, kTile))
+    if (!encode_bnhd(&mk, a.k, dtype, a.B, a.Nk, a.Hkv, a.D, kRows) ||
+        !encode_bnhd(&mv, a.v, dtype, a.B, a.Nk, a.Hkv, a.D, kRows) ||
+        !encode_bnhd(&mq, a.q, dtype, a.B, a.Nq, a.Hq, a.D, kTile) ||
+        !encode_bnhd(&mdo, a.dout, dtype, a.B, a.Nq, a.Hq, a.D, kTile))
       return KF_ERR_CUDA;
     auto kernel = fa_bwd_dkdv_sm100_kernel<T, D>;
     const int prep = kf_host::prepare_kernel(reinterpret_cast<const void*>(kernel), kThreads, C::kSmemBytes, nullptr);
@@ -552,7 +555,8 @@ int kf_internal_fa_bwd_error(unsigned int* code) {
 
 namespace kf::fa {
 
-bool sm100_bwd_supported(const BwdArgs& a) { return a.D == 64 || a.D == 128; }
+// Head dims 64 and 72..128: 72..120 run the D = 128 kernels on zero-padded tiles.
+bool sm100_bwd_supported(const BwdArgs& a) { return a.D == 64 || (a.D > 64 && a.D <= 128); }
 
 int launch_sm100_bwd(const BwdArgs& a, int dtype, cudaStream_t s) {
   if (dtype == KF_DTYPE_BF16) return a.D == 64 ? launch<__nv_bfloat16, 64>(a, dtype, s) : launch<__nv_bfloat16, 128>(a, dtype, s);

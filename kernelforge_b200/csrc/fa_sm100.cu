@@ -402,7 +402,7 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     ok = __all_sync(0xffffffffu, ok);
     if (ok) {
       kf::tc::fence_after_sync();
-      const int64_t roff = ((static_cast<int64_t>(b) * p.Nq + qrow) * p.Hq + h) * D;
+      const int64_t roff = ((static_cast<int64_t>(b) * p.Nq + qrow) * p.Hq + h) * p.D;  // real head dim
       const T* orow = static_cast<const T*>(p.o_in) + roff;
       T* trow = static_cast<T*>(p.to_out) + roff;
 #pragma unroll
@@ -414,6 +414,7 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         if (qrow < p.Nq) {
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
+            if (c * 32 + v * 8 >= p.D) break;  // padding columns (D < 128): zero, not stored
             const uint4 o = *reinterpret_cast<const uint4*>(orow + c * 32 + v * 8);
             const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
             uint32_t tw[4];
@@ -699,7 +700,7 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       kf::tc::fence_after_sync();
       const float inv_l = l_tot > 0.f ? 1.f / l_tot : 0.f;
       const float rl = r_tot * inv_l;
-      const int64_t roff = ((static_cast<int64_t>(b) * p.Nq + qrow) * p.Hq + h) * D;
+      const int64_t roff = ((static_cast<int64_t>(b) * p.Nq + qrow) * p.Hq + h) * p.D;  // real head dim
       T* orow = static_cast<T*>(p.o_out) + roff;
       T* trow = kJvp ? static_cast<T*>(p.to_out) + roff : nullptr;
       if (group == 0 && qrow < p.Nq) {
@@ -717,6 +718,7 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         if (qrow < p.Nq) {
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
+            if (col + v * 8 >= p.D) break;  // padding columns (D < 128): zero, not stored
             uint32_t ow[4], tw[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
@@ -749,12 +751,13 @@ template <typename T, int D>
 int launch_jvp(const FaArgs& a, int dtype, cudaStream_t stream) {
   using C = Cfg<D>;
   CUtensorMap mq, mtq, mk, mtk, mv, mtv;
-  if (!encode_bnhd(&mq, a.q, dtype, a.B, a.Nq, a.Hq, D, kBM) ||
-      !encode_bnhd(&mtq, a.tq ? a.tq : a.q, dtype, a.B, a.Nq, a.Hq, D, kBM) ||
-      !encode_bnhd(&mk, a.k, dtype, a.B, a.Nk, a.Hkv, D, kBN) ||
-      !encode_bnhd(&mtk, a.tk ? a.tk : a.k, dtype, a.B, a.Nk, a.Hkv, D, kBN) ||
-      !encode_bnhd(&mv, a.v, dtype, a.B, a.Nk, a.Hkv, D, kBN) ||
-      !encode_bnhd(&mtv, a.tv ? a.tv : a.v, dtype, a.B, a.Nk, a.Hkv, D, kBN))
+  // The maps carry the real head dim: boxes past it (D < 128) read as zeros.
+  if (!encode_bnhd(&mq, a.q, dtype, a.B, a.Nq, a.Hq, a.D, kBM) ||
+      !encode_bnhd(&mtq, a.tq ? a.tq : a.q, dtype, a.B, a.Nq, a.Hq, a.D, kBM) ||
+      !encode_bnhd(&mk, a.k, dtype, a.B, a.Nk, a.Hkv, a.D, kBN) ||
+      !encode_bnhd(&mtk, a.tk ? a.tk : a.k, dtype, a.B, a.Nk, a.Hkv, a.D, kBN) ||
+      !encode_bnhd(&mv, a.v, dtype, a.B, a.Nk, a.Hkv, a.D, kBN) ||
+      !encode_bnhd(&mtv, a.tv ? a.tv : a.v, dtype, a.B, a.Nk, a.Hkv, a.D, kBN))
     return KF_ERR_CUDA;
   auto kernel = fa_jvp_sm100_kernel<T, D>;
   const int prep = kf_host::prepare_kernel(reinterpret_cast<const void*>(kernel), kThreads, C::kSmemBytes, nullptr);
@@ -769,12 +772,13 @@ template <typename T, int D, bool kJvp>
 int launch_fused(const FaArgs& a, int dtype, cudaStream_t stream) {
   using C = Cfg<D>;
   CUtensorMap mq, mtq, mk, mtk, mv, mtv;
-  if (!encode_bnhd(&mq, a.q, dtype, a.B, a.Nq, a.Hq, D, kBM) ||
-      !encode_bnhd(&mtq, a.tq ? a.tq : a.q, dtype, a.B, a.Nq, a.Hq, D, kBM) ||
-      !encode_bnhd(&mk, a.k, dtype, a.B, a.Nk, a.Hkv, D, kBN) ||
-      !encode_bnhd(&mtk, a.tk ? a.tk : a.k, dtype, a.B, a.Nk, a.Hkv, D, kBN) ||
-      !encode_bnhd(&mv, a.v, dtype, a.B, a.Nk, a.Hkv, D, kBN) ||
-      !encode_bnhd(&mtv, a.tv ? a.tv : a.v, dtype, a.B, a.Nk, a.Hkv, D, kBN))
+  // The maps carry the real head dim: boxes past it (D < 128) read as zeros.
+  if (!encode_bnhd(&mq, a.q, dtype, a.B, a.Nq, a.Hq, a.D, kBM) ||
+      !encode_bnhd(&mtq, a.tq ? a.tq : a.q, dtype, a.B, a.Nq, a.Hq, a.D, kBM) ||
+      !encode_bnhd(&mk, a.k, dtype, a.B, a.Nk, a.Hkv, a.D, kBN) ||
+      !encode_bnhd(&mtk, a.tk ? a.tk : a.k, dtype, a.B, a.Nk, a.Hkv, a.D, kBN) ||
+      !encode_bnhd(&mv, a.v, dtype, a.B, a.Nk, a.Hkv, a.D, kBN) ||
+      !encode_bnhd(&mtv, a.tv ? a.tv : a.v, dtype, a.B, a.Nk, a.Hkv, a.D, kBN))
     return KF_ERR_CUDA;
   auto kernel = fa_fused_sm100_kernel<T, D, kJvp>;
   const int prep = kf_host::prepare_kernel(reinterpret_cast<const void*>(kernel), kThreads, C::kSmemBytes, nullptr);
@@ -800,12 +804,16 @@ int kf_internal_fa_error(unsigned int* code) {
 
 namespace kf::fa {
 
+// Head dims 64 and 72..128 (multiples of 8): 72..120 run the D = 128 kernels on zero-padded
+// tiles (TMA fills the columns past D with zeros; the epilogues store only real columns).
+bool sm100_head_dim(int d) { return d == 64 || (d > 64 && d <= 128); }
+
 bool sm100_jvp_supported(const FaArgs& a) {
-  return (a.D == 64 || a.D == 128) && (a.tq != nullptr || a.tk != nullptr || a.tv != nullptr);
+  return sm100_head_dim(a.D) && (a.tq != nullptr || a.tk != nullptr || a.tv != nullptr);
 }
 
 bool sm100_fused_supported(const FaArgs& a, int mode) {
-  if (a.D != 64 && a.D != 128) return false;
+  if (!sm100_head_dim(a.D)) return false;
   if (mode == kModeFwd) return true;
   return a.tq != nullptr || a.tk != nullptr || a.tv != nullptr;
 }

@@ -38,6 +38,9 @@ CASES = (
     (1, 200, 450, 4, 1, 128, True, None),
     (1, 1000, 1000, 2, 2, 128, False, None),
     (3, 130, 70, 6, 3, 64, True, 0.3),
+    (1, 300, 257, 4, 2, 96, True, None),
+    (2, 129, 200, 2, 2, 72, False, 0.11),
+    (1, 256, 256, 2, 1, 120, False, None),
 )
 
 

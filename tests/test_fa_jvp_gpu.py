@@ -32,6 +32,9 @@ CASES = (
     (1, 17, 29, 2, 2, 16, False, 0.05),
     (1, 23, 37, 2, 2, 80, False, 0.15),
     (1, 999, 515, 2, 2, 64, False, None),
+    (1, 300, 257, 4, 2, 96, True, None),
+    (2, 129, 200, 2, 2, 72, False, 0.11),
+    (1, 256, 256, 2, 1, 120, False, None),
 )
 
 
