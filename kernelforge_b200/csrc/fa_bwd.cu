@@ -10,7 +10,7 @@
 //   dQ = gamma dS K,  dK = gamma dS^T Q,  dV = P^T dO
 //
 // Three kernels, deterministic (no atomics). The first is shared with the tcgen05 kernels of
-// fa_bwd_sm100.cu (head dims 64 and 72..128); the other two serve every other head dim:
+// fa_bwd_sm100.cu (head dims up to 128); the other two serve head dims 136..256:
 //   fa_bwd_rowstat_kernel one warp per (batch, head, query) row: -LSE log2(e) and -delta into
 //                        the padded row-statistics arrays
 //   fa_bwd_dq_kernel     query-stationary: 64 query rows per CTA, key tiles streamed through a

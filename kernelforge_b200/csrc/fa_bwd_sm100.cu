@@ -1,5 +1,5 @@
 // FlashAttention backward (reverse-mode VJP) on the 5th-generation tensor cores
-// (tcgen05 + TMEM + TMA), head dims 64 and 72..128 (the latter on zero-padded D = 128 tiles),
+// (tcgen05 + TMEM + TMA), head dims up to 128 (other than 64 and 128 on zero-padded tiles),
 // fp16 / bf16, causal (bottom-right), GQA.
 //
 // Replaces the flash_attn binary's _flash_attn_backward that FlashAttentionFunction.backward
@@ -555,12 +555,13 @@ int kf_internal_fa_bwd_error(unsigned int* code) {
 
 namespace kf::fa {
 
-// Head dims 64 and 72..128: 72..120 run the D = 128 kernels on zero-padded tiles.
-bool sm100_bwd_supported(const BwdArgs& a) { return a.D == 64 || (a.D > 64 && a.D <= 128); }
+// Head dims up to 128: 8..56 run the D = 64 kernels and 72..120 the D = 128 kernels on
+// zero-padded tiles.
+bool sm100_bwd_supported(const BwdArgs& a) { return a.D >= 8 && a.D <= 128; }
 
 int launch_sm100_bwd(const BwdArgs& a, int dtype, cudaStream_t s) {
-  if (dtype == KF_DTYPE_BF16) return a.D == 64 ? launch<__nv_bfloat16, 64>(a, dtype, s) : launch<__nv_bfloat16, 128>(a, dtype, s);
-  return a.D == 64 ? launch<__half, 64>(a, dtype, s) : launch<__half, 128>(a, dtype, s);
+  if (dtype == KF_DTYPE_BF16) return a.D <= 64 ? launch<__nv_bfloat16, 64>(a, dtype, s) : launch<__nv_bfloat16, 128>(a, dtype, s);
+  return a.D <= 64 ? launch<__half, 64>(a, dtype, s) : launch<__half, 128>(a, dtype, s);
 }
 
 }  // namespace kf::fa

@@ -52,8 +52,8 @@ struct BwdArgs {
   int causal;
 };
 
-// Row statistics, then dQ, dK, dV (deterministic; no atomics). D in {64, 72..128} runs on the
-// tcgen05 kernels, every other D (8..256, multiple of 8) on the mma.sync ones.
+// Row statistics, then dQ, dK, dV (deterministic; no atomics). D up to 128 runs on the tcgen05
+// kernels (zero-padded to 64 or 128), D in 136..256 on the mma.sync ones.
 int launch_bwd(const BwdArgs& a, int dtype, cudaStream_t stream);
 bool sm100_bwd_supported(const BwdArgs& a);
 int launch_sm100_bwd(const BwdArgs& a, int dtype, cudaStream_t stream);
@@ -114,13 +114,13 @@ __device__ __forceinline__ void load_tile(uint32_t smem, const T* __restrict__ b
 // mma.sync path: any D in 8..256 (multiple of 8), fp16 / bf16.
 int launch_general(const FaArgs& a, int mode, int dtype, cudaStream_t stream);
 
-// tcgen05 / TMEM / TMA path of the standalone JVP: D = 64 or 72..128 (zero-padded to 128), at
+// tcgen05 / TMEM / TMA path of the standalone JVP: D up to 128 (zero-padded to 64 or 128), at
 // least one tangent.
 bool sm100_jvp_supported(const FaArgs& a);
 int launch_sm100_jvp(const FaArgs& a, int dtype, cudaStream_t stream);
 
 // tcgen05 / TMEM / TMA path of the forward (kModeFwd) and one-pass forward + JVP
-// (kModeFwdJvp): D = 64 or 72..128; the one-pass mode needs at least one tangent.
+// (kModeFwdJvp): D up to 128; the one-pass mode needs at least one tangent.
 bool sm100_fused_supported(const FaArgs& a, int mode);
 int launch_sm100_fused(const FaArgs& a, int mode, int dtype, cudaStream_t stream);
 

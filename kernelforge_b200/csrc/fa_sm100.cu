@@ -804,9 +804,10 @@ int kf_internal_fa_error(unsigned int* code) {
 
 namespace kf::fa {
 
-// Head dims 64 and 72..128 (multiples of 8): 72..120 run the D = 128 kernels on zero-padded
-// tiles (TMA fills the columns past D with zeros; the epilogues store only real columns).
-bool sm100_head_dim(int d) { return d == 64 || (d > 64 && d <= 128); }
+// Head dims up to 128 (multiples of 8): 8..56 run the D = 64 kernels and 72..120 the D = 128
+// kernels on zero-padded tiles (TMA fills the columns past D with zeros; the epilogues store
+// only real columns).
+bool sm100_head_dim(int d) { return d >= 8 && d <= 128; }
 
 bool sm100_jvp_supported(const FaArgs& a) {
   return sm100_head_dim(a.D) && (a.tq != nullptr || a.tk != nullptr || a.tv != nullptr);
@@ -821,16 +822,16 @@ bool sm100_fused_supported(const FaArgs& a, int mode) {
 int launch_sm100_fused(const FaArgs& a, int mode, int dtype, cudaStream_t s) {
   const bool jvp = mode == kModeFwdJvp;
   if (dtype == KF_DTYPE_BF16) {
-    if (a.D == 64) return jvp ? launch_fused<__nv_bfloat16, 64, true>(a, dtype, s) : launch_fused<__nv_bfloat16, 64, false>(a, dtype, s);
+    if (a.D <= 64) return jvp ? launch_fused<__nv_bfloat16, 64, true>(a, dtype, s) : launch_fused<__nv_bfloat16, 64, false>(a, dtype, s);
     return jvp ? launch_fused<__nv_bfloat16, 128, true>(a, dtype, s) : launch_fused<__nv_bfloat16, 128, false>(a, dtype, s);
   }
-  if (a.D == 64) return jvp ? launch_fused<__half, 64, true>(a, dtype, s) : launch_fused<__half, 64, false>(a, dtype, s);
+  if (a.D <= 64) return jvp ? launch_fused<__half, 64, true>(a, dtype, s) : launch_fused<__half, 64, false>(a, dtype, s);
   return jvp ? launch_fused<__half, 128, true>(a, dtype, s) : launch_fused<__half, 128, false>(a, dtype, s);
 }
 
 int launch_sm100_jvp(const FaArgs& a, int dtype, cudaStream_t s) {
-  if (dtype == KF_DTYPE_BF16) return a.D == 64 ? launch_jvp<__nv_bfloat16, 64>(a, dtype, s) : launch_jvp<__nv_bfloat16, 128>(a, dtype, s);
-  return a.D == 64 ? launch_jvp<__half, 64>(a, dtype, s) : launch_jvp<__half, 128>(a, dtype, s);
+  if (dtype == KF_DTYPE_BF16) return a.D <= 64 ? launch_jvp<__nv_bfloat16, 64>(a, dtype, s) : launch_jvp<__nv_bfloat16, 128>(a, dtype, s);
+  return a.D <= 64 ? launch_jvp<__half, 64>(a, dtype, s) : launch_jvp<__half, 128>(a, dtype, s);
 }
 
 }  // namespace kf::fa
