@@ -427,10 +427,7 @@ int launch_t(const BwdArgs& a, int dtype, cudaStream_t s) {
   }
   if (kf::fa::sm100_bwd_supported(a)) return kf::fa::launch_sm100_bwd(a, dtype, s);
   const int d = a.D;
-  if (d <= 32) return launch_dp<T, 32>(a, s);
-  if (d <= 64) return launch_dp<T, 64>(a, s);
-  if (d <= 96) return launch_dp<T, 96>(a, s);
-  if (d <= 128) return launch_dp<T, 128>(a, s);
+  // Head dims up to 128 went to the tcgen05 kernels above; these serve 136..256.
   if (d <= 192) return launch_dp<T, 192>(a, s);
   return launch_dp<T, 256>(a, s);
 }
