@@ -1,5 +1,27 @@
-"""SANA ReLU linear attention (drop-in for SANA_LinearAttention/__init__.py:3-12)."""
+"""SANA ReLU linear attention (drop-in for SANA_LinearAttention/__init__.py:3-27)."""
 
 from .custom import QKVAttnMatmul, qkv_attn_matmul, sana_linattn_into
+from .modules import (
+    CUDAGraphJointLiteLA,
+    CustomLiteLA,
+    CustomOpJointLiteLA,
+    GroupedFull64QOutLiteLA,
+    JointLiteLA,
+    LiteLA,
+    optimized_joint_litela,
+    qkv_projection,
+)
 
-__all__ = ["QKVAttnMatmul", "qkv_attn_matmul", "sana_linattn_into"]
+__all__ = [
+    "CUDAGraphJointLiteLA",
+    "CustomLiteLA",
+    "CustomOpJointLiteLA",
+    "GroupedFull64QOutLiteLA",
+    "JointLiteLA",
+    "LiteLA",
+    "QKVAttnMatmul",
+    "optimized_joint_litela",
+    "qkv_attn_matmul",
+    "qkv_projection",
+    "sana_linattn_into",
+]

@@ -90,8 +90,9 @@ def qkv_attn_matmul(
     """Return ``run(qkv)`` for packed ``[batch, seq_len, 3, heads*dim]`` QKV.
 
     ``reduce_splits`` selected between two partial-reduction kernels in the reference; here the
-    split partials are always reduced once, by the last producer CTA of each head group, so
-    the flag is accepted for signature compatibility and does not change the result.
+    K^T V partials are always summed once, in a fixed order (in shared memory on the one-launch
+    path, while building the epilogue's B operand on the split path), so the flag is accepted
+    for signature compatibility and does not change the result.
     """
     if dim <= 0 or dim > THREADS or THREADS % dim != 0:
         raise ValueError(f"dim must divide {THREADS} and be at most {THREADS}")

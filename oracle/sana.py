@@ -68,3 +68,28 @@ def attn_exact(qkv: torch.Tensor, heads: int, dim: int, eps: float = 1e-15) -> t
     num = torch.einsum("bhrc,bnhc->bnhr", vk, q)
     den = torch.einsum("bhc,bnhc->bnh", ksum, q)[..., None]
     return (num / (den + eps)).reshape(batch, seq_len, channels)
+
+
+def rmsnorm_exact(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """Float64 RMSNorm over the last axis (rmsnorm/original.py:27-52, without roundings)."""
+    x = x.to(torch.float64)
+    return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * weight.to(torch.float64)
+
+
+def litela_forward_exact(x, qkv_weight, qkv_bias, proj_weight, proj_bias, dim, eps=1e-15,
+                         q_norm_weight=None, k_norm_weight=None, norm_eps=1e-5):
+    """Float64 ``LiteLA.forward`` (SANA_LinearAttention/original.py:119-145) without rotary
+    embeddings: packed QKV projection, optional q / k RMSNorm over the channels, ReLU linear
+    attention with the ones-row denominator, output projection. ``x``: ``[B, N, C]``."""
+    x = x.detach().to("cpu", torch.float64)
+    batch, seq_len, channels = x.shape
+    qkv = x @ qkv_weight.detach().to("cpu", torch.float64).t()
+    if qkv_bias is not None:
+        qkv = qkv + qkv_bias.detach().to("cpu", torch.float64)
+    q, k, v = qkv.reshape(batch, seq_len, 3, channels).unbind(2)
+    if q_norm_weight is not None:
+        q = rmsnorm_exact(q, q_norm_weight.detach().cpu(), norm_eps)
+        k = rmsnorm_exact(k, k_norm_weight.detach().cpu(), norm_eps)
+    out = attn_exact(torch.stack([q, k, v], dim=2), channels // dim, dim, eps)
+    return out @ proj_weight.detach().to("cpu", torch.float64).t() + proj_bias.detach().to("cpu", torch.float64)
+
