@@ -3,6 +3,7 @@
 from .custom import QKVAttnMatmul, qkv_attn_matmul, sana_linattn_into
 from .modules import (
     CUDAGraphJointLiteLA,
+    apply_rotary_emb,
     CustomLiteLA,
     CustomOpJointLiteLA,
     GroupedFull64QOutLiteLA,
@@ -13,6 +14,7 @@ from .modules import (
 )
 
 __all__ = [
+    "apply_rotary_emb",
     "CUDAGraphJointLiteLA",
     "CustomLiteLA",
     "CustomOpJointLiteLA",

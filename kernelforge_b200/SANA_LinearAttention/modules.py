@@ -18,8 +18,9 @@ The attention runs on ``kf_sana_linattn_fwd`` (``qkv_attn_matmul``). The two pro
 plain GEMMs through torch (cuBLAS); the output projection fuses its bias (``addmm``).
 ``qk_norm`` runs this library's RMSNorm kernel on the q and k slices of the packed QKV. The
 reference's custom modules reject it.
-Rotary embeddings (original.py:14-63) are outside this library's path: passing ``rotary_emb``
-raises ``NotImplementedError``.
+``apply_rotary_emb`` restates original.py:14-63. With ``rotary_emb`` the modules rotate q and k in
+the reference's ``[B, h, d, N]`` layout (SANA's ``use_real_unbind_dim=-2``) and repack them for the
+attention kernel.
 """
 
 from __future__ import annotations
@@ -31,6 +32,7 @@ from ..rmsnorm import RMSNorm
 from .custom import TORCH_DTYPES, QKVAttnMatmul
 
 __all__ = [
+    "apply_rotary_emb",
     "CUDAGraphJointLiteLA",
     "CustomLiteLA",
     "CustomOpJointLiteLA",
@@ -61,6 +63,31 @@ def qkv_projection(batch: int, seq_len: int, channels: int, dtype: str = "bfloat
         return torch.matmul(x, weight_t)
 
     return project
+
+
+def apply_rotary_emb(x: torch.Tensor, freqs_cis, use_real: bool = True, use_real_unbind_dim: int = -1) -> torch.Tensor:
+    """Rotary position embedding of ``x`` (original.py:14-63).
+
+    ``use_real``: ``freqs_cis = (cos, sin)``, each ``[S, D]``. Element pairs (2i, 2i+1) of the
+    head dim become ``(a cos - b sin, b cos + a sin)``: along the last axis of ``[B, H, S, D]``
+    (``use_real_unbind_dim=-1``), or along axis -2 of SANA's ``[B, H, D, S]`` with ``cos``/``sin``
+    transposed (``-2``). Computed in fp32, returned in ``x``'s dtype. Otherwise ``freqs_cis`` is a
+    complex ``[S, D/2]`` tensor multiplying ``x [B, S, H, D]`` viewed as complex pairs.
+    """
+    if not use_real:
+        pairs = torch.view_as_complex(x.float().reshape(*x.shape[:-1], -1, 2))
+        return torch.view_as_real(pairs * freqs_cis.unsqueeze(2)).flatten(3).type_as(x)
+    cos, sin = (f[None, None].to(x.device) for f in freqs_cis)
+    if use_real_unbind_dim == -1:
+        a, b = x.reshape(*x.shape[:-1], -1, 2).unbind(-1)
+        rotated = torch.stack([-b, a], dim=-1).flatten(3)
+    elif use_real_unbind_dim == -2:
+        cos, sin = cos.transpose(-1, -2), sin.transpose(-1, -2)
+        a, b = x.reshape(*x.shape[:-2], -1, 2, x.shape[-1]).unbind(-2)
+        rotated = torch.stack([-b, a], dim=-2).flatten(2, 3)
+    else:
+        raise ValueError(f"`use_real_unbind_dim={use_real_unbind_dim}` but should be -1 or -2.")
+    return (x.float() * cos + rotated.float() * sin).to(x.dtype)
 
 
 class LiteLA(torch.nn.Module):
@@ -137,13 +164,26 @@ class LiteLA(torch.nn.Module):
             return out.to(qkv.dtype)
         return self._attention_kernel(batch, seq_len, qkv.dtype)(qkv)
 
+    def _rotate_qk(self, qkv: torch.Tensor, rotary_emb) -> torch.Tensor:
+        """Rotary embedding of q and k in the reference's [B, h, d, N] layout (original.py:133-135),
+        repacked into [B, N, 3, C] for the attention kernel."""
+        if rotary_emb is None:
+            return qkv
+        batch, seq_len, _, channels = qkv.shape
+        heads = channels // self.dim
+
+        def rotate(t):  # [B, N, C] -> [B, h, d, N] -> rotated -> [B, N, C]
+            hdn = t.transpose(1, 2).reshape(batch, heads, self.dim, seq_len)
+            out = apply_rotary_emb(hdn, rotary_emb, use_real_unbind_dim=-2)
+            return out.reshape(batch, channels, seq_len).transpose(1, 2)
+
+        return torch.stack([rotate(qkv[:, :, 0]), rotate(qkv[:, :, 1]), qkv[:, :, 2]], dim=2).contiguous()
+
     def forward(self, x, mask=None, HW=None, rotary_emb=None, block_id=None, block_mask=None):
-        if rotary_emb is not None:
-            raise NotImplementedError("rotary embeddings are outside this library's LiteLA path")
         self._validate_input(x)
         batch, seq_len, channels = x.shape
         qkv = self._project_qkv(x).reshape(batch, seq_len, 3, channels)
-        out = self.attention(self._normalise_qk(qkv))
+        out = self.attention(self._rotate_qk(self._normalise_qk(qkv), rotary_emb))
         return self.proj(out)
 
 
@@ -184,12 +224,10 @@ class JointLiteLA(LiteLA):
             batch, seq_len, channels)
 
     def forward(self, x, mask=None, HW=None, rotary_emb=None, block_id=None, block_mask=None):
-        if rotary_emb is not None:
-            raise NotImplementedError("rotary embeddings are outside this library's LiteLA path")
         self._validate_input(x)
         batch, seq_len, channels = x.shape
         qkv = self._project_qkv(x).reshape(batch, seq_len, 3, channels)
-        return self._project_output(self.attention(self._normalise_qk(qkv)))
+        return self._project_output(self.attention(self._rotate_qk(self._normalise_qk(qkv), rotary_emb)))
 
 
 GROUPED_SHAPE = dict(batch=1, seq_len=1024, channels=1152, heads=36, dim=32)

@@ -5,13 +5,16 @@ files of zzd1992/KernelForge) from a checkout of the reference and runs them on 
 small, seeded inputs. It writes ``*.pt`` fixtures holding the inputs and the reference's
 outputs. The fixtures are committed; the tests never need the reference checkout.
 
-Usage:  python tests/golden/make_golden.py /path/to/KernelForge
+Usage:  python tests/golden/make_golden.py /path/to/KernelForge [rmsnorm sana sana_modules fa_jvp]
 
 ``SANA_LinearAttention/original.py`` imports ``timm`` only for the ``Attention`` base class
 of ``LiteLA`` (original.py:10, 65, 83); ``timm`` is not installed here, so a stub base class
 that creates the ``qkv``/``proj`` linear layers is registered before the import. The
 function under test, ``LiteLA.attn_matmul`` (original.py:99-117), touches only
-``self.kernel_func`` and ``self.eps``, so the stub does not change its arithmetic.
+``self.kernel_func`` and ``self.eps``, so the stub does not change its arithmetic. The module
+fixtures run ``LiteLA.forward`` (original.py:119-145), which uses only the base class's
+``qkv = Linear(C, 3C, bias=qkv_bias)`` and ``proj = Linear(C, C)``, the layers the stub creates
+as timm's ``Attention`` does.
 """
 
 from __future__ import annotations
@@ -107,6 +110,46 @@ def make_sana(ref_root: Path):
     return len(cases)
 
 
+def make_sana_modules(ref_root: Path):
+    """``apply_rotary_emb`` (original.py:14-63) and a full ``LiteLA.forward`` (original.py:119-145)
+    with qk_norm and rotary embeddings, from the reference's own module."""
+    _install_timm_stub()
+    from SANA_LinearAttention.original import LiteLA, apply_rotary_emb  # noqa: E402  (reference)
+
+    g = _gen(300)
+    rotary = []
+    for dtype in (torch.float32, torch.bfloat16):
+        x = torch.randn(2, 3, 10, 8, generator=g).to(dtype)          # [B, H, S, D]
+        cos, sin = torch.randn(10, 8, generator=g), torch.randn(10, 8, generator=g)
+        rotary.append(dict(x=x, cos=cos, sin=sin, dim=-1, out=apply_rotary_emb(x, (cos, sin), True, -1)))
+        xt = torch.randn(2, 3, 8, 10, generator=g).to(dtype)         # [B, H, D, S] (SANA)
+        rotary.append(dict(x=xt, cos=cos, sin=sin, dim=-2, out=apply_rotary_emb(xt, (cos, sin), True, -2)))
+    xc = torch.randn(2, 10, 3, 8, generator=g)                        # [B, S, H, D], complex form
+    freqs = torch.polar(torch.ones(1, 10, 4), torch.randn(1, 10, 4, generator=g))  # [1, S, D/2]
+    rotary.append(dict(x=xc, freqs=freqs, out=apply_rotary_emb(xc, freqs, use_real=False)))
+
+    modules = []
+    # (batch, seq_len, channels, heads, qk_norm, use_bias, rotary)
+    for i, (b, n, c, h, qk_norm, bias, use_rot) in enumerate([(2, 77, 128, 4, True, True, True),
+                                                            (1, 130, 64, 2, False, False, True),
+                                                            (1, 64, 96, 3, True, False, False)]):
+        gm = _gen(310 + i)
+        torch.manual_seed(310 + i)
+        module = LiteLA(c, c, heads=h, dim=c // h, qk_norm=qk_norm, use_bias=bias).eval()
+        if qk_norm:
+            with torch.no_grad():
+                module.q_norm.weight.uniform_(0.5, 1.5)
+                module.k_norm.weight.uniform_(0.5, 1.5)
+        x = torch.randn(b, n, c, generator=gm)
+        rot = (torch.randn(n, c // h, generator=gm), torch.randn(n, c // h, generator=gm)) if use_rot else None
+        with torch.no_grad():
+            out = module(x, rotary_emb=rot)
+        modules.append(dict(x=x, rotary=rot, heads=h, dim=c // h, qk_norm=qk_norm, use_bias=bias,
+                            state=module.state_dict(), out=out))
+    torch.save(dict(rotary=rotary, modules=modules), HERE / "sana_modules_golden.pt")
+    return len(rotary) + len(modules)
+
+
 def make_fa(ref_root: Path):
     from flash_attention_jvp.original import attention, attention_jvp, attention_jvp_from_forward
 
@@ -164,14 +207,15 @@ def _lse64(q, k, scale, causal):
 
 
 def main():
-    if len(sys.argv) != 2:
+    if len(sys.argv) < 2:
         raise SystemExit(__doc__)
     ref_root = Path(sys.argv[1]).resolve()
+    parts = sys.argv[2:] or ["rmsnorm", "sana", "sana_modules", "fa_jvp"]
     sys.path.insert(0, str(ref_root))
     torch.set_num_threads(4)
-    print("rmsnorm cases:", make_rmsnorm(ref_root))
-    print("sana cases:", make_sana(ref_root))
-    print("fa_jvp cases:", make_fa(ref_root))
+    makers = {"rmsnorm": make_rmsnorm, "sana": make_sana, "sana_modules": make_sana_modules, "fa_jvp": make_fa}
+    for part in parts:
+        print(f"{part} cases:", makers[part](ref_root))
 
 
 if __name__ == "__main__":

@@ -30,8 +30,8 @@ def test_shape_contracts_and_validation():
     m = sana.JointLiteLA(64, 64, batch=1, seq_len=32, dtype=torch.bfloat16, heads=2, dim=32)
     with pytest.raises(ValueError, match="input shape"):
         m(torch.zeros(1, 16, 64, dtype=torch.bfloat16))
-    with pytest.raises(NotImplementedError):
-        sana.LiteLA(64, 64)(torch.zeros(1, 8, 64), rotary_emb=(torch.zeros(8, 32), torch.zeros(8, 32)))
+    with pytest.raises(ValueError, match="CUDA"):  # the attention kernel needs a GPU tensor
+        sana.LiteLA(64, 64)(torch.zeros(1, 8, 64))
     project = sana.qkv_projection(1, 8, 64, "bfloat16")
     with pytest.raises(ValueError, match="weight_t"):
         project(torch.zeros(1, 8, 64, dtype=torch.bfloat16), torch.zeros(64, 64, dtype=torch.bfloat16))
@@ -43,3 +43,18 @@ def test_optimized_joint_litela_picks_the_reference_module():
     joint = sana.optimized_joint_litela(1152, 1152, batch=2, seq_len=1024, **kwargs)
     assert type(grouped) is sana.GroupedFull64QOutLiteLA and type(joint) is sana.JointLiteLA
     assert sana.CustomLiteLA is sana.LiteLA
+
+
+GOLDEN = __import__("pathlib").Path(__file__).resolve().parent / "golden" / "sana_modules_golden.pt"
+
+
+def test_apply_rotary_emb_matches_the_reference_fixtures():
+    """Fixtures from the reference's own apply_rotary_emb (original.py:14-63), all three forms."""
+    cases = torch.load(GOLDEN)["rotary"]
+    for case in cases:
+        if "freqs" in case:
+            out = sana.apply_rotary_emb(case["x"], case["freqs"], use_real=False)
+        else:
+            out = sana.apply_rotary_emb(case["x"], (case["cos"], case["sin"]), True, case["dim"])
+        assert out.dtype == case["out"].dtype
+        torch.testing.assert_close(out, case["out"], rtol=0, atol=0)

@@ -98,3 +98,20 @@ def test_fp32_attention_flag(sana):
     x = torch.randn(2, 256, 256, device="cuda", dtype=torch.bfloat16)
     with torch.inference_mode():
         assert_close(m(x), expected(m, x))
+
+
+@pytest.mark.parametrize("index", range(3))
+def test_reference_module_fixtures(sana, index):
+    """The reference's own LiteLA.forward (original.py:119-145; qk_norm, bias, rotary embeddings)
+    on fp32 inputs, its state dict loaded into this library's module (tests/golden)."""
+    from pathlib import Path
+
+    case = torch.load(Path(__file__).resolve().parent / "golden" / "sana_modules_golden.pt")["modules"][index]
+    b, n, c = case["x"].shape
+    m = sana.LiteLA(c, c, heads=case["heads"], dim=case["dim"], qk_norm=case["qk_norm"],
+                    use_bias=case["use_bias"]).cuda().eval()
+    m.load_state_dict(case["state"])
+    rot = tuple(t.cuda() for t in case["rotary"]) if case["rotary"] is not None else None
+    with torch.inference_mode():
+        out = m(case["x"].cuda(), rotary_emb=rot)
+    torch.testing.assert_close(out.cpu(), case["out"], rtol=1e-3, atol=1e-4)
