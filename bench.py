@@ -63,14 +63,12 @@ RMSNORM_NCU_TRAFFIC_BYTES = 8 * (536_926_976 + 486_499_328)
 SANA_NCU_TRAFFIC_BYTES = {"sana_cfg1": 113_272_832 + 7_127_808}
 
 
-def sana_launches_per_call(B, H):
-    """Kernel launches of one default-schedule qkv_attn_matmul call (bf16, head dim 32): the
-    library picks its one-launch path when batch x heads fills at least 90% of the CTA slots of
-    the last wave of SMs (kf_sana_linattn_fwd, splits = 0), else producer + epilogue."""
-    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
-    units = B * H
-    waves = -(-units // sms)
-    return 1 if units * 10 >= waves * sms * 9 else 2
+def sana_launches_per_call(B, H, N):
+    """Kernel launches of one default-schedule qkv_attn_matmul call (bf16, head dim 32), as the
+    library plans it on this device (kf_sana_linattn_plan)."""
+    from kernelforge_b200.SANA_LinearAttention import QKVAttnMatmul
+
+    return QKVAttnMatmul(B, H, 32, N, 1e-15, "bfloat16", "bfloat16").plan()[0]
 
 
 # ---------------------------------------------------------------------------------------------
@@ -396,7 +394,7 @@ def bench_sana(args, dist, peaks, peak_kind, cfg):
     nbytes = sana_bytes(cfg)
     value = dist.world * nbytes / (ms / 1e3) / 1e9
     flops = 4 * B * H * N * D * (D + 1)
-    launches = sana_launches_per_call(B, H)
+    launches = sana_launches_per_call(B, H, N)
     result = {
         "value": round(value, 1), "unit": "GB/s", "ms_per_step": round(ms, 4),
         "gpu_launches": launches * args.steps,

@@ -76,10 +76,14 @@ int kf_rmsnorm_fwd(const void* x, const void* weight, void* y,
  *   VK_h = sum_t v_t relu(k_t)^T,  ksum_h = sum_t relu(k_t)           (fp32 accumulation)
  *   out[t, h*dim + r] = (VK_h relu(q_t))_r / (ksum_h . relu(q_t) + eps)
  * `splits` picks the schedule of the bf16/fp16 head_dim-32 path:
- *   0       automatic: the one-launch path when batch*heads fills the GPU's SMs (at least 90%
- *           of the CTA slots of the last wave), else the split path with a default split count;
+ *   0       automatic: the one-launch path when its CTAs fill the GPU's SMs (at least 90%
+ *           of the CTA slots of the last wave) or outnumber the split path's producer CTAs,
+ *           else the split path with a default split count;
  *   -1      the one-launch path: each CTA owns whole (batch, head) units, reduces K^T V and
- *           ksum in shared memory and writes the output (the workspace is not touched);
+ *           ksum in shared memory and writes the output (the workspace is not touched); with
+ *           fewer units than SMs, a thread-block cluster of up to 8 CTAs shares each unit,
+ *           splitting its tokens and summing the CTAs' K^T V and ksum over distributed shared
+ *           memory in a fixed order;
  *   s > 0   the split path: the token axis in s chunks whose fp32 partials go through the
  *           workspace to a tcgen05 epilogue launch.
  * Other shapes (fp32 input, other head dims) keep fp32 partials in the workspace and reduce them
@@ -94,6 +98,17 @@ size_t kf_sana_linattn_workspace_size(int64_t batch, int64_t heads, int64_t dim,
 int kf_sana_linattn_fwd(const void* qkv, void* out, void* workspace, size_t workspace_bytes,
                         int64_t batch, int64_t heads, int64_t dim, int64_t seq_len, int64_t splits,
                         float eps, int in_dtype, int out_dtype, void* stream);
+
+/*
+ * The schedule kf_sana_linattn_fwd runs for these arguments on the current CUDA device, without
+ * launching anything (16-byte aligned qkv and out assumed). No counterpart in the reference.
+ *   *launches       kernel launches per call (1: the one-launch path; 2: the other paths);
+ *   *ctas_per_unit  on the one-launch path, the CTAs that share one (batch, head) unit: 1, or
+ *                   the size of the thread-block cluster that splits its tokens (used when
+ *                   batch*heads is below the SM count); 0 on the other paths.
+ */
+int kf_sana_linattn_plan(int64_t batch, int64_t heads, int64_t dim, int64_t seq_len, int64_t splits,
+                         int in_dtype, int64_t* launches, int64_t* ctas_per_unit);
 
 /*
  * kf_sana_linattn_fwd without a workspace, for callers that cannot allocate device memory

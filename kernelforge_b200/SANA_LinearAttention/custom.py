@@ -28,8 +28,9 @@ class QKVAttnMatmul:
     by every later call, so the callable is CUDA-graph capturable after its first call.
     Calls through one callable must be ordered on one stream (they share the workspace).
     ``splits``: None or 0 picks the schedule automatically, -1 forces the one-launch path
-    (whole heads per CTA, no workspace traffic), a positive count the split path with that many
-    token chunks (``kf_sana_linattn_fwd`` in include/kernelforge_b200.h).
+    (whole heads per CTA, or per thread-block cluster when there are fewer heads than SMs; no
+    workspace traffic), a positive count the split path with that many token chunks
+    (``kf_sana_linattn_fwd`` in include/kernelforge_b200.h). :meth:`plan` reports the choice.
     """
 
     def __init__(self, batch, heads, dim, seq_len, eps, dtype, output_dtype, splits=None):
@@ -49,6 +50,20 @@ class QKVAttnMatmul:
             ws = torch.zeros(self.workspace_bytes, dtype=torch.uint8, device=device)
             self._workspaces[device] = ws
         return ws
+
+    def plan(self, device=None) -> tuple[int, int]:
+        """(kernel launches per call, CTAs per (batch, head) unit on the one-launch path or 0)
+        for this shape on ``device`` (default: the current CUDA device), without launching."""
+        import ctypes
+
+        launches, ctas = ctypes.c_int64(0), ctypes.c_int64(0)
+        device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        with torch.cuda.device(device):
+            status = _lib.lib.kf_sana_linattn_plan(self.batch, self.heads, self.dim, self.seq_len, self.splits,
+                                                   _lib.dtype_code(self.dtype), ctypes.byref(launches),
+                                                   ctypes.byref(ctas))
+        _lib.check(status, "kf_sana_linattn_plan")
+        return launches.value, ctas.value
 
     def __call__(self, qkv: torch.Tensor) -> torch.Tensor:
         expected = (self.batch, self.seq_len, 3, self.heads * self.dim)

@@ -87,6 +87,20 @@ __device__ __forceinline__ bool mbar_try_wait_relaxed(uint64_t* bar, uint32_t pa
   return ok != 0;
 }
 
+// Probe with acquire semantics at cluster scope: the phase may have been completed by arrivals
+// from other CTAs of the cluster, whose writes the waiter then reads.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Non-blocking probe of a phase (never suspends the thread).
 __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
@@ -103,11 +117,13 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait that also gives up as soon as another thread of the CTA has set *abort (a
 // shared-memory flag), so a CTA whose roles synchronise with each other never waits out one
 // timeout per remaining step after the first failure. A timeout sets *abort itself.
-// kPoll: probe with test_wait (no suspension) instead of try_wait.
-template <bool kRelaxed = false, bool kPoll = false>
+// kPoll: probe with test_wait (no suspension) instead of try_wait. kCluster: acquire at cluster
+// scope (the phase completes through other CTAs' arrivals).
+template <bool kRelaxed = false, bool kPoll = false, bool kCluster = false>
 __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, unsigned int* err,
                                                    volatile int* abort) {
   auto probe = [&]() {
+    if constexpr (kCluster) return mbar_try_wait_cluster(bar, parity);
     return kPoll ? mbar_test_wait(bar, parity)
                  : (kRelaxed ? mbar_try_wait_relaxed(bar, parity) : mbar_try_wait(bar, parity));
   };
@@ -125,6 +141,59 @@ __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parit
       }
     }
   }
+}
+
+// ------------------------------------------------------------------------------------------
+// Thread-block clusters: distributed shared memory and mbarrier arrivals across CTAs
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+// Cluster index and cluster count along x (clusters tile the grid in blockIdx order).
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_count_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// Shared-memory address (shared::cta window) -> the same offset in CTA `rank` of the cluster
+// (shared::cluster window).
+__device__ __forceinline__ uint32_t cluster_map(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+// One arrival on an mbarrier of any CTA of the cluster. Release at cluster scope: writes this
+// thread made, or saw through a CTA barrier before it, are visible to whoever acquires the phase.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// Orders this thread's earlier shared-memory writes before its later operations at cluster
+// scope (before the CTA barrier that hands them to the thread that arrives remotely).
+__device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t cluster_addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(cluster_addr)
+               : "memory");
+  return v;
+}
+// Every thread of every CTA of the cluster (each warp converged). Used once, right after the
+// mbarriers are initialised and before any CTA waits on anything, so every thread reaches it.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 // Named barrier over `nthreads` threads (a multiple of 32) that use barrier `id` (1..15; 0 is

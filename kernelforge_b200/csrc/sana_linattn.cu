@@ -728,7 +728,7 @@ sana_out_generic(const T* __restrict__ qkv, const float* __restrict__ final_vk, 
 }
 
 // ------------------------------------------------------------------------------------------
-// Fused path: one launch, one (batch, head) unit per CTA at a time, no workspace.
+// Fused path: one launch, one (batch, head) unit per CTA (or per cluster) at a time, no workspace.
 //
 // When the batch x head units fill the SMs (or when the caller asks for it with splits = -1),
 // every CTA owns whole heads, so the K^T V reduction never leaves the CTA and no second launch
@@ -747,6 +747,16 @@ sana_out_generic(const T* __restrict__ qkv, const float* __restrict__ final_vk, 
 // The producer runs ahead into the next unit, so the next K/V tiles and the first Q tiles are
 // in flight while the warps reduce. fp16 inputs scale B by a power of two that keeps max|B|
 // below 2^14, with eps scaled alike.
+//
+// Cluster form (kCluster): when there are fewer units than SMs, a cluster of CS CTAs shares one
+// unit. CTA rank r takes the r-th of CS equal ranges of K/V tiles and of Q tiles, sums its warp
+// partials into `red`, and the CTAs exchange them through distributed shared memory: each CTA
+// arrives on every peer's `xready` mbarrier once its `red` is written, waits for its own
+// `xready`, sums the CS partials in rank order into `tot` (so every CTA of the cluster holds
+// the same bits, and the result does not depend on timing), then arrives on every peer's
+// `xdone`. A CTA rewrites `red` for its next unit, and leaves the kernel, only after its
+// `xdone` phase for the previous unit has completed (every peer has finished reading it).
+// All of these waits are bounded like the ring's.
 // ------------------------------------------------------------------------------------------
 constexpr int kFusedWarps = 16;                          // compute warps
 constexpr int kFusedThreads = 32 * (kFusedWarps + 1);    // + the TMA producer warp
@@ -763,10 +773,16 @@ struct FusedSmem {
   // Warp w's slot: its phase-1 partial, then (reused) its phase-2 output staging, two 16-token
   // buffers at 1024-byte aligned offsets (the swizzled TMA store tiles need that alignment).
   static constexpr int kPartOff = kFusedStages * kFusedStageBytes;
-  static constexpr int kRedOff = kPartOff + kFusedWarps * kFusedSlotBytes;  // reduced [VK ; ksum]
-  static constexpr int kBarOff = kRedOff + kFusedPartBytes + 16;            // + two max|B| words
-  static constexpr int kBytes = kBarOff + 2 * kFusedStages * 8 + 16 + 1024;
+  static constexpr int kRedOff = kPartOff + kFusedWarps * kFusedSlotBytes;  // this CTA's [VK ; ksum]
+  static constexpr int kTotOff = kRedOff + kFusedPartBytes;                 // cluster sum (cluster form)
+  static constexpr int kMaxOff = kTotOff + kFusedPartBytes;                 // two max|B| words
+  static constexpr int kBarOff = kMaxOff + 16;
+  // full[], empty[], the abort word (16 bytes), xready, xdone; + alignment slack
+  static constexpr int kBytes = kBarOff + 2 * kFusedStages * 8 + 16 + 16 + 1024;
 };
+static_assert(FusedSmem::kRedOff % 16 == 0 && FusedSmem::kTotOff % 16 == 0 && kFusedPartBytes % 16 == 0,
+              "the cluster exchange moves 16-byte vectors");
+constexpr int kFusedMaxCluster = 8;  // portable cluster size limit
 static_assert(kFusedPartBytes <= kFusedSlotBytes && 2 * 2048 <= kFusedSlotBytes, "slot sizes");
 // Ring slot x % kFusedStages is consumed by warp x % kFusedWarps: with equal counts the warp that
 // waits for a slot's next fill is the one that released the previous fill, so no parity wait on
@@ -778,7 +794,7 @@ __device__ __forceinline__ uint32_t swz64(uint32_t row, uint32_t chunk) {
   return row * 64 + ((chunk ^ ((row >> 1) & 3)) << 4);
 }
 
-template <typename T, typename O>
+template <typename T, typename O, bool kCluster>
 __global__ void __launch_bounds__(kFusedThreads, 1)
 sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constant__ CUtensorMap q_map,
                 const __grid_constant__ CUtensorMap out_map, int B, int H, int N, float eps) {
@@ -788,14 +804,27 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + FusedSmem::kBarOff);
   uint64_t* empty = full + kFusedStages;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kFusedStages);
+  uint64_t* xready = empty + kFusedStages + 2;  // past the 16-byte abort word
+  uint64_t* xdone = xready + 1;
   float* red = reinterpret_cast<float*>(smem + FusedSmem::kRedOff);
-  unsigned int* max_bits = reinterpret_cast<unsigned int*>(red + kRows * kD);
+  float* tot = reinterpret_cast<float*>(smem + FusedSmem::kTotOff);
+  unsigned int* max_bits = reinterpret_cast<unsigned int*>(smem + FusedSmem::kMaxOff);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, tig = lane & 3, sub = lane >> 3;
   const int units = B * H;
-  const int kv_tiles = (N + kFusedKTok - 1) / kFusedKTok;
-  const int q_tiles = (N + kFusedQTok - 1) / kFusedQTok;
+  // Cluster form: CS CTAs per unit, this CTA is rank `rank`; otherwise one CTA per unit.
+  const int cs = kCluster ? static_cast<int>(kf::cluster_nctarank()) : 1;
+  const int rank = kCluster ? static_cast<int>(kf::cluster_ctarank()) : 0;
+  const int first_unit = kCluster ? static_cast<int>(kf::cluster_id_x()) : static_cast<int>(blockIdx.x);
+  const int unit_step = kCluster ? static_cast<int>(kf::cluster_count_x()) : static_cast<int>(gridDim.x);
+  // This CTA's share of every unit: K/V tiles [kv0, kv0 + kv_tiles), Q tiles [q0, q0 + q_tiles).
+  const int kv_all = (N + kFusedKTok - 1) / kFusedKTok;
+  const int q_all = (N + kFusedQTok - 1) / kFusedQTok;
+  const int kv_per = (kv_all + cs - 1) / cs, q_per = (q_all + cs - 1) / cs;
+  const int kv0 = min(kv_all, rank * kv_per), q0 = min(q_all, rank * q_per);
+  const int kv_tiles = min(kv_all, kv0 + kv_per) - kv0;
+  const int q_tiles = min(q_all, q0 + q_per) - q0;
   const int per_unit = kv_tiles + q_tiles;  // ring stages per unit
 
   if (threadIdx.x == 0) {
@@ -806,17 +835,21 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
       kf::mbar_init(&full[s], 1);
       kf::mbar_init(&empty[s], 1);
     }
+    kf::mbar_init(xready, cs > 1 ? cs - 1 : 1);  // one arrival per peer
+    kf::mbar_init(xdone, cs > 1 ? cs - 1 : 1);
     *abort_flag = 0;
     max_bits[0] = max_bits[1] = 0u;
     kf::fence_mbar_init();
   }
-  __syncthreads();
+  // Peers arrive on this CTA's xready / xdone, so they must be initialised cluster-wide first.
+  if constexpr (kCluster) kf::cluster_sync_all();
+  else __syncthreads();
 
   if (warp == kFusedWarps) {
     // ---- TMA producer (one thread): every unit's K/V tiles, then its Q tiles ----
     if (lane == 0) {
       int seq = 0;
-      for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      for (int u = first_unit; u < units; u += unit_step) {
         const int b = u / H, h = u % H;
         for (int i = 0; i < per_unit; ++i, ++seq) {
           const int st = seq % kFusedStages;
@@ -826,10 +859,11 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
           uint8_t* base = smem + FusedSmem::kRingOff + st * kFusedStageBytes;
           kf::mbar_arrive_expect_tx(&full[st], kFusedStageBytes);
           if (i < kv_tiles) {
-            kf::tma_load_4d(base, &kv_map, &full[st], h * kD, 1, i * kFusedKTok, b);
-            kf::tma_load_4d(base + kFusedStageBytes / 2, &kv_map, &full[st], h * kD, 2, i * kFusedKTok, b);
+            const int tok = (kv0 + i) * kFusedKTok;
+            kf::tma_load_4d(base, &kv_map, &full[st], h * kD, 1, tok, b);
+            kf::tma_load_4d(base + kFusedStageBytes / 2, &kv_map, &full[st], h * kD, 2, tok, b);
           } else {
-            kf::tma_load_4d(base, &q_map, &full[st], h * kD, 0, (i - kv_tiles) * kFusedQTok, b);
+            kf::tma_load_4d(base, &q_map, &full[st], h * kD, 0, (q0 + i - kv_tiles) * kFusedQTok, b);
           }
         }
       }
@@ -842,7 +876,8 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
   int seq0 = 0;  // ring sequence number of the unit's first stage
   bool ok = true;
   int parity = 0;  // max|B| word of this unit (two words: one is reset while the other is in use)
-  for (int u = blockIdx.x; u < units; u += gridDim.x, seq0 += per_unit, parity ^= 1) {
+  int k = 0;       // units this CTA has finished (the phase of xready / xdone)
+  for (int u = first_unit; u < units; u += unit_step, seq0 += per_unit, parity ^= 1, ++k) {
     const int b = u / H, h = u % H;
     // Phase 1: this warp's K/V tiles.
     float acc[2][4][4];
@@ -919,6 +954,11 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
     kf::named_bar_sync(kFusedBar, 32 * kFusedWarps);
     // Every compute thread is past the previous unit's read of the other word.
     if (threadIdx.x == 0) max_bits[parity ^ 1] = 0u;
+    const bool exchange = kCluster && cs > 1;
+    // Cluster form: every peer has finished reading this CTA's previous `red`.
+    if (exchange && k > 0 && ok)
+      ok = __all_sync(0xffffffffu,
+                      kf::mbar_wait_or_abort<false, false, true>(xdone, (k - 1) & 1, &g_sana_error, abort_flag));
     // Sum of the 16 partials in warp order, and max|B| for the fp16 scale.
     float m = 0.f;
     for (int e = threadIdx.x; e < kRows * kD; e += 32 * kFusedWarps) {
@@ -929,12 +969,54 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
       red[e] = s;
       m = fmaxf(m, fabsf(s));
     }
+    if (exchange) {
+      // Publish `red` to the peers, then sum the cluster's partials in rank order.
+      kf::fence_acq_rel_cluster();
+      kf::named_bar_sync(kFusedBar, 32 * kFusedWarps);
+      if (threadIdx.x == 0) {
+        for (int r = 0; r < cs; ++r)
+          if (r != rank) kf::mbar_arrive_cluster(kf::cluster_map(kf::smem_u32(xready), r));
+      }
+      if (ok)
+        ok = __all_sync(0xffffffffu,
+                        kf::mbar_wait_or_abort<false, false, true>(xready, k & 1, &g_sana_error, abort_flag));
+      m = 0.f;
+      const uint32_t red_addr = kf::smem_u32(red);
+      for (int e4 = threadIdx.x; e4 < kRows * kD / 4; e4 += 32 * kFusedWarps) {
+        float4 v[kFusedMaxCluster];
+#pragma unroll
+        for (int r = 0; r < kFusedMaxCluster; ++r)
+          v[r] = (r < cs && ok) ? kf::ld_cluster_f4(kf::cluster_map(red_addr + e4 * 16, r))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 s = v[0];
+#pragma unroll
+        for (int r = 1; r < kFusedMaxCluster; ++r) {
+          if (r < cs) {
+            s.x += v[r].x;
+            s.y += v[r].y;
+            s.z += v[r].z;
+            s.w += v[r].w;
+          }
+        }
+        reinterpret_cast<float4*>(tot)[e4] = s;
+        m = fmaxf(fmaxf(m, fmaxf(fabsf(s.x), fabsf(s.y))), fmaxf(fabsf(s.z), fabsf(s.w)));
+      }
+    }
     if (kFp16) {
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
       if (lane == 0) atomicMax(&max_bits[parity], __float_as_uint(m));  // non-negative floats order as integers
     }
     kf::named_bar_sync(kFusedBar, 32 * kFusedWarps);
+    const float* vk = red;
+    if (exchange) {
+      // Every thread of this CTA has read the peers' `red`.
+      if (threadIdx.x == 0) {
+        for (int r = 0; r < cs; ++r)
+          if (r != rank) kf::mbar_arrive_cluster(kf::cluster_map(kf::smem_u32(xdone), r));
+      }
+      vk = tot;
+    }
     const float scale = operand_scale(__uint_as_float(max_bits[parity]), kFp16);
     const float eps_s = eps * scale;
     // B fragments (K = q channel c, N = output row r: VK[r][c], r = 32 is ksum[c], rows 33..39 zero)
@@ -950,8 +1032,8 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
           const int c = ks * 16 + tig * 2 + half * 8;
           float x0 = 0.f, x1 = 0.f;
           if (r <= kD) {
-            x0 = red[r * kD + c] * scale;
-            x1 = red[r * kD + c + 1] * scale;
+            x0 = vk[r * kD + c] * scale;
+            x1 = vk[r * kD + c + 1] * scale;
           }
           bhi[ks][nt][half] = kf::Mma<T>::from_f2(x0, x1);
           const float2 hf = kf::Mma<T>::to_f2(bhi[ks][nt][half]);
@@ -967,8 +1049,11 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
                                                                   &g_sana_error, abort_flag));
       if (!ok) break;
       const uint32_t qbase = kf::smem_u32(smem + FusedSmem::kRingOff + st * kFusedStageBytes);
+      // Tokens tok0 .. tok0 + 127, of which n_sub blocks of 16 reach into the sequence (>= 1).
+      const int tok0 = (q0 + j) * kFusedQTok;
+      const int n_sub = min(kFusedQTok / kFusedSub, (N - tok0 + kFusedSub - 1) / kFusedSub);
 #pragma unroll 1
-      for (int m16 = 0; m16 < kFusedQTok / kFusedSub; ++m16) {
+      for (int m16 = 0; m16 < n_sub; ++m16) {
         uint32_t a[2][4];
 #pragma unroll
         for (int ks = 0; ks < 2; ++ks) {
@@ -977,7 +1062,7 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
 #pragma unroll
           for (int e = 0; e < 4; ++e) a[ks][e] = kf::Mma<T>::relu2(a[ks][e]);
         }
-        if (m16 == kFusedQTok / kFusedSub - 1) {  // the stage is no longer read
+        if (m16 == n_sub - 1) {  // the stage is no longer read
           __syncwarp();
           if (lane == 0) kf::mbar_arrive(&empty[st]);
         }
@@ -1023,7 +1108,7 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
         kf::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          kf::tma_store_3d(&out_map, stage, h * kD, j * kFusedQTok + m16 * kFusedSub, b);
+          kf::tma_store_3d(&out_map, stage, h * kD, tok0 + m16 * kFusedSub, b);
           kf::tma_store_commit();
         }
         ++nstore;
@@ -1031,6 +1116,9 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
     }
   }
   if (lane == 0) kf::tma_store_wait_read0();  // shared memory outlives the stores' reads
+  // Cluster form: this CTA's shared memory also outlives the peers' reads of its last `red`.
+  if (kCluster && cs > 1 && k > 0 && threadIdx.x == 0)
+    (void)kf::mbar_wait_bounded(xdone, (k - 1) & 1, &g_sana_error);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -1038,11 +1126,67 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
 // ------------------------------------------------------------------------------------------
 constexpr int kFastStages = 3;
 
-// Fused path (no workspace): one CTA per SM over the batch x head units.
-bool fused_fills_device(int64_t B, int64_t H) {
+// Most clusters of `cs` fused CTAs resident at once on the current device (0: that size does
+// not launch). Cached per device; every instantiation has the same shape (threads, shared
+// memory, one CTA per SM), so one of them answers for all.
+int fused_max_clusters(int cs) {
+  static int cache[64][kFusedMaxCluster + 1] = {};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  if (dev < 0 || dev >= 64 || cs < 1 || cs > kFusedMaxCluster) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev][cs] != 0) return cache[dev][cs] > 0 ? cache[dev][cs] : 0;
+  auto kernel = sana_head_fused<__nv_bfloat16, __nv_bfloat16, true>;
+  int n = 0;
+  if (kf_host::prepare_kernel(reinterpret_cast<const void*>(kernel), kFusedThreads, FusedSmem::kBytes, nullptr) ==
+      KF_OK) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cs);
+    cfg.blockDim = dim3(kFusedThreads);
+    cfg.dynamicSmemBytes = FusedSmem::kBytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) {
+      (void)cudaGetLastError();
+      n = 0;
+    }
+  }
+  cache[dev][cs] = n > 0 ? n : -1;
+  return n > 0 ? n : 0;
+}
+
+// CTAs per (batch, head) unit on the fused path: 1 when the units alone give every SM work;
+// otherwise the largest cluster size (at most 8, and at most one CTA per 64-token K/V stage) whose
+// clusters, one per unit, are all resident at once.
+int fused_cluster_size(int64_t B, int64_t H, int64_t N) {
   const int64_t units = B * H, sms = kf_host::current_device_sms();
-  const int64_t waves = (units + sms - 1) / sms;
-  return units * 10 >= waves * sms * 9;  // at least 90% of the CTA slots of the last wave busy
+  if (units >= sms) return 1;
+  const int64_t kv_all = (N + kFusedKTok - 1) / kFusedKTok;
+  int best = 1;
+  for (int cs = 2; cs <= kFusedMaxCluster && cs <= kv_all && units * cs <= sms; ++cs)
+    if (units <= fused_max_clusters(cs)) best = cs;
+  return best;
+}
+
+// The fused path (no workspace) is the automatic choice when its CTAs give the SMs work (at
+// least 90% of the CTA slots of the last wave busy), or when they outnumber the split path's
+// producer CTAs (few heads: the split path caps its splits per head pair). Both rules follow
+// same-box timings of the two paths over batch 1-4, 4-100 heads, 1K-16K tokens.
+bool fused_preferred(int64_t B, int64_t H, int64_t N) {
+  const int64_t sms = kf_host::current_device_sms();
+  const int64_t ctas = B * H * fused_cluster_size(B, H, N);
+  const int64_t waves = (ctas + sms - 1) / sms;
+  if (ctas * 10 >= waves * sms * 9) return true;
+  return B * ceil_div(H, kFastHeads) * fast_splits(B, H, N, 0) < ctas;
 }
 
 template <typename T>
@@ -1070,19 +1214,41 @@ int launch_fused(const void* qkv, void* out, int B, int H, int N, float eps, int
   if (!kf_host::encode_tiled(&out_map, kf_host::map_type(out_dtype), 3, out, odims, ostrides, obox,
                              os == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
     return KF_ERR_CUDA;
-  const int grid = static_cast<int>(std::min<int64_t>(static_cast<int64_t>(B) * H, kf_host::current_device_sms()));
-  auto run = [&](auto kernel) -> int {
-    const int prep = kf_host::prepare_kernel(reinterpret_cast<const void*>(kernel), kFusedThreads, FusedSmem::kBytes,
-                                             nullptr);
+  const int64_t units = static_cast<int64_t>(B) * H;
+  const int cs = fused_cluster_size(B, H, N);
+  auto run = [&](auto one_cta, auto clustered) -> int {
+    if (cs == 1) {
+      const int grid = static_cast<int>(std::min<int64_t>(units, kf_host::current_device_sms()));
+      const int prep = kf_host::prepare_kernel(reinterpret_cast<const void*>(one_cta), kFusedThreads,
+                                               FusedSmem::kBytes, nullptr);
+      if (prep != KF_OK) return prep;
+      one_cta<<<grid, kFusedThreads, FusedSmem::kBytes, stream>>>(kv_map, q_map, out_map, B, H, N, eps);
+      KF_LAUNCH_CHECK();
+      return KF_OK;
+    }
+    const int prep = kf_host::prepare_kernel(reinterpret_cast<const void*>(clustered), kFusedThreads,
+                                             FusedSmem::kBytes, nullptr);
     if (prep != KF_OK) return prep;
-    kernel<<<grid, kFusedThreads, FusedSmem::kBytes, stream>>>(kv_map, q_map, out_map, B, H, N, eps);
-    KF_LAUNCH_CHECK();
+    // One cluster per unit (fused_cluster_size checked that they are all resident at once).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(units * cs));
+    cfg.blockDim = dim3(kFusedThreads);
+    cfg.dynamicSmemBytes = FusedSmem::kBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    KF_CUDA_TRY(cudaLaunchKernelEx(&cfg, clustered, kv_map, q_map, out_map, B, H, N, eps));
     return KF_OK;
   };
   switch (out_dtype) {
-    case KF_DTYPE_F32: return run(sana_head_fused<T, float>);
-    case KF_DTYPE_F16: return run(sana_head_fused<T, __half>);
-    default: return run(sana_head_fused<T, __nv_bfloat16>);
+    case KF_DTYPE_F32: return run(sana_head_fused<T, float, false>, sana_head_fused<T, float, true>);
+    case KF_DTYPE_F16: return run(sana_head_fused<T, __half, false>, sana_head_fused<T, __half, true>);
+    default: return run(sana_head_fused<T, __nv_bfloat16, false>, sana_head_fused<T, __nv_bfloat16, true>);
   }
 }
 
@@ -1252,8 +1418,8 @@ KF_API int kf_sana_linattn_fwd(const void* qkv, void* out, void* workspace, size
 
   const bool fast = d == kD && (in_dtype == KF_DTYPE_BF16 || in_dtype == KF_DTYPE_F16) &&
                     H * kD >= 64 && N >= kTok && kf::aligned(qkv, 16) && kf::aligned(out, 16);
-  if (fast && (splits == -1 || (splits == 0 && fused_fills_device(B, H)))) {
-    // Whole heads per CTA, one launch, no workspace traffic.
+  if (fast && (splits == -1 || (splits == 0 && fused_preferred(B, H, N)))) {
+    // Whole heads per CTA (or per cluster of CTAs), one launch, no workspace traffic.
     if (in_dtype == KF_DTYPE_BF16) return launch_fused<__nv_bfloat16>(qkv, out, B, H, N, eps, out_dtype, s);
     return launch_fused<__half>(qkv, out, B, H, N, eps, out_dtype, s);
   }
@@ -1273,6 +1439,31 @@ KF_API int kf_sana_linattn_fwd(const void* qkv, void* out, void* workspace, size
     default:
       return launch_generic<__nv_bfloat16>(qkv, out, partial, final_vk, counters, B, H, d, N, S_gen, eps, out_dtype, s);
   }
+}
+
+KF_API int kf_sana_linattn_plan(int64_t batch, int64_t heads, int64_t dim, int64_t seq_len, int64_t splits,
+                                int in_dtype, int64_t* launches, int64_t* ctas_per_unit) {
+  if (launches == nullptr || ctas_per_unit == nullptr) return KF_ERR_INVALID_ARGUMENT;
+  if (!kf::dtype_valid(in_dtype)) return KF_ERR_UNSUPPORTED;
+  if (batch <= 0 || heads <= 0 || seq_len <= 0) return KF_ERR_INVALID_ARGUMENT;
+  if (!valid_head_dim(dim)) return KF_ERR_UNSUPPORTED;
+  if (batch > 65535 || seq_len > (int64_t(1) << 30) || heads * dim > (int64_t(1) << 24)) return KF_ERR_UNSUPPORTED;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return KF_ERR_CUDA;
+  }
+  // The same tests as kf_sana_linattn_fwd, for 16-byte aligned qkv and out.
+  const bool fast = dim == kD && (in_dtype == KF_DTYPE_BF16 || in_dtype == KF_DTYPE_F16) && heads * kD >= 64 &&
+                    seq_len >= kTok;
+  if (fast && (splits == -1 || (splits == 0 && fused_preferred(batch, heads, seq_len)))) {
+    *launches = 1;
+    *ctas_per_unit = fused_cluster_size(batch, heads, seq_len);
+  } else {
+    *launches = 2;
+    *ctas_per_unit = 0;
+  }
+  return KF_OK;
 }
 
 // ------------------------------------------------------------------------------------------

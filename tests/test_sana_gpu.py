@@ -113,6 +113,52 @@ def test_fused_path_shapes(kf, b, n, h, dtype, out_dtype):
     check_exact(first, qkv, h, 32)
 
 
+# Fewer (batch, head) units than SMs: the one-launch path splits each unit's tokens over a
+# thread-block cluster (up to 8 CTAs, at most one per 64-token K/V stage). Ragged cases leave
+# the last ranks without K/V or Q tiles (they still take part in the exchange).
+@pytest.mark.parametrize("dtype,out_dtype", [(torch.bfloat16, torch.bfloat16), (torch.float16, torch.float32),
+                                             (torch.bfloat16, torch.float16)])
+@pytest.mark.parametrize("b,n,h", [(1, 4096, 36), (1, 2048, 70), (1, 16384, 18), (3, 500, 7), (1, 8192, 29),
+                                   (1, 300, 48), (1, 130, 5), (1, 200, 2), (2, 4097, 9), (1, 1000, 4)])
+def test_cluster_path_shapes(kf, b, n, h, dtype, out_dtype):
+    g = torch.Generator().manual_seed(b * 9000 + n + h)
+    qkv = torch.randn(b, n, 3, h * 32, generator=g).to(dtype)
+    fn = kf.QKVAttnMatmul(b, h, 32, n, 1e-15, NAMES[dtype], NAMES[out_dtype], splits=-1)
+    launches, ctas = fn.plan()
+    assert launches == 1 and 1 <= ctas <= 8
+    assert ctas <= -(-n // 64) and b * h * ctas <= torch.cuda.get_device_properties(0).multi_processor_count
+    q = qkv.cuda()
+    outs = [fn(q).clone() for _ in range(3)]
+    assert outs[0].shape == (b, n, h * 32) and outs[0].dtype == out_dtype
+    for other in outs[1:]:
+        assert torch.equal(outs[0], other)  # the CTAs' partials are summed in rank order
+    check_exact(outs[0], qkv, h, 32)
+
+
+def test_cluster_path_is_used_below_the_sm_count(kf):
+    """Batch 1 with 70 heads (a reference harness shape) runs one launch over clusters."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    launches, ctas = kf.QKVAttnMatmul(1, 70, 32, 4096, 1e-15, "bfloat16", "bfloat16").plan()
+    assert launches == 1 and ctas >= 2 and 70 * ctas <= sms
+    # Units that fill the SMs keep one CTA per unit. Otherwise the automatic choice takes the
+    # path with more CTAs: the split path for 36 heads (18 head pairs x 8 splits), the cluster
+    # path for 2 heads (8-CTA clusters against one head pair x 8 splits).
+    assert kf.QKVAttnMatmul(4, 36, 32, 4096, 1e-15, "bfloat16", "bfloat16").plan() == (1, 1)
+    if sms >= 144:
+        assert kf.QKVAttnMatmul(1, 36, 32, 4096, 1e-15, "bfloat16", "bfloat16").plan() == (2, 0)
+    assert kf.QKVAttnMatmul(1, 2, 32, 4096, 1e-15, "bfloat16", "bfloat16").plan() == (1, 8)
+    assert kf.QKVAttnMatmul(1, 2, 32, 4096, 1e-15, "bfloat16", "bfloat16", splits=-1).plan() == (1, 8)
+    assert kf.QKVAttnMatmul(1, 2, 32, 4096, 1e-15, "bfloat16", "bfloat16", splits=3).plan() == (2, 0)
+
+
+def test_cluster_and_split_paths_agree(kf):
+    g = torch.Generator().manual_seed(17)
+    qkv = torch.randn(1, 4096, 3, 36 * 32, generator=g).to(torch.bfloat16).cuda()
+    clustered = kf.QKVAttnMatmul(1, 36, 32, 4096, 1e-15, "bfloat16", "float", splits=-1)(qkv)
+    split = kf.QKVAttnMatmul(1, 36, 32, 4096, 1e-15, "bfloat16", "float", splits=4)(qkv)
+    torch.testing.assert_close(clustered, split, rtol=1e-5, atol=1e-6)
+
+
 def test_fused_and_split_paths_agree(kf):
     g = torch.Generator().manual_seed(13)
     qkv = torch.randn(2, 2048, 3, 6 * 32, generator=g).to(torch.bfloat16).cuda()
