@@ -117,13 +117,11 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait that also gives up as soon as another thread of the CTA has set *abort (a
 // shared-memory flag), so a CTA whose roles synchronise with each other never waits out one
 // timeout per remaining step after the first failure. A timeout sets *abort itself.
-// kPoll: probe with test_wait (no suspension) instead of try_wait. kCluster: acquire at cluster
-// scope (the phase completes through other CTAs' arrivals).
-template <bool kRelaxed = false, bool kPoll = false, bool kCluster = false>
+// kPoll: probe with test_wait (no suspension) instead of try_wait.
+template <bool kRelaxed = false, bool kPoll = false>
 __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, unsigned int* err,
                                                    volatile int* abort) {
   auto probe = [&]() {
-    if constexpr (kCluster) return mbar_try_wait_cluster(bar, parity);
     return kPoll ? mbar_test_wait(bar, parity)
                  : (kRelaxed ? mbar_try_wait_relaxed(bar, parity) : mbar_try_wait(bar, parity));
   };
@@ -132,6 +130,26 @@ __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parit
   uint32_t spins = 0;
   while (true) {
     if (probe()) return true;
+    if ((++spins & 63u) == 0) {
+      if (*abort) return false;
+      if (globaltimer_ns() - start > kWaitTimeoutNs) {
+        atomicCAS(err, 0u, static_cast<unsigned int>(KF_ERR_DEVICE_TIMEOUT));
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// mbar_wait_or_abort for a phase that other CTAs of the cluster complete (their arrivals
+// release their writes): probes with acquire at cluster scope.
+__device__ __forceinline__ bool mbar_wait_cluster_or_abort(uint64_t* bar, uint32_t parity, unsigned int* err,
+                                                           volatile int* abort) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t start = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
     if ((++spins & 63u) == 0) {
       if (*abort) return false;
       if (globaltimer_ns() - start > kWaitTimeoutNs) {

@@ -748,15 +748,17 @@ sana_out_generic(const T* __restrict__ qkv, const float* __restrict__ final_vk, 
 // in flight while the warps reduce. fp16 inputs scale B by a power of two that keeps max|B|
 // below 2^14, with eps scaled alike.
 //
-// Cluster form (kCluster): when there are fewer units than SMs, a cluster of CS CTAs shares one
-// unit. CTA rank r takes the r-th of CS equal ranges of K/V tiles and of Q tiles, sums its warp
+// Cluster form (sana_head_cluster): when there are fewer units than SMs, a cluster of CS CTAs
+// shares one unit. CTA rank r takes the r-th of CS equal ranges of K/V tiles and of Q tiles, sums its warp
 // partials into `red`, and the CTAs exchange them through distributed shared memory: each CTA
 // arrives on every peer's `xready` mbarrier once its `red` is written, waits for its own
 // `xready`, sums the CS partials in rank order into `tot` (so every CTA of the cluster holds
 // the same bits, and the result does not depend on timing), then arrives on every peer's
 // `xdone`. A CTA rewrites `red` for its next unit, and leaves the kernel, only after its
 // `xdone` phase for the previous unit has completed (every peer has finished reading it).
-// All of these waits are bounded like the ring's.
+// All of these waits are bounded like the ring's. It is its own kernel: one template for both
+// forms measured 2% slower on the one-CTA form (B=2, H=70, N=16384), with identical source for
+// that form.
 // ------------------------------------------------------------------------------------------
 constexpr int kFusedWarps = 16;                          // compute warps
 constexpr int kFusedThreads = 32 * (kFusedWarps + 1);    // + the TMA producer warp
@@ -773,14 +775,22 @@ struct FusedSmem {
   // Warp w's slot: its phase-1 partial, then (reused) its phase-2 output staging, two 16-token
   // buffers at 1024-byte aligned offsets (the swizzled TMA store tiles need that alignment).
   static constexpr int kPartOff = kFusedStages * kFusedStageBytes;
-  static constexpr int kRedOff = kPartOff + kFusedWarps * kFusedSlotBytes;  // this CTA's [VK ; ksum]
-  static constexpr int kTotOff = kRedOff + kFusedPartBytes;                 // cluster sum (cluster form)
-  static constexpr int kMaxOff = kTotOff + kFusedPartBytes;                 // two max|B| words
+  static constexpr int kRedOff = kPartOff + kFusedWarps * kFusedSlotBytes;  // reduced [VK ; ksum]
+  static constexpr int kBarOff = kRedOff + kFusedPartBytes + 16;            // + two max|B| words
+  static constexpr int kBytes = kBarOff + 2 * kFusedStages * 8 + 16 + 1024;
+};
+// Cluster form: the same up to `red` (this CTA's [VK ; ksum]), then the cluster sum `tot`, and
+// two more mbarriers (xready, xdone) after the abort word.
+struct ClusterSmem {
+  static constexpr int kRingOff = FusedSmem::kRingOff;
+  static constexpr int kPartOff = FusedSmem::kPartOff;
+  static constexpr int kRedOff = FusedSmem::kRedOff;
+  static constexpr int kTotOff = kRedOff + kFusedPartBytes;
+  static constexpr int kMaxOff = kTotOff + kFusedPartBytes;  // two max|B| words
   static constexpr int kBarOff = kMaxOff + 16;
-  // full[], empty[], the abort word (16 bytes), xready, xdone; + alignment slack
   static constexpr int kBytes = kBarOff + 2 * kFusedStages * 8 + 16 + 16 + 1024;
 };
-static_assert(FusedSmem::kRedOff % 16 == 0 && FusedSmem::kTotOff % 16 == 0 && kFusedPartBytes % 16 == 0,
+static_assert(ClusterSmem::kRedOff % 16 == 0 && ClusterSmem::kTotOff % 16 == 0 && kFusedPartBytes % 16 == 0,
               "the cluster exchange moves 16-byte vectors");
 constexpr int kFusedMaxCluster = 8;  // portable cluster size limit
 static_assert(kFusedPartBytes <= kFusedSlotBytes && 2 * 2048 <= kFusedSlotBytes, "slot sizes");
@@ -794,7 +804,7 @@ __device__ __forceinline__ uint32_t swz64(uint32_t row, uint32_t chunk) {
   return row * 64 + ((chunk ^ ((row >> 1) & 3)) << 4);
 }
 
-template <typename T, typename O, bool kCluster>
+template <typename T, typename O>
 __global__ void __launch_bounds__(kFusedThreads, 1)
 sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constant__ CUtensorMap q_map,
                 const __grid_constant__ CUtensorMap out_map, int B, int H, int N, float eps) {
@@ -804,27 +814,14 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + FusedSmem::kBarOff);
   uint64_t* empty = full + kFusedStages;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kFusedStages);
-  uint64_t* xready = empty + kFusedStages + 2;  // past the 16-byte abort word
-  uint64_t* xdone = xready + 1;
   float* red = reinterpret_cast<float*>(smem + FusedSmem::kRedOff);
-  float* tot = reinterpret_cast<float*>(smem + FusedSmem::kTotOff);
-  unsigned int* max_bits = reinterpret_cast<unsigned int*>(smem + FusedSmem::kMaxOff);
+  unsigned int* max_bits = reinterpret_cast<unsigned int*>(red + kRows * kD);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, tig = lane & 3, sub = lane >> 3;
   const int units = B * H;
-  // Cluster form: CS CTAs per unit, this CTA is rank `rank`; otherwise one CTA per unit.
-  const int cs = kCluster ? static_cast<int>(kf::cluster_nctarank()) : 1;
-  const int rank = kCluster ? static_cast<int>(kf::cluster_ctarank()) : 0;
-  const int first_unit = kCluster ? static_cast<int>(kf::cluster_id_x()) : static_cast<int>(blockIdx.x);
-  const int unit_step = kCluster ? static_cast<int>(kf::cluster_count_x()) : static_cast<int>(gridDim.x);
-  // This CTA's share of every unit: K/V tiles [kv0, kv0 + kv_tiles), Q tiles [q0, q0 + q_tiles).
-  const int kv_all = (N + kFusedKTok - 1) / kFusedKTok;
-  const int q_all = (N + kFusedQTok - 1) / kFusedQTok;
-  const int kv_per = (kv_all + cs - 1) / cs, q_per = (q_all + cs - 1) / cs;
-  const int kv0 = min(kv_all, rank * kv_per), q0 = min(q_all, rank * q_per);
-  const int kv_tiles = min(kv_all, kv0 + kv_per) - kv0;
-  const int q_tiles = min(q_all, q0 + q_per) - q0;
+  const int kv_tiles = (N + kFusedKTok - 1) / kFusedKTok;
+  const int q_tiles = (N + kFusedQTok - 1) / kFusedQTok;
   const int per_unit = kv_tiles + q_tiles;  // ring stages per unit
 
   if (threadIdx.x == 0) {
@@ -835,21 +832,17 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
       kf::mbar_init(&full[s], 1);
       kf::mbar_init(&empty[s], 1);
     }
-    kf::mbar_init(xready, cs > 1 ? cs - 1 : 1);  // one arrival per peer
-    kf::mbar_init(xdone, cs > 1 ? cs - 1 : 1);
     *abort_flag = 0;
     max_bits[0] = max_bits[1] = 0u;
     kf::fence_mbar_init();
   }
-  // Peers arrive on this CTA's xready / xdone, so they must be initialised cluster-wide first.
-  if constexpr (kCluster) kf::cluster_sync_all();
-  else __syncthreads();
+  __syncthreads();
 
   if (warp == kFusedWarps) {
     // ---- TMA producer (one thread): every unit's K/V tiles, then its Q tiles ----
     if (lane == 0) {
       int seq = 0;
-      for (int u = first_unit; u < units; u += unit_step) {
+      for (int u = blockIdx.x; u < units; u += gridDim.x) {
         const int b = u / H, h = u % H;
         for (int i = 0; i < per_unit; ++i, ++seq) {
           const int st = seq % kFusedStages;
@@ -859,11 +852,10 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
           uint8_t* base = smem + FusedSmem::kRingOff + st * kFusedStageBytes;
           kf::mbar_arrive_expect_tx(&full[st], kFusedStageBytes);
           if (i < kv_tiles) {
-            const int tok = (kv0 + i) * kFusedKTok;
-            kf::tma_load_4d(base, &kv_map, &full[st], h * kD, 1, tok, b);
-            kf::tma_load_4d(base + kFusedStageBytes / 2, &kv_map, &full[st], h * kD, 2, tok, b);
+            kf::tma_load_4d(base, &kv_map, &full[st], h * kD, 1, i * kFusedKTok, b);
+            kf::tma_load_4d(base + kFusedStageBytes / 2, &kv_map, &full[st], h * kD, 2, i * kFusedKTok, b);
           } else {
-            kf::tma_load_4d(base, &q_map, &full[st], h * kD, 0, (q0 + i - kv_tiles) * kFusedQTok, b);
+            kf::tma_load_4d(base, &q_map, &full[st], h * kD, 0, (i - kv_tiles) * kFusedQTok, b);
           }
         }
       }
@@ -876,8 +868,7 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
   int seq0 = 0;  // ring sequence number of the unit's first stage
   bool ok = true;
   int parity = 0;  // max|B| word of this unit (two words: one is reset while the other is in use)
-  int k = 0;       // units this CTA has finished (the phase of xready / xdone)
-  for (int u = first_unit; u < units; u += unit_step, seq0 += per_unit, parity ^= 1, ++k) {
+  for (int u = blockIdx.x; u < units; u += gridDim.x, seq0 += per_unit, parity ^= 1) {
     const int b = u / H, h = u % H;
     // Phase 1: this warp's K/V tiles.
     float acc[2][4][4];
@@ -954,11 +945,6 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
     kf::named_bar_sync(kFusedBar, 32 * kFusedWarps);
     // Every compute thread is past the previous unit's read of the other word.
     if (threadIdx.x == 0) max_bits[parity ^ 1] = 0u;
-    const bool exchange = kCluster && cs > 1;
-    // Cluster form: every peer has finished reading this CTA's previous `red`.
-    if (exchange && k > 0 && ok)
-      ok = __all_sync(0xffffffffu,
-                      kf::mbar_wait_or_abort<false, false, true>(xdone, (k - 1) & 1, &g_sana_error, abort_flag));
     // Sum of the 16 partials in warp order, and max|B| for the fp16 scale.
     float m = 0.f;
     for (int e = threadIdx.x; e < kRows * kD; e += 32 * kFusedWarps) {
@@ -966,6 +952,284 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
 #pragma unroll
       for (int w = 0; w < kFusedWarps; ++w)
         s += reinterpret_cast<const float*>(smem + FusedSmem::kPartOff + w * kFusedSlotBytes)[e];
+      red[e] = s;
+      m = fmaxf(m, fabsf(s));
+    }
+    if (kFp16) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (lane == 0) atomicMax(&max_bits[parity], __float_as_uint(m));  // non-negative floats order as integers
+    }
+    kf::named_bar_sync(kFusedBar, 32 * kFusedWarps);
+    const float scale = operand_scale(__uint_as_float(max_bits[parity]), kFp16);
+    const float eps_s = eps * scale;
+    // B fragments (K = q channel c, N = output row r: VK[r][c], r = 32 is ksum[c], rows 33..39 zero)
+    // as hi and lo halves.
+    uint32_t bhi[2][5][2], blo[2][5][2];
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks)
+#pragma unroll
+      for (int nt = 0; nt < 5; ++nt) {
+        const int r = nt * 8 + gid;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int c = ks * 16 + tig * 2 + half * 8;
+          float x0 = 0.f, x1 = 0.f;
+          if (r <= kD) {
+            x0 = red[r * kD + c] * scale;
+            x1 = red[r * kD + c + 1] * scale;
+          }
+          bhi[ks][nt][half] = kf::Mma<T>::from_f2(x0, x1);
+          const float2 hf = kf::Mma<T>::to_f2(bhi[ks][nt][half]);
+          blo[ks][nt][half] = kf::Mma<T>::from_f2(x0 - hf.x, x1 - hf.y);
+        }
+      }
+    // Phase 2: this warp's Q tiles, 16 tokens at a time.
+    int nstore = 0;
+    for (int j = (warp - (seq0 + kv_tiles) % kFusedWarps + kFusedWarps) % kFusedWarps; j < q_tiles;
+         j += kFusedWarps) {
+      const int seq = seq0 + kv_tiles + j, st = seq % kFusedStages;
+      if (ok) ok = __all_sync(0xffffffffu, kf::mbar_wait_or_abort(&full[st], (seq / kFusedStages) & 1,
+                                                                  &g_sana_error, abort_flag));
+      if (!ok) break;
+      const uint32_t qbase = kf::smem_u32(smem + FusedSmem::kRingOff + st * kFusedStageBytes);
+#pragma unroll 1
+      for (int m16 = 0; m16 < kFusedQTok / kFusedSub; ++m16) {
+        uint32_t a[2][4];
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+          const int row = m16 * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          kf::ldsm_x4(qbase + swz64(row, ks * 2 + (lane >> 4)), a[ks][0], a[ks][1], a[ks][2], a[ks][3]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) a[ks][e] = kf::Mma<T>::relu2(a[ks][e]);
+        }
+        if (m16 == kFusedQTok / kFusedSub - 1) {  // the stage is no longer read
+          __syncwarp();
+          if (lane == 0) kf::mbar_arrive(&empty[st]);
+        }
+        float d[5][4];
+#pragma unroll
+        for (int nt = 0; nt < 5; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) d[nt][e] = 0.f;
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks)
+#pragma unroll
+          for (int nt = 0; nt < 5; ++nt) {
+            kf::Mma<T>::run(d[nt], a[ks], bhi[ks][nt]);
+            kf::Mma<T>::run(d[nt], a[ks], blo[ks][nt]);
+          }
+        // Denominator D[row][32]: column 0 of n-tile 4, held by the quad's first thread.
+        const float den0 = __shfl_sync(0xffffffffu, d[4][0], lane & ~3);
+        const float den1 = __shfl_sync(0xffffffffu, d[4][2], lane & ~3);
+        const float inv0 = __frcp_rn(den0 + eps_s), inv1 = __frcp_rn(den1 + eps_s);
+        // Stage 16 tokens x 32 channels in buffer (nstore & 1) once its previous store has read it.
+        uint8_t* stage = part + (nstore & 1) * (kFusedSub * kD * int(sizeof(O)));
+        if (lane == 0) kf::tma_store_wait_read1();
+        __syncwarp();
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          const int c = nt * 8 + tig * 2;
+          if constexpr (sizeof(O) == 4) {
+            // rows of 128 bytes, 128-byte swizzle
+            const uint32_t off = (c & 3) * 4;
+            *reinterpret_cast<float2*>(stage + gid * 128 + (((c >> 2) ^ (gid & 7)) << 4) + off) =
+                make_float2(d[nt][0] * inv0, d[nt][1] * inv0);
+            *reinterpret_cast<float2*>(stage + (gid + 8) * 128 + (((c >> 2) ^ ((gid + 8) & 7)) << 4) + off) =
+                make_float2(d[nt][2] * inv1, d[nt][3] * inv1);
+          } else {
+            // rows of 64 bytes, 64-byte swizzle
+            const uint32_t off = (c & 7) * 2;
+            *reinterpret_cast<uint32_t*>(stage + swz64(gid, c >> 3) + off) =
+                kf::Mma<O>::from_f2(d[nt][0] * inv0, d[nt][1] * inv0);
+            *reinterpret_cast<uint32_t*>(stage + swz64(gid + 8, c >> 3) + off) =
+                kf::Mma<O>::from_f2(d[nt][2] * inv1, d[nt][3] * inv1);
+          }
+        }
+        kf::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          kf::tma_store_3d(&out_map, stage, h * kD, j * kFusedQTok + m16 * kFusedSub, b);
+          kf::tma_store_commit();
+        }
+        ++nstore;
+      }
+    }
+  }
+  if (lane == 0) kf::tma_store_wait_read0();  // shared memory outlives the stores' reads
+}
+
+template <typename T, typename O>
+__global__ void __launch_bounds__(kFusedThreads, 1)
+sana_head_cluster(const __grid_constant__ CUtensorMap kv_map, const __grid_constant__ CUtensorMap q_map,
+                const __grid_constant__ CUtensorMap out_map, int B, int H, int N, float eps) {
+  constexpr bool kFp16 = std::is_same<T, __half>::value;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (kf::smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + ClusterSmem::kBarOff);
+  uint64_t* empty = full + kFusedStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kFusedStages);
+  uint64_t* xready = empty + kFusedStages + 2;  // past the 16-byte abort word
+  uint64_t* xdone = xready + 1;
+  float* red = reinterpret_cast<float*>(smem + ClusterSmem::kRedOff);
+  float* tot = reinterpret_cast<float*>(smem + ClusterSmem::kTotOff);
+  unsigned int* max_bits = reinterpret_cast<unsigned int*>(smem + ClusterSmem::kMaxOff);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gid = lane >> 2, tig = lane & 3, sub = lane >> 3;
+  const int units = B * H;
+  // CS CTAs per unit (one cluster); this CTA is rank `rank`.
+  const int cs = static_cast<int>(kf::cluster_nctarank());
+  const int rank = static_cast<int>(kf::cluster_ctarank());
+  const int first_unit = static_cast<int>(kf::cluster_id_x());
+  const int unit_step = static_cast<int>(kf::cluster_count_x());
+  // This CTA's share of every unit: K/V tiles [kv0, kv0 + kv_tiles), Q tiles [q0, q0 + q_tiles).
+  const int kv_all = (N + kFusedKTok - 1) / kFusedKTok;
+  const int q_all = (N + kFusedQTok - 1) / kFusedQTok;
+  const int kv_per = (kv_all + cs - 1) / cs, q_per = (q_all + cs - 1) / cs;
+  const int kv0 = min(kv_all, rank * kv_per), q0 = min(q_all, rank * q_per);
+  const int kv_tiles = min(kv_all, kv0 + kv_per) - kv0;
+  const int q_tiles = min(q_all, q0 + q_per) - q0;
+  const int per_unit = kv_tiles + q_tiles;  // ring stages per unit
+
+  if (threadIdx.x == 0) {
+    kf::prefetch_tensormap(&kv_map);
+    kf::prefetch_tensormap(&q_map);
+    kf::prefetch_tensormap(&out_map);
+    for (int s = 0; s < kFusedStages; ++s) {
+      kf::mbar_init(&full[s], 1);
+      kf::mbar_init(&empty[s], 1);
+    }
+    kf::mbar_init(xready, cs > 1 ? cs - 1 : 1);  // one arrival per peer
+    kf::mbar_init(xdone, cs > 1 ? cs - 1 : 1);
+    *abort_flag = 0;
+    max_bits[0] = max_bits[1] = 0u;
+    kf::fence_mbar_init();
+  }
+  // Peers arrive on this CTA's xready / xdone, so they must be initialised cluster-wide first.
+  kf::cluster_sync_all();
+
+  if (warp == kFusedWarps) {
+    // ---- TMA producer (one thread): every unit's K/V tiles, then its Q tiles ----
+    if (lane == 0) {
+      int seq = 0;
+      for (int u = first_unit; u < units; u += unit_step) {
+        const int b = u / H, h = u % H;
+        for (int i = 0; i < per_unit; ++i, ++seq) {
+          const int st = seq % kFusedStages;
+          if (seq >= kFusedStages &&
+              !kf::mbar_wait_or_abort<true>(&empty[st], ((seq / kFusedStages) - 1) & 1, &g_sana_error, abort_flag))
+            return;
+          uint8_t* base = smem + ClusterSmem::kRingOff + st * kFusedStageBytes;
+          kf::mbar_arrive_expect_tx(&full[st], kFusedStageBytes);
+          if (i < kv_tiles) {
+            const int tok = (kv0 + i) * kFusedKTok;
+            kf::tma_load_4d(base, &kv_map, &full[st], h * kD, 1, tok, b);
+            kf::tma_load_4d(base + kFusedStageBytes / 2, &kv_map, &full[st], h * kD, 2, tok, b);
+          } else {
+            kf::tma_load_4d(base, &q_map, &full[st], h * kD, 0, (q0 + i - kv_tiles) * kFusedQTok, b);
+          }
+        }
+      }
+    }
+    return;
+  }
+
+  // ---- compute warps ----
+  uint8_t* part = smem + ClusterSmem::kPartOff + warp * kFusedSlotBytes;  // this warp's slot
+  int seq0 = 0;  // ring sequence number of the unit's first stage
+  bool ok = true;
+  int parity = 0;  // max|B| word of this unit (two words: one is reset while the other is in use)
+  int k = 0;       // units this CTA has finished (the phase of xready / xdone)
+  for (int u = first_unit; u < units; u += unit_step, seq0 += per_unit, parity ^= 1, ++k) {
+    const int b = u / H, h = u % H;
+    // Phase 1: this warp's K/V tiles.
+    float acc[2][4][4];
+    float ksum[4];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      ksum[nt] = 0.f;
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[mt][nt][j] = 0.f;
+    }
+    for (int i = (warp - seq0 % kFusedWarps + kFusedWarps) % kFusedWarps; i < kv_tiles; i += kFusedWarps) {
+      const int seq = seq0 + i, st = seq % kFusedStages;
+      if (ok) ok = __all_sync(0xffffffffu, kf::mbar_wait_or_abort(&full[st], (seq / kFusedStages) & 1,
+                                                                  &g_sana_error, abort_flag));
+      if (!ok) break;
+      const uint32_t kbase = kf::smem_u32(smem + ClusterSmem::kRingOff + st * kFusedStageBytes);
+      const uint32_t vbase = kbase + kFusedStageBytes / 2;
+#pragma unroll
+      for (int ks = 0; ks < kFusedKTok / 16; ++ks) {
+        uint32_t a[2][4];
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          // A = V^T (M = v channel, K = token): transposed 8x8 loads of token-major rows.
+          const int row = ks * 16 + (lane & 7) + (sub >> 1) * 8;
+          kf::ldsm_x4_t(vbase + swz64(row, mt * 2 + (sub & 1)), a[mt][0], a[mt][1], a[mt][2], a[mt][3]);
+        }
+        uint32_t bf[4][2];
+#pragma unroll
+        for (int np = 0; np < 2; ++np) {
+          // B = relu(K) (K = token, N = k channel), two n-tiles per x4 load.
+          const int row = ks * 16 + (lane & 7) + (sub & 1) * 8;
+          kf::ldsm_x4_t(kbase + swz64(row, np * 2 + (sub >> 1)), bf[2 * np][0], bf[2 * np][1], bf[2 * np + 1][0],
+                        bf[2 * np + 1][1]);
+        }
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          bf[nt][0] = kf::Mma<T>::relu2(bf[nt][0]);
+          bf[nt][1] = kf::Mma<T>::relu2(bf[nt][1]);
+          const float2 x = kf::Mma<T>::to_f2(bf[nt][0]);
+          const float2 y = kf::Mma<T>::to_f2(bf[nt][1]);
+          ksum[nt] += (x.x + x.y) + (y.x + y.y);
+        }
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+          for (int nt = 0; nt < 4; ++nt) kf::Mma<T>::run(acc[mt][nt], a[mt], bf[nt]);
+      }
+      __syncwarp();
+      if (lane == 0) kf::mbar_arrive(&empty[st]);
+    }
+    // This warp's partial [VK ; ksum] into its slot (its previous output stores must have read it).
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      ksum[nt] += __shfl_xor_sync(0xffffffffu, ksum[nt], 1);
+      ksum[nt] += __shfl_xor_sync(0xffffffffu, ksum[nt], 2);
+    }
+    if (lane == 0) kf::tma_store_wait_read0();
+    __syncwarp();
+    float* pw = reinterpret_cast<float*>(part);
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const int r = mt * 16 + gid, c = nt * 8 + tig * 2;
+        *reinterpret_cast<float2*>(pw + r * kD + c) = make_float2(acc[mt][nt][0], acc[mt][nt][1]);
+        *reinterpret_cast<float2*>(pw + (r + 8) * kD + c) = make_float2(acc[mt][nt][2], acc[mt][nt][3]);
+      }
+    if (tig == 0) {
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) pw[kD * kD + nt * 8 + gid] = ksum[nt];
+    }
+    kf::named_bar_sync(kFusedBar, 32 * kFusedWarps);
+    // Every compute thread is past the previous unit's read of the other word.
+    if (threadIdx.x == 0) max_bits[parity ^ 1] = 0u;
+    const bool exchange = cs > 1;
+    // Cluster form: every peer has finished reading this CTA's previous `red`.
+    if (exchange && k > 0 && ok)
+      ok = __all_sync(0xffffffffu,
+                      kf::mbar_wait_cluster_or_abort(xdone, (k - 1) & 1, &g_sana_error, abort_flag));
+    // Sum of the 16 partials in warp order, and max|B| for the fp16 scale.
+    float m = 0.f;
+    for (int e = threadIdx.x; e < kRows * kD; e += 32 * kFusedWarps) {
+      float s = 0.f;
+#pragma unroll
+      for (int w = 0; w < kFusedWarps; ++w)
+        s += reinterpret_cast<const float*>(smem + ClusterSmem::kPartOff + w * kFusedSlotBytes)[e];
       red[e] = s;
       m = fmaxf(m, fabsf(s));
     }
@@ -979,7 +1243,7 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
       }
       if (ok)
         ok = __all_sync(0xffffffffu,
-                        kf::mbar_wait_or_abort<false, false, true>(xready, k & 1, &g_sana_error, abort_flag));
+                        kf::mbar_wait_cluster_or_abort(xready, k & 1, &g_sana_error, abort_flag));
       m = 0.f;
       const uint32_t red_addr = kf::smem_u32(red);
       for (int e4 = threadIdx.x; e4 < kRows * kD / 4; e4 += 32 * kFusedWarps) {
@@ -1048,7 +1312,7 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
       if (ok) ok = __all_sync(0xffffffffu, kf::mbar_wait_or_abort(&full[st], (seq / kFusedStages) & 1,
                                                                   &g_sana_error, abort_flag));
       if (!ok) break;
-      const uint32_t qbase = kf::smem_u32(smem + FusedSmem::kRingOff + st * kFusedStageBytes);
+      const uint32_t qbase = kf::smem_u32(smem + ClusterSmem::kRingOff + st * kFusedStageBytes);
       // Tokens tok0 .. tok0 + 127, of which n_sub blocks of 16 reach into the sequence (>= 1).
       const int tok0 = (q0 + j) * kFusedQTok;
       const int n_sub = min(kFusedQTok / kFusedSub, (N - tok0 + kFusedSub - 1) / kFusedSub);
@@ -1117,7 +1381,7 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
   }
   if (lane == 0) kf::tma_store_wait_read0();  // shared memory outlives the stores' reads
   // Cluster form: this CTA's shared memory also outlives the peers' reads of its last `red`.
-  if (kCluster && cs > 1 && k > 0 && threadIdx.x == 0)
+  if (cs > 1 && k > 0 && threadIdx.x == 0)
     (void)kf::mbar_wait_bounded(xdone, (k - 1) & 1, &g_sana_error);
 }
 
@@ -1140,14 +1404,14 @@ int fused_max_clusters(int cs) {
   if (dev < 0 || dev >= 64 || cs < 1 || cs > kFusedMaxCluster) return 0;
   std::lock_guard<std::mutex> lock(mu);
   if (cache[dev][cs] != 0) return cache[dev][cs] > 0 ? cache[dev][cs] : 0;
-  auto kernel = sana_head_fused<__nv_bfloat16, __nv_bfloat16, true>;
+  auto kernel = sana_head_cluster<__nv_bfloat16, __nv_bfloat16>;
   int n = 0;
-  if (kf_host::prepare_kernel(reinterpret_cast<const void*>(kernel), kFusedThreads, FusedSmem::kBytes, nullptr) ==
+  if (kf_host::prepare_kernel(reinterpret_cast<const void*>(kernel), kFusedThreads, ClusterSmem::kBytes, nullptr) ==
       KF_OK) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(cs);
     cfg.blockDim = dim3(kFusedThreads);
-    cfg.dynamicSmemBytes = FusedSmem::kBytes;
+    cfg.dynamicSmemBytes = ClusterSmem::kBytes;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = cs;
@@ -1227,13 +1491,13 @@ int launch_fused(const void* qkv, void* out, int B, int H, int N, float eps, int
       return KF_OK;
     }
     const int prep = kf_host::prepare_kernel(reinterpret_cast<const void*>(clustered), kFusedThreads,
-                                             FusedSmem::kBytes, nullptr);
+                                             ClusterSmem::kBytes, nullptr);
     if (prep != KF_OK) return prep;
     // One cluster per unit (fused_cluster_size checked that they are all resident at once).
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(units * cs));
     cfg.blockDim = dim3(kFusedThreads);
-    cfg.dynamicSmemBytes = FusedSmem::kBytes;
+    cfg.dynamicSmemBytes = ClusterSmem::kBytes;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1246,9 +1510,9 @@ int launch_fused(const void* qkv, void* out, int B, int H, int N, float eps, int
     return KF_OK;
   };
   switch (out_dtype) {
-    case KF_DTYPE_F32: return run(sana_head_fused<T, float, false>, sana_head_fused<T, float, true>);
-    case KF_DTYPE_F16: return run(sana_head_fused<T, __half, false>, sana_head_fused<T, __half, true>);
-    default: return run(sana_head_fused<T, __nv_bfloat16, false>, sana_head_fused<T, __nv_bfloat16, true>);
+    case KF_DTYPE_F32: return run(sana_head_fused<T, float>, sana_head_cluster<T, float>);
+    case KF_DTYPE_F16: return run(sana_head_fused<T, __half>, sana_head_cluster<T, __half>);
+    default: return run(sana_head_fused<T, __nv_bfloat16>, sana_head_cluster<T, __nv_bfloat16>);
   }
 }
 
