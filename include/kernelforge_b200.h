@@ -66,6 +66,23 @@ int kf_rmsnorm_fwd(const void* x, const void* weight, void* y,
                    int64_t rows, int64_t dim, int64_t x_row_stride, int64_t y_row_stride,
                    float eps, int dtype, void* stream);
 
+/*
+ * RMSNorm backward. No counterpart in the reference, whose RMSNorm is forward-only
+ * (rmsnorm/README.md:5). Gradients of kf_rmsnorm_fwd's y = cast(cast(x r) w),
+ * r = 1 / sqrt(mean(x^2) + eps), with the casts taken as identities (as torch autograd does):
+ *   dx = r (dy w) - x r^3 ((dy w) . x) / dim          (fp32, rounded to dtype)
+ *   dweight = sum over rows of dy cast(x r)            (fp32, summed in a fixed order)
+ * x, dy, dx: `rows` rows of `dim` elements with their own row strides (elements). weight and
+ * dweight: `dim` elements, both NULL for no weight (then dx = r dy - x r^3 (dy . x) / dim).
+ * With a weight, `workspace` (kf_rmsnorm_bwd_workspace_size(dim) bytes, 16-byte aligned,
+ * contents ignored) holds the per-CTA dweight partials. rows == 0 writes zeros to dweight.
+ */
+size_t kf_rmsnorm_bwd_workspace_size(int64_t dim);
+int kf_rmsnorm_bwd(const void* x, const void* weight, const void* dy, void* dx, void* dweight,
+                   void* workspace, size_t workspace_bytes, int64_t rows, int64_t dim,
+                   int64_t x_row_stride, int64_t dy_row_stride, int64_t dx_row_stride, float eps,
+                   int dtype, void* stream);
+
 /* ------------------------------------------------------------------------------------------
  * SANA ReLU linear attention over packed QKV.
  * Replaces qkv_attn_matmul(batch, heads, dim, seq_len, eps, dtype, output_dtype,

@@ -32,6 +32,9 @@ SIGNATURES = {
     "kf_query_device_error": (ctypes.c_int, [_c_ptr, ctypes.POINTER(ctypes.c_int)]),
     "kf_rmsnorm_fwd": (ctypes.c_int, [_c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64,
                                       ctypes.c_float, ctypes.c_int, _c_ptr]),
+    "kf_rmsnorm_bwd_workspace_size": (ctypes.c_size_t, [_c_i64]),
+    "kf_rmsnorm_bwd": (ctypes.c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, ctypes.c_size_t, _c_i64,
+                                      _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_float, ctypes.c_int, _c_ptr]),
     "kf_sana_linattn_workspace_size": (ctypes.c_size_t, [_c_i64, _c_i64, _c_i64, _c_i64, _c_i64]),
     "kf_sana_linattn_fwd": (ctypes.c_int, [_c_ptr, _c_ptr, _c_ptr, ctypes.c_size_t, _c_i64, _c_i64,
                                            _c_i64, _c_i64, _c_i64, ctypes.c_float, ctypes.c_int,

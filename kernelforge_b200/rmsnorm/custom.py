@@ -74,6 +74,59 @@ def rmsnorm_into(x: torch.Tensor, weight: torch.Tensor | None, out: torch.Tensor
     return out
 
 
+def rmsnorm_backward(dy: torch.Tensor, x: torch.Tensor, weight: torch.Tensor | None, eps: float = 1e-6):
+    """Gradients ``(dx, dweight)`` of :func:`rmsnorm_forward` for the output gradient ``dy``.
+
+    The reference's RMSNorm is forward-only (rmsnorm/README.md:5); this is the gradient of its
+    forward with the casts taken as identities, as torch autograd treats ``.type_as``:
+    ``dx = r (dy w) - x r^3 ((dy w) . x) / dim`` and ``dweight = sum_rows dy * cast(x r)``,
+    in fp32 (``kf_rmsnorm_bwd``). ``dweight`` is None without a weight.
+    """
+    _lib.require_cuda(x, "x")
+    _lib.require_cuda(dy, "dy")
+    if dy.shape != x.shape or dy.dtype != x.dtype or dy.device != x.device:
+        raise ValueError("dy must have x's shape, dtype and device")
+    dim = x.shape[-1]
+    if weight is not None:
+        _lib.require_cuda(weight, "weight")
+        if weight.dtype != x.dtype or weight.device != x.device or weight.shape != (dim,):
+            raise ValueError("weight must be a [dim] tensor with x's dtype and device")
+        weight = weight.contiguous()
+    rows, dy_rows = _as_rows(x), _as_rows(dy)
+    dx = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    dx_rows = dx.view(-1, dim)
+    dweight = torch.empty(dim, dtype=x.dtype, device=x.device) if weight is not None else None
+    ws = (torch.empty(_lib.lib.kf_rmsnorm_bwd_workspace_size(dim), dtype=torch.uint8, device=x.device)
+          if weight is not None else None)
+    n = rows.shape[0]
+    with torch.cuda.device(x.device):
+        status = _lib.lib.kf_rmsnorm_bwd(
+            rows.data_ptr(), weight.data_ptr() if weight is not None else None, dy_rows.data_ptr(),
+            dx_rows.data_ptr(), dweight.data_ptr() if dweight is not None else None,
+            ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0, n, dim,
+            rows.stride(0) if n > 1 else dim, dy_rows.stride(0) if n > 1 else dim, dim, float(eps),
+            _lib.dtype_code(x.dtype), _lib.stream_handle(x.device),
+        )
+    _lib.check(status, "kf_rmsnorm_bwd")
+    return dx, dweight
+
+
+class RMSNormFunction(torch.autograd.Function):
+    """Autograd op over the two kernels: ``RMSNormFunction.apply(x, weight, eps)``."""
+
+    @staticmethod
+    def forward(ctx, x, weight, eps):
+        ctx.save_for_backward(x, weight)
+        ctx.eps = float(eps)
+        return rmsnorm_forward(x, weight, eps)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, weight = ctx.saved_tensors
+        dx, dweight = rmsnorm_backward(dy.contiguous(), x, weight, ctx.eps)
+        return dx, dweight, None
+
+
 @functools.lru_cache(maxsize=None)
 def rms_norm(batch: int, seq_len: int, dim: int, eps: float = 1e-6, dtype: str = "bfloat16"):
     """Return the RMSNorm kernel for ``[batch, seq_len, dim]`` inputs of ``dtype``."""
@@ -101,7 +154,9 @@ class RMSNorm(torch.nn.Module):
     When the weight has the input's dtype the whole forward is one kernel launch. With a
     different weight dtype (the reference module keeps an fp32 weight unless cast), the
     normalised row comes from the kernel and the weight multiply follows torch's type
-    promotion, exactly as ``output * self.weight`` does in the reference.
+    promotion, exactly as ``output * self.weight`` does in the reference. Gradients flow to
+    the input and the weight through :class:`RMSNormFunction` (the reference module is
+    forward-only).
     """
 
     def __init__(self, dim: int, scale_factor=1.0, eps: float = 1e-6):
@@ -110,7 +165,6 @@ class RMSNorm(torch.nn.Module):
         self.weight = torch.nn.Parameter(torch.ones(dim) * scale_factor)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        w = self.weight.detach()
-        if w.dtype == x.dtype:
-            return rmsnorm_forward(x, w, self.eps)
-        return rmsnorm_forward(x, None, self.eps) * w
+        if self.weight.dtype == x.dtype:
+            return RMSNormFunction.apply(x, self.weight, self.eps)
+        return RMSNormFunction.apply(x, None, self.eps) * self.weight

@@ -41,3 +41,27 @@ def rmsnorm_exact(x: torch.Tensor, weight: torch.Tensor | None, eps: float = 1e-
     if weight is None:
         return normed
     return (normed.double() * weight.detach().to("cpu", torch.float64)).to(x.dtype)
+
+
+def rmsnorm_backward(x: torch.Tensor, weight: torch.Tensor | None, dy: torch.Tensor, eps: float = 1e-6):
+    """Float64 gradients (dx, dweight) of the reference forward (rmsnorm/original.py:40-52).
+
+    The reference has no backward (rmsnorm/README.md:5); this differentiates its forward
+    ``y = (x * rsqrt(mean(x^2) + eps)).type_as(x) * weight`` with torch autograd, the casts
+    taken as identities as autograd does, while the weight gradient sees the rounded
+    normalised row ``(x * r).type_as(x)`` the forward multiplies by. ``dweight`` is None when
+    ``weight`` is None.
+    """
+    xd = x.detach().to("cpu", torch.float64).requires_grad_()
+    dim = xd.shape[-1]
+    scale = 1.0 / torch.sqrt((xd * xd).sum(dim=-1, keepdim=True) / dim + eps)
+    normed = xd * scale
+    dyd = dy.detach().to("cpu", torch.float64)
+    if weight is None:
+        (dx,) = torch.autograd.grad(normed, (xd,), dyd)
+        return dx, None
+    wd = weight.detach().to("cpu", torch.float64).requires_grad_()
+    (dx,) = torch.autograd.grad(normed * wd, (xd,), dyd)
+    rounded = (x.detach().to("cpu", torch.float64) * scale.detach()).to(x.dtype).double()
+    dw = (dyd * rounded).reshape(-1, dim).sum(0)
+    return dx, dw
