@@ -352,6 +352,88 @@ def rmsnorm_cpu_baseline(seconds=10.0):
                       f"{nbytes / 1e6:.0f} MB, oracle/rmsnorm.py (torch CPU, {cores} threads)"}
 
 
+# RMSNorm backward (no counterpart in the reference): one BASELINE sweep shape, bf16.
+RMSNORM_BWD_CONFIG = {"rows": 32768, "hidden": 8192}
+
+
+def rmsnorm_bwd_bytes(rows, hidden):
+    """x and dy read, dx written (bf16); the weight and dweight are negligible."""
+    return 3 * rows * hidden * 2 + 2 * 2 * hidden
+
+
+def bench_rmsnorm_bwd(args, dist, peaks, peak_kind):
+    from kernelforge_b200.rmsnorm import rmsnorm_backward
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    rows, hidden = RMSNORM_BWD_CONFIG["rows"], RMSNORM_BWD_CONFIG["hidden"]
+    gen = torch.Generator(device=dev).manual_seed(4321 + dist.rank)
+    x = torch.randn(rows, hidden, device=dev, dtype=torch.bfloat16, generator=gen)
+    dy = torch.randn(rows, hidden, device=dev, dtype=torch.bfloat16, generator=gen)
+    w = (1 + 0.1 * torch.randn(hidden, device=dev, generator=gen)).to(torch.bfloat16)
+    call = lambda: rmsnorm_backward(dy, x, w, 1e-6)  # noqa: E731
+    timer = LaunchTimer()
+    ms, dom_ms = time_region(lambda _: timer.around(call), args.steps, args.warmup, dist, timer)
+    nbytes = rmsnorm_bwd_bytes(rows, hidden)
+    result = {
+        "value": round(dist.world * nbytes / (ms / 1e3) / 1e9, 1), "unit": "GB/s", "ms_per_step": round(ms, 4),
+        "gpu_launches": 2 * args.steps,
+        "config": {"rows": rows, "hidden": hidden, "dtype": "bf16", "eps": 1e-6,
+                   "call": "rmsnorm_backward(dy, x, weight) -> (dx, dweight)",
+                   "bytes_per_step": nbytes, "l2": "inputs larger than L2 (x, dy 537 MB each)"},
+        "roofline": roofline(nbytes, dom_ms, peaks["hbm_gbs"], "GB/s", "hbm"),
+        "roofline_note": f"x and dy read and dx written once per call; one call = 2 launches (dx with per-CTA "
+                         f"dweight partials, then their fixed-order sum), {dom_ms * 1e3:.1f} us avg per call; "
+                         f"peak = {peak_kind} HBM copy GB/s",
+    }
+    if not args.no_e2e:
+        host_x, host_dy = x.cpu().pin_memory(), dy.cpu().pin_memory()
+        host_dx = torch.empty_like(host_x).pin_memory()
+        dev_x, dev_dy = torch.empty_like(x), torch.empty_like(dy)
+
+        def e2e_step(_):
+            dev_x.copy_(host_x, non_blocking=True)
+            dev_dy.copy_(host_dy, non_blocking=True)
+            dx, _ = rmsnorm_backward(dev_dy, dev_x, w, 1e-6)
+            host_dx.copy_(dx, non_blocking=True)
+
+        steps = max(3, min(args.steps, args.e2e_steps))
+        ems, _ = time_region(e2e_step, steps, args.warmup, dist)
+        result["e2e"] = {"value": round(dist.world * nbytes / (ems / 1e3) / 1e9, 2), "unit": "GB/s",
+                         "h2d_bytes_per_step": 2 * x.numel() * 2, "d2h_bytes_per_step": x.numel() * 2,
+                         "steps": steps, "ms_per_step": round(ems, 3),
+                         "api": "kernelforge_b200.rmsnorm.rmsnorm_backward"}
+    if dist.world == 1 and dist.rank == 0 and not args.no_cpu:
+        result["cpu_baseline"] = rmsnorm_bwd_cpu_baseline(seconds=args.cpu_seconds / 2)
+    del x, dy
+    torch.cuda.empty_cache()
+    return result
+
+
+def rmsnorm_bwd_cpu_baseline(seconds=5.0):
+    """oracle.rmsnorm.rmsnorm_backward (float64 autograd) on the host cores: 256-row samples of the
+    bench shape, repeated until ~`seconds` elapsed."""
+    from oracle.rmsnorm import rmsnorm_backward
+
+    cores = cpu_threads()
+    g = torch.Generator().manual_seed(0)
+    rows, hidden = 256, RMSNORM_BWD_CONFIG["hidden"]
+    x = torch.randn(rows, hidden, generator=g).to(torch.bfloat16)
+    dy = torch.randn(rows, hidden, generator=g).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(hidden, generator=g)).to(torch.bfloat16)
+    rmsnorm_backward(x, w, dy, 1e-6)
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        rmsnorm_backward(x, w, dy, 1e-6)
+        reps += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": round(rmsnorm_bwd_bytes(rows, hidden) / dt / 1e9, 3), "unit": "GB/s", "cores": cores,
+            "kind": "port", "sample": f"{rows} x {hidden} bf16 rows, {reps} passes, oracle/rmsnorm.py "
+                                      f"rmsnorm_backward (torch float64 autograd on the CPU, {cores} threads)"}
+
+
 # ---------------------------------------------------------------------------------------------
 # SANA linear attention
 # ---------------------------------------------------------------------------------------------
@@ -734,7 +816,7 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("all", "rmsnorm", "sana", "fajvp", "fabwd"), default="all")
+    ap.add_argument("--workload", choices=("all", "rmsnorm", "rmsnormbwd", "sana", "fajvp", "fabwd"), default="all")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-e2e", action="store_true")
@@ -763,6 +845,8 @@ def main():
     head = None
     if args.workload in ("all", "rmsnorm"):
         head = bench_rmsnorm(args, dist, peaks, peak_kind)
+    if args.workload in ("all", "rmsnormbwd"):
+        workloads["rmsnormbwd_bf16_32768x8192"] = bench_rmsnorm_bwd(args, dist, peaks, peak_kind)
     if args.workload in ("all", "sana"):
         for cfg in (SANA_CONFIGS[:1] if CASE == "ncu-small" else SANA_CONFIGS):
             workloads[cfg["name"]] = bench_sana(args, dist, peaks, peak_kind, cfg)
