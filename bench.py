@@ -61,6 +61,8 @@ SANA_CONFIGS = (
 # still in L2 when the kernel ends).
 RMSNORM_NCU_TRAFFIC_BYTES = 8 * (536_926_976 + 486_499_328)
 SANA_NCU_TRAFFIC_BYTES = {"sana_cfg1": 113_272_832 + 7_127_808}
+# RMSNorm backward at the bench size, from the capture in profiles/rmsnorm_bwd_vec_32768x8192_bf16.md.
+RMSNORM_BWD_NCU_TRAFFIC_BYTES = 1_073_874_000 + 503_786_496
 
 
 def sana_launches_per_call(B, H, N):
@@ -380,7 +382,7 @@ def bench_rmsnorm_bwd(args, dist, peaks, peak_kind):
         "config": {"rows": rows, "hidden": hidden, "dtype": "bf16", "eps": 1e-6,
                    "call": "rmsnorm_backward(dy, x, weight) -> (dx, dweight)",
                    "bytes_per_step": nbytes, "l2": "inputs larger than L2 (x, dy 537 MB each)"},
-        "roofline": roofline(nbytes, dom_ms, peaks["hbm_gbs"], "GB/s", "hbm"),
+        "roofline": roofline(nbytes, dom_ms, peaks["hbm_gbs"], "GB/s", "hbm", RMSNORM_BWD_NCU_TRAFFIC_BYTES),
         "roofline_note": f"x and dy read and dx written once per call; one call = 2 launches (dx with per-CTA "
                          f"dweight partials, then their fixed-order sum), {dom_ms * 1e3:.1f} us avg per call; "
                          f"peak = {peak_kind} HBM copy GB/s",
