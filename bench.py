@@ -51,6 +51,9 @@ SWEEP_HIDDEN = (1024, 2048, 4096, 8192)
 SANA_CONFIGS = (
     {"name": "sana_cfg1", "B": 4, "H": 36, "N": 4096, "D": 32},
     {"name": "sana_cfg2", "B": 2, "H": 70, "N": 16384, "D": 32},
+    # One of the reference harness's own shapes (SANA test.py:184-186: batch 1, 2240 channels =
+    # 70 heads, 4096 tokens): fewer heads than SMs, so the one-launch path runs in clusters.
+    {"name": "sana_harness_b1h70", "B": 1, "H": 70, "N": 4096, "D": 32},
 )
 
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from `ncu --set full`
