@@ -94,3 +94,18 @@ def test_python_signature_validation():
         kernel(torch.zeros(1, 3, 8, dtype=torch.bfloat16), torch.zeros(8, dtype=torch.bfloat16))
     with pytest.raises(ValueError, match="CUDA"):
         kernel(torch.zeros(1, 2, 8, dtype=torch.bfloat16), torch.zeros(8, dtype=torch.bfloat16))
+
+
+def test_rmsnorm_backward_validation_without_launching():
+    ws = _lib.lib.kf_rmsnorm_bwd_workspace_size
+    assert ws(8192) == 320 * 8192 * 4 and ws(0) == 0
+    f = _lib.lib.kf_rmsnorm_bwd
+    need = ws(64)
+    # x, weight, dy, dx, dweight, workspace, workspace_bytes, rows, dim, strides, eps, dtype, stream
+    assert f(256, 256, 256, 256, 256, 256, need, 4, 64, 64, 64, 64, 1e-6, 7, None) == 2      # dtype
+    assert f(256, 256, 256, 256, 256, 256, need, -1, 64, 64, 64, 64, 1e-6, 2, None) == 1     # rows
+    assert f(256, 256, 256, 256, None, 256, need, 4, 64, 64, 64, 64, 1e-6, 2, None) == 1    # weight without dweight
+    assert f(256, 256, 256, 256, 256, 256, need - 1, 4, 64, 64, 64, 64, 1e-6, 2, None) == 4  # workspace
+    assert f(256, 256, 256, 256, 256, None, need, 4, 64, 64, 64, 64, 1e-6, 2, None) == 1    # no workspace
+    assert f(256, 256, 256, 256, 256, 256, need, 4, 64, 32, 64, 64, 1e-6, 2, None) == 1     # stride < dim
+    assert f(257, 256, 256, 256, 256, 256, need, 4, 64, 64, 64, 64, 1e-6, 2, None) == 3     # misaligned bf16
