@@ -93,9 +93,9 @@ int kf_rmsnorm_bwd(const void* x, const void* weight, const void* dy, void* dx, 
  *   VK_h = sum_t v_t relu(k_t)^T,  ksum_h = sum_t relu(k_t)           (fp32 accumulation)
  *   out[t, h*dim + r] = (VK_h relu(q_t))_r / (ksum_h . relu(q_t) + eps)
  * `splits` picks the schedule of the bf16/fp16 head_dim-32 path:
- *   0       automatic: the one-launch path when its CTAs fill the GPU's SMs (at least 90%
- *           of the CTA slots of the last wave) or outnumber the split path's producer CTAs,
- *           else the split path with a default split count;
+ *   0       automatic: the one-launch path when its CTAs fill the GPU's SMs or outnumber
+ *           the split path's producer CTAs (with clusters, only for token shares of 1024-4096
+ *           per CTA), else the split path with a default split count;
  *   -1      the one-launch path: each CTA owns whole (batch, head) units, reduces K^T V and
  *           ksum in shared memory and writes the output (the workspace is not touched); with
  *           fewer units than SMs, a thread-block cluster of up to 8 CTAs shares each unit,

@@ -1441,15 +1441,25 @@ int fused_cluster_size(int64_t B, int64_t H, int64_t N) {
   return best;
 }
 
-// The fused path (no workspace) is the automatic choice when its CTAs give the SMs work (at
-// least 90% of the CTA slots of the last wave busy), or when they outnumber the split path's
-// producer CTAs (few heads: the split path caps its splits per head pair). Both rules follow
-// same-box timings of the two paths over batch 1-4, 4-100 heads, 1K-16K tokens.
+// The fused path (no workspace) is the automatic choice when its CTAs give the SMs work, or
+// when they outnumber the split path's producer CTAs (few heads: the split path caps its
+// splits per head pair). One CTA per unit: at least 90% of the CTA slots of the last wave busy.
+// Clusters: each CTA's share of the tokens between 1024 and 4096 (shorter shares carry too much
+// fixed cost, and on longer ones the split path's pipeline streams faster), and at least 85% of
+// the SMs busy. The rules follow same-box timings of the two paths over batch 1-4, 2-100 heads,
+// 1K-16K tokens.
 bool fused_preferred(int64_t B, int64_t H, int64_t N) {
   const int64_t sms = kf_host::current_device_sms();
-  const int64_t ctas = B * H * fused_cluster_size(B, H, N);
-  const int64_t waves = (ctas + sms - 1) / sms;
-  if (ctas * 10 >= waves * sms * 9) return true;
+  const int cs = fused_cluster_size(B, H, N);
+  const int64_t ctas = B * H * cs;
+  if (cs == 1) {
+    const int64_t waves = (ctas + sms - 1) / sms;
+    if (ctas * 10 >= waves * sms * 9) return true;
+  } else {
+    const int64_t share = N / cs;
+    if (share < 1024 || share > 4096) return false;
+    if (ctas * 100 >= sms * 85) return true;
+  }
   return B * ceil_div(H, kFastHeads) * fast_splits(B, H, N, 0) < ctas;
 }
 

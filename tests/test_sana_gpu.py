@@ -140,13 +140,14 @@ def test_cluster_path_is_used_below_the_sm_count(kf):
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     launches, ctas = kf.QKVAttnMatmul(1, 70, 32, 4096, 1e-15, "bfloat16", "bfloat16").plan()
     assert launches == 1 and ctas >= 2 and 70 * ctas <= sms
-    # Units that fill the SMs keep one CTA per unit. Otherwise the automatic choice takes the
-    # path with more CTAs: the split path for 36 heads (18 head pairs x 8 splits), the cluster
-    # path for 2 heads (8-CTA clusters against one head pair x 8 splits).
+    # Units that fill the SMs keep one CTA per unit. Otherwise clusters need token shares of
+    # 1024-4096 and either most SMs busy or more CTAs than the split path's producer.
     assert kf.QKVAttnMatmul(4, 36, 32, 4096, 1e-15, "bfloat16", "bfloat16").plan() == (1, 1)
     if sms >= 144:
         assert kf.QKVAttnMatmul(1, 36, 32, 4096, 1e-15, "bfloat16", "bfloat16").plan() == (2, 0)
-    assert kf.QKVAttnMatmul(1, 2, 32, 4096, 1e-15, "bfloat16", "bfloat16").plan() == (1, 8)
+        assert kf.QKVAttnMatmul(1, 70, 32, 16384, 1e-15, "bfloat16", "bfloat16").plan() == (2, 0)  # 8192-token shares
+    assert kf.QKVAttnMatmul(1, 4, 32, 16384, 1e-15, "bfloat16", "bfloat16").plan() == (1, 8)
+    assert kf.QKVAttnMatmul(1, 2, 32, 4096, 1e-15, "bfloat16", "bfloat16").plan() == (2, 0)  # 512-token shares
     assert kf.QKVAttnMatmul(1, 2, 32, 4096, 1e-15, "bfloat16", "bfloat16", splits=-1).plan() == (1, 8)
     assert kf.QKVAttnMatmul(1, 2, 32, 4096, 1e-15, "bfloat16", "bfloat16", splits=3).plan() == (2, 0)
 
