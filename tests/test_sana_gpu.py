@@ -152,6 +152,21 @@ def test_cluster_path_is_used_below_the_sm_count(kf):
     assert kf.QKVAttnMatmul(1, 2, 32, 4096, 1e-15, "bfloat16", "bfloat16", splits=3).plan() == (2, 0)
 
 
+@pytest.mark.parametrize("b,h,n,splits", [(1, 8, 16384, -1), (1, 8, 16384, 4), (4, 36, 4096, -1), (2, 6, 3000, 0)])
+def test_fp16_large_sums_are_rescaled(kf, b, h, n, splits):
+    """fp16 inputs whose sum(relu(K)) passes 2^14 (x16 inputs over thousands of tokens; at 16K
+    tokens it passes the fp16 range itself): every schedule scales B = [VK ; ksum] by a power of
+    two per head before its 16-bit split, and eps with it, so the output still matches the
+    float64 oracle within 1 ulp."""
+    g = torch.Generator().manual_seed(b * 100 + h + n)
+    qkv = (16 * torch.randn(b, n, 3, h * 32, generator=g)).to(torch.float16)
+    assert qkv[:, :, 1].double().clamp_min(0).sum(1).max() > 2 ** 14
+    fn = kf.QKVAttnMatmul(b, h, 32, n, 1e-15, "float16", "float16", splits=splits)
+    out = fn(qkv.cuda())
+    assert torch.isfinite(out).all()
+    check_exact(out, qkv, h, 32)
+
+
 def test_cluster_and_split_paths_agree(kf):
     g = torch.Generator().manual_seed(17)
     qkv = torch.randn(1, 4096, 3, 36 * 32, generator=g).to(torch.bfloat16).cuda()
