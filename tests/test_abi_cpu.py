@@ -109,3 +109,13 @@ def test_rmsnorm_backward_validation_without_launching():
     assert f(256, 256, 256, 256, 256, None, need, 4, 64, 64, 64, 64, 1e-6, 2, None) == 1    # no workspace
     assert f(256, 256, 256, 256, 256, 256, need, 4, 64, 32, 64, 64, 1e-6, 2, None) == 1     # stride < dim
     assert f(257, 256, 256, 256, 256, 256, need, 4, 64, 64, 64, 64, 1e-6, 2, None) == 3     # misaligned bf16
+
+
+def test_sana_plan_validation_without_launching():
+    f = _lib.lib.kf_sana_linattn_plan
+    launches, ctas = ctypes.c_int64(-1), ctypes.c_int64(-1)
+    assert f(1, 36, 32, 4096, 0, 2, None, ctypes.byref(ctas)) == 1                          # no output
+    assert f(1, 36, 32, 4096, 0, 7, ctypes.byref(launches), ctypes.byref(ctas)) == 2         # dtype
+    assert f(0, 36, 32, 4096, 0, 2, ctypes.byref(launches), ctypes.byref(ctas)) == 1         # batch
+    assert f(1, 36, 48, 4096, 0, 2, ctypes.byref(launches), ctypes.byref(ctas)) == 2         # head dim
+    assert launches.value == -1 and ctas.value == -1                                          # nothing written
