@@ -52,6 +52,15 @@ int kf_abi_version(void);
  */
 int kf_query_device_error(void* stream, int* code);
 
+/*
+ * Self-test of the failure-detection path. No counterpart in the reference. Launches one warp
+ * that waits on an mbarrier nothing arrives on, through the bounded wait every kernel here uses:
+ * after the library's 4 s bound it records KF_ERR_DEVICE_TIMEOUT (6) and returns, so the next
+ * kf_query_device_error reports 6 and the context stays usable. Diagnostic only: it occupies
+ * one SM for 4 s.
+ */
+int kf_selftest_bounded_wait(void* stream);
+
 /* ------------------------------------------------------------------------------------------
  * RMSNorm forward.
  * Replaces rms_norm(batch, seq_len, dim, eps, dtype) -> kernel(X, Weight) -> Output

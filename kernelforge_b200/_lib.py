@@ -30,6 +30,7 @@ SIGNATURES = {
     "kf_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "kf_abi_version": (ctypes.c_int, []),
     "kf_query_device_error": (ctypes.c_int, [_c_ptr, ctypes.POINTER(ctypes.c_int)]),
+    "kf_selftest_bounded_wait": (ctypes.c_int, [_c_ptr]),
     "kf_rmsnorm_fwd": (ctypes.c_int, [_c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64,
                                       ctypes.c_float, ctypes.c_int, _c_ptr]),
     "kf_rmsnorm_bwd_workspace_size": (ctypes.c_size_t, [_c_i64]),

@@ -1,5 +1,7 @@
-// ABI-level helpers: status strings, version, and the device error words of the modules.
+// ABI-level helpers: status strings, version, the device error words of the modules, and a
+// self-test of the bounded-wait path.
 #include "kf_common.cuh"
+#include "kf_sm100.cuh"
 
 int kf_internal_sana_error(unsigned int* code);
 int kf_internal_fa_error(unsigned int* code);
@@ -20,6 +22,41 @@ KF_API const char* kf_status_string(int status) {
 
 KF_API int kf_abi_version(void) { return 1; }
 
+namespace {
+
+__device__ unsigned int g_selftest_error = 0;
+
+// One warp waits on an mbarrier that nothing ever arrives on, through the same bounded wait the
+// kernels use: it gives up after kf::kWaitTimeoutNs, records KF_ERR_DEVICE_TIMEOUT and returns.
+__global__ void selftest_bounded_wait_kernel() {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    kf::mbar_init(&bar, 1);
+    kf::fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) (void)kf::mbar_wait_bounded(&bar, 0, &g_selftest_error);
+}
+
+int selftest_error(unsigned int* code) {
+  unsigned int v = 0;
+  KF_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_selftest_error, sizeof(v)));
+  if (v != 0) {
+    const unsigned int zero = 0;
+    KF_CUDA_TRY(cudaMemcpyToSymbol(g_selftest_error, &zero, sizeof(zero)));
+  }
+  *code = v;
+  return KF_OK;
+}
+
+}  // namespace
+
+KF_API int kf_selftest_bounded_wait(void* stream) {
+  selftest_bounded_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>();
+  KF_LAUNCH_CHECK();
+  return KF_OK;
+}
+
 KF_API int kf_query_device_error(void* stream, int* code) {
   if (code == nullptr) return KF_ERR_INVALID_ARGUMENT;
   *code = KF_OK;
@@ -36,5 +73,9 @@ KF_API int kf_query_device_error(void* stream, int* code) {
   st = kf_internal_fa_bwd_error(&fa_bwd);
   if (st != KF_OK) return st;
   if (fa_bwd != 0 && *code == KF_OK) *code = static_cast<int>(fa_bwd);
+  unsigned int self = 0;
+  st = selftest_error(&self);
+  if (st != KF_OK) return st;
+  if (self != 0 && *code == KF_OK) *code = static_cast<int>(self);
   return KF_OK;
 }
