@@ -78,3 +78,40 @@ def test_oracle_detects_a_planted_error():
     wrong = rmsnorm.rmsnorm_forward(case["x"], case["weight"], case["eps"] * 1e4 + 1e-1)
     with pytest.raises(AssertionError):
         assert_within_ulps(wrong, case["y"], ulps=1)
+
+
+@pytest.mark.parametrize("weighted", [True, False])
+def test_rmsnorm_backward_oracle_matches_finite_differences(weighted):
+    """The backward oracle (the reference has no RMSNorm backward) against central finite
+    differences of the float64 forward y = x r w: dx exactly, dweight through the unrounded row
+    (fp32 inputs, so the forward's cast is the identity)."""
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(3, 6, generator=g, dtype=torch.float64).float()
+    w = (1 + 0.1 * torch.randn(6, generator=g, dtype=torch.float64)).float() if weighted else None
+    dy = torch.randn(3, 6, generator=g, dtype=torch.float64).float()
+    eps = 1e-6
+    dx, dw = rmsnorm.rmsnorm_backward(x, w, dy, eps)
+
+    def loss(xd, wd):
+        r = 1.0 / torch.sqrt((xd * xd).mean(-1, keepdim=True) + eps)
+        y = xd * r * (wd if wd is not None else 1.0)
+        return (y * dy.double()).sum()
+
+    xd, wd = x.double(), None if w is None else w.double()
+    h = 1e-6
+    num_dx = torch.zeros_like(xd)
+    for i in range(xd.numel()):
+        e = torch.zeros_like(xd).view(-1)
+        e[i] = h
+        e = e.view_as(xd)
+        num_dx.view(-1)[i] = (loss(xd + e, wd) - loss(xd - e, wd)) / (2 * h)
+    torch.testing.assert_close(dx, num_dx, rtol=1e-6, atol=1e-8)
+    if weighted:
+        num_dw = torch.zeros_like(wd)
+        for i in range(wd.numel()):
+            e = torch.zeros_like(wd)
+            e[i] = h
+            num_dw[i] = (loss(xd, wd + e) - loss(xd, wd - e)) / (2 * h)
+        torch.testing.assert_close(dw, num_dw, rtol=1e-6, atol=1e-8)
+    else:
+        assert dw is None
