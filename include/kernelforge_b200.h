@@ -2,9 +2,10 @@
  * kernelforge_b200.h -- C ABI of the B200-native KernelForge hot path.
  *
  * Every entry point takes raw device pointers, sizes and strides (in ELEMENTS), a cudaStream_t
- * passed as `void*` (NULL = legacy default stream), and returns a kf_status. None of them
- * allocates device memory, synchronises the host, or keeps a pointer past the call: the caller
- * owns every buffer, including the workspace where one is needed. Launches are asynchronous
+ * passed as `void*` (NULL = legacy default stream), and returns a kf_status. No compute entry
+ * point allocates device memory, synchronises the host, or keeps a pointer past the call: the
+ * caller owns every buffer, including the workspace where one is needed (the diagnostic
+ * kf_query_device_error synchronises; kf_sana_linattn_fwd_noalloc uses a built-in array). Launches are asynchronous
  * on `stream`; a kernel-side failure (a bounded wait that timed out) is recorded in a device
  * error word that kf_query_device_error() reads.
  *
