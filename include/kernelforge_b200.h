@@ -143,11 +143,19 @@ int kf_sana_linattn_plan(int64_t batch, int64_t heads, int64_t dim, int64_t seq_
  * memory budget). No counterpart in the reference. It allocates nothing: its scratch is a
  * file-scope device array of kf_sana_noalloc_scratch_bytes() bytes (16 MiB), which every GPU
  * that loads the library holds until exit. The caller still passes qkv and out.
- * - Shapes whose scratch does not fit are rejected with KF_ERR_WORKSPACE before any launch
- *   (the bf16/fp16 head_dim-32 path needs batch*heads*4224 bytes; other shapes use fewer
- *   splits until their partials fit).
- * - The first call on a device looks up the array's device address (cudaGetSymbolAddress);
- *   make that first call outside any stream capture.
+ * - `splits` means what it means for kf_sana_linattn_fwd, and the schedule is the one
+ *   kf_sana_linattn_plan reports: 0 automatic, -1 the one-launch path (which needs no
+ *   scratch), s > 0 the split path with s chunks. The one difference: when the split path's
+ *   partials for the requested (or default) split count do not fit the array, fewer splits
+ *   are used, down to 1; the result stays within the same tolerance, but the fp32 summation
+ *   order differs from kf_sana_linattn_fwd with the same `splits`.
+ * - Shapes whose scratch does not fit even with one split are rejected with KF_ERR_WORKSPACE
+ *   before any launch (the bf16/fp16 head_dim-32 split path needs batch*heads*4224 bytes per
+ *   split; shapes the automatic schedule sends to the one-launch path are never rejected).
+ * - The array's device address belongs to a CUDA context. The first call in a context (the
+ *   first call on each device, and the first after a cudaDeviceReset or on another context)
+ *   loads the library's module there if needed and looks the address up
+ *   (cudaGetSymbolAddress); make that first call outside any stream capture.
  * - Every call shares the one array: calls that overlap on the GPU (other streams, other
  *   threads) race. Order them on one stream. The arrival counters are zeroed by each call.
  */

@@ -444,12 +444,34 @@ inline int tmem_kernel_occupancy(const void* fn, int threads, int smem, int tmem
   return std::max(occ, 1);
 }
 
-// Opt the kernel in to `smem` bytes of dynamic shared memory (cached per device) and, when
-// asked, report how many CTAs of it fit on an SM. tmem_cols > 0: the kernel allocates that
-// many tensor-memory columns per CTA.
+// Id of the CUDA context current on this thread (cuCtxGetId), or 0 when none is current or it
+// was destroyed (cudaDeviceReset). Ids are unique for the life of the process, so state that
+// belongs to a context (function attributes, module symbol addresses) can be cached under it.
+inline unsigned long long context_id() {
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static GetId fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      (void)cudaGetLastError();
+      return static_cast<GetId>(nullptr);
+    }
+    return reinterpret_cast<GetId>(p);
+  }();
+  unsigned long long id = 0;
+  if (fn == nullptr || fn(nullptr, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+// Opt the kernel in to `smem` bytes of dynamic shared memory (cached per device and context:
+// a new context, after a cudaDeviceReset, starts without the opt-ins) and, when asked, report
+// how many CTAs of it fit on an SM (a property of the device, cached per device). tmem_cols > 0:
+// the kernel allocates that many tensor-memory columns per CTA.
 inline int prepare_kernel(const void* fn, int threads, int smem, int* occupancy_out, int tmem_cols = 0) {
   constexpr int kSlots = 256;
   static KernelPrep attr_cache[64][kSlots];
+  static unsigned long long attr_ctx[64] = {};
   static KernelPrep occ_cache[64][kSlots];
   static std::mutex mu;
   std::lock_guard<std::mutex> lock(mu);
@@ -458,7 +480,16 @@ inline int prepare_kernel(const void* fn, int threads, int smem, int* occupancy_
     (void)cudaGetLastError();
     return KF_ERR_CUDA;
   }
-  const bool cached_dev = dev >= 0 && dev < 64;
+  bool cached_dev = dev >= 0 && dev < 64;
+  if (cached_dev) {
+    const unsigned long long ctx = context_id();
+    if (ctx == 0) {
+      cached_dev = false;  // no context yet: the runtime creates one on the calls below
+    } else if (attr_ctx[dev] != ctx) {
+      for (int i = 0; i < kSlots; ++i) attr_cache[dev][i] = KernelPrep{};
+      attr_ctx[dev] = ctx;
+    }
+  }
   // 1. shared-memory opt-in
   KernelPrep* attr = nullptr;
   if (cached_dev) {

@@ -1754,10 +1754,17 @@ static __device__ __align__(256) uint8_t g_sana_noalloc_scratch[kNoAllocScratchB
 
 namespace {
 
-// Device address of the scratch array on the current device. In host code the array's name is
-// only a host-side stand-in, so the address comes from cudaGetSymbolAddress, once per device.
+// Device address of the scratch array in the current context. In host code the array's name is
+// only a host-side stand-in, so the address comes from cudaGetSymbolAddress. A __device__
+// array's address belongs to a context, not to a device: it is looked up once per device and
+// again whenever that device's current context is a different one (a cudaDeviceReset, or a
+// driver-API caller's own context), never reused across contexts.
 int noalloc_scratch(uint8_t** out) {
-  static uint8_t* addr[64] = {};
+  struct Entry {
+    unsigned long long ctx;
+    uint8_t* addr;
+  };
+  static Entry cache[64] = {};
   static std::mutex mu;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) {
@@ -1766,15 +1773,21 @@ int noalloc_scratch(uint8_t** out) {
   }
   if (dev < 0 || dev >= 64) return KF_ERR_UNSUPPORTED;
   std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_sana_noalloc_scratch) != cudaSuccess || p == nullptr) {
-      (void)cudaGetLastError();
-      return KF_ERR_CUDA;
-    }
-    addr[dev] = static_cast<uint8_t*>(p);
+  const unsigned long long ctx = kf_host::context_id();
+  if (ctx != 0 && cache[dev].ctx == ctx && cache[dev].addr != nullptr) {
+    *out = cache[dev].addr;
+    return KF_OK;
   }
-  *out = addr[dev];
+  // Loads the library's module into the current context if needed (creating the runtime's
+  // primary context first when none is current).
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_sana_noalloc_scratch) != cudaSuccess || p == nullptr) {
+    (void)cudaGetLastError();
+    return KF_ERR_CUDA;
+  }
+  const unsigned long long now = kf_host::context_id();
+  cache[dev] = Entry{now, now != 0 ? static_cast<uint8_t*>(p) : nullptr};
+  *out = static_cast<uint8_t*>(p);
   return KF_OK;
 }
 
@@ -1800,8 +1813,14 @@ KF_API int kf_sana_linattn_fwd_noalloc(const void* qkv, void* out, int64_t batch
   const bool fast = d == kD && (in_dtype == KF_DTYPE_BF16 || in_dtype == KF_DTYPE_F16) &&
                     H * kD >= 64 && N >= kTok && kf::aligned(qkv, 16) && kf::aligned(out, 16);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (fast && (splits == -1 || (splits == 0 && fused_preferred(B, H, N)))) {
+    // The one-launch schedule, chosen exactly as kf_sana_linattn_fwd chooses it: it keeps
+    // whole heads in shared memory and needs no scratch at all.
+    if (in_dtype == KF_DTYPE_BF16) return launch_fused<__nv_bfloat16>(qkv, out, B, H, N, eps, out_dtype, s);
+    return launch_fused<__half>(qkv, out, B, H, N, eps, out_dtype, s);
+  }
   if (fast) {
-    // As many splits as the default asks for and the scratch holds.
+    // As many splits as requested (or the default) and the scratch holds.
     int S = fast_splits(B, H, N, splits);
     while (S > 1 && fast_layout(B, H, S).total > kNoAllocScratchBytes) --S;
     if (fast_layout(B, H, S).total > kNoAllocScratchBytes) return KF_ERR_WORKSPACE;
@@ -1812,7 +1831,7 @@ KF_API int kf_sana_linattn_fwd_noalloc(const void* qkv, void* out, int64_t batch
       return launch_fast<__nv_bfloat16, kFastHeads>(qkv, out, scratch, B, H, N, S, eps, out_dtype, s);
     return launch_fast<__half, kFastHeads>(qkv, out, scratch, B, H, N, S, eps, out_dtype, s);
   }
-  // Generic path: as many splits as the default asks for and the scratch holds.
+  // Generic path: as many splits as requested (or the default) and the scratch holds.
   int S = generic_splits(batch, heads, seq_len, splits);
   while (S > 1 && layout_for(batch, heads, dim, S).total > kNoAllocScratchBytes) --S;
   const WorkspaceLayout lay = layout_for(batch, heads, dim, S);

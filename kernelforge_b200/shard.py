@@ -27,3 +27,25 @@ def batch_head_shard(batch: int, heads: int, world: int, rank: int) -> list[tupl
     """(batch, head) pairs of an attention problem that ``rank`` computes, in row-major order."""
     start, stop = contiguous_range(batch * heads, world, rank)
     return [divmod(u, heads) for u in range(start, stop)]
+
+
+def batch_head_blocks(batch: int, heads: int, world: int, rank: int) -> list[tuple[int, int, int, int]]:
+    """``rank``'s contiguous (batch, head) range as at most three rectangles
+    ``(b_start, b_stop, h_start, h_stop)``: the tail of a first, partly owned batch, a run of whole
+    batches, and the head of a last, partly owned batch. Each rectangle is one dense slice of a
+    [batch, ..., heads, ...] tensor (SANA's packed qkv [B, N, 3, H*d], FlashAttention's
+    [B, N, H, D]) and one kernel call."""
+    start, stop = contiguous_range(batch * heads, world, rank)
+    blocks = []
+    u = start
+    while u < stop:
+        b, h = divmod(u, heads)
+        if h == 0 and stop - u >= heads:
+            nb = (stop - u) // heads
+            blocks.append((b, b + nb, 0, heads))
+            u += nb * heads
+        else:
+            h_stop = min(heads, h + (stop - u))
+            blocks.append((b, b + 1, h, h_stop))
+            u += h_stop - h
+    return blocks

@@ -11,7 +11,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from kernelforge_b200.shard import batch_head_shard, contiguous_range, row_shard
+from kernelforge_b200.shard import batch_head_blocks, batch_head_shard, contiguous_range, row_shard
 
 
 def _free_port():
@@ -32,6 +32,17 @@ def test_contiguous_ranges_partition_units():
     assert pairs == [(b, h) for b in range(2) for h in range(70)]
     with pytest.raises(ValueError):
         contiguous_range(4, 2, 2)
+
+
+def test_batch_head_blocks_are_dense_rectangles_of_the_shard():
+    for batch, heads, world in ((4, 36, 8), (2, 70, 8), (4, 16, 2), (2, 70, 3), (1, 70, 8), (3, 5, 4), (4, 16, 1)):
+        for rank in range(world):
+            blocks = batch_head_blocks(batch, heads, world, rank)
+            assert len(blocks) <= 3
+            units = [(b, h) for b0, b1, h0, h1 in blocks for b in range(b0, b1) for h in range(h0, h1)]
+            assert units == batch_head_shard(batch, heads, world, rank)
+            # A rectangle spanning several batches holds whole batches, so it is one dense slice.
+            assert all(b1 - b0 == 1 or (h0, h1) == (0, heads) for b0, b1, h0, h1 in blocks)
 
 
 def _worker(rank, world, port, mode, queue):
@@ -55,6 +66,35 @@ def _worker(rank, world, port, mode, queue):
             t = torch.tensor([float(rank + 1)])
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             queue.put((rank, bool(torch.equal(full, rmsnorm_forward(x, w, 1e-6))), float(t)))
+        elif mode in ("blocks", "blocks_planted"):
+            # bench.py's verification: each rank digests its (batch, head) blocks, rank 0 compares
+            # them with the same slices of its unsharded result. The "planted" run changes one
+            # element of rank 1's block on the CPU, which the comparison must report.
+            os.environ.update(WORLD_SIZE=str(world), RANK=str(rank))
+            import bench
+
+            g = torch.Generator().manual_seed(5)
+            x = torch.randn(3, 8, 5, 16, generator=g).to(torch.bfloat16)
+            op = lambda t: (t.float() * 1.5 + 0.25).to(torch.bfloat16)  # noqa: E731
+            mine = torch.zeros(3, 2, dtype=torch.int64)
+            for j, blk in enumerate(batch_head_blocks(3, 5, world, rank)):
+                out = op(bench.fa_block(x, blk))
+                if mode == "blocks_planted" and rank == 1 and j == 0:
+                    out.view(-1)[3] += 1
+                mine[j] = bench.digest(out)
+
+            def reference():
+                full = op(x)
+                refs = []
+                for r in range(world):
+                    ref = torch.zeros(3, 2, dtype=torch.int64)
+                    for j, blk in enumerate(batch_head_blocks(3, 5, world, r)):
+                        ref[j] = bench.digest(bench.fa_block(full, blk))
+                    refs.append(ref)
+                return refs
+
+            res = bench.verify_digests(bench.Dist(), mine, reference)
+            queue.put((rank, None if res is None else (res["ok"], res["mismatched_ranks"])))
         else:
             if rank == 1:
                 raise RuntimeError("injected host failure before the collective")
@@ -100,3 +140,10 @@ def test_host_failure_ends_peer_collective_with_error():
     out = _run("fail")
     assert out[1][0].startswith("raised")
     assert out[0][0].startswith("error"), out[0]
+
+
+def test_bench_verification_gathers_block_digests():
+    out = _run("blocks")
+    assert out[0][0] == (True, []) and out[1][0] is None
+    planted = _run("blocks_planted")
+    assert planted[0][0] == (False, [1])
