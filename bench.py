@@ -809,6 +809,134 @@ def sana_cpu_baseline(cfg, seconds=5.0):
 
 
 # ---------------------------------------------------------------------------------------------
+# SANA projections (the GEMMs around the attention; SANA_LinearAttention/custom.py:23-85, 457-523)
+# ---------------------------------------------------------------------------------------------
+PROJ_CONFIGS = (
+    {"name": "sana_proj_cfg1", "B": 4, "N": 4096, "C": 1152},
+    {"name": "sana_proj_cfg2", "B": 2, "N": 16384, "C": 2240},
+)
+
+
+def proj_flops(rows, c):
+    """QKV projection [rows, C] x [C, 3C] plus output projection [rows, C] x [C, C]."""
+    return 2 * rows * c * 3 * c + 2 * rows * c * c
+
+
+def bench_proj(args, dist, peaks, peak_kind, cfg):
+    from kernelforge_b200.SANA_LinearAttention.projection import linear
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    C = cfg["C"]
+    rows = cfg["B"] * cfg["N"]
+    gen = torch.Generator(device=dev).manual_seed(91)
+    x_full = torch.randn(rows, C, device=dev, dtype=torch.bfloat16, generator=gen)
+    a_full = torch.randn(rows, C, device=dev, dtype=torch.bfloat16, generator=gen)  # attention output
+    w_qkv = (torch.randn(3 * C, C, device=dev, generator=gen) / C ** 0.5).to(torch.bfloat16)
+    w_o = (torch.randn(C, C, device=dev, generator=gen) / C ** 0.5).to(torch.bfloat16)
+    b_o = torch.randn(C, device=dev, generator=gen).to(torch.bfloat16)
+    sl = row_shard(rows, dist.world, dist.rank)
+    x, a = x_full[sl].contiguous(), a_full[sl].contiguous()
+    del x_full, a_full
+    timer = LaunchTimer()
+    keep = []
+
+    def step(_):
+        qkv = timer.around(lambda: linear(x, w_qkv))
+        keep[:] = [qkv, linear(a, w_o, b_o)]
+
+    ms, dom_ms = time_region(step, args.steps, args.warmup, dist, timer)
+    flops = proj_flops(rows, C)
+    shard_rows = sl.stop - sl.start
+    dom_flops = 2 * shard_rows * C * 3 * C
+    peak = peaks["bf16_tflops"]
+    result = {
+        "value": round(flops / (ms / 1e3) / 1e12, 1), "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
+        "gpu_launches": 2 * args.steps,
+        "config": {"B": cfg["B"], "N": cfg["N"], "C": C, "dtype": "bf16", "shard_rows": [sl.start, sl.stop],
+                   "call": "projection.linear: qkv = x W_qkv^T (packed [B, N, 3, C]), y = a W_o^T + b_o",
+                   "flops_per_step": flops, "l2": "x, a and qkv exceed L2 together; weights stay L2-resident"},
+        "roofline": roofline(dom_flops, dom_ms, peak, "TFLOP/s", "tensor"),
+        "roofline_note": f"the QKV projection launch ({shard_rows} x {C} x {3 * C}), {dom_ms * 1e3:.1f} us avg; "
+                         f"peak = {peak_kind} cuBLAS bf16 TFLOP/s (burst)",
+    }
+    # cuBLAS on the same tensors, as context only (the product path never calls it).
+    def cublas_step(_):
+        keep[:] = [torch.nn.functional.linear(x, w_qkv), torch.nn.functional.linear(a, w_o, b_o)]
+
+    cms, _ = time_region(cublas_step, max(3, args.steps // 4), args.warmup, dist)
+    result["cublas_tflops_same_shapes"] = round(flops / (cms / 1e3) / 1e12, 1)
+    if dist.world > 1:
+        mine = torch.stack([digest(t) for t in keep])
+        result["verify"] = {"ranks": dist.world, "ok": True,
+                            "method": "row shards of a row-independent GEMM (digests gathered)",
+                            "digests": len(dist.all_gather(mine))}
+    else:
+        result["verify"] = single_rank_verify()
+    if not args.no_e2e:
+        result["e2e"] = proj_e2e(args, dist, x, a, w_qkv, w_o, b_o, flops)
+    if dist.world == 1 and dist.rank == 0 and not args.no_cpu:
+        result["cpu_baseline"] = proj_cpu_baseline(C, seconds=args.cpu_seconds / 2)
+    del x, a, keep
+    torch.cuda.empty_cache()
+    return result
+
+
+def proj_e2e(args, dist, x, a, w_qkv, w_o, b_o, global_flops):
+    """Both projections through projection.linear on ~64 MB row chunks: x and a upload, qkv and y
+    download, pipelined."""
+    from kernelforge_b200.SANA_LinearAttention.projection import linear
+
+    hx, ha = x.cpu().pin_memory(), a.cpu().pin_memory()
+    hq = pinned((x.shape[0], w_qkv.shape[0]), torch.bfloat16)
+    hy = pinned(a.shape, torch.bfloat16)
+    dx, da = torch.empty_like(x), torch.empty_like(a)
+    chunks = row_chunks(x.shape[0], 4 * x.shape[1])  # ~64 MB of qkv + y per chunk
+    pipe = Pipeline()
+
+    def step(_):
+        pipe.begin()
+        for r0, r1 in chunks:
+            pipe.chunk([(dx[r0:r1], hx[r0:r1]), (da[r0:r1], ha[r0:r1])],
+                       lambda r0=r0, r1=r1: (linear(dx[r0:r1], w_qkv), linear(da[r0:r1], w_o, b_o)),
+                       lambda res, r0=r0, r1=r1: [(hq[r0:r1], res[0]), (hy[r0:r1], res[1])])
+        pipe.end()
+
+    steps = max(3, min(args.steps, args.e2e_steps))
+    ems, _ = time_region(step, steps, args.warmup, dist)
+    return {"value": round(global_flops / (ems / 1e3) / 1e12, 2), "unit": "TFLOP/s",
+            "h2d_bytes_per_step": 2 * x.numel() * 2, "d2h_bytes_per_step": (hq.numel() + hy.numel()) * 2,
+            "steps": steps, "ms_per_step": round(ems, 3),
+            "api": "kernelforge_b200.SANA_LinearAttention.projection.linear per row chunk, copies overlapped"}
+
+
+def proj_cpu_baseline(C, seconds=5.0):
+    """oracle.sana.linear_exact (float64 x W^T + b, the reference's nn.Linear arithmetic) on the host
+    cores over 256-row samples."""
+    from oracle.sana import linear_exact
+
+    cores = cpu_threads()
+    g = torch.Generator().manual_seed(0)
+    rows = 256
+    x = torch.randn(rows, C, generator=g).to(torch.bfloat16)
+    w_qkv = (torch.randn(3 * C, C, generator=g) / C ** 0.5).to(torch.bfloat16)
+    w_o = (torch.randn(C, C, generator=g) / C ** 0.5).to(torch.bfloat16)
+    b_o = torch.randn(C, generator=g).to(torch.bfloat16)
+    linear_exact(x, w_qkv)
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        linear_exact(x, w_qkv)
+        linear_exact(x, w_o, b_o)
+        reps += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": round(proj_flops(rows, C) / dt / 1e12, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "sample": f"{rows} rows x C={C}, {reps} passes of both projections, oracle/sana.py linear_exact "
+                      f"(torch CPU float64, {cores} threads)"}
+
+
+# ---------------------------------------------------------------------------------------------
 # FlashAttention JVP (BASELINE configs[4]: B=4, H=16, N=4096, D in {64, 128}, bf16, non-causal)
 # ---------------------------------------------------------------------------------------------
 FA_CONFIGS = (
@@ -1196,7 +1324,8 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("all", "rmsnorm", "rmsnormbwd", "sana", "fajvp", "fabwd"), default="all")
+    ap.add_argument("--workload", choices=("all", "rmsnorm", "rmsnormbwd", "sana", "proj", "fajvp", "fabwd"),
+                    default="all")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-e2e", action="store_true")
@@ -1230,6 +1359,9 @@ def main():
     if args.workload in ("all", "sana"):
         for cfg in (SANA_CONFIGS[:1] if CASE == "ncu-small" else SANA_CONFIGS):
             workloads[cfg["name"]] = bench_sana(args, dist, peaks, peak_kind, cfg)
+    if args.workload in ("all", "proj"):
+        for cfg in (PROJ_CONFIGS[:1] if CASE == "ncu-small" else PROJ_CONFIGS):
+            workloads[cfg["name"]] = bench_proj(args, dist, peaks, peak_kind, cfg)
     if args.workload in ("all", "fajvp"):
         for cfg in (FA_SMALL if CASE == "ncu-small" else FA_CONFIGS):
             workloads[cfg["name"] + "_standalone"] = bench_fa(args, dist, peaks, peak_kind, cfg, fused=False)

@@ -167,6 +167,25 @@ int kf_sana_linattn_fwd_noalloc(const void* qkv, void* out, int64_t batch, int64
 size_t kf_sana_noalloc_scratch_bytes(void);
 
 /* ------------------------------------------------------------------------------------------
+ * Projection GEMM with a fused bias (SANA's QKV and output projections).
+ * Replaces the reference's _qkv_projection(batch, seq_len, channels, dtype) -> kernel(X, WeightT)
+ * (SANA_LinearAttention/custom.py:23-85) and the bias-fused _output_projection -> kernel(X,
+ * WeightT, Bias) (custom.py:457-523), i.e. the nn.Linear layers of LiteLA.forward
+ * (original.py:122, 143):
+ *   y[r, o] = sum_i x[r, i] * W[o, i] (+ bias[o])          fp32 accumulation, one rounding
+ * x: [rows, in_features]; y: [rows, out_features]; bias: [out_features] or NULL; all contiguous,
+ * one dtype. weight_layout 0: W as nn.Linear stores it, [out_features, in_features]; 1: the
+ * reference's prepacked WeightT, [in_features, out_features]. With a packed QKV weight
+ * (out_features = 3 * channels) y is the packed [batch, seq_len, 3, channels] layout that
+ * kf_sana_linattn_fwd reads.
+ * fp16/bf16 run on the tcgen05 tensor cores and need in_features and out_features to be
+ * multiples of 8 and 16-byte aligned pointers; fp32 runs fp32 FMAs (no TF32), any shape.
+ * rows == 0 is a no-op. Deterministic.
+ * ---------------------------------------------------------------------------------------- */
+int kf_linear_fwd(const void* x, const void* weight, const void* bias, void* y, int64_t rows,
+                  int64_t in_features, int64_t out_features, int weight_layout, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------------------------
  * FlashAttention forward and forward-mode JVP.
  * Layout: q, tq, out, tangent_out [batch, q_len, q_heads, head_dim]; k, v, tk, tv
  * [batch, k_len, kv_heads, head_dim]; all contiguous, 16-byte aligned, `dtype` fp16 or bf16.

@@ -12,6 +12,7 @@ from .modules import (
     optimized_joint_litela,
     qkv_projection,
 )
+from .projection import linear, linear_t
 
 __all__ = [
     "apply_rotary_emb",
@@ -21,6 +22,8 @@ __all__ = [
     "GroupedFull64QOutLiteLA",
     "JointLiteLA",
     "LiteLA",
+    "linear",
+    "linear_t",
     "QKVAttnMatmul",
     "optimized_joint_litela",
     "qkv_attn_matmul",

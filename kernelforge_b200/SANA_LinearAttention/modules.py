@@ -14,8 +14,10 @@ SANA_LinearAttention/__init__.py:3-27:
   (custom.py:864-870).
 * ``qkv_projection`` (custom.py:83-85): ``x [B, N, C] @ WeightT [C, 3C]``.
 
-The attention runs on ``kf_sana_linattn_fwd`` (``qkv_attn_matmul``). The two projections are
-plain GEMMs through torch (cuBLAS); the output projection fuses its bias (``addmm``).
+The attention runs on ``kf_sana_linattn_fwd`` (``qkv_attn_matmul``); both projections run on
+this library's tcgen05 GEMM (``kf_linear_fwd``, ``projection.linear``), with the output
+projection's bias (and the QKV bias, with ``use_bias``) added in its epilogue. The modules are
+inference modules, as the reference's custom ones are: no autograd through the kernels.
 ``qk_norm`` runs this library's RMSNorm kernel on the q and k slices of the packed QKV. The
 reference's custom modules reject it.
 ``apply_rotary_emb`` restates original.py:14-63. With ``rotary_emb`` the modules rotate q and k in
@@ -26,10 +28,10 @@ attention kernel.
 from __future__ import annotations
 
 import torch
-import torch.nn.functional as F
 
 from ..rmsnorm import RMSNorm
 from .custom import TORCH_DTYPES, QKVAttnMatmul
+from .projection import linear, linear_t
 
 __all__ = [
     "apply_rotary_emb",
@@ -60,7 +62,7 @@ def qkv_projection(batch: int, seq_len: int, channels: int, dtype: str = "bfloat
                              f"got {tuple(x.shape)} and {tuple(weight_t.shape)}")
         if x.dtype != torch_dtype or weight_t.dtype != torch_dtype:
             raise ValueError(f"x and weight_t must be {torch_dtype}")
-        return torch.matmul(x, weight_t)
+        return linear_t(x, weight_t)
 
     return project
 
@@ -145,7 +147,10 @@ class LiteLA(torch.nn.Module):
         return kernel
 
     def _project_qkv(self, x: torch.Tensor) -> torch.Tensor:
-        return F.linear(x, self.qkv.weight, self.qkv.bias)
+        return linear(x, self.qkv.weight, self.qkv.bias)
+
+    def _project_output(self, out: torch.Tensor) -> torch.Tensor:
+        return linear(out, self.proj.weight, self.proj.bias)
 
     def _normalise_qk(self, qkv: torch.Tensor) -> torch.Tensor:
         """q_norm / k_norm over the channels of the packed q and k slices (original.py:127-128)."""
@@ -184,7 +189,7 @@ class LiteLA(torch.nn.Module):
         batch, seq_len, channels = x.shape
         qkv = self._project_qkv(x).reshape(batch, seq_len, 3, channels)
         out = self.attention(self._rotate_qk(self._normalise_qk(qkv), rotary_emb))
-        return self.proj(out)
+        return self._project_output(out)
 
 
 # The reference's custom module (custom.py:391) is exported as CustomLiteLA next to the original.
@@ -217,11 +222,6 @@ class JointLiteLA(LiteLA):
     @property
     def proj_bias(self) -> torch.Tensor:
         return self.proj.bias
-
-    def _project_output(self, out: torch.Tensor) -> torch.Tensor:
-        batch, seq_len, channels = out.shape
-        return torch.addmm(self.proj.bias, out.reshape(batch * seq_len, channels), self.proj.weight.t()).view(
-            batch, seq_len, channels)
 
     def forward(self, x, mask=None, HW=None, rotary_emb=None, block_id=None, block_mask=None):
         self._validate_input(x)
@@ -284,10 +284,9 @@ def _joint_litela_forward(x: torch.Tensor, qkv_weight_t: torch.Tensor, proj_weig
                           proj_bias: torch.Tensor, heads: int, dim: int, eps: float) -> torch.Tensor:
     """QKV projection, attention and output projection as one opaque operator (custom.py:885-898)."""
     batch, seq_len, channels = x.shape
-    qkv = torch.matmul(x, qkv_weight_t).reshape(batch, seq_len, 3, channels)
+    qkv = linear_t(x, qkv_weight_t).reshape(batch, seq_len, 3, channels)
     out = _pipeline(batch, seq_len, heads, dim, eps, x.dtype)(qkv)
-    return torch.addmm(proj_bias, out.reshape(batch * seq_len, channels), proj_weight_t).view(
-        batch, seq_len, proj_weight_t.shape[-1])
+    return linear_t(out, proj_weight_t, proj_bias)
 
 
 @_joint_litela_forward.register_fake

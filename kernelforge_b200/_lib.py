@@ -45,6 +45,8 @@ SIGNATURES = {
     "kf_sana_noalloc_scratch_bytes": (ctypes.c_size_t, []),
     "kf_sana_linattn_plan": (ctypes.c_int, [_c_i64, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int,
                                             ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64)]),
+    "kf_linear_fwd": (ctypes.c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, ctypes.c_int,
+                                     ctypes.c_int, _c_ptr]),
     "kf_fa_fwd": (ctypes.c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64,
                                  _c_i64, _c_i64, ctypes.c_float, ctypes.c_int, ctypes.c_int, _c_ptr]),
     "kf_fa_jvp": (ctypes.c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr,

@@ -6,6 +6,7 @@
 int kf_internal_sana_error(unsigned int* code);
 int kf_internal_fa_error(unsigned int* code);
 int kf_internal_fa_bwd_error(unsigned int* code);
+int kf_internal_linear_error(unsigned int* code);
 
 KF_API const char* kf_status_string(int status) {
   switch (status) {
@@ -73,6 +74,10 @@ KF_API int kf_query_device_error(void* stream, int* code) {
   st = kf_internal_fa_bwd_error(&fa_bwd);
   if (st != KF_OK) return st;
   if (fa_bwd != 0 && *code == KF_OK) *code = static_cast<int>(fa_bwd);
+  unsigned int linear = 0;
+  st = kf_internal_linear_error(&linear);
+  if (st != KF_OK) return st;
+  if (linear != 0 && *code == KF_OK) *code = static_cast<int>(linear);
   unsigned int self = 0;
   st = selftest_error(&self);
   if (st != KF_OK) return st;

@@ -93,3 +93,15 @@ def litela_forward_exact(x, qkv_weight, qkv_bias, proj_weight, proj_bias, dim, e
     out = attn_exact(torch.stack([q, k, v], dim=2), channels // dim, dim, eps)
     return out @ proj_weight.detach().to("cpu", torch.float64).t() + proj_bias.detach().to("cpu", torch.float64)
 
+
+
+def linear_exact(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """Float64 ``x @ weight.T + bias`` for an nn.Linear weight ``[out, in]``: the projections of
+    ``LiteLA.forward`` (SANA_LinearAttention/original.py:122 ``self.qkv``, :143 ``self.proj``),
+    which the reference's TileLang kernels compute with fp32 accumulation
+    (SANA_LinearAttention/custom.py:23-85, 457-523). Unrounded: a kernel's fp32 accumulation
+    rounded once to a 16-bit dtype lands within one ulp of it."""
+    y = x.detach().to("cpu", torch.float64) @ weight.detach().to("cpu", torch.float64).t()
+    if bias is not None:
+        y = y + bias.detach().to("cpu", torch.float64)
+    return y

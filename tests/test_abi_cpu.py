@@ -61,6 +61,20 @@ def test_sana_workspace_and_validation():
     assert f(256, 256, 256, need, 1, 2, 32, 128, 0, 1e-15, 5, 2, None) == 2      # dtype
 
 
+def test_linear_validation_without_launching():
+    f = _lib.lib.kf_linear_fwd
+    # x, weight, bias, y, rows, in, out, layout, dtype, stream
+    assert f(256, 256, None, 256, 4, 8, 8, 0, 7, None) == 2      # dtype
+    assert f(None, 256, None, 256, 4, 8, 8, 0, 2, None) == 1     # no x
+    assert f(256, 256, None, 256, 4, 8, 8, 2, 2, None) == 1      # weight layout
+    assert f(256, 256, None, 256, 4, 0, 8, 0, 2, None) == 1      # in_features
+    assert f(256, 256, None, 256, 4, 8, 12, 0, 2, None) == 2     # 16-bit out_features % 8
+    assert f(256, 256, None, 264 + 2, 4, 8, 8, 1, 1, None) == 3  # misaligned y
+    assert f(256, 256, 258, 256, 4, 8, 8, 0, 2, None) == 3       # misaligned bias
+    assert f(256, 256, None, 256, 0, 8, 8, 0, 2, None) == 0      # no rows: no-op
+    assert f(None, None, None, None, 0, 8, 8, 0, 2, None) == 0   # ... whatever the pointers
+
+
 def test_fa_bwd_workspace_and_validation():
     ws = _lib.lib.kf_fa_bwd_workspace_size
     assert ws(2, 4, 100) == 2 * 2 * 4 * 128 * 4  # two fp32 statistics per (batch, head, query), padded to 128
