@@ -68,6 +68,9 @@ SANA_CONFIGS = (
     # One of the reference harness's own shapes (SANA test.py:184-186: batch 1, 2240 channels =
     # 70 heads, 4096 tokens): fewer heads than SMs, so the one-launch path runs in clusters.
     {"name": "sana_harness_b1h70", "B": 1, "H": 70, "N": 4096, "D": 32},
+    # Config 1 with LiteLA's qk_norm applied inside the attention kernels (the per-token norm
+    # statistics need every head of a token, so this line runs on one rank only).
+    {"name": "sana_cfg1_qknorm", "B": 4, "H": 36, "N": 4096, "D": 32, "qk_norm": True},
 )
 PARALLELISM = ("strong scaling: rows (RMSNorm) and (batch, head) blocks (SANA, FlashAttention) split "
                "over {n} rank(s), no data-path collective; NCCL gathers output digests / outputs to "
@@ -674,6 +677,11 @@ def bench_sana(args, dist, peaks, peak_kind, cfg):
     parts = [sana_block_input(qkv_full, blk, D) for blk in blocks]
     fns = [qkv_attn_matmul(b1 - b0, h1 - h0, D, N, dtype="bfloat16", output_dtype="bfloat16")
            for b0, b1, h0, h1 in blocks]
+    if cfg.get("qk_norm"):
+        wg = torch.Generator(device=dev).manual_seed(78)
+        qw, kw = ((0.5 + torch.rand(H * D, device=dev, generator=wg)).to(torch.bfloat16) for _ in range(2))
+        plain = fns
+        fns = [lambda x, f=f: f.with_qk_norm(x, qw, kw, 1e-5) for f in plain]
     one = sum(p.numel() * 2 for p in parts)
     copies = max(1, math.ceil(2 * L2_BYTES / one))  # rotate inputs so each step's data is not L2-hot
     rotations = [parts] + [[p.clone() for p in parts] for _ in range(copies - 1)]
@@ -704,6 +712,8 @@ def bench_sana(args, dist, peaks, peak_kind, cfg):
     value = nbytes / (ms / 1e3) / 1e9
     flops = 4 * B * H * N * D * (D + 1)
     launches = sum(sana_launches_per_call(b1 - b0, h1 - h0, N) for b0, b1, h0, h1 in blocks)
+    if cfg.get("qk_norm"):
+        launches += len(blocks)  # the per-token norm statistics
     result = {
         "value": round(value, 1), "unit": "GB/s", "ms_per_step": round(ms, 4),
         "gpu_launches": launches * args.steps,
@@ -718,8 +728,11 @@ def bench_sana(args, dist, peaks, peak_kind, cfg):
                          f"replays; {flops / dist.world / (dom_ms / 1e3) / 1e12:.1f} TFLOP/s of algorithmic "
                          f"FMA work; peak = {peak_kind} HBM copy GB/s",
     }
+    if cfg.get("qk_norm"):
+        result["config"]["qk_norm"] = ("q_norm / k_norm (RMSNorm over the 1152 channels, eps 1e-5) inside the "
+                                       "attention kernels; one extra launch reads q and k for the per-token scales")
     result["verify"] = sana_verify(dist, cfg, qkv_full, fns, parts) if dist.world > 1 else single_rank_verify()
-    if not args.no_e2e:
+    if not args.no_e2e and not cfg.get("qk_norm"):
         result["e2e"] = sana_e2e(args, dist, cfg, blocks, parts, nbytes)
     if dist.world == 1 and dist.rank == 0 and not args.no_cpu:
         result["cpu_baseline"] = sana_cpu_baseline(cfg, seconds=args.cpu_seconds / 2)
@@ -1358,6 +1371,8 @@ def main():
         workloads["rmsnormbwd_bf16_32768x8192"] = bench_rmsnorm_bwd(args, dist, peaks, peak_kind)
     if args.workload in ("all", "sana"):
         for cfg in (SANA_CONFIGS[:1] if CASE == "ncu-small" else SANA_CONFIGS):
+            if cfg.get("qk_norm") and dist.world > 1:
+                continue
             workloads[cfg["name"]] = bench_sana(args, dist, peaks, peak_kind, cfg)
     if args.workload in ("all", "proj"):
         for cfg in (PROJ_CONFIGS[:1] if CASE == "ncu-small" else PROJ_CONFIGS):

@@ -127,6 +127,26 @@ int kf_sana_linattn_fwd(const void* qkv, void* out, void* workspace, size_t work
                         float eps, int in_dtype, int out_dtype, void* stream);
 
 /*
+ * kf_sana_linattn_fwd after LiteLA's qk_norm (SANA_LinearAttention/original.py:92-96, 127-128):
+ * q and k each pass through an RMSNorm over the heads*dim channels of their token
+ * (rmsnorm/original.py:40-52, y = cast(cast(x r) w), r = 1/sqrt(mean(x^2) + norm_eps) in fp32)
+ * before the attention. Replaces the q_norm / k_norm calls of LiteLA.forward; the reference's
+ * custom kernels have no such form (they reject qk_norm). One launch computes r for every
+ * token's q and k into the workspace; the attention kernels then apply the norm to q and k as
+ * they read them, so no normalised copy is written. q_weight / k_weight: [heads*dim] in
+ * in_dtype, 16-byte aligned. The workspace is kf_sana_linattn_qknorm_workspace_size bytes (the
+ * kf_sana_linattn_fwd layout followed by 8 bytes per token, rounded up to 128 tokens per batch)
+ * and may be shared with kf_sana_linattn_fwd. Other arguments as for kf_sana_linattn_fwd.
+ */
+size_t kf_sana_linattn_qknorm_workspace_size(int64_t batch, int64_t heads, int64_t dim, int64_t seq_len,
+                                             int64_t splits);
+
+int kf_sana_linattn_qknorm_fwd(const void* qkv, void* out, void* workspace, size_t workspace_bytes,
+                               int64_t batch, int64_t heads, int64_t dim, int64_t seq_len, int64_t splits,
+                               float eps, const void* q_weight, const void* k_weight, float norm_eps,
+                               int in_dtype, int out_dtype, void* stream);
+
+/*
  * The schedule kf_sana_linattn_fwd runs for these arguments on the current CUDA device, without
  * launching anything (16-byte aligned qkv and out assumed). No counterpart in the reference.
  *   *launches       kernel launches per call (1: the one-launch path; 2: the other paths);

@@ -39,7 +39,10 @@ class QKVAttnMatmul:
         self.dtype = _lib.DTYPE_NAMES[dtype]
         self.output_dtype = _lib.DTYPE_NAMES[output_dtype]
         self.splits = int(splits) if splits else 0
-        self.workspace_bytes = _lib.lib.kf_sana_linattn_workspace_size(batch, heads, dim, seq_len, self.splits)
+        # Sized for the qk_norm form too (the same layout plus the per-token norm statistics), so
+        # one workspace serves both entry points.
+        self.workspace_bytes = _lib.lib.kf_sana_linattn_qknorm_workspace_size(batch, heads, dim, seq_len,
+                                                                               self.splits)
         if self.workspace_bytes == 0:
             raise ValueError("unsupported SANA attention shape")
         self._workspaces = {}
@@ -77,6 +80,33 @@ class QKVAttnMatmul:
                           device=qkv.device)
         return sana_linattn_into(qkv, out, self.workspace(qkv.device), self.heads, self.dim,
                                  self.eps, self.splits)
+
+
+    def with_qk_norm(self, qkv: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor,
+                     norm_eps: float) -> torch.Tensor:
+        """The attention of ``qkv`` after LiteLA's qk_norm (SANA_LinearAttention/original.py:127-128):
+        q and k each through an RMSNorm over their token's channels with ``q_weight`` /
+        ``k_weight`` (``[heads * dim]``, qkv's dtype) and ``norm_eps``, applied inside the
+        attention kernels as they read q and k (``kf_sana_linattn_qknorm_fwd``); qkv is not
+        modified and no normalised copy is made."""
+        expected = (self.batch, self.seq_len, 3, self.heads * self.dim)
+        if tuple(qkv.shape) != expected or qkv.dtype != self.dtype:
+            raise ValueError(f"qkv must be a {expected} {self.dtype} tensor")
+        channels = self.heads * self.dim
+        for name, w in (("q_weight", q_weight), ("k_weight", k_weight)):
+            if w.shape != (channels,) or w.dtype != qkv.dtype or w.device != qkv.device:
+                raise ValueError(f"{name} must be a [{channels}] tensor with qkv's dtype and device")
+        qkv = qkv.contiguous()
+        out = torch.empty((self.batch, self.seq_len, channels), dtype=self.output_dtype, device=qkv.device)
+        ws = self.workspace(qkv.device)
+        q_weight, k_weight = q_weight.contiguous(), k_weight.contiguous()
+        with torch.cuda.device(qkv.device):
+            status = _lib.lib.kf_sana_linattn_qknorm_fwd(
+                qkv.data_ptr(), out.data_ptr(), ws.data_ptr(), ws.numel(), self.batch, self.heads, self.dim,
+                self.seq_len, self.splits, self.eps, q_weight.data_ptr(), k_weight.data_ptr(), float(norm_eps),
+                _lib.dtype_code(qkv.dtype), _lib.dtype_code(out.dtype), _lib.stream_handle(qkv.device))
+        _lib.check(status, "kf_sana_linattn_qknorm_fwd")
+        return out
 
 
 def sana_linattn_into(qkv, out, workspace, heads, dim, eps, splits=0):

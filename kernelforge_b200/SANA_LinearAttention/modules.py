@@ -18,8 +18,10 @@ The attention runs on ``kf_sana_linattn_fwd`` (``qkv_attn_matmul``); both projec
 this library's tcgen05 GEMM (``kf_linear_fwd``, ``projection.linear``), with the output
 projection's bias (and the QKV bias, with ``use_bias``) added in its epilogue. The modules are
 inference modules, as the reference's custom ones are: no autograd through the kernels.
-``qk_norm`` runs this library's RMSNorm kernel on the q and k slices of the packed QKV. The
-reference's custom modules reject it.
+``qk_norm`` runs inside the attention kernels (``kf_sana_linattn_qknorm_fwd``: per-token norm
+statistics, then q and k normalised as the kernels read them); with rotary embeddings, which
+come after the norm, q and k are normalised by this library's RMSNorm kernel first. The
+reference's custom modules reject qk_norm.
 ``apply_rotary_emb`` restates original.py:14-63. With ``rotary_emb`` the modules rotate q and k in
 the reference's ``[B, h, d, N]`` layout (SANA's ``use_real_unbind_dim=-2``) and repack them for the
 attention kernel.
@@ -161,6 +163,16 @@ class LiteLA(torch.nn.Module):
         qkv[:, :, 1] = self.k_norm(qkv[:, :, 1])
         return qkv
 
+    def _attend(self, qkv: torch.Tensor, rotary_emb) -> torch.Tensor:
+        """qk_norm (when set), rotary embedding (when given) and attention of a packed qkv. Without
+        rotary embedding the norm runs inside the attention kernels (no normalised copy)."""
+        if (self.qk_norm and rotary_emb is None and not getattr(self, "fp32_attention", False)
+                and self.q_norm.weight.dtype == qkv.dtype and self.k_norm.weight.dtype == qkv.dtype
+                and self.q_norm.eps == self.k_norm.eps):
+            kernel = self._attention_kernel(qkv.shape[0], qkv.shape[1], qkv.dtype)
+            return kernel.with_qk_norm(qkv, self.q_norm.weight, self.k_norm.weight, self.q_norm.eps)
+        return self.attention(self._rotate_qk(self._normalise_qk(qkv), rotary_emb))
+
     def attention(self, qkv: torch.Tensor) -> torch.Tensor:
         """Packed ``[B, N, 3, C]`` QKV -> ``[B, N, C]`` in QKV's dtype (original.py:99-117)."""
         batch, seq_len = qkv.shape[0], qkv.shape[1]
@@ -188,8 +200,7 @@ class LiteLA(torch.nn.Module):
         self._validate_input(x)
         batch, seq_len, channels = x.shape
         qkv = self._project_qkv(x).reshape(batch, seq_len, 3, channels)
-        out = self.attention(self._rotate_qk(self._normalise_qk(qkv), rotary_emb))
-        return self._project_output(out)
+        return self._project_output(self._attend(qkv, rotary_emb))
 
 
 # The reference's custom module (custom.py:391) is exported as CustomLiteLA next to the original.
@@ -227,7 +238,7 @@ class JointLiteLA(LiteLA):
         self._validate_input(x)
         batch, seq_len, channels = x.shape
         qkv = self._project_qkv(x).reshape(batch, seq_len, 3, channels)
-        return self._project_output(self.attention(self._rotate_qk(self._normalise_qk(qkv), rotary_emb)))
+        return self._project_output(self._attend(qkv, rotary_emb))
 
 
 GROUPED_SHAPE = dict(batch=1, seq_len=1024, channels=1152, heads=36, dim=32)

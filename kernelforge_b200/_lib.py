@@ -40,6 +40,10 @@ SIGNATURES = {
     "kf_sana_linattn_fwd": (ctypes.c_int, [_c_ptr, _c_ptr, _c_ptr, ctypes.c_size_t, _c_i64, _c_i64,
                                            _c_i64, _c_i64, _c_i64, ctypes.c_float, ctypes.c_int,
                                            ctypes.c_int, _c_ptr]),
+    "kf_sana_linattn_qknorm_workspace_size": (ctypes.c_size_t, [_c_i64, _c_i64, _c_i64, _c_i64, _c_i64]),
+    "kf_sana_linattn_qknorm_fwd": (ctypes.c_int, [_c_ptr, _c_ptr, _c_ptr, ctypes.c_size_t, _c_i64, _c_i64, _c_i64,
+                                                  _c_i64, _c_i64, ctypes.c_float, _c_ptr, _c_ptr, ctypes.c_float,
+                                                  ctypes.c_int, ctypes.c_int, _c_ptr]),
     "kf_sana_linattn_fwd_noalloc": (ctypes.c_int, [_c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
                                                    ctypes.c_float, ctypes.c_int, ctypes.c_int, _c_ptr]),
     "kf_sana_noalloc_scratch_bytes": (ctypes.c_size_t, []),

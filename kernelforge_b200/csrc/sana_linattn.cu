@@ -107,12 +107,139 @@ __device__ __forceinline__ float operand_scale(float max_abs, bool fp16) {
 }
 
 // ------------------------------------------------------------------------------------------
+// qk_norm of LiteLA.forward (SANA_LinearAttention/original.py:92-96, 127-128): q and k each go
+// through an RMSNorm over the C channels of their token (rmsnorm/original.py:40-52) before the
+// attention, y = cast(cast(x r) w) with r = 1 / sqrt(mean(x^2) + eps). The kernels below apply
+// it where they read q and k (fragment registers, or the Q rows bound for tensor memory), so the
+// normalised q and k never exist in memory; r of every token comes from one stats pass
+// (sana_qk_stats) into the workspace, padded to kStatsPad tokens per batch so that every tile's
+// lookups stay in bounds (padded tokens carry r = 0).
+// ------------------------------------------------------------------------------------------
+constexpr int kStatsPad = 128;
+struct QkNorm {
+  const float* stats;  // [B][npad][2]: r of q, r of k per token
+  const void* wq;      // [C] q_norm weight, input dtype
+  const void* wk;      // [C] k_norm weight, input dtype
+  int npad;            // tokens per batch in `stats` (N rounded up to kStatsPad)
+};
+
+// Two packed 16-bit values through the reference's two roundings: cast(cast(x r) w).
+template <typename T>
+__device__ __forceinline__ uint32_t qk_apply2(uint32_t v, float r0, float r1, float w0, float w1) {
+  const float2 x = kf::Mma<T>::to_f2(v);
+  const float2 n = kf::Mma<T>::to_f2(kf::Mma<T>::from_f2(x.x * r0, x.y * r1));
+  return kf::Mma<T>::from_f2(n.x * w0, n.y * w1);
+}
+template <typename T>
+__device__ __forceinline__ float qk_apply1(float x, float r, float w) {
+  return kf::Elem<T>::round_f(kf::Elem<T>::round_f(x * r) * w);
+}
+template <typename T>
+__device__ __forceinline__ float weight_at(const void* w, int c) {
+  return kf::Elem<T>::to_f(static_cast<const T*>(w)[c]);
+}
+// r of q (which = 0) or k (which = 1) of token `tok` of batch b.
+__device__ __forceinline__ float stats_at(const QkNorm& n, int b, int tok, int which) {
+  return __ldg(n.stats + (static_cast<int64_t>(b) * n.npad + tok) * 2 + which);
+}
+
+// r of q (which = 0) or k (which = 1) of the even token t0 and of t0 + 1: one 16-byte load.
+__device__ __forceinline__ float2 stats_pair(const QkNorm& n, int b, int t0, int which) {
+  const float4 v = __ldg(reinterpret_cast<const float4*>(n.stats + (static_cast<int64_t>(b) * n.npad + t0) * 2));
+  return which ? make_float2(v.y, v.w) : make_float2(v.x, v.z);
+}
+
+// The K fragments of one 16-token step (mma.sync B operand: register 0 holds tokens t0 + 2 tig
+// and + 1, register 1 tokens + 8 and + 9, of channel 8 nt + gid) through the k norm of head h.
+// The weights are read where they are used (L1-resident), so nothing stays live across loops.
+template <typename T>
+__device__ __forceinline__ void qk_norm_k(uint32_t (&bf)[4][2], const QkNorm& n, int b, int t0, int lane, int h) {
+  const int tig = lane & 3, gid = lane >> 2;
+  const float2 ra = stats_pair(n, b, t0 + 2 * tig, 1), rb = stats_pair(n, b, t0 + 8 + 2 * tig, 1);
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt) {
+    const float w = weight_at<T>(n.wk, h * kD + nt * 8 + gid);
+    bf[nt][0] = qk_apply2<T>(bf[nt][0], ra.x, ra.y, w, w);
+    bf[nt][1] = qk_apply2<T>(bf[nt][1], rb.x, rb.y, w, w);
+  }
+}
+
+// The Q fragments of one 16-token step (mma.sync A operand, k step ks: registers 0 / 1 hold
+// tokens t0 + gid / + 8 at channels 16 ks + 2 tig, + 1; registers 2 / 3 the same at + 8)
+// through the q norm of head h.
+template <typename T>
+__device__ __forceinline__ void qk_norm_q(uint32_t (&a)[2][4], const QkNorm& n, int b, int t0, int lane, int h) {
+  const int tig = lane & 3, gid = lane >> 2;
+  const float r0 = stats_at(n, b, t0 + gid, 0), r8 = stats_at(n, b, t0 + gid + 8, 0);
+  const T* w = static_cast<const T*>(n.wq) + h * kD + 2 * tig;
+#pragma unroll
+  for (int ks = 0; ks < 2; ++ks) {
+    const float2 lo = kf::Mma<T>::to_f2(__ldg(reinterpret_cast<const unsigned int*>(w + ks * 16)));
+    const float2 hi = kf::Mma<T>::to_f2(__ldg(reinterpret_cast<const unsigned int*>(w + ks * 16 + 8)));
+    a[ks][0] = qk_apply2<T>(a[ks][0], r0, r0, lo.x, lo.y);
+    a[ks][1] = qk_apply2<T>(a[ks][1], r8, r8, lo.x, lo.y);
+    a[ks][2] = qk_apply2<T>(a[ks][2], r0, r0, hi.x, hi.y);
+    a[ks][3] = qk_apply2<T>(a[ks][3], r8, r8, hi.x, hi.y);
+  }
+}
+
+// One warp per token: r of its q and k rows, 1 / sqrt(sum(x^2) / C + eps) in fp32 (the
+// reference's rsqrt of the mean), 0 for the padding tokens N .. npad - 1.
+template <typename T>
+__global__ void __launch_bounds__(256)
+sana_qk_stats(const T* __restrict__ qkv, float* __restrict__ stats, int N, int C, int npad, float eps) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tok = blockIdx.x * 8 + warp, b = blockIdx.y;
+  if (tok >= npad) return;
+  float rq = 0.f, rk = 0.f;
+  if (tok < N) {
+    const T* q = qkv + (static_cast<int64_t>(b) * N + tok) * 3 * C;
+    const T* k = q + C;
+    float sq = 0.f, sk = 0.f;
+    if constexpr (sizeof(T) == 2) {
+      if ((C & 7) == 0) {
+        for (int c = lane * 8; c < C; c += 256) {
+          const uint4 a = *reinterpret_cast<const uint4*>(q + c), e = *reinterpret_cast<const uint4*>(k + c);
+          const uint32_t av[4] = {a.x, a.y, a.z, a.w}, ev[4] = {e.x, e.y, e.z, e.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 x = kf::Mma<T>::to_f2(av[i]), y = kf::Mma<T>::to_f2(ev[i]);
+            sq = fmaf(x.x, x.x, fmaf(x.y, x.y, sq));
+            sk = fmaf(y.x, y.x, fmaf(y.y, y.y, sk));
+          }
+        }
+      } else {
+        for (int c = lane; c < C; c += 32) {
+          const float x = kf::Elem<T>::to_f(q[c]), y = kf::Elem<T>::to_f(k[c]);
+          sq = fmaf(x, x, sq);
+          sk = fmaf(y, y, sk);
+        }
+      }
+    } else {
+      for (int c = lane; c < C; c += 32) {
+        sq = fmaf(q[c], q[c], sq);
+        sk = fmaf(k[c], k[c], sk);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      sq += __shfl_xor_sync(0xffffffffu, sq, o);
+      sk += __shfl_xor_sync(0xffffffffu, sk, o);
+    }
+    rq = 1.f / sqrtf(sq / static_cast<float>(C) + eps);
+    rk = 1.f / sqrtf(sk / static_cast<float>(C) + eps);
+  }
+  if (lane == 0)
+    *reinterpret_cast<float2*>(stats + (static_cast<int64_t>(b) * npad + tok) * 2) = make_float2(rq, rk);
+}
+
+// ------------------------------------------------------------------------------------------
 // Fast path, kernel 1: K^T V and ksum per split; each split writes its fp32 partial.
 // ------------------------------------------------------------------------------------------
-template <typename T, int G, int STAGES>
+template <typename T, int G, int STAGES, bool kNorm>
 __global__ void __launch_bounds__(G * 32)
 sana_vk_producer(const __grid_constant__ CUtensorMap qkv_map, float* __restrict__ partial, int H,
-                 int tiles, int tiles_per_split) {
+                 int tiles, int tiles_per_split, const QkNorm nrm) {
   constexpr int kPairs = G / 2;
   constexpr int kStageBytes = 2 * kPairs * kBoxBytes;  // K boxes, then V boxes
   constexpr int kHeadElems = kRows * kD;
@@ -187,6 +314,10 @@ sana_vk_producer(const __grid_constant__ CUtensorMap qkv_map, float* __restrict_
           const int chunk = g * 4 + np * 2 + (sub >> 1);
           kf::ldsm_x4_t(kbase + kf::swz128(row, chunk), bf[2 * np][0], bf[2 * np][1],
                         bf[2 * np + 1][0], bf[2 * np + 1][1]);
+        }
+        // A head past H (odd H) reads zeros: its weights are not read.
+        if constexpr (kNorm) {
+          if (h0 + warp < H) qk_norm_k<T>(bf, nrm, b, (t_begin + i) * kTok + ks * 16, lane, h0 + warp);
         }
 #pragma unroll
         for (int nt = 0; nt < 4; ++nt) {
@@ -333,11 +464,11 @@ __device__ __forceinline__ void store_b_chunk(uint8_t* tile, int n, int kg, cons
   *reinterpret_cast<uint4*>(row + (((4 + kg) ^ (n & 7)) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
 }
 
-template <typename T, typename O>
+template <typename T, typename O, bool kNorm>
 __global__ void __maxnreg__(96)
 sana_out_tc(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap out_map,
             const float* __restrict__ partial, int H, int S, int head_pairs, int tiles_out, int total_items,
-            int items_per_cta, float eps) {
+            int items_per_cta, float eps, const QkNorm nrm) {
   using Cfg = EpiCfg<O>;
   constexpr int kStages = Cfg::kStages;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
@@ -535,10 +666,29 @@ sana_out_tc(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ C
         const bool got = kf::mbar_wait_or_abort(&q_full[st], (k / kStages) & 1, &g_sana_error, &abort_flag);
         if (!__all_sync(0xffffffffu, got)) return false;  // warp-uniform: the tcgen05 copy is .sync.aligned
         const uint8_t* row = smem + Cfg::kQOff + st * kQTileBytes + r * 128;
+        float rq = 0.f;
+        int head = 0;
+        if constexpr (kNorm) {  // this thread's token: r of its q row; the head's q_norm weights
+          const int it = first + k;
+          const int unit = it / tiles_out;
+          head = 2 * (unit % head_pairs) + hd;
+          rq = stats_at(nrm, unit / head_pairs, (it % tiles_out) * kOutTok + r, 0);
+        }
         uint32_t w[16];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const uint4 x = *reinterpret_cast<const uint4*>(row + (((hd * 4 + j) ^ (r & 7)) << 4));
+          uint4 x = *reinterpret_cast<const uint4*>(row + (((hd * 4 + j) ^ (r & 7)) << 4));
+          if constexpr (kNorm) {
+            // channels 8 j .. 8 j + 7 of the head (a head past H is all zero: weights unread)
+            const uint4 wv = head < H ? __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(nrm.wq) + head * kD) + j)
+                                      : make_uint4(0, 0, 0, 0);
+            const float2 w0 = kf::Mma<T>::to_f2(wv.x), w1 = kf::Mma<T>::to_f2(wv.y);
+            const float2 w2 = kf::Mma<T>::to_f2(wv.z), w3 = kf::Mma<T>::to_f2(wv.w);
+            x.x = qk_apply2<T>(x.x, rq, rq, w0.x, w0.y);
+            x.y = qk_apply2<T>(x.y, rq, rq, w1.x, w1.y);
+            x.z = qk_apply2<T>(x.z, rq, rq, w2.x, w2.y);
+            x.w = qk_apply2<T>(x.w, rq, rq, w3.x, w3.y);
+          }
           w[4 * j + 0] = kf::Mma<T>::relu2(x.x);
           w[4 * j + 1] = kf::Mma<T>::relu2(x.y);
           w[4 * j + 2] = kf::Mma<T>::relu2(x.z);
@@ -633,10 +783,10 @@ sana_out_tc(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ C
 constexpr int kGenThreads = 256;
 constexpr int kGenTok = 32;
 
-template <typename T>
+template <typename T, bool kNorm>
 __global__ void __launch_bounds__(kGenThreads)
 sana_vk_generic(const T* __restrict__ qkv, float* __restrict__ partial, float* __restrict__ final_vk,
-                unsigned int* __restrict__ counters, int H, int d, int N, int tiles_per_split) {
+                unsigned int* __restrict__ counters, int H, int d, int N, int tiles_per_split, const QkNorm nrm) {
   extern __shared__ float gsm[];
   const int nelem = (d + 1) * d;
   float* acc = gsm;
@@ -656,7 +806,9 @@ sana_vk_generic(const T* __restrict__ qkv, float* __restrict__ partial, float* _
       float kv = 0.f, vv = 0.f;
       if (tok < tok1) {
         const T* row = qkv + (static_cast<int64_t>(b) * N + tok) * 3 * C + static_cast<int64_t>(h) * d + c;
-        kv = fmaxf(kf::Elem<T>::to_f(row[C]), 0.f);
+        kv = kf::Elem<T>::to_f(row[C]);
+        if constexpr (kNorm) kv = qk_apply1<T>(kv, stats_at(nrm, b, tok, 1), weight_at<T>(nrm.wk, h * d + c));
+        kv = fmaxf(kv, 0.f);
         vv = kf::Elem<T>::to_f(row[2 * C]);
       }
       kt[e] = kv;
@@ -690,10 +842,10 @@ sana_vk_generic(const T* __restrict__ qkv, float* __restrict__ partial, float* _
   if (threadIdx.x == 0) *counter = 0u;
 }
 
-template <typename T, typename O>
+template <typename T, typename O, bool kNorm>
 __global__ void __launch_bounds__(kGenThreads)
 sana_out_generic(const T* __restrict__ qkv, const float* __restrict__ final_vk, O* __restrict__ out,
-                 int H, int d, int N, float eps) {
+                 int H, int d, int N, float eps, const QkNorm nrm) {
   extern __shared__ float gsm[];
   const int nelem = (d + 1) * d;
   float* vk = gsm;
@@ -706,8 +858,11 @@ sana_out_generic(const T* __restrict__ qkv, const float* __restrict__ final_vk, 
   for (int e = threadIdx.x; e < kGenTok * d; e += kGenThreads) {
     const int tt = e / d, c = e % d, tok = t0 + tt;
     float qv = 0.f;
-    if (tok < N)
-      qv = fmaxf(kf::Elem<T>::to_f(qkv[(static_cast<int64_t>(b) * N + tok) * 3 * C + static_cast<int64_t>(h) * d + c]), 0.f);
+    if (tok < N) {
+      qv = kf::Elem<T>::to_f(qkv[(static_cast<int64_t>(b) * N + tok) * 3 * C + static_cast<int64_t>(h) * d + c]);
+      if constexpr (kNorm) qv = qk_apply1<T>(qv, stats_at(nrm, b, tok, 0), weight_at<T>(nrm.wq, h * d + c));
+      qv = fmaxf(qv, 0.f);
+    }
     qt[e] = qv;
   }
   __syncthreads();
@@ -804,10 +959,11 @@ __device__ __forceinline__ uint32_t swz64(uint32_t row, uint32_t chunk) {
   return row * 64 + ((chunk ^ ((row >> 1) & 3)) << 4);
 }
 
-template <typename T, typename O>
+template <typename T, typename O, bool kNorm>
 __global__ void __launch_bounds__(kFusedThreads, 1)
 sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constant__ CUtensorMap q_map,
-                const __grid_constant__ CUtensorMap out_map, int B, int H, int N, float eps) {
+                const __grid_constant__ CUtensorMap out_map, int B, int H, int N, float eps,
+                const QkNorm nrm) {
   constexpr bool kFp16 = std::is_same<T, __half>::value;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (kf::smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -905,6 +1061,7 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
           kf::ldsm_x4_t(kbase + swz64(row, np * 2 + (sub >> 1)), bf[2 * np][0], bf[2 * np][1], bf[2 * np + 1][0],
                         bf[2 * np + 1][1]);
         }
+        if constexpr (kNorm) qk_norm_k<T>(bf, nrm, b, i * kFusedKTok + ks * 16, lane, h);
 #pragma unroll
         for (int nt = 0; nt < 4; ++nt) {
           bf[nt][0] = kf::Mma<T>::relu2(bf[nt][0]);
@@ -1000,8 +1157,17 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
         for (int ks = 0; ks < 2; ++ks) {
           const int row = m16 * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
           kf::ldsm_x4(qbase + swz64(row, ks * 2 + (lane >> 4)), a[ks][0], a[ks][1], a[ks][2], a[ks][3]);
+          if constexpr (!kNorm) {
 #pragma unroll
-          for (int e = 0; e < 4; ++e) a[ks][e] = kf::Mma<T>::relu2(a[ks][e]);
+            for (int e = 0; e < 4; ++e) a[ks][e] = kf::Mma<T>::relu2(a[ks][e]);
+          }
+        }
+        if constexpr (kNorm) {
+          qk_norm_q<T>(a, nrm, b, j * kFusedQTok + m16 * kFusedSub, lane, h);
+#pragma unroll
+          for (int ks = 0; ks < 2; ++ks)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) a[ks][e] = kf::Mma<T>::relu2(a[ks][e]);
         }
         if (m16 == kFusedQTok / kFusedSub - 1) {  // the stage is no longer read
           __syncwarp();
@@ -1059,10 +1225,11 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
   if (lane == 0) kf::tma_store_wait_read0();  // shared memory outlives the stores' reads
 }
 
-template <typename T, typename O>
+template <typename T, typename O, bool kNorm>
 __global__ void __launch_bounds__(kFusedThreads, 1)
 sana_head_cluster(const __grid_constant__ CUtensorMap kv_map, const __grid_constant__ CUtensorMap q_map,
-                const __grid_constant__ CUtensorMap out_map, int B, int H, int N, float eps) {
+                const __grid_constant__ CUtensorMap out_map, int B, int H, int N, float eps,
+                const QkNorm nrm) {
   constexpr bool kFp16 = std::is_same<T, __half>::value;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (kf::smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -1178,6 +1345,7 @@ sana_head_cluster(const __grid_constant__ CUtensorMap kv_map, const __grid_const
           kf::ldsm_x4_t(kbase + swz64(row, np * 2 + (sub >> 1)), bf[2 * np][0], bf[2 * np][1], bf[2 * np + 1][0],
                         bf[2 * np + 1][1]);
         }
+        if constexpr (kNorm) qk_norm_k<T>(bf, nrm, b, (kv0 + i) * kFusedKTok + ks * 16, lane, h);
 #pragma unroll
         for (int nt = 0; nt < 4; ++nt) {
           bf[nt][0] = kf::Mma<T>::relu2(bf[nt][0]);
@@ -1323,8 +1491,17 @@ sana_head_cluster(const __grid_constant__ CUtensorMap kv_map, const __grid_const
         for (int ks = 0; ks < 2; ++ks) {
           const int row = m16 * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
           kf::ldsm_x4(qbase + swz64(row, ks * 2 + (lane >> 4)), a[ks][0], a[ks][1], a[ks][2], a[ks][3]);
+          if constexpr (!kNorm) {
 #pragma unroll
-          for (int e = 0; e < 4; ++e) a[ks][e] = kf::Mma<T>::relu2(a[ks][e]);
+            for (int e = 0; e < 4; ++e) a[ks][e] = kf::Mma<T>::relu2(a[ks][e]);
+          }
+        }
+        if constexpr (kNorm) {
+          qk_norm_q<T>(a, nrm, b, tok0 + m16 * kFusedSub, lane, h);
+#pragma unroll
+          for (int ks = 0; ks < 2; ++ks)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) a[ks][e] = kf::Mma<T>::relu2(a[ks][e]);
         }
         if (m16 == n_sub - 1) {  // the stage is no longer read
           __syncwarp();
@@ -1404,7 +1581,7 @@ int fused_max_clusters(int cs) {
   if (dev < 0 || dev >= 64 || cs < 1 || cs > kFusedMaxCluster) return 0;
   std::lock_guard<std::mutex> lock(mu);
   if (cache[dev][cs] != 0) return cache[dev][cs] > 0 ? cache[dev][cs] : 0;
-  auto kernel = sana_head_cluster<__nv_bfloat16, __nv_bfloat16>;
+  auto kernel = sana_head_cluster<__nv_bfloat16, __nv_bfloat16, false>;
   int n = 0;
   if (kf_host::prepare_kernel(reinterpret_cast<const void*>(kernel), kFusedThreads, ClusterSmem::kBytes, nullptr) ==
       KF_OK) {
@@ -1464,7 +1641,9 @@ bool fused_preferred(int64_t B, int64_t H, int64_t N) {
 }
 
 template <typename T>
-int launch_fused(const void* qkv, void* out, int B, int H, int N, float eps, int out_dtype, cudaStream_t stream) {
+int launch_fused(const void* qkv, void* out, int B, int H, int N, float eps, int out_dtype, cudaStream_t stream,
+                 const QkNorm* nrm) {
+  const QkNorm nv = nrm ? *nrm : QkNorm{};
   const int C = H * kD;
   const int in_dtype = std::is_same<T, __half>::value ? KF_DTYPE_F16 : KF_DTYPE_BF16;
   const size_t es = 2;
@@ -1496,7 +1675,7 @@ int launch_fused(const void* qkv, void* out, int B, int H, int N, float eps, int
       const int prep = kf_host::prepare_kernel(reinterpret_cast<const void*>(one_cta), kFusedThreads,
                                                FusedSmem::kBytes, nullptr);
       if (prep != KF_OK) return prep;
-      one_cta<<<grid, kFusedThreads, FusedSmem::kBytes, stream>>>(kv_map, q_map, out_map, B, H, N, eps);
+      one_cta<<<grid, kFusedThreads, FusedSmem::kBytes, stream>>>(kv_map, q_map, out_map, B, H, N, eps, nv);
       KF_LAUNCH_CHECK();
       return KF_OK;
     }
@@ -1516,20 +1695,28 @@ int launch_fused(const void* qkv, void* out, int B, int H, int N, float eps, int
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    KF_CUDA_TRY(cudaLaunchKernelEx(&cfg, clustered, kv_map, q_map, out_map, B, H, N, eps));
+    KF_CUDA_TRY(cudaLaunchKernelEx(&cfg, clustered, kv_map, q_map, out_map, B, H, N, eps, nv));
     return KF_OK;
   };
+  if (nrm) {
+    switch (out_dtype) {
+      case KF_DTYPE_F32: return run(sana_head_fused<T, float, true>, sana_head_cluster<T, float, true>);
+      case KF_DTYPE_F16: return run(sana_head_fused<T, __half, true>, sana_head_cluster<T, __half, true>);
+      default: return run(sana_head_fused<T, __nv_bfloat16, true>, sana_head_cluster<T, __nv_bfloat16, true>);
+    }
+  }
   switch (out_dtype) {
-    case KF_DTYPE_F32: return run(sana_head_fused<T, float>, sana_head_cluster<T, float>);
-    case KF_DTYPE_F16: return run(sana_head_fused<T, __half>, sana_head_cluster<T, __half>);
-    default: return run(sana_head_fused<T, __nv_bfloat16>, sana_head_cluster<T, __nv_bfloat16>);
+    case KF_DTYPE_F32: return run(sana_head_fused<T, float, false>, sana_head_cluster<T, float, false>);
+    case KF_DTYPE_F16: return run(sana_head_fused<T, __half, false>, sana_head_cluster<T, __half, false>);
+    default: return run(sana_head_fused<T, __nv_bfloat16, false>, sana_head_cluster<T, __nv_bfloat16, false>);
   }
 }
 
 // ws: the workspace laid out by fast_layout(B, H, S); its counters are zero between calls.
 template <typename T, int G>
 int launch_fast(const void* qkv, void* out, uint8_t* ws, int B, int H, int N, int S, float eps, int out_dtype,
-                cudaStream_t stream) {
+                cudaStream_t stream, const QkNorm* nrm) {
+  const QkNorm nv = nrm ? *nrm : QkNorm{};
   static_assert(G == 2, "the epilogue works on head pairs");
   const int C = H * kD;
   const int in_dtype = std::is_same<T, __half>::value ? KF_DTYPE_F16 : KF_DTYPE_BF16;
@@ -1564,11 +1751,11 @@ int launch_fast(const void* qkv, void* out, uint8_t* ws, int B, int H, int N, in
   const int tiles = (N + kTok - 1) / kTok;
   const int tps = (tiles + S - 1) / S;
   {
-    auto kernel = sana_vk_producer<T, G, kFastStages>;
+    auto kernel = nrm ? sana_vk_producer<T, G, kFastStages, true> : sana_vk_producer<T, G, kFastStages, false>;
     const int smem = kFastStages * 2 * (G / 2) * kBoxBytes + kFastStages * 8 + 1024;
     const int prep = kf_host::prepare_kernel(reinterpret_cast<const void*>(kernel), G * 32, smem, nullptr);
     if (prep != KF_OK) return prep;
-    kernel<<<dim3(S, HG, B), G * 32, smem, stream>>>(kv_map, partial, H, tiles, tps);
+    kernel<<<dim3(S, HG, B), G * 32, smem, stream>>>(kv_map, partial, H, tiles, tps, nv);
     KF_LAUNCH_CHECK();
   }
   auto run = [&](auto kernel, int smem) -> int {
@@ -1594,30 +1781,38 @@ int launch_fast(const void* qkv, void* out, uint8_t* ws, int B, int H, int N, in
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     KF_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, q_map, out_map, static_cast<const float*>(partial), H, S, HG,
-                                   tiles_out, total, per, eps));
+                                   tiles_out, total, per, eps, nv));
     return KF_OK;
   };
+  if (nrm) {
+    switch (out_dtype) {
+      case KF_DTYPE_F32: return run(sana_out_tc<T, float, true>, EpiCfg<float>::kSmemBytes);
+      case KF_DTYPE_F16: return run(sana_out_tc<T, __half, true>, EpiCfg<__half>::kSmemBytes);
+      default: return run(sana_out_tc<T, __nv_bfloat16, true>, EpiCfg<__nv_bfloat16>::kSmemBytes);
+    }
+  }
   switch (out_dtype) {
-    case KF_DTYPE_F32: return run(sana_out_tc<T, float>, EpiCfg<float>::kSmemBytes);
-    case KF_DTYPE_F16: return run(sana_out_tc<T, __half>, EpiCfg<__half>::kSmemBytes);
-    default: return run(sana_out_tc<T, __nv_bfloat16>, EpiCfg<__nv_bfloat16>::kSmemBytes);
+    case KF_DTYPE_F32: return run(sana_out_tc<T, float, false>, EpiCfg<float>::kSmemBytes);
+    case KF_DTYPE_F16: return run(sana_out_tc<T, __half, false>, EpiCfg<__half>::kSmemBytes);
+    default: return run(sana_out_tc<T, __nv_bfloat16, false>, EpiCfg<__nv_bfloat16>::kSmemBytes);
   }
 }
 
 template <typename T>
 int launch_generic(const void* qkv, void* out, float* partial, float* final_vk,
                    unsigned int* counters, int B, int H, int d, int N, int S, float eps,
-                   int out_dtype, cudaStream_t stream) {
+                   int out_dtype, cudaStream_t stream, const QkNorm* nrm) {
+  const QkNorm nv = nrm ? *nrm : QkNorm{};
   const T* q = static_cast<const T*>(qkv);
   const int nelem = (d + 1) * d;
   const int tiles = (N + kTok - 1) / kTok;
   const int tps = (tiles + S - 1) / S;
   {
     const int smem = (nelem + 2 * kGenTok * d) * static_cast<int>(sizeof(float));
-    auto kernel = sana_vk_generic<T>;
+    auto kernel = nrm ? sana_vk_generic<T, true> : sana_vk_generic<T, false>;
     const int prep = kf_host::prepare_kernel(reinterpret_cast<const void*>(kernel), kGenThreads, smem, nullptr);
     if (prep != KF_OK) return prep;
-    kernel<<<dim3(S, H, B), kGenThreads, smem, stream>>>(q, partial, final_vk, counters, H, d, N, tps);
+    kernel<<<dim3(S, H, B), kGenThreads, smem, stream>>>(q, partial, final_vk, counters, H, d, N, tps, nv);
     KF_LAUNCH_CHECK();
   }
   const int smem = (nelem + kGenTok * d + kGenTok) * static_cast<int>(sizeof(float));
@@ -1625,14 +1820,21 @@ int launch_generic(const void* qkv, void* out, float* partial, float* final_vk,
   auto run = [&](auto kernel, auto* optr) -> int {
     const int prep = kf_host::prepare_kernel(reinterpret_cast<const void*>(kernel), kGenThreads, smem, nullptr);
     if (prep != KF_OK) return prep;
-    kernel<<<grid, kGenThreads, smem, stream>>>(q, final_vk, optr, H, d, N, eps);
+    kernel<<<grid, kGenThreads, smem, stream>>>(q, final_vk, optr, H, d, N, eps, nv);
     KF_LAUNCH_CHECK();
     return KF_OK;
   };
+  if (nrm) {
+    switch (out_dtype) {
+      case KF_DTYPE_F32: return run(sana_out_generic<T, float, true>, static_cast<float*>(out));
+      case KF_DTYPE_F16: return run(sana_out_generic<T, __half, true>, static_cast<__half*>(out));
+      default: return run(sana_out_generic<T, __nv_bfloat16, true>, static_cast<__nv_bfloat16*>(out));
+    }
+  }
   switch (out_dtype) {
-    case KF_DTYPE_F32: return run(sana_out_generic<T, float>, static_cast<float*>(out));
-    case KF_DTYPE_F16: return run(sana_out_generic<T, __half>, static_cast<__half*>(out));
-    default: return run(sana_out_generic<T, __nv_bfloat16>, static_cast<__nv_bfloat16*>(out));
+    case KF_DTYPE_F32: return run(sana_out_generic<T, float, false>, static_cast<float*>(out));
+    case KF_DTYPE_F16: return run(sana_out_generic<T, __half, false>, static_cast<__half*>(out));
+    default: return run(sana_out_generic<T, __nv_bfloat16, false>, static_cast<__nv_bfloat16*>(out));
   }
 }
 
@@ -1663,56 +1865,121 @@ KF_API size_t kf_sana_linattn_workspace_size(int64_t batch, int64_t heads, int64
   return workspace_bytes_for(batch, heads, dim, seq_len, splits);
 }
 
-KF_API int kf_sana_linattn_fwd(const void* qkv, void* out, void* workspace, size_t workspace_bytes,
-                               int64_t batch, int64_t heads, int64_t dim, int64_t seq_len,
-                               int64_t splits, float eps, int in_dtype, int out_dtype,
-                               void* stream) {
+namespace {
+
+// Validation shared by the workspace entry points.
+int check_args(const void* qkv, const void* out, int64_t batch, int64_t heads, int64_t dim, int64_t seq_len,
+               float eps, int in_dtype, int out_dtype) {
   if (!kf::dtype_valid(in_dtype) || !kf::dtype_valid(out_dtype)) return KF_ERR_UNSUPPORTED;
   if (batch <= 0 || heads <= 0 || seq_len <= 0) return KF_ERR_INVALID_ARGUMENT;
   if (!valid_head_dim(dim)) return KF_ERR_UNSUPPORTED;
-  if (qkv == nullptr || out == nullptr || workspace == nullptr) return KF_ERR_INVALID_ARGUMENT;
+  if (qkv == nullptr || out == nullptr) return KF_ERR_INVALID_ARGUMENT;
   if (!(eps >= 0.f)) return KF_ERR_INVALID_ARGUMENT;
   // TMA coordinates and kernel indices are 32-bit.
   if (batch > 65535 || seq_len > (int64_t(1) << 30) || heads * dim > (int64_t(1) << 24) ||
       batch * seq_len * 3 * heads * dim > (int64_t(1) << 40))
     return KF_ERR_UNSUPPORTED;
-  const int S_gen = generic_splits(batch, heads, seq_len, splits);
-  const WorkspaceLayout lay = layout_for(batch, heads, dim, S_gen);
-  if (workspace_bytes < workspace_bytes_for(batch, heads, dim, seq_len, splits)) return KF_ERR_WORKSPACE;
-  if (!kf::aligned(workspace, 256)) return KF_ERR_MISALIGNED;
   if (!kf::aligned(qkv, kf::dtype_size(in_dtype)) || !kf::aligned(out, kf::dtype_size(out_dtype)))
     return KF_ERR_MISALIGNED;
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  return KF_OK;
+}
+
+// The attention proper, after validation; nrm != nullptr applies qk_norm from nrm->stats.
+int sana_forward(const void* qkv, void* out, uint8_t* ws, int64_t batch, int64_t heads, int64_t dim,
+                 int64_t seq_len, int64_t splits, float eps, int in_dtype, int out_dtype, cudaStream_t s,
+                 const QkNorm* nrm) {
+  const int S_gen = generic_splits(batch, heads, seq_len, splits);
+  const WorkspaceLayout lay = layout_for(batch, heads, dim, S_gen);
   float* partial = reinterpret_cast<float*>(ws + lay.partial_off);
   float* final_vk = reinterpret_cast<float*>(ws + lay.final_off);
   unsigned int* counters = reinterpret_cast<unsigned int*>(ws + lay.counter_off);
   const int B = static_cast<int>(batch), H = static_cast<int>(heads), d = static_cast<int>(dim);
   const int N = static_cast<int>(seq_len);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-
   const bool fast = d == kD && (in_dtype == KF_DTYPE_BF16 || in_dtype == KF_DTYPE_F16) &&
                     H * kD >= 64 && N >= kTok && kf::aligned(qkv, 16) && kf::aligned(out, 16);
   if (fast && (splits == -1 || (splits == 0 && fused_preferred(B, H, N)))) {
     // Whole heads per CTA (or per cluster of CTAs), one launch, no workspace traffic.
-    if (in_dtype == KF_DTYPE_BF16) return launch_fused<__nv_bfloat16>(qkv, out, B, H, N, eps, out_dtype, s);
-    return launch_fused<__half>(qkv, out, B, H, N, eps, out_dtype, s);
+    if (in_dtype == KF_DTYPE_BF16) return launch_fused<__nv_bfloat16>(qkv, out, B, H, N, eps, out_dtype, s, nrm);
+    return launch_fused<__half>(qkv, out, B, H, N, eps, out_dtype, s, nrm);
   }
   if (fast) {
     // Two heads (one 128-byte TMA box) per CTA measured at or above four heads on every
     // benchmark shape.
     const int S = fast_splits(B, H, N, splits);
     if (in_dtype == KF_DTYPE_BF16)
-      return launch_fast<__nv_bfloat16, kFastHeads>(qkv, out, ws, B, H, N, S, eps, out_dtype, s);
-    return launch_fast<__half, kFastHeads>(qkv, out, ws, B, H, N, S, eps, out_dtype, s);
+      return launch_fast<__nv_bfloat16, kFastHeads>(qkv, out, ws, B, H, N, S, eps, out_dtype, s, nrm);
+    return launch_fast<__half, kFastHeads>(qkv, out, ws, B, H, N, S, eps, out_dtype, s, nrm);
   }
   switch (in_dtype) {
     case KF_DTYPE_F32:
-      return launch_generic<float>(qkv, out, partial, final_vk, counters, B, H, d, N, S_gen, eps, out_dtype, s);
+      return launch_generic<float>(qkv, out, partial, final_vk, counters, B, H, d, N, S_gen, eps, out_dtype, s, nrm);
     case KF_DTYPE_F16:
-      return launch_generic<__half>(qkv, out, partial, final_vk, counters, B, H, d, N, S_gen, eps, out_dtype, s);
+      return launch_generic<__half>(qkv, out, partial, final_vk, counters, B, H, d, N, S_gen, eps, out_dtype, s, nrm);
     default:
-      return launch_generic<__nv_bfloat16>(qkv, out, partial, final_vk, counters, B, H, d, N, S_gen, eps, out_dtype, s);
+      return launch_generic<__nv_bfloat16>(qkv, out, partial, final_vk, counters, B, H, d, N, S_gen, eps, out_dtype,
+                                           s, nrm);
   }
+}
+
+int64_t stats_tokens(int64_t N) { return (N + kStatsPad - 1) / kStatsPad * kStatsPad; }
+
+}  // namespace
+
+KF_API int kf_sana_linattn_fwd(const void* qkv, void* out, void* workspace, size_t workspace_bytes,
+                               int64_t batch, int64_t heads, int64_t dim, int64_t seq_len,
+                               int64_t splits, float eps, int in_dtype, int out_dtype,
+                               void* stream) {
+  const int st = check_args(qkv, out, batch, heads, dim, seq_len, eps, in_dtype, out_dtype);
+  if (st != KF_OK) return st;
+  if (workspace == nullptr) return KF_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < workspace_bytes_for(batch, heads, dim, seq_len, splits)) return KF_ERR_WORKSPACE;
+  if (!kf::aligned(workspace, 256)) return KF_ERR_MISALIGNED;
+  return sana_forward(qkv, out, static_cast<uint8_t*>(workspace), batch, heads, dim, seq_len, splits, eps,
+                      in_dtype, out_dtype, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+KF_API size_t kf_sana_linattn_qknorm_workspace_size(int64_t batch, int64_t heads, int64_t dim, int64_t seq_len,
+                                                    int64_t splits) {
+  if (batch <= 0 || heads <= 0 || seq_len <= 0 || !valid_head_dim(dim)) return 0;
+  return align256(workspace_bytes_for(batch, heads, dim, seq_len, splits)) +
+         align256(static_cast<size_t>(batch) * stats_tokens(seq_len) * 2 * sizeof(float));
+}
+
+KF_API int kf_sana_linattn_qknorm_fwd(const void* qkv, void* out, void* workspace, size_t workspace_bytes,
+                                      int64_t batch, int64_t heads, int64_t dim, int64_t seq_len, int64_t splits,
+                                      float eps, const void* q_weight, const void* k_weight, float norm_eps,
+                                      int in_dtype, int out_dtype, void* stream) {
+  const int st = check_args(qkv, out, batch, heads, dim, seq_len, eps, in_dtype, out_dtype);
+  if (st != KF_OK) return st;
+  if (workspace == nullptr || q_weight == nullptr || k_weight == nullptr) return KF_ERR_INVALID_ARGUMENT;
+  if (!(norm_eps >= 0.f)) return KF_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < kf_sana_linattn_qknorm_workspace_size(batch, heads, dim, seq_len, splits))
+    return KF_ERR_WORKSPACE;
+  if (!kf::aligned(workspace, 256)) return KF_ERR_MISALIGNED;
+  // The tensor-core epilogue reads each head's 32 q weights as 16-byte vectors.
+  if (!kf::aligned(q_weight, 16) || !kf::aligned(k_weight, 16)) return KF_ERR_MISALIGNED;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const int64_t npad = stats_tokens(seq_len);
+  float* stats = reinterpret_cast<float*>(ws + align256(workspace_bytes_for(batch, heads, dim, seq_len, splits)));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int C = static_cast<int>(heads * dim), N = static_cast<int>(seq_len);
+  const dim3 grid(static_cast<unsigned>((npad + 7) / 8), static_cast<unsigned>(batch));
+  switch (in_dtype) {
+    case KF_DTYPE_F32:
+      sana_qk_stats<float><<<grid, 256, 0, s>>>(static_cast<const float*>(qkv), stats, N, C, static_cast<int>(npad),
+                                                norm_eps);
+      break;
+    case KF_DTYPE_F16:
+      sana_qk_stats<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(qkv), stats, N, C,
+                                                 static_cast<int>(npad), norm_eps);
+      break;
+    default:
+      sana_qk_stats<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(qkv), stats, N, C,
+                                                        static_cast<int>(npad), norm_eps);
+  }
+  KF_LAUNCH_CHECK();
+  const QkNorm nrm{stats, q_weight, k_weight, static_cast<int>(npad)};
+  return sana_forward(qkv, out, ws, batch, heads, dim, seq_len, splits, eps, in_dtype, out_dtype, s, &nrm);
 }
 
 KF_API int kf_sana_linattn_plan(int64_t batch, int64_t heads, int64_t dim, int64_t seq_len, int64_t splits,
@@ -1816,8 +2083,8 @@ KF_API int kf_sana_linattn_fwd_noalloc(const void* qkv, void* out, int64_t batch
   if (fast && (splits == -1 || (splits == 0 && fused_preferred(B, H, N)))) {
     // The one-launch schedule, chosen exactly as kf_sana_linattn_fwd chooses it: it keeps
     // whole heads in shared memory and needs no scratch at all.
-    if (in_dtype == KF_DTYPE_BF16) return launch_fused<__nv_bfloat16>(qkv, out, B, H, N, eps, out_dtype, s);
-    return launch_fused<__half>(qkv, out, B, H, N, eps, out_dtype, s);
+    if (in_dtype == KF_DTYPE_BF16) return launch_fused<__nv_bfloat16>(qkv, out, B, H, N, eps, out_dtype, s, nullptr);
+    return launch_fused<__half>(qkv, out, B, H, N, eps, out_dtype, s, nullptr);
   }
   if (fast) {
     // As many splits as requested (or the default) and the scratch holds.
@@ -1828,8 +2095,8 @@ KF_API int kf_sana_linattn_fwd_noalloc(const void* qkv, void* out, int64_t batch
     const int st = noalloc_scratch(&scratch);
     if (st != KF_OK) return st;
     if (in_dtype == KF_DTYPE_BF16)
-      return launch_fast<__nv_bfloat16, kFastHeads>(qkv, out, scratch, B, H, N, S, eps, out_dtype, s);
-    return launch_fast<__half, kFastHeads>(qkv, out, scratch, B, H, N, S, eps, out_dtype, s);
+      return launch_fast<__nv_bfloat16, kFastHeads>(qkv, out, scratch, B, H, N, S, eps, out_dtype, s, nullptr);
+    return launch_fast<__half, kFastHeads>(qkv, out, scratch, B, H, N, S, eps, out_dtype, s, nullptr);
   }
   // Generic path: as many splits as requested (or the default) and the scratch holds.
   int S = generic_splits(batch, heads, seq_len, splits);
@@ -1846,10 +2113,10 @@ KF_API int kf_sana_linattn_fwd_noalloc(const void* qkv, void* out, int64_t batch
   KF_CUDA_TRY(cudaMemsetAsync(counters, 0, static_cast<size_t>(batch) * heads * sizeof(unsigned int), s));
   switch (in_dtype) {
     case KF_DTYPE_F32:
-      return launch_generic<float>(qkv, out, partial, final_vk, counters, B, H, d, N, S, eps, out_dtype, s);
+      return launch_generic<float>(qkv, out, partial, final_vk, counters, B, H, d, N, S, eps, out_dtype, s, nullptr);
     case KF_DTYPE_F16:
-      return launch_generic<__half>(qkv, out, partial, final_vk, counters, B, H, d, N, S, eps, out_dtype, s);
+      return launch_generic<__half>(qkv, out, partial, final_vk, counters, B, H, d, N, S, eps, out_dtype, s, nullptr);
     default:
-      return launch_generic<__nv_bfloat16>(qkv, out, partial, final_vk, counters, B, H, d, N, S, eps, out_dtype, s);
+      return launch_generic<__nv_bfloat16>(qkv, out, partial, final_vk, counters, B, H, d, N, S, eps, out_dtype, s, nullptr);
   }
 }

@@ -105,3 +105,26 @@ def linear_exact(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | Non
     if bias is not None:
         y = y + bias.detach().to("cpu", torch.float64)
     return y
+
+
+def qk_inv_rms(qkv: torch.Tensor, eps: float) -> torch.Tensor:
+    """Float64 ``1 / sqrt(mean(x^2) + eps)`` of every token's q and k rows of a packed
+    ``[B, N, 3, C]`` qkv -> ``[B, N, 2]``: the scale of LiteLA's q_norm / k_norm
+    (SANA_LinearAttention/original.py:127-128, RMSNorm._norm of rmsnorm/original.py:27-38)."""
+    x = qkv.detach().to("cpu", torch.float64)[:, :, :2]
+    return 1.0 / torch.sqrt((x * x).mean(-1) + eps)
+
+
+def qk_norm_apply(qkv: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor, inv_rms: torch.Tensor):
+    """q_norm / k_norm of a packed qkv with the given per-token scales ``inv_rms [B, N, 2]``
+    (fp32 values), with the reference's rounding points (rmsnorm/original.py:51-52): the
+    normalised row rounded to the input dtype, then multiplied by the weight and rounded again
+    (fp32 inputs: two fp32 multiplies). v is unchanged."""
+    q, k, v = qkv.detach().cpu().unbind(2)
+    r = inv_rms.detach().cpu().to(torch.float32)
+    dtype = qkv.dtype
+
+    def norm(x, rr, w):
+        return (x.float() * rr[..., None]).to(dtype) * w.detach().cpu().to(dtype)
+
+    return torch.stack([norm(q, r[..., 0], q_weight), norm(k, r[..., 1], k_weight), v], dim=2)

@@ -211,3 +211,69 @@ def test_nonfinite_free_on_zero_queries(kf):
     qkv[:, :, 0] = -1.0
     out = run(kf, qkv.cuda(), 2, 32, torch.float32)
     assert torch.count_nonzero(out) == 0
+
+
+# ---------------------------------------------------------------------------------------------
+# qk_norm inside the attention kernels (kf_sana_linattn_qknorm_fwd). The per-token scales r are
+# read back from the workspace and checked against float64 (fp32 sums of squares: rtol 2e-5);
+# the oracle then normalises q and k with those same r values and the reference's rounding
+# points, so the normalised q and k are bit-identical to what the kernels use, and the attention
+# is held to the bars above.
+# ---------------------------------------------------------------------------------------------
+def _qknorm_case(kf, b, n, h, d, dtype, out_dtype, splits, seed):
+    from kernelforge_b200 import _lib
+
+    g = torch.Generator().manual_seed(seed)
+    qkv = (torch.randn(b, n, 3, h * d, generator=g) * 1.7).to(dtype)
+    qw = (0.5 + torch.rand(h * d, generator=g)).to(dtype)
+    kw = (0.5 + torch.rand(h * d, generator=g)).to(dtype)
+    run = kf.QKVAttnMatmul(b, h, d, n, 1e-15, NAMES[dtype], NAMES[out_dtype], splits=splits)
+    out = run.with_qk_norm(qkv.cuda(), qw.cuda(), kw.cuda(), 1e-5)
+    torch.cuda.synchronize()
+    ws = run.workspace(torch.device("cuda", 0))
+    start = (_lib.lib.kf_sana_linattn_workspace_size(b, h, d, n, run.splits) + 255) // 256 * 256
+    npad = (n + 127) // 128 * 128
+    r = ws[start:start + b * npad * 8].view(torch.float32).view(b, npad, 2)[:, :n].cpu()
+    torch.testing.assert_close(r.double(), oracle.qk_inv_rms(qkv, 1e-5), rtol=2e-5, atol=0)
+    assert torch.count_nonzero(ws[start:start + b * npad * 8].view(torch.float32).view(b, npad, 2)[:, n:]) == 0
+    return out, oracle.qk_norm_apply(qkv, qw, kw, r)
+
+
+@pytest.mark.parametrize("dtype,out_dtype", [(torch.bfloat16, torch.bfloat16), (torch.bfloat16, torch.float32),
+                                             (torch.float16, torch.float16)])
+@pytest.mark.parametrize("b,n,h,splits", [
+    (2, 512, 80, 0),     # one CTA per (batch, head): 160 units on 148 SMs
+    (1, 1000, 4, -1),    # thread-block clusters share each head
+    (2, 1000, 6, 3),     # split path: producer (K) and tcgen05 epilogue (Q)
+    (1, 333, 5, 2),      # split path, odd head count (a head pair with one head past H)
+])
+def test_qk_norm_fast_paths(kf, b, n, h, splits, dtype, out_dtype):
+    out, normed = _qknorm_case(kf, b, n, h, 32, dtype, out_dtype, splits, seed=b * 100 + n + h)
+    check_exact(out, normed, h, 32)
+
+
+@pytest.mark.parametrize("dtype,d", [(torch.float32, 32), (torch.bfloat16, 64), (torch.float32, 128)])
+def test_qk_norm_generic_path(kf, dtype, d):
+    out, normed = _qknorm_case(kf, 2, 300, 4, d, dtype, dtype if dtype == torch.float32 else torch.float32, 0, seed=d)
+    check_exact(out, normed, 4, d)
+
+
+def test_qk_norm_does_not_modify_qkv_and_matches_explicit_norm(kf):
+    """The fused form against normalising q and k first (this library's RMSNorm kernel) and
+    running the plain attention: the same up to last-bit differences of r."""
+    from kernelforge_b200.rmsnorm import rmsnorm_forward
+
+    g = torch.Generator().manual_seed(9)
+    b, n, h = 2, 777, 36
+    qkv = torch.randn(b, n, 3, h * 32, generator=g).to(torch.bfloat16).cuda()
+    qw = (0.5 + torch.rand(h * 32, generator=g)).to(torch.bfloat16).cuda()
+    kw = (0.5 + torch.rand(h * 32, generator=g)).to(torch.bfloat16).cuda()
+    before = qkv.clone()
+    run = kf.QKVAttnMatmul(b, h, 32, n, 1e-15, "bfloat16", "float")
+    fused = run.with_qk_norm(qkv, qw, kw, 1e-5)
+    assert torch.equal(qkv, before)
+    explicit = qkv.clone()
+    explicit[:, :, 0] = rmsnorm_forward(qkv[:, :, 0], qw, 1e-5)
+    explicit[:, :, 1] = rmsnorm_forward(qkv[:, :, 1], kw, 1e-5)
+    torch.testing.assert_close(fused, run(explicit), rtol=5e-3, atol=1e-4)
+    assert torch.equal(run.with_qk_norm(qkv, qw, kw, 1e-5), fused)  # deterministic
