@@ -206,6 +206,28 @@ int kf_linear_fwd(const void* x, const void* weight, const void* bias, void* y, 
                   int64_t in_features, int64_t out_features, int weight_layout, int dtype, void* stream);
 
 /* ------------------------------------------------------------------------------------------
+ * SANA linear attention fused with its QKV projection (heads of 32 channels, no qk_norm).
+ * Replaces the grouped kernels of GroupedFull64QOutLiteLA.grouped_attention
+ * (SANA_LinearAttention/custom.py:595-868: grouped_full64_kv_vk_producer and
+ * partial_reduce_joint_qout, which the reference writes for B=1, N=1024, C=1152 only), for any
+ * batch, seq_len and channels (a multiple of 32, at least 64):
+ *   qkv = x W^T (+ bias), rounded to dtype, as LiteLA.forward's self.qkv (original.py:122)
+ *   out = LiteLA.attn_matmul of that qkv (original.py:99-117), in dtype
+ * without writing q, k or v: a first launch projects K and V and accumulates each split's
+ * [K^T V ; sum relu(K)] into the workspace; a second projects Q and writes out.
+ * x: [batch, seq_len, channels]; qkv_weight: [3*channels, channels] (nn.Linear layout);
+ * qkv_bias: [3*channels] or NULL; out: [batch, seq_len, channels]; dtype bf16 (as the
+ * reference's grouped kernels; other dtypes return KF_ERR_UNSUPPORTED); x,
+ * qkv_weight, out and workspace 16-byte aligned. Size the workspace with
+ * kf_sana_proj_attn_workspace_size (fp32 partials; nothing needs zeroing). Deterministic.
+ * ---------------------------------------------------------------------------------------- */
+size_t kf_sana_proj_attn_workspace_size(int64_t batch, int64_t seq_len, int64_t channels);
+
+int kf_sana_proj_attn_fwd(const void* x, const void* qkv_weight, const void* qkv_bias, void* out,
+                          void* workspace, size_t workspace_bytes, int64_t batch, int64_t seq_len,
+                          int64_t channels, float eps, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------------------------
  * FlashAttention forward and forward-mode JVP.
  * Layout: q, tq, out, tangent_out [batch, q_len, q_heads, head_dim]; k, v, tk, tv
  * [batch, k_len, kv_heads, head_dim]; all contiguous, 16-byte aligned, `dtype` fp16 or bf16.

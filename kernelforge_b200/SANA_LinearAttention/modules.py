@@ -33,7 +33,7 @@ import torch
 
 from ..rmsnorm import RMSNorm
 from .custom import TORCH_DTYPES, QKVAttnMatmul
-from .projection import linear, linear_t
+from .projection import linear, linear_t, proj_attention
 
 __all__ = [
     "apply_rotary_emb",
@@ -246,8 +246,14 @@ GROUPED_SHAPE = dict(batch=1, seq_len=1024, channels=1152, heads=36, dim=32)
 
 class GroupedFull64QOutLiteLA(JointLiteLA):
     """The reference's fixed-shape specialisation (custom.py:812-862): B=1, N=1024, C=1152, H=36,
-    D=32, bf16, no qk_norm and no bias. Here it runs the same kernels as JointLiteLA (the one-launch
-    attention path needs no per-shape specialisation); the constructor keeps its shape contract."""
+    D=32, bf16, no qk_norm and no bias. Like the reference's grouped kernels, its attention never
+    writes q, k or v: the QKV projection and the attention run as two fused launches
+    (``projection.proj_attention``, ``kf_sana_proj_attn_fwd``, which are not tied to this shape),
+    then the bias-fused output projection. The constructor keeps the reference's shape contract."""
+
+    def grouped_attention(self, x: torch.Tensor) -> torch.Tensor:
+        """QKV projection + attention without materialising q, k, v (custom.py:851-853)."""
+        return proj_attention(x, self.qkv.weight, self.qkv.bias, self.eps)
 
     def __init__(self, *args, **kwargs):
         in_dim = args[0] if args else kwargs.get("in_dim")
@@ -266,7 +272,10 @@ class GroupedFull64QOutLiteLA(JointLiteLA):
     def forward(self, x, mask=None, HW=None, rotary_emb=None, block_id=None, block_mask=None):
         if rotary_emb is not None:
             raise ValueError("GroupedFull64QOutLiteLA requires rotary_emb=None")
-        return super().forward(x, mask, HW, None, block_id, block_mask)
+        self._validate_input(x)
+        if getattr(self, "fp32_attention", False):
+            return super().forward(x, mask, HW, None, block_id, block_mask)
+        return self._project_output(self.grouped_attention(x))
 
 
 def optimized_joint_litela(in_dim: int, out_dim: int, **kwargs):

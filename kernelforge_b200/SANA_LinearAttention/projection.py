@@ -57,3 +57,35 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
 def linear_t(x: torch.Tensor, weight_t: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
     """``x @ weight_t + bias`` for a prepacked ``weight_t [in, out]``."""
     return _project(x, weight_t.t(), bias)
+
+
+def proj_attention(x: torch.Tensor, qkv_weight: torch.Tensor, qkv_bias: torch.Tensor | None = None,
+                   eps: float = 1e-15) -> torch.Tensor:
+    """LiteLA's QKV projection and linear attention in two launches that never write q, k or v
+    (``kf_sana_proj_attn_fwd``): ``x [B, N, C]`` and the packed nn.Linear weight
+    ``qkv_weight [3C, C]`` (bias ``[3C]`` or None) -> the attention output ``[B, N, C]`` in x's
+    dtype, before the output projection. Heads of 32 channels; bf16 (as the reference's grouped
+    kernels)."""
+    _lib.require_cuda(x, "x")
+    if x.dim() != 3:
+        raise ValueError("x must be [batch, seq_len, channels]")
+    batch, seq_len, channels = x.shape
+    if tuple(qkv_weight.shape) != (3 * channels, channels) or qkv_weight.dtype != x.dtype:
+        raise ValueError(f"qkv_weight must be a [{3 * channels}, {channels}] tensor of x's dtype")
+    if qkv_bias is not None and (tuple(qkv_bias.shape) != (3 * channels,) or qkv_bias.dtype != x.dtype):
+        raise ValueError(f"qkv_bias must be a [{3 * channels}] tensor of x's dtype")
+    x = x.contiguous()
+    weight = qkv_weight.contiguous()
+    bias = None if qkv_bias is None else qkv_bias.contiguous()
+    ws_bytes = _lib.lib.kf_sana_proj_attn_workspace_size(batch, seq_len, channels)
+    if ws_bytes == 0:
+        raise ValueError("channels must be a positive multiple of 32")
+    workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
+    out = torch.empty_like(x)
+    with torch.cuda.device(x.device):
+        status = _lib.lib.kf_sana_proj_attn_fwd(x.data_ptr(), weight.data_ptr(), None if bias is None else bias.data_ptr(),
+                                                out.data_ptr(), workspace.data_ptr(), ws_bytes, batch, seq_len,
+                                                channels, float(eps), _lib.dtype_code(x.dtype),
+                                                _lib.stream_handle(x.device))
+    _lib.check(status, "kf_sana_proj_attn_fwd")
+    return out

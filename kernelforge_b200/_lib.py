@@ -51,6 +51,9 @@ SIGNATURES = {
                                             ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64)]),
     "kf_linear_fwd": (ctypes.c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, ctypes.c_int,
                                      ctypes.c_int, _c_ptr]),
+    "kf_sana_proj_attn_workspace_size": (ctypes.c_size_t, [_c_i64, _c_i64, _c_i64]),
+    "kf_sana_proj_attn_fwd": (ctypes.c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, ctypes.c_size_t, _c_i64, _c_i64,
+                                             _c_i64, ctypes.c_float, ctypes.c_int, _c_ptr]),
     "kf_fa_fwd": (ctypes.c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64,
                                  _c_i64, _c_i64, ctypes.c_float, ctypes.c_int, ctypes.c_int, _c_ptr]),
     "kf_fa_jvp": (ctypes.c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr,

@@ -214,10 +214,7 @@ fa_general_kernel(const FaArgs p) {
       for (int e = 0; e < 4; ++e) {
         lsum[e >> 1] += s[nt][e];
         if constexpr (kJvp) {
-          // H rounded to the operand dtype here, so that its row sum is that of the values
-          // the H V product consumes: tO = sum_j H_j (V_j - O) then holds exactly for the
-          // rounded H, and rows dominated by one key lose the rounding error with V_j - O.
-          ts[nt][e] = kf::Mma<T>::to_f2(kf::Mma<T>::from_f2(s[nt][e] * ts[nt][e] * p.scale, 0.f)).x;
+          ts[nt][e] = s[nt][e] * ts[nt][e] * p.scale;
           hsum[e >> 1] += ts[nt][e];
         }
       }

@@ -220,14 +220,6 @@ __device__ __forceinline__ void issue_scores(uint32_t q_addr, uint32_t tq_addr, 
 __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
   return bf16 ? kf::Mma<__nv_bfloat16>::from_f2(a, b) : kf::Mma<__half>::from_f2(a, b);
 }
-// A packed 16-bit pair back as an f32x2 pair. The row sum of H is taken over these rounded
-// values, the ones the H V MMA consumes, so that tO = sum_j H_j (V_j - O) holds exactly for the
-// rounded H: the rounding error of H is then multiplied by V_j - O, which vanishes on rows
-// dominated by one key (few visible keys: causal rows near the diagonal).
-__device__ __forceinline__ uint64_t unpack2(uint32_t v, bool bf16) {
-  const float2 f = bf16 ? kf::Mma<__nv_bfloat16>::to_f2(v) : kf::Mma<__half>::to_f2(v);
-  return kf::f2_pack(f.x, f.y);
-}
 
 // 2^x with the MUFU instruction (flushes subnormal results to zero; exp2(-inf) = 0).
 __device__ __forceinline__ float ex2(float x) {
@@ -390,10 +382,9 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         if (has_h) {
           const uint64_t hv = kf::f2_mul(
               kf::f2_mul(kf::f2_pack(p0, p1), kf::f2_pack(__uint_as_float(tr[2 * i]), __uint_as_float(tr[2 * i + 1]))), g2);
+          csum2 = kf::f2_add(csum2, hv);
           const float2 hf = kf::f2_unpack(hv);
           hh[i] = pack2(hf.x, hf.y, kBf16);
-          // rowsum(H) of the rounded H that the output MMA consumes (see unpack2).
-          csum2 = kf::f2_add(csum2, unpack2(hh[i], kBf16));
         }
       }
       kf::tc::st_32x32b_x16(p_col, pp);
@@ -681,9 +672,9 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
           if (has_h) {
             const uint64_t hv =
                 kf::f2_mul(kf::f2_mul(e2, kf::f2_pack(__uint_as_float(tr[2 * i]), __uint_as_float(tr[2 * i + 1]))), g2);
+            r2 = kf::f2_add(r2, hv);
             const float2 hf = kf::f2_unpack(hv);
             hh[i] = pack2(hf.x, hf.y, kBf16);
-            r2 = kf::f2_add(r2, unpack2(hh[i], kBf16));
           }
         }
         kf::tc::st_32x32b_x16(s_col, pp);

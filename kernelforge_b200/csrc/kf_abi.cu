@@ -7,6 +7,7 @@ int kf_internal_sana_error(unsigned int* code);
 int kf_internal_fa_error(unsigned int* code);
 int kf_internal_fa_bwd_error(unsigned int* code);
 int kf_internal_linear_error(unsigned int* code);
+int kf_internal_proj_attn_error(unsigned int* code);
 
 KF_API const char* kf_status_string(int status) {
   switch (status) {
@@ -78,6 +79,10 @@ KF_API int kf_query_device_error(void* stream, int* code) {
   st = kf_internal_linear_error(&linear);
   if (st != KF_OK) return st;
   if (linear != 0 && *code == KF_OK) *code = static_cast<int>(linear);
+  unsigned int proj_attn = 0;
+  st = kf_internal_proj_attn_error(&proj_attn);
+  if (st != KF_OK) return st;
+  if (proj_attn != 0 && *code == KF_OK) *code = static_cast<int>(proj_attn);
   unsigned int self = 0;
   st = selftest_error(&self);
   if (st != KF_OK) return st;
