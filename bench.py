@@ -236,10 +236,11 @@ def time_region(step, steps, warmup, dist, dominant=None):
     torch.cuda.synchronize()
     dist.barrier()
     ms = dist.max(start.elapsed_time(end)) / steps
-    dom = None
-    if dominant:
-        dom = dist.max(sum(a.elapsed_time(b) for a, b in dominant) / len(dominant))
-    return ms, dom
+    # Every rank takes part in the max, also one without launches of its own (an idle rank of a
+    # split that gives it no work), so that all ranks issue the same collectives.
+    local = sum(a.elapsed_time(b) for a, b in dominant) / len(dominant) if dominant else 0.0
+    dom = dist.max(local)
+    return ms, (dom if dom > 0 else None)
 
 
 class LaunchTimer(list):
@@ -1483,8 +1484,26 @@ def main():
         if clocks:
             line["clocks"] = clocks
         line["workloads"] = workloads
+        line["summary"] = summarise(workload_name, head, workloads)
         print(json.dumps(line), flush=True)
     dist.close()
+
+
+def summarise(head_name, head, workloads):
+    """One short string per workload (value, roofline fraction, e2e, verification), kept as the
+    line's last key so that a reader holding only the end of a long line still sees every figure."""
+    out = {}
+    for name, w in [(head_name, head), *workloads.items()]:
+        roof = w.get("roofline") or {}
+        text = f"{w['value']:.1f} {w['unit']}"
+        if roof.get("frac") is not None:
+            text += f", frac {roof['frac']:.3f}"
+        e2e = w.get("e2e")
+        if e2e:
+            text += f", e2e {e2e['value']:.1f} {e2e['unit']}"
+        text += ", verified" if w.get("verify", {}).get("ok") else ", NOT verified"
+        out[name] = text
+    return out
 
 
 if __name__ == "__main__":

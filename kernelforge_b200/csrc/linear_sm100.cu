@@ -16,8 +16,11 @@
 //   warp 1      MMA issuer (one thread): four tcgen05.mma kind::f16 M128 N=BN K16 per stage into
 //               one of two tensor-memory accumulators, so the epilogue of tile i overlaps the
 //               main loop of tile i+1;
-//   warps 2-5   epilogue: each warp reads its 32 accumulator lanes (rows) with tcgen05.ld, adds
-//               the bias in fp32, rounds once to the output dtype and stores 16-byte vectors.
+//   warps 2-5   epilogue: each warp reads its 32 accumulator lanes (rows) with tcgen05.ld, 32
+//               columns at a time, adds the bias in fp32, rounds once to the output dtype, writes
+//               the 32 x 32 chunk to shared memory (64-byte swizzle, conflict-free) and stores it
+//               with one TMA store (double-buffered per warp; the TMA clips rows past M and
+//               columns past N). Per-thread row stores would touch 32 rows per instruction.
 // Every wait is bounded (kf::mbar_wait_or_abort): a timeout records KF_ERR_DEVICE_TIMEOUT in
 // g_linear_error, the roles leave their loops, the producer waits (bounded) for its copies in
 // flight, the MMA thread for its MMAs, and the tensor memory is freed.
@@ -47,7 +50,9 @@ struct LinearCfg {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kAccStride = BN <= 128 ? 128 : 256;  // accumulator b at column b * kAccStride
   static constexpr int kTmemCols = 2 * kAccStride;            // a power of two
-  static constexpr int kBarOffset = kStages * kStageBytes;
+  static constexpr int kOutOffset = kStages * kStageBytes;     // 4 warps x 2 buffers x 32 x 32 outputs
+  static constexpr int kOutChunkBytes = 32 * 32 * 2;
+  static constexpr int kBarOffset = kOutOffset + 4 * 2 * kOutChunkBytes;
   static constexpr int kSmemBytes = kBarOffset + 256 + 1024;  // barriers + 1024-byte alignment slack
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
@@ -59,7 +64,7 @@ __device__ __forceinline__ uint64_t dsw(uint32_t base, uint32_t off, uint32_t lb
 template <typename T, int BN, bool kWeightKN>
 __global__ void __launch_bounds__(kThreads, 1)
 linear_sm100_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-                    T* __restrict__ y, const T* __restrict__ bias, int M, int N, int K) {
+                    const __grid_constant__ CUtensorMap tm_y, const T* __restrict__ bias, int M, int N, int K) {
   using C = LinearCfg<BN>;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ uint8_t smem_raw[];
@@ -168,6 +173,11 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_const
     }
   } else {
     const int quarter = warp & 3;  // tensor-memory lanes [32 quarter, 32 quarter + 32)
+    uint8_t* out_stage = smem + C::kOutOffset + quarter * 2 * C::kOutChunkBytes;
+    // Row `lane` of a staged chunk is 64 bytes; 64-byte swizzle: 16-byte piece v sits at
+    // v ^ ((lane >> 1) & 3), so each quarter-warp phase of the 16-byte stores hits all 32 banks.
+    const uint32_t swz = (lane >> 1) & 3;
+    int chunks = 0;  // chunks this warp has stored (buffer chunks & 1)
     int local = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
       const int ab = local & 1;
@@ -176,9 +186,8 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_const
       if (!__all_sync(0xffffffffu, ok)) break;
       kf::tc::fence_after_sync();
       const int mt = t % m_tiles, nt = t / m_tiles;
-      const int row = mt * kBM + quarter * 32 + lane;
+      const int row0 = mt * kBM + quarter * 32;  // first row of this warp's chunks
       const uint32_t acc = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + ab * C::kAccStride;
-      T* yrow = y + static_cast<int64_t>(row) * N;
 #pragma unroll 1
       for (int cc = 0; cc < BN / 32; ++cc) {
         const int col0 = nt * BN + cc * 32;
@@ -186,37 +195,49 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_const
         uint32_t r[32];
         kf::tc::ld_32x32b_x32(acc + cc * 32, r);
         kf::tc::wait_ld();
-        if (row < M) {
+        if (row0 >= M) continue;  // warp-uniform: the whole chunk lies past the last row
+        uint8_t* st = out_stage + (chunks & 1) * C::kOutChunkBytes;
+        // The store issued from this buffer two chunks ago has finished reading it.
+        if (chunks >= 2 && lane == 0) kf::tma_store_wait_read1();
+        __syncwarp();
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            const int c = col0 + v * 8;
-            if (c >= N) break;  // N is a multiple of 8
-            float f[8];
+        for (int v = 0; v < 4; ++v) {
+          const int c = col0 + v * 8;
+          float f[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(r[v * 8 + e]);
-            if (bias != nullptr) {
-              const uint4 bv = *reinterpret_cast<const uint4*>(bias + c);
-              const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+          for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(r[v * 8 + e]);
+          if (bias != nullptr && c < N) {  // N is a multiple of 8
+            const uint4 bv = *reinterpret_cast<const uint4*>(bias + c);
+            const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float2 bf = kf::Mma<T>::to_f2(bw[e]);
-                f[2 * e] += bf.x;
-                f[2 * e + 1] += bf.y;
-              }
+            for (int e = 0; e < 4; ++e) {
+              const float2 bf = kf::Mma<T>::to_f2(bw[e]);
+              f[2 * e] += bf.x;
+              f[2 * e + 1] += bf.y;
             }
-            uint4 o;
-            o.x = kf::Mma<T>::from_f2(f[0], f[1]);
-            o.y = kf::Mma<T>::from_f2(f[2], f[3]);
-            o.z = kf::Mma<T>::from_f2(f[4], f[5]);
-            o.w = kf::Mma<T>::from_f2(f[6], f[7]);
-            *reinterpret_cast<uint4*>(yrow + c) = o;
           }
+          uint4 o;
+          o.x = kf::Mma<T>::from_f2(f[0], f[1]);
+          o.y = kf::Mma<T>::from_f2(f[2], f[3]);
+          o.z = kf::Mma<T>::from_f2(f[4], f[5]);
+          o.w = kf::Mma<T>::from_f2(f[6], f[7]);
+          *reinterpret_cast<uint4*>(st + lane * 64 + ((v ^ swz) << 4)) = o;
         }
+        kf::fence_proxy_async_smem();  // the TMA reads the chunk through the async proxy
+        __syncwarp();
+        if (lane == 0) {
+          kf::tma_store_2d(&tm_y, st, col0, row0);
+          kf::tma_store_commit();
+        }
+        ++chunks;
       }
       kf::tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) kf::mbar_arrive(&acc_empty[ab]);
     }
+    // Shared memory outlives the stores in flight, and they complete before the kernel ends.
+    if (lane == 0) kf::tma_store_wait_all0();
+    __syncwarp();
   }
   kf::tc::fence_before_sync();
   __syncthreads();
@@ -301,7 +322,13 @@ int launch_tc(const void* x, const void* w, const void* bias, void* y, int M, in
               cudaStream_t stream) {
   using C = LinearCfg<BN>;
   const CUtensorMapDataType type = kf_host::map_type(dtype);
-  CUtensorMap tm_x, tm_w;
+  CUtensorMap tm_x, tm_w, tm_y;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(M)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(N) * 2};
+    const uint32_t box[2] = {32, 32};
+    if (!kf_host::encode_tiled(&tm_y, type, 2, y, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B)) return KF_ERR_CUDA;
+  }
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
     const uint64_t strides[1] = {static_cast<uint64_t>(K) * 2};
@@ -324,8 +351,7 @@ int launch_tc(const void* x, const void* w, const void* bias, void* y, int M, in
   if (prep != KF_OK) return prep;
   const int64_t tiles = ((M + kBM - 1) / kBM) * static_cast<int64_t>((N + BN - 1) / BN);
   const int grid = static_cast<int>(std::min<int64_t>(tiles, kf_host::current_device_sms()));
-  kernel<<<grid, kThreads, C::kSmemBytes, stream>>>(tm_x, tm_w, static_cast<T*>(y), static_cast<const T*>(bias), M, N,
-                                                   K);
+  kernel<<<grid, kThreads, C::kSmemBytes, stream>>>(tm_x, tm_w, tm_y, static_cast<const T*>(bias), M, N, K);
   KF_LAUNCH_CHECK();
   return KF_OK;
 }
