@@ -18,9 +18,9 @@
 // barrier the other issues.
 // Double-buffered S / dS in tensor memory let the tensor core compute tile j+1's scores while
 // the softmax warps turn tile j into P and H. Per 64-key tile the MMA warp issues
-//   S  = Q K^T            (D/16 x M128 N64 K16, operands from shared memory)
-//   dS = tQ K^T + Q tK^T  (2 D/16 x M128 N64 K16)
-//   tO += P tV + H V      (2 x 4 x M128 N=D K16, A from tensor memory, B MN-major)
+//   [S | Q tK^T] = Q [K ; tK]^T   (D/16 x M128 N128 K16, operands from shared memory)
+//   dS += tQ K^T                   (D/16 x M128 N64 K16)
+//   tO += P tV + H V               (2 x 4 x M128 N=D K16, A from tensor memory, B MN-major)
 // All operand tiles arrive by TMA with 128-byte swizzle; every wait is a bounded mbarrier
 // wait that records KF_ERR_DEVICE_TIMEOUT in the module's error word and gives up.
 #include "fa_common.cuh"
@@ -44,18 +44,17 @@ constexpr uint32_t kAccCol = 0;
 constexpr uint32_t kBufCol = 128;  // S of buffer b at kBufCol + 128 b, dS 64 columns further
 constexpr float kLog2e = 1.4426950408889634f;
 
-// Shared-memory plan: Q, tQ once; a two-stage ring of {K, tK} (a stage is free again once the
-// tile's score MMAs complete) and a separate two-stage ring of {V, tV} (free once the tile's
-// output MMAs complete), so the next tile's K streams in while the current tile's V is in use.
-// With two stages, stage (j & 1) and score / output buffer (j & 1) coincide: the producer waits
-// on the same completion barriers as the softmax warps (s_full, pv_done) instead of on
-// separate "empty" barriers, which saves the MMA thread two commits per tile.
+// Shared-memory plan: Q, tQ once; a ring of {K, tK} stages (a stage is free again once the
+// tile's score MMAs complete: k_empty) and a separate ring of {V, tV} stages (free once the
+// tile's output MMAs complete: v_empty), so K and V tiles stream in ahead of their use (a TMA
+// load of a tile from L2 takes ~1000-1400 cycles, about one tile period). D = 64 has room for
+// four stages of each; D = 128 (32 KB stages next to 64 KB of Q and tQ) for two.
 template <int D> struct Cfg {
   static constexpr int kKB = D / 64;                    // 128-byte boxes along the head dim
   static constexpr int kQBytes = kKB * kBM * 128;       // Q or tQ
   static constexpr int kTileBytes = kKB * kBN * 128;    // K, tK, V or tV of one tile
-  static constexpr int kKStages = 2;
-  static constexpr int kVStages = 2;
+  static constexpr int kKStages = D == 64 ? 4 : 2;
+  static constexpr int kVStages = D == 64 ? 4 : 2;
   static constexpr int kKOffset = 2 * kQBytes;
   static constexpr int kVOffset = kKOffset + kKStages * 2 * kTileBytes;
   static constexpr int kBarOffset = kVOffset + kVStages * 2 * kTileBytes;
@@ -66,32 +65,42 @@ template <int D> struct Cfg {
 // Barriers, in shared memory after the operand tiles.
 template <int D> struct Bars {
   uint64_t* q_full;
-  uint64_t* k_full;   // [2]
-  uint64_t* v_full;   // [2]
-  uint64_t* s_full;   // [2] scores of tile j complete (also: K stage j & 1 free)
+  uint64_t* k_full;   // [kKStages] K / tK of the stage's tile landed (+ k_extra arrivals)
+  uint64_t* k_empty;  // [kKStages] the score MMAs of the stage's tile completed
+  uint64_t* v_full;   // [kVStages] V / tV of the stage's tile landed (+ v_extra arrivals)
+  uint64_t* v_empty;  // [kVStages] the output MMAs of the stage's tile completed
+  uint64_t* s_full;   // [2] scores of tile j complete
   uint64_t* p_full;   // [2] P / H of tile j written
-  uint64_t* pv_done;  // [2] output MMAs of tile j complete (also: V stage j & 1 free)
+  uint64_t* pv_done;  // [2] output MMAs of tile j complete
   uint64_t* acc_full;
   uint32_t* tmem_slot;
   __device__ explicit Bars(uint8_t* smem) {
     using C = Cfg<D>;
     q_full = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
     k_full = q_full + 1;
-    v_full = k_full + C::kKStages;
-    s_full = v_full + C::kVStages;
+    k_empty = k_full + C::kKStages;
+    v_full = k_empty + C::kKStages;
+    v_empty = v_full + C::kVStages;
+    s_full = v_empty + C::kVStages;
     p_full = s_full + 2;
     pv_done = p_full + 2;
     acc_full = pv_done + 2;
     tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
   }
   // k_extra / v_extra: arrivals besides the producer's that complete a K or V stage. The kernels
-  // fold "score buffer j & 1 free" into k_full and "P / H of tile j written" into v_full, so each
-  // MMA thread waits on one barrier per tile.
+  // fold "score buffer j & 1 free" into the k_full phase of tile j and "P / H of tile j written"
+  // into v_full, so each MMA thread waits on one barrier per tile.
   __device__ void init(int p_arrivals, int k_extra, int v_extra) const {
     using C = Cfg<D>;
     kf::mbar_init(q_full, 1);
-    for (int s = 0; s < C::kKStages; ++s) kf::mbar_init(&k_full[s], 1 + k_extra);
-    for (int s = 0; s < C::kVStages; ++s) kf::mbar_init(&v_full[s], 1 + v_extra);
+    for (int s = 0; s < C::kKStages; ++s) {
+      kf::mbar_init(&k_full[s], 1 + k_extra);
+      kf::mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < C::kVStages; ++s) {
+      kf::mbar_init(&v_full[s], 1 + v_extra);
+      kf::mbar_init(&v_empty[s], 1);
+    }
     for (int i = 0; i < 2; ++i) {
       kf::mbar_init(&s_full[i], 1);
       kf::mbar_init(&p_full[i], p_arrivals);
@@ -100,6 +109,11 @@ template <int D> struct Bars {
     kf::mbar_init(acc_full, 1);
   }
 };
+
+// A K stage holds the 128-byte boxes of K and tK interleaved, [K box 0 | tK box 0 | K box 1 |
+// tK box 1]: box kb of K and of tK together are the 128 rows of one N = 128 operand [K ; tK].
+constexpr int kKBox = kBN * 128;     // one 128-byte box of a K or tK tile
+constexpr int kKPair = 2 * kKBox;    // K box kb to K box kb + 1
 
 // TMA producer (one thread): Q, tQ, then K tiles one ahead of V tiles -- the order in which
 // the MMA warp consumes them -- each behind its ring's "empty" barrier.
@@ -119,20 +133,22 @@ __device__ void produce(const Bars<D>& bars, uint8_t* smem, const CUtensorMap* t
   const uint32_t k_bytes = C::kTileBytes * (has_tk ? 2 : 1);
   const uint32_t v_bytes = C::kTileBytes * ((need_v ? 1 : 0) + (has_tv ? 1 : 0));
   auto load_k = [&](int j) -> bool {
-    const int st = j & 1;  // stage j & 1 was last read by tile j-2's score MMAs
-    if (j >= 2 && !kf::mbar_wait_or_abort<true>(&bars.s_full[st], ((j >> 1) - 1) & 1, &g_fa_error, abort))
+    const int st = j % C::kKStages;  // last read by the score MMAs of tile j - kKStages
+    if (j >= C::kKStages &&
+        !kf::mbar_wait_or_abort<true>(&bars.k_empty[st], (j / C::kKStages - 1) & 1, &g_fa_error, abort))
       return false;
     uint8_t* base = smem + C::kKOffset + st * 2 * C::kTileBytes;
     kf::mbar_arrive_expect_tx(&bars.k_full[st], k_bytes);
-    for (int kb = 0; kb < C::kKB; ++kb) {
-      kf::tma_load_4d(base + kb * kBN * 128, tm_k, &bars.k_full[st], kb * 64, kvh, j * kBN, b);
-      if (has_tk) kf::tma_load_4d(base + C::kTileBytes + kb * kBN * 128, tm_tk, &bars.k_full[st], kb * 64, kvh, j * kBN, b);
+    for (int kb = 0; kb < C::kKB; ++kb) {  // boxes interleaved: K kb, tK kb (kKPair bytes apart)
+      kf::tma_load_4d(base + kb * kKPair, tm_k, &bars.k_full[st], kb * 64, kvh, j * kBN, b);
+      if (has_tk) kf::tma_load_4d(base + kb * kKPair + kKBox, tm_tk, &bars.k_full[st], kb * 64, kvh, j * kBN, b);
     }
     return true;
   };
   auto load_v = [&](int j) -> bool {
-    const int st = j & 1;  // stage j & 1 was last read by tile j-2's output MMAs
-    if (j >= 2 && !kf::mbar_wait_or_abort<true>(&bars.pv_done[st], ((j >> 1) - 1) & 1, &g_fa_error, abort))
+    const int st = j % C::kVStages;  // last read by the output MMAs of tile j - kVStages
+    if (j >= C::kVStages &&
+        !kf::mbar_wait_or_abort<true>(&bars.v_empty[st], (j / C::kVStages - 1) & 1, &g_fa_error, abort))
       return false;
     uint8_t* base = smem + C::kVOffset + st * 2 * C::kTileBytes;
     kf::mbar_arrive_expect_tx(&bars.v_full[st], v_bytes);
@@ -142,9 +158,12 @@ __device__ void produce(const Bars<D>& bars, uint8_t* smem, const CUtensorMap* t
     }
     return true;
   };
-  if (ntiles > 0 && !load_k(0)) return;
+  // K tiles run up to kKStages - 1 ahead of V tiles: the score MMAs of tile j+1 come before the
+  // output MMAs of tile j.
+  int kj = 0;
   for (int j = 0; j < ntiles; ++j) {
-    if (j + 1 < ntiles && !load_k(j + 1)) return;
+    for (; kj < ntiles && kj < j + C::kKStages; ++kj)
+      if (!load_k(kj)) return;
     if (!load_v(j)) return;
   }
 }
@@ -161,20 +180,20 @@ __device__ __forceinline__ void issue_s(uint32_t q_addr, uint32_t k_base, uint32
 #pragma unroll
   for (int k = 0; k < D / 16; ++k) {
     const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
-    const uint32_t koff = (k >> 2) * kBN * 128 + (k & 3) * 32;
+    const uint32_t koff = (k >> 2) * kKPair + (k & 3) * 32;
     kf::tc::mma_ss(s_col, dsw(q_addr, off, 16), dsw(k_base, koff, 16),
                    idS, k > 0);
   }
 }
 template <int D>
-__device__ __forceinline__ void issue_ds(uint32_t q_addr, uint32_t tq_addr, uint32_t k_base, int tile_bytes,
+__device__ __forceinline__ void issue_ds(uint32_t q_addr, uint32_t tq_addr, uint32_t k_base,
                                          uint32_t ts_col, uint32_t idS, bool has_tq, bool has_tk) {
   uint32_t started = 0;
   if (has_tq) {
 #pragma unroll
     for (int k = 0; k < D / 16; ++k) {
       const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
-      const uint32_t koff = (k >> 2) * kBN * 128 + (k & 3) * 32;
+      const uint32_t koff = (k >> 2) * kKPair + (k & 3) * 32;
       kf::tc::mma_ss(ts_col, dsw(tq_addr, off, 16),
                      dsw(k_base, koff, 16), idS, started);
       started = 1;
@@ -184,37 +203,43 @@ __device__ __forceinline__ void issue_ds(uint32_t q_addr, uint32_t tq_addr, uint
 #pragma unroll
     for (int k = 0; k < D / 16; ++k) {
       const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
-      const uint32_t koff = (k >> 2) * kBN * 128 + (k & 3) * 32;
+      const uint32_t koff = (k >> 2) * kKPair + kKBox + (k & 3) * 32;
       kf::tc::mma_ss(ts_col, dsw(q_addr, off, 16),
-                     dsw(k_base + tile_bytes, koff, 16), idS, started);
+                     dsw(k_base, koff, 16), idS, started);
       started = 1;
     }
   }
 }
 
-// S into s_col and dS into s_col + 64 for one key tile. For D = 64 the N = 64 MMAs use the
-// tensor core at 2/3 of its N = 128 rate, so [S | Q tK^T] = Q [K ; tK]^T is one N = 128 MMA
-// (K and tK are adjacent in the stage) and tQ K^T is added to its second half.
+// S into s_col and dS into s_col + 64 for one key tile. An N = 64 MMA with both operands in
+// shared memory reads 6 KB per K step against 8 KB for N = 128 in twice the tensor time, so it
+// is bound by shared-memory bandwidth at 2/3 of the tensor core's rate. With a tangent tK,
+// [S | Q tK^T] = Q [K ; tK]^T is one N = 128 MMA per K step (box kb of K and of tK are adjacent
+// in the stage) and tQ K^T is added to its second half.
 template <int D>
-__device__ __forceinline__ void issue_scores(uint32_t q_addr, uint32_t tq_addr, uint32_t k_base, int tile_bytes,
+__device__ __forceinline__ void issue_scores(uint32_t q_addr, uint32_t tq_addr, uint32_t k_base,
                                              uint32_t s_col, bool has_tq, bool has_tk, bool bf16) {
   const uint32_t idS = kf::tc::idesc_f16(bf16 ? 1 : 0, kBM, kBN, false, false);
-  if (D == 64 && has_tk) {
+  if (has_tk) {
     const uint32_t idS2 = kf::tc::idesc_f16(bf16 ? 1 : 0, kBM, 2 * kBN, false, false);
 #pragma unroll
-    for (int k = 0; k < D / 16; ++k)
-      kf::tc::mma_ss(s_col, dsw(q_addr, k * 32, 16), dsw(k_base, k * 32, 16),
-                     idS2, k > 0);
+    for (int k = 0; k < D / 16; ++k) {
+      const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
+      const uint32_t koff = (k >> 2) * kKPair + (k & 3) * 32;
+      kf::tc::mma_ss(s_col, dsw(q_addr, off, 16), dsw(k_base, koff, 16), idS2, k > 0);
+    }
     if (has_tq) {
 #pragma unroll
-      for (int k = 0; k < D / 16; ++k)
-        kf::tc::mma_ss(s_col + 64, dsw(tq_addr, k * 32, 16),
-                       dsw(k_base, k * 32, 16), idS, 1);
+      for (int k = 0; k < D / 16; ++k) {
+        const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
+        const uint32_t koff = (k >> 2) * kKPair + (k & 3) * 32;
+        kf::tc::mma_ss(s_col + 64, dsw(tq_addr, off, 16), dsw(k_base, koff, 16), idS, 1);
+      }
     }
     return;
   }
   issue_s<D>(q_addr, k_base, s_col, idS);
-  issue_ds<D>(q_addr, tq_addr, k_base, tile_bytes, s_col + 64, idS, has_tq, has_tk);
+  issue_ds<D>(q_addr, tq_addr, k_base, s_col + 64, idS, has_tq, has_tk);
 }
 
 __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
@@ -267,9 +292,10 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 
   if (threadIdx.x == 0) {
     // Each MMA thread waits on one barrier per tile (a probe costs ~200 cycles while the tensor
-    // cores read shared memory): k_full[j & 1] completes when K / tK of tile j have landed AND
-    // every softmax thread has read tile j-2's scores out of buffer j & 1; v_full[j & 1] when
-    // V / tV of tile j have landed AND every softmax thread has written tile j's P and H.
+    // cores read shared memory): the k_full phase of tile j completes when K / tK of tile j have
+    // landed AND every softmax thread has read tile j-2's scores out of buffer j & 1; the v_full
+    // phase of tile j when V / tV of tile j have landed AND every softmax thread has written
+    // tile j's P and H.
     bars.init(1, 2 * kBM, 2 * kBM);  // p_full is not used here
     // Buffers 0 and 1 start free: the softmax threads' share of tiles 0 and 1's k_full phases.
     *abort_flag = 0;
@@ -296,13 +322,15 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       const uint32_t q_addr = kf::smem_u32(smem), tq_addr = q_addr + C::kQBytes;
       bool ok = kf::mbar_wait_or_abort<true>(bars.q_full, 0, &g_fa_error, abort_flag);
       for (int j = 0; ok && j < ntiles; ++j) {
-        const int buf = j & 1;
-        if (!(ok = kf::mbar_wait_or_abort<true>(&bars.k_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag))) break;
+        const int buf = j & 1, st = j % C::kKStages;
+        if (!(ok = kf::mbar_wait_or_abort<true>(&bars.k_full[st], (j / C::kKStages) & 1, &g_fa_error, abort_flag)))
+          break;
         kf::tc::fence_after_sync();
-        const uint32_t k_base = kf::smem_u32(smem + C::kKOffset + buf * 2 * C::kTileBytes);
+        const uint32_t k_base = kf::smem_u32(smem + C::kKOffset + st * 2 * C::kTileBytes);
         const uint32_t s_col = tmem + kBufCol + 128 * buf;
-        issue_scores<D>(q_addr, tq_addr, k_base, C::kTileBytes, s_col, has_tq, has_tk, kBf16);
+        issue_scores<D>(q_addr, tq_addr, k_base, s_col, has_tq, has_tk, kBf16);
         kf::tc::commit(&bars.s_full[buf]);
+        kf::tc::commit(&bars.k_empty[st]);
       }
     }
   } else if (warp == kPvWarp) {
@@ -313,10 +341,11 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       uint32_t acc_started = 0;
       bool ok = true;
       for (int j = 0; ok && j < ntiles; ++j) {
-        const int buf = j & 1;
-        if (!(ok = kf::mbar_wait_or_abort<true>(&bars.v_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag))) break;
+        const int buf = j & 1, st = j % C::kVStages;
+        if (!(ok = kf::mbar_wait_or_abort<true>(&bars.v_full[st], (j / C::kVStages) & 1, &g_fa_error, abort_flag)))
+          break;
         kf::tc::fence_after_sync();
-        const uint32_t v_base = kf::smem_u32(smem + C::kVOffset + buf * 2 * C::kTileBytes);
+        const uint32_t v_base = kf::smem_u32(smem + C::kVOffset + st * 2 * C::kTileBytes);
         const uint32_t p_col = tmem + kPCol + 64 * buf;
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
@@ -332,6 +361,7 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
           }
         }
         kf::tc::commit(&bars.pv_done[buf]);
+        kf::tc::commit(&bars.v_empty[st]);
       }
       kf::tc::commit(bars.acc_full);
     }
@@ -366,9 +396,10 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       kf::tc::ld_32x32b_x32(s_col, sr);
       if (has_h) kf::tc::ld_32x32b_x32(s_col + 64, tr);
       kf::tc::wait_ld();
-      // This thread's share of buffer j & 1 is read: tile j+2's scores may go there.
+      // This thread's share of buffer j & 1 is read: tile j+2's scores may go there (its share
+      // of the k_full phase of tile j+2).
       kf::tc::fence_before_sync();
-      kf::mbar_arrive(&bars.k_full[buf]);
+      kf::mbar_arrive(&bars.k_full[(j + 2) % C::kKStages]);
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const float2 a = kf::f2_unpack(kf::f2_fma(kf::f2_pack(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])),
@@ -391,7 +422,7 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       if (has_h) kf::tc::st_32x32b_x16(p_col + 32, hh);
       kf::tc::wait_st();
       kf::tc::fence_before_sync();
-      kf::mbar_arrive(&bars.v_full[buf]);
+      kf::mbar_arrive(&bars.v_full[j % C::kVStages]);
     }
     const float2 cs = kf::f2_unpack(csum2);
     row_sums[group * kBM + row] = cs.x + cs.y;
@@ -454,10 +485,10 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 //   D = 64:  [0, 64) U | [64, 128) G | [128, 384) S / dS double buffer
 // P and H (16-bit) overwrite the first 16 columns of each warpgroup's 32-column S / dS half, so
 // tile j's score MMAs wait for tile j-2's output MMAs (same buffer).
-// For D = 64 the N = 64 MMAs use the tensor core at 2/3 of its N = 128 rate, so pairs are
-// merged into N = 128 MMAs: [S | Q tK^T] = Q [K ; tK]^T (K and tK are adjacent in the stage)
-// then dS += tQ K^T; and [U | G] += E [V | tV] (V, tV adjacent: two 64-wide MN blocks) then
-// G += H V. That takes U at [0, 64) and G at [64, 128), next to each other.
+// The scores are issued as in the standalone kernel ([S | Q tK^T] = Q [K ; tK]^T, then
+// dS += tQ K^T). For D = 64 the output MMAs are merged the same way, since an N = 64 MMA runs at
+// 2/3 of the tensor core's rate: [U | G] += E [V | tV] (V, tV adjacent: two 64-wide MN blocks)
+// then G += H V. That takes U at [0, 64) and G at [64, 128), next to each other.
 // ============================================================================================
 template <int D>
 struct FusedCols {
@@ -494,10 +525,10 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
   const int ntiles = (k_end + kBN - 1) / kBN;
 
   if (threadIdx.x == 0) {
-    // k_full[j & 1] completes when K / tK of tile j have landed AND tile j-2's output MMAs (which
-    // read the P / H written over score buffer j & 1) are done: the output thread commits to it.
-    // v_full[j & 1] completes when V / tV of tile j have landed AND every softmax thread has
-    // written tile j's P and H. p_full is not used here.
+    // The k_full phase of tile j completes when K / tK of tile j have landed AND tile j-2's output
+    // MMAs (which read the P / H written over score buffer j & 1) are done: the output thread
+    // commits to it. The v_full phase of tile j completes when V / tV of tile j have landed AND
+    // every softmax thread has written tile j's P and H. p_full is not used here.
     bars.init(1, 1, 2 * kBM);
     *abort_flag = 0;
     kf::fence_mbar_init();
@@ -519,13 +550,15 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       const uint32_t q_addr = kf::smem_u32(smem), tq_addr = q_addr + C::kQBytes;
       bool ok = kf::mbar_wait_or_abort<true>(bars.q_full, 0, &g_fa_error, abort_flag);
       for (int j = 0; ok && j < ntiles; ++j) {
-        const int buf = j & 1;
-        if (!(ok = kf::mbar_wait_or_abort<true>(&bars.k_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag))) break;
+        const int buf = j & 1, st = j % C::kKStages;
+        if (!(ok = kf::mbar_wait_or_abort<true>(&bars.k_full[st], (j / C::kKStages) & 1, &g_fa_error, abort_flag)))
+          break;
         kf::tc::fence_after_sync();
-        const uint32_t k_base = kf::smem_u32(smem + C::kKOffset + buf * 2 * C::kTileBytes);
+        const uint32_t k_base = kf::smem_u32(smem + C::kKOffset + st * 2 * C::kTileBytes);
         const uint32_t s_col = tmem + kBufCol + 128 * buf;
-        issue_scores<D>(q_addr, tq_addr, k_base, C::kTileBytes, s_col, has_tq, has_tk, kBf16);
+        issue_scores<D>(q_addr, tq_addr, k_base, s_col, has_tq, has_tk, kBf16);
         kf::tc::commit(&bars.s_full[buf]);
+        kf::tc::commit(&bars.k_empty[st]);
       }
     }
   } else if (warp == kPvWarp) {
@@ -539,10 +572,11 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       kf::mbar_arrive(&bars.k_full[0]);
       kf::mbar_arrive(&bars.k_full[1]);
       for (int j = 0; ok && j < ntiles; ++j) {
-        const int buf = j & 1;
-        if (!(ok = kf::mbar_wait_or_abort<true>(&bars.v_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag))) break;
+        const int buf = j & 1, st = j % C::kVStages;
+        if (!(ok = kf::mbar_wait_or_abort<true>(&bars.v_full[st], (j / C::kVStages) & 1, &g_fa_error, abort_flag)))
+          break;
         kf::tc::fence_after_sync();
-        const uint32_t v_base = kf::smem_u32(smem + C::kVOffset + buf * 2 * C::kTileBytes);
+        const uint32_t v_base = kf::smem_u32(smem + C::kVOffset + st * 2 * C::kTileBytes);
         const uint32_t p_col = tmem + kBufCol + 128 * buf;
         const uint32_t h_col = p_col + 64;
 #pragma unroll
@@ -571,7 +605,8 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
           }
         }
         kf::tc::commit(&bars.pv_done[buf]);
-        kf::tc::commit(&bars.k_full[buf]);  // score buffer j & 1 is free for tile j+2
+        kf::tc::commit(&bars.v_empty[st]);
+        kf::tc::commit(&bars.k_full[(j + 2) % C::kKStages]);  // score buffer j & 1 is free for tile j+2
       }
       kf::tc::commit(bars.acc_full);
     }
@@ -682,7 +717,7 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         kf::tc::wait_st();
       }
       kf::tc::fence_before_sync();
-      kf::mbar_arrive(&bars.v_full[buf]);
+      kf::mbar_arrive(&bars.v_full[j % C::kVStages]);
     }
     // Combine the two warpgroups' row sums.
     const float2 lf = kf::f2_unpack(l2), rf = kf::f2_unpack(r2);
