@@ -23,6 +23,7 @@
 #include "kf_sm100.cuh"
 #include "kf_tcgen05.cuh"
 
+#include <climits>
 #include <type_traits>
 
 namespace {
@@ -276,7 +277,9 @@ struct QoutCfg {
   static constexpr int kBBytes = kGC * kKB * 2;      // 16 KB
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kBImgOff = kStages * kStageBytes;
-  static constexpr int kBarOff = kBImgOff + kGroup * kBImage;
+  static constexpr int kOutOff = kBImgOff + kGroup * kBImage;  // 4 warps x 2 buffers x 32 x 32 outputs
+  static constexpr int kOutChunk = 32 * kHd * 2;
+  static constexpr int kBarOff = kOutOff + 4 * 2 * kOutChunk;
   static constexpr int kSmemBytes = kBarOff + 256 + 1024;
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
@@ -287,8 +290,8 @@ __device__ __forceinline__ uint32_t qo_slot(int h) { return 256u + 64u * h; }
 template <typename T>
 __global__ void __launch_bounds__(kPT, 1)
 sana_proj_qout(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-               const T* __restrict__ qkv_bias, const float* __restrict__ partial, T* __restrict__ out, int N, int C,
-               int H, int S, int tiles_per_cta, float eps) {
+               const __grid_constant__ CUtensorMap tm_out, const T* __restrict__ qkv_bias,
+               const float* __restrict__ partial, int N, int C, int H, int S, int tiles_per_cta, float eps) {
   using Cf = QoutCfg;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (kf::smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -431,11 +434,16 @@ sana_proj_qout(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     const uint32_t lanes = static_cast<uint32_t>(quarter * 32) << 16;
     bool ok = true;
     int local = 0;
-    // out of tile j: D / (D[:, 32] + eps) for the group's heads; this thread's token row.
+    // out of tile j: D / (D[:, 32] + eps) for the group's heads. Each warp's 32 tokens x 32
+    // channels of a head go through shared memory (64-byte swizzle: 16-byte piece v of row r at
+    // v ^ ((r >> 1) & 3)) into one TMA store, which clips tokens past N.
+    uint8_t* out_stage = smem + Cf::kOutOff + quarter * 2 * Cf::kOutChunk;
+    const uint32_t swz = (lane >> 1) & 3;
+    int chunks = 0;
     auto store_out = [&](int j) -> bool {
       if (!__all_sync(0xffffffffu, kf::mbar_wait_or_abort(d_full, j & 1, &g_proj_attn_error, abort_flag))) return false;
       kf::tc::fence_after_sync();
-      const int tok = (t_begin + j) * kTokT + row;
+      const int tok0 = (t_begin + j) * kTokT + quarter * 32;
 #pragma unroll 1
       for (int hh = 0; hh < kGroup; ++hh) {
         uint32_t dr[32], den[2];
@@ -443,19 +451,28 @@ sana_proj_qout(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         kf::tc::ld_32x32b_x2(tmem + lanes + qo_slot(hh) + 32, den);
         kf::tc::wait_ld();
         const int h = grp * kGroup + hh;
-        if (tok < N && h < H) {
-          const float inv = __frcp_rn(__uint_as_float(den[0]) + eps);
-          T* dst = out + (static_cast<int64_t>(b) * N + tok) * C + h * kHd;
+        if (h >= H || tok0 >= N) continue;  // warp-uniform
+        uint8_t* st = out_stage + (chunks & 1) * Cf::kOutChunk;
+        // The store issued from this buffer two chunks ago has finished reading it.
+        if (chunks >= 2 && lane == 0) kf::tma_store_wait_read1();
+        __syncwarp();
+        const float inv = __frcp_rn(__uint_as_float(den[0]) + eps);
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            uint4 o;
-            o.x = kf::Mma<T>::from_f2(__uint_as_float(dr[8 * v]) * inv, __uint_as_float(dr[8 * v + 1]) * inv);
-            o.y = kf::Mma<T>::from_f2(__uint_as_float(dr[8 * v + 2]) * inv, __uint_as_float(dr[8 * v + 3]) * inv);
-            o.z = kf::Mma<T>::from_f2(__uint_as_float(dr[8 * v + 4]) * inv, __uint_as_float(dr[8 * v + 5]) * inv);
-            o.w = kf::Mma<T>::from_f2(__uint_as_float(dr[8 * v + 6]) * inv, __uint_as_float(dr[8 * v + 7]) * inv);
-            *reinterpret_cast<uint4*>(dst + 8 * v) = o;
-          }
+        for (int v = 0; v < 4; ++v) {
+          uint4 o;
+          o.x = kf::Mma<T>::from_f2(__uint_as_float(dr[8 * v]) * inv, __uint_as_float(dr[8 * v + 1]) * inv);
+          o.y = kf::Mma<T>::from_f2(__uint_as_float(dr[8 * v + 2]) * inv, __uint_as_float(dr[8 * v + 3]) * inv);
+          o.z = kf::Mma<T>::from_f2(__uint_as_float(dr[8 * v + 4]) * inv, __uint_as_float(dr[8 * v + 5]) * inv);
+          o.w = kf::Mma<T>::from_f2(__uint_as_float(dr[8 * v + 6]) * inv, __uint_as_float(dr[8 * v + 7]) * inv);
+          *reinterpret_cast<uint4*>(st + lane * 64 + ((v ^ swz) << 4)) = o;
         }
+        kf::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          kf::tma_store_3d(&tm_out, st, h * kHd, tok0, b);
+          kf::tma_store_commit();
+        }
+        ++chunks;
       }
       return true;
     };
@@ -495,6 +512,9 @@ sana_proj_qout(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
       }
     }
     if (ok && local > 0) (void)store_out(local - 1);
+    // Shared memory outlives the stores in flight, and they complete before the kernel ends.
+    if (lane == 0) kf::tma_store_wait_all0();
+    __syncwarp();
   }
   kf::tc::fence_before_sync();
   __syncthreads();
@@ -519,18 +539,28 @@ int kf_internal_proj_attn_error(unsigned int* code) {
 
 namespace {
 
-// Token splits of kernel 1: about two CTAs per SM over (batch, head group) units; each split
-// covers whole 128-token tiles.
+// Token splits of kernel 1 (each split covers whole 128-token tiles). One CTA fits per SM, so
+// the kernel takes waves x tiles-per-split tile times: the split count minimising that, the
+// smallest on ties (fewer partials). B = 2, C = 2240 (36 units of 128 tiles): 4 splits, one
+// wave of 144 CTAs and 32 tiles each; 5 splits would take two waves of 26.
 int kv_splits(int64_t B, int64_t G, int64_t ntiles) {
   const int64_t units = B * G;
-  const int64_t target = static_cast<int64_t>(kf_host::current_device_sms());
-  int64_t s = (target + units - 1) / units;
-  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(s, ntiles)));
+  const int64_t sms = static_cast<int64_t>(kf_host::current_device_sms());
+  int64_t best = 1, best_cost = INT64_MAX;
+  for (int64_t s = 1; s <= ntiles && s <= 4 * sms; ++s) {
+    const int64_t waves = (units * s + sms - 1) / sms;
+    const int64_t cost = waves * ((ntiles + s - 1) / s);
+    if (cost < best_cost) {
+      best = s;
+      best_cost = cost;
+    }
+  }
+  return static_cast<int>(best);
 }
 
 template <typename T>
-int launch_proj_attn(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const void* qkv_bias, float* partial,
-                     void* out, int B, int N, int C, float eps, cudaStream_t s) {
+int launch_proj_attn(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const CUtensorMap& tm_out, const void* qkv_bias,
+                     float* partial, int B, int N, int C, float eps, cudaStream_t s) {
   const int H = C / kHd, G = (H + kGroup - 1) / kGroup, ntiles = (N + kTokT - 1) / kTokT;
   const int S = kv_splits(B, G, ntiles);
   const int tps = (ntiles + S - 1) / S;
@@ -551,8 +581,8 @@ int launch_proj_attn(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const voi
     const int64_t sms = kf_host::current_device_sms();
     const int tpc = static_cast<int>(std::min<int64_t>(ntiles, std::max<int64_t>(1, (items + sms - 1) / sms)));
     const int splits2 = (ntiles + tpc - 1) / tpc;
-    k2<<<dim3(splits2, G, B), kPT, QoutCfg::kSmemBytes, s>>>(tm_x, tm_w, bias, partial, static_cast<T*>(out), N, C,
-                                                             H, S, tpc, eps);
+    k2<<<dim3(splits2, G, B), kPT, QoutCfg::kSmemBytes, s>>>(tm_x, tm_w, tm_out, bias, partial, N, C, H, S, tpc,
+                                                             eps);
     KF_LAUNCH_CHECK();
   }
   return KF_OK;
@@ -587,7 +617,14 @@ KF_API int kf_sana_proj_attn_fwd(const void* x, const void* qkv_weight, const vo
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const CUtensorMapDataType type = kf_host::map_type(dtype);
   // x [B, N, C] as (channel, token, batch, 1): boxes of 64 channels x 128 tokens, zero past N.
-  CUtensorMap tm_x, tm_w;
+  CUtensorMap tm_x, tm_w, tm_out;
+  {
+    // out [B, N, C] as (channel, token, batch): stores of 32 channels (one head) x 32 tokens.
+    const uint64_t dims[3] = {static_cast<uint64_t>(C), static_cast<uint64_t>(N), static_cast<uint64_t>(B)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(C) * 2, static_cast<uint64_t>(N) * C * 2};
+    const uint32_t box[3] = {kHd, 32, 1};
+    if (!kf_host::encode_tiled(&tm_out, type, 3, out, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B)) return KF_ERR_CUDA;
+  }
   {
     const uint64_t dims[4] = {static_cast<uint64_t>(C), static_cast<uint64_t>(N), static_cast<uint64_t>(B), 1};
     const uint64_t strides[3] = {static_cast<uint64_t>(C) * 2, static_cast<uint64_t>(N) * C * 2,
@@ -604,5 +641,5 @@ KF_API int kf_sana_proj_attn_fwd(const void* x, const void* qkv_weight, const vo
       return KF_ERR_CUDA;
   }
   float* partial = static_cast<float*>(workspace);
-  return launch_proj_attn<__nv_bfloat16>(tm_x, tm_w, qkv_bias, partial, out, B, N, C, eps, s);
+  return launch_proj_attn<__nv_bfloat16>(tm_x, tm_w, tm_out, qkv_bias, partial, B, N, C, eps, s);
 }
