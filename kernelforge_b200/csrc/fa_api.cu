@@ -93,6 +93,15 @@ KF_API int kf_fa_fwd_jvp(const void* q, const void* k, const void* v, const void
   a.to_out = tangent_out;
   if (kf::fa::sm100_fused_supported(a, kf::fa::kModeFwdJvp))
     return kf::fa::launch_sm100_fused(a, kf::fa::kModeFwdJvp, dtype, static_cast<cudaStream_t>(stream));
+  if (kf::fa::sm100_fused_supported(a, kf::fa::kModeFwd) && kf::fa::sm100_jvp_supported(a)) {
+    // Head dims 136..256: tensor memory holds one D = 256 accumulator, not O and tO together, so
+    // the forward (O, LSE) runs first and the standalone JVP reads them back.
+    st = kf::fa::launch_sm100_fused(a, kf::fa::kModeFwd, dtype, static_cast<cudaStream_t>(stream));
+    if (st != KF_OK) return st;
+    a.o_in = out;
+    a.lse_in = lse;
+    return kf::fa::launch_sm100_jvp(a, dtype, static_cast<cudaStream_t>(stream));
+  }
   return kf::fa::launch_general(a, kf::fa::kModeFwdJvp, dtype, static_cast<cudaStream_t>(stream));
 }
 

@@ -41,7 +41,6 @@ constexpr int kMmaWarp = 9;     // TMEM owner; issues the score MMAs
 constexpr int kPvWarp = 10;     // issues the output MMAs
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAccCol = 0;
-constexpr uint32_t kBufCol = 128;  // S of buffer b at kBufCol + 128 b, dS 64 columns further
 constexpr float kLog2e = 1.4426950408889634f;
 
 // Shared-memory plan: Q, tQ once; a ring of {K, tK} stages (a stage is free again once the
@@ -49,21 +48,37 @@ constexpr float kLog2e = 1.4426950408889634f;
 // tile's output MMAs complete: v_empty), so K and V tiles stream in ahead of their use (a TMA
 // load of a tile from L2 takes ~1000-1400 cycles, about one tile period). D = 64 has room for
 // four stages of each; D = 128 (32 KB stages next to 64 KB of Q and tQ) for two.
-template <int D> struct Cfg {
+// kTan: room for the tangents tQ, tK, tV next to Q, K, V (the forward alone has none, which
+// leaves room for D = 256: 64 KB of Q and two stages of 32 KB K and V tiles). BN: keys per tile.
+// The standalone JVP at D = 256 (128 KB of Q and tQ) takes 32-key tiles, two K stages and one V
+// stage: 224 KB.
+template <int D, bool kTan = true, int BN = kBN> struct Cfg {
+  static constexpr int kKeys = BN;
   static constexpr int kKB = D / 64;                    // 128-byte boxes along the head dim
   static constexpr int kQBytes = kKB * kBM * 128;       // Q or tQ
-  static constexpr int kTileBytes = kKB * kBN * 128;    // K, tK, V or tV of one tile
+  static constexpr int kTileBytes = kKB * BN * 128;     // K, tK, V or tV of one tile
+  static constexpr int kKBox = BN * 128;                // one 128-byte box of a K or tK tile
+  // A K stage holds the boxes of K and tK interleaved, [K box 0 | tK box 0 | K box 1 | ...]:
+  // box kb of K and of tK together are the 128 rows of one N = 128 operand [K ; tK].
+  static constexpr int kKPair = kTan ? 2 * kKBox : kKBox;  // K box kb to K box kb + 1
+  static constexpr int kStageBytes = kTan ? 2 * kTileBytes : kTileBytes;  // {K, tK} or {V, tV}
   static constexpr int kKStages = D == 64 ? 4 : 2;
-  static constexpr int kVStages = D == 64 ? 4 : 2;
-  static constexpr int kKOffset = 2 * kQBytes;
-  static constexpr int kVOffset = kKOffset + kKStages * 2 * kTileBytes;
-  static constexpr int kBarOffset = kVOffset + kVStages * 2 * kTileBytes;
-  static constexpr int kScratchOffset = kBarOffset + 512;                 // row statistics
-  static constexpr int kSmemBytes = kScratchOffset + 6 * kBM * 4 + 64 + 1024;  // + abort flag, slack
+  static constexpr int kVStages = D == 64 ? 4 : (D == 256 && kTan ? 1 : 2);
+  static constexpr int kKOffset = kTan ? 2 * kQBytes : kQBytes;
+  static constexpr int kVOffset = kKOffset + kKStages * kStageBytes;
+  static constexpr int kBarOffset = kVOffset + kVStages * kStageBytes;
+  // Tensor memory: S of score buffer b at kBufCol + 128 b, dS 64 columns further; the
+  // accumulators below kBufCol.
+  static constexpr uint32_t kBufCol = D <= 128 ? 128 : 256;
+  static constexpr int kScratchOffset = kBarOffset + 512;  // row statistics
+  // [2][kBM] row sums (standalone JVP) or [6][kBM] maxima and sums (one-pass kernel)
+  static constexpr int kScratchBytes = (D == 256 && kTan ? 2 : 6) * kBM * 4;
+  static constexpr int kSmemBytes = kScratchOffset + kScratchBytes + 64 + 1024;  // + abort flag, slack
+  static_assert(kSmemBytes <= 232448, "shared memory");
 };
 
 // Barriers, in shared memory after the operand tiles.
-template <int D> struct Bars {
+template <int D, bool kTan = true, int BN = kBN> struct Bars {
   uint64_t* q_full;
   uint64_t* k_full;   // [kKStages] K / tK of the stage's tile landed (+ k_extra arrivals)
   uint64_t* k_empty;  // [kKStages] the score MMAs of the stage's tile completed
@@ -75,7 +90,7 @@ template <int D> struct Bars {
   uint64_t* acc_full;
   uint32_t* tmem_slot;
   __device__ explicit Bars(uint8_t* smem) {
-    using C = Cfg<D>;
+    using C = Cfg<D, kTan, BN>;
     q_full = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
     k_full = q_full + 1;
     k_empty = k_full + C::kKStages;
@@ -91,7 +106,7 @@ template <int D> struct Bars {
   // fold "score buffer j & 1 free" into the k_full phase of tile j and "P / H of tile j written"
   // into v_full, so each MMA thread waits on one barrier per tile.
   __device__ void init(int p_arrivals, int k_extra, int v_extra) const {
-    using C = Cfg<D>;
+    using C = Cfg<D, kTan, BN>;
     kf::mbar_init(q_full, 1);
     for (int s = 0; s < C::kKStages; ++s) {
       kf::mbar_init(&k_full[s], 1 + k_extra);
@@ -110,19 +125,14 @@ template <int D> struct Bars {
   }
 };
 
-// A K stage holds the 128-byte boxes of K and tK interleaved, [K box 0 | tK box 0 | K box 1 |
-// tK box 1]: box kb of K and of tK together are the 128 rows of one N = 128 operand [K ; tK].
-constexpr int kKBox = kBN * 128;     // one 128-byte box of a K or tK tile
-constexpr int kKPair = 2 * kKBox;    // K box kb to K box kb + 1
-
 // TMA producer (one thread): Q, tQ, then K tiles one ahead of V tiles -- the order in which
 // the MMA warp consumes them -- each behind its ring's "empty" barrier.
-template <int D>
-__device__ void produce(const Bars<D>& bars, uint8_t* smem, const CUtensorMap* tm_q, const CUtensorMap* tm_tq,
+template <int D, bool kTan, int BN>
+__device__ void produce(const Bars<D, kTan, BN>& bars, uint8_t* smem, const CUtensorMap* tm_q, const CUtensorMap* tm_tq,
                         const CUtensorMap* tm_k, const CUtensorMap* tm_tk, const CUtensorMap* tm_v,
                         const CUtensorMap* tm_tv, bool has_tq, bool has_tk, bool need_v, bool has_tv,
                         int h, int kvh, int q0, int b, int ntiles, volatile int* abort) {
-  using C = Cfg<D>;
+  using C = Cfg<D, kTan, BN>;
   kf::prefetch_tensormap(tm_q);
   kf::prefetch_tensormap(tm_k);
   kf::mbar_arrive_expect_tx(bars.q_full, C::kQBytes * (has_tq ? 2 : 1));
@@ -137,11 +147,11 @@ __device__ void produce(const Bars<D>& bars, uint8_t* smem, const CUtensorMap* t
     if (j >= C::kKStages &&
         !kf::mbar_wait_or_abort<true>(&bars.k_empty[st], (j / C::kKStages - 1) & 1, &g_fa_error, abort))
       return false;
-    uint8_t* base = smem + C::kKOffset + st * 2 * C::kTileBytes;
+    uint8_t* base = smem + C::kKOffset + st * C::kStageBytes;
     kf::mbar_arrive_expect_tx(&bars.k_full[st], k_bytes);
     for (int kb = 0; kb < C::kKB; ++kb) {  // boxes interleaved: K kb, tK kb (kKPair bytes apart)
-      kf::tma_load_4d(base + kb * kKPair, tm_k, &bars.k_full[st], kb * 64, kvh, j * kBN, b);
-      if (has_tk) kf::tma_load_4d(base + kb * kKPair + kKBox, tm_tk, &bars.k_full[st], kb * 64, kvh, j * kBN, b);
+      kf::tma_load_4d(base + kb * C::kKPair, tm_k, &bars.k_full[st], kb * 64, kvh, j * BN, b);
+      if (has_tk) kf::tma_load_4d(base + kb * C::kKPair + C::kKBox, tm_tk, &bars.k_full[st], kb * 64, kvh, j * BN, b);
     }
     return true;
   };
@@ -150,11 +160,11 @@ __device__ void produce(const Bars<D>& bars, uint8_t* smem, const CUtensorMap* t
     if (j >= C::kVStages &&
         !kf::mbar_wait_or_abort<true>(&bars.v_empty[st], (j / C::kVStages - 1) & 1, &g_fa_error, abort))
       return false;
-    uint8_t* base = smem + C::kVOffset + st * 2 * C::kTileBytes;
+    uint8_t* base = smem + C::kVOffset + st * C::kStageBytes;
     kf::mbar_arrive_expect_tx(&bars.v_full[st], v_bytes);
     for (int kb = 0; kb < C::kKB; ++kb) {
-      if (need_v) kf::tma_load_4d(base + kb * kBN * 128, tm_v, &bars.v_full[st], kb * 64, kvh, j * kBN, b);
-      if (has_tv) kf::tma_load_4d(base + C::kTileBytes + kb * kBN * 128, tm_tv, &bars.v_full[st], kb * 64, kvh, j * kBN, b);
+      if (need_v) kf::tma_load_4d(base + kb * C::kKBox, tm_v, &bars.v_full[st], kb * 64, kvh, j * BN, b);
+      if (has_tv) kf::tma_load_4d(base + C::kTileBytes + kb * C::kKBox, tm_tv, &bars.v_full[st], kb * 64, kvh, j * BN, b);
     }
     return true;
   };
@@ -175,7 +185,7 @@ __device__ __forceinline__ uint64_t dsw(uint32_t base, uint32_t off, uint32_t lb
 }
 
 // Score MMAs of tile j: S = Q K^T into s_col, then dS = tQ K^T + Q tK^T into ts_col.
-template <int D>
+template <int D, int kKPair>
 __device__ __forceinline__ void issue_s(uint32_t q_addr, uint32_t k_base, uint32_t s_col, uint32_t idS) {
 #pragma unroll
   for (int k = 0; k < D / 16; ++k) {
@@ -185,7 +195,7 @@ __device__ __forceinline__ void issue_s(uint32_t q_addr, uint32_t k_base, uint32
                    idS, k > 0);
   }
 }
-template <int D>
+template <int D, int kKPair, int kKBox>
 __device__ __forceinline__ void issue_ds(uint32_t q_addr, uint32_t tq_addr, uint32_t k_base,
                                          uint32_t ts_col, uint32_t idS, bool has_tq, bool has_tk) {
   uint32_t started = 0;
@@ -211,17 +221,17 @@ __device__ __forceinline__ void issue_ds(uint32_t q_addr, uint32_t tq_addr, uint
   }
 }
 
-// S into s_col and dS into s_col + 64 for one key tile. An N = 64 MMA with both operands in
+// S into s_col and dS into s_col + BN for one key tile. An N = 64 MMA with both operands in
 // shared memory reads 6 KB per K step against 8 KB for N = 128 in twice the tensor time, so it
 // is bound by shared-memory bandwidth at 2/3 of the tensor core's rate. With a tangent tK,
 // [S | Q tK^T] = Q [K ; tK]^T is one N = 128 MMA per K step (box kb of K and of tK are adjacent
 // in the stage) and tQ K^T is added to its second half.
-template <int D>
+template <int D, int kKPair, int kKBox, int BN>
 __device__ __forceinline__ void issue_scores(uint32_t q_addr, uint32_t tq_addr, uint32_t k_base,
                                              uint32_t s_col, bool has_tq, bool has_tk, bool bf16) {
-  const uint32_t idS = kf::tc::idesc_f16(bf16 ? 1 : 0, kBM, kBN, false, false);
+  const uint32_t idS = kf::tc::idesc_f16(bf16 ? 1 : 0, kBM, BN, false, false);
   if (has_tk) {
-    const uint32_t idS2 = kf::tc::idesc_f16(bf16 ? 1 : 0, kBM, 2 * kBN, false, false);
+    const uint32_t idS2 = kf::tc::idesc_f16(bf16 ? 1 : 0, kBM, 2 * BN, false, false);
 #pragma unroll
     for (int k = 0; k < D / 16; ++k) {
       const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
@@ -233,13 +243,13 @@ __device__ __forceinline__ void issue_scores(uint32_t q_addr, uint32_t tq_addr, 
       for (int k = 0; k < D / 16; ++k) {
         const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
         const uint32_t koff = (k >> 2) * kKPair + (k & 3) * 32;
-        kf::tc::mma_ss(s_col + 64, dsw(tq_addr, off, 16), dsw(k_base, koff, 16), idS, 1);
+        kf::tc::mma_ss(s_col + BN, dsw(tq_addr, off, 16), dsw(k_base, koff, 16), idS, 1);
       }
     }
     return;
   }
-  issue_s<D>(q_addr, k_base, s_col, idS);
-  issue_ds<D>(q_addr, tq_addr, k_base, s_col + 64, idS, has_tq, has_tk);
+  issue_s<D, kKPair>(q_addr, k_base, s_col, idS);
+  issue_ds<D, kKPair, kKBox>(q_addr, tq_addr, k_base, s_col + BN, idS, has_tq, has_tk);
 }
 
 __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
@@ -259,12 +269,32 @@ __device__ __forceinline__ void softmax_groups_sync() {
 }
 
 // ============================================================================================
-// Standalone JVP. Tensor memory:
-//   [0, D) tO accumulator | S_b at 128 + 128 b, dS_b at 192 + 128 b | P_b at 384 + 64 b, H_b +32
+// Standalone JVP. Tensor memory (JvpLayout):
+//   D <= 128: [0, D) tO accumulator | S_b at 128 + 128 b, dS_b at 192 + 128 b | P_b at
+//             384 + 64 b, H_b + 32; 64-key tiles, softmax warpgroup g on keys [32 g, 32 g + 32)
+//             (P and H at + 16 g)
+//   D = 256:  [0, 256) tO | S_b at 256 + 64 b, dS_b + 32 | P_b at 384 + 32 b, H_b + 16; 32-key
+//             tiles (the 128 KB of Q and tQ leave room for 32 KB K and V stages only), warpgroup
+//             g on keys [16 g, 16 g + 16) (P and H at + 8 g)
 // P and H have their own columns, so tile j+2's score MMAs never wait for tile j's output MMAs.
-// Softmax warpgroup g handles keys [32 g, 32 g + 32) of every tile (P and H at +16 g).
 // ============================================================================================
-constexpr uint32_t kPCol = 384;
+template <int D> struct JvpLayout {
+  static constexpr int kN = D <= 128 ? 64 : 32;          // keys per tile
+  static constexpr int kKeysG = kN / 2;                   // keys per softmax warpgroup
+  static constexpr uint32_t kS = D <= 128 ? 128 : 256;    // S of buffer b at kS + 2 kN b, dS kN further
+  static constexpr uint32_t kP = 384;                     // P of buffer b at kP + kN b, H kN / 2 further
+};
+
+template <int N>
+__device__ __forceinline__ void tm_load(uint32_t taddr, uint32_t (&r)[N]) {
+  if constexpr (N == 32) kf::tc::ld_32x32b_x32(taddr, r);
+  else kf::tc::ld_32x32b_x16(taddr, r);
+}
+template <int N>
+__device__ __forceinline__ void tm_store(uint32_t taddr, const uint32_t (&r)[N]) {
+  if constexpr (N == 16) kf::tc::st_32x32b_x16(taddr, r);
+  else kf::tc::st_32x32b_x8(taddr, r);
+}
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -272,13 +302,18 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                     const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_tk,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_tv,
                     const FaArgs p) {
-  using C = Cfg<D>;
+  using L = JvpLayout<D>;
+  constexpr int BN = L::kN, KG = L::kKeysG;
+  using C = Cfg<D, true, BN>;
+  // With one V stage, "P / H of tile j written" cannot share the V stage's barrier (tile j+1's
+  // softmax arrivals could land in tile j's phase): the output thread waits on p_full as well.
+  constexpr bool kFoldP = C::kVStages >= 2;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (kf::smem_u32(smem_raw) & 1023u)) & 1023u);
-  const Bars<D> bars(smem);
+  const Bars<D, true, BN> bars(smem);
   float* row_sums = reinterpret_cast<float*>(smem + C::kScratchOffset);  // [2][kBM]
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(row_sums + 6 * kBM);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kScratchOffset + C::kScratchBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qtile = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -288,16 +323,16 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   const bool has_h = has_tq || has_tk;
   int k_end = p.Nk;
   if (p.causal) k_end = min(p.Nk, max(0, q0 + kBM + p.Nk - p.Nq));
-  const int ntiles = (k_end + kBN - 1) / kBN;
+  const int ntiles = (k_end + BN - 1) / BN;
 
   if (threadIdx.x == 0) {
-    // Each MMA thread waits on one barrier per tile (a probe costs ~200 cycles while the tensor
-    // cores read shared memory): the k_full phase of tile j completes when K / tK of tile j have
-    // landed AND every softmax thread has read tile j-2's scores out of buffer j & 1; the v_full
-    // phase of tile j when V / tV of tile j have landed AND every softmax thread has written
-    // tile j's P and H.
-    bars.init(1, 2 * kBM, 2 * kBM);  // p_full is not used here
-    // Buffers 0 and 1 start free: the softmax threads' share of tiles 0 and 1's k_full phases.
+    // Each MMA thread waits on one barrier per tile where it can (a probe costs ~200 cycles
+    // while the tensor cores read shared memory): the k_full phase of tile j completes when
+    // K / tK of tile j have landed AND every softmax thread has read tile j-2's scores out of
+    // buffer j & 1; the v_full phase of tile j when V / tV of tile j have landed AND (kFoldP)
+    // every softmax thread has written tile j's P and H.
+    if (kFoldP) bars.init(1, 2 * kBM, 2 * kBM);  // p_full is not used
+    else bars.init(2 * kBM, 2 * kBM, 0);
     *abort_flag = 0;
     kf::fence_mbar_init();
   }
@@ -306,6 +341,7 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   __syncthreads();
   kf::tc::fence_after_sync();
   const uint32_t tmem = *bars.tmem_slot;
+  // Buffers 0 and 1 start free: the softmax threads' share of tiles 0 and 1's k_full phases.
   if (warp < 8) {
     kf::mbar_arrive(&bars.k_full[0]);
     kf::mbar_arrive(&bars.k_full[1]);
@@ -326,17 +362,16 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         if (!(ok = kf::mbar_wait_or_abort<true>(&bars.k_full[st], (j / C::kKStages) & 1, &g_fa_error, abort_flag)))
           break;
         kf::tc::fence_after_sync();
-        const uint32_t k_base = kf::smem_u32(smem + C::kKOffset + st * 2 * C::kTileBytes);
-        const uint32_t s_col = tmem + kBufCol + 128 * buf;
-        issue_scores<D>(q_addr, tq_addr, k_base, s_col, has_tq, has_tk, kBf16);
+        const uint32_t k_base = kf::smem_u32(smem + C::kKOffset + st * C::kStageBytes);
+        const uint32_t s_col = tmem + L::kS + 2 * BN * buf;
+        issue_scores<D, C::kKPair, C::kKBox, BN>(q_addr, tq_addr, k_base, s_col, has_tq, has_tk, kBf16);
         kf::tc::commit(&bars.s_full[buf]);
         kf::tc::commit(&bars.k_empty[st]);
       }
     }
   } else if (warp == kPvWarp) {
     if (lane == 0) {
-      // tO += P tV + H V for tile j once its V / tV have arrived and its P / H are written (one
-      // barrier).
+      // tO += P tV + H V for tile j once its V / tV have arrived and its P / H are written.
       constexpr uint32_t idPV = kf::tc::idesc_f16(kBf16 ? 1 : 0, kBM, D, false, true);
       uint32_t acc_started = 0;
       bool ok = true;
@@ -344,19 +379,21 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         const int buf = j & 1, st = j % C::kVStages;
         if (!(ok = kf::mbar_wait_or_abort<true>(&bars.v_full[st], (j / C::kVStages) & 1, &g_fa_error, abort_flag)))
           break;
+        if (!kFoldP && !(ok = kf::mbar_wait_or_abort<true>(&bars.p_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag)))
+          break;
         kf::tc::fence_after_sync();
-        const uint32_t v_base = kf::smem_u32(smem + C::kVOffset + st * 2 * C::kTileBytes);
-        const uint32_t p_col = tmem + kPCol + 64 * buf;
+        const uint32_t v_base = kf::smem_u32(smem + C::kVOffset + st * C::kStageBytes);
+        const uint32_t p_col = tmem + L::kP + BN * buf;
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
+        for (int kk = 0; kk < BN / 16; ++kk) {
           if (has_tv) {
             kf::tc::mma_ts(tmem + kAccCol, p_col + kk * 8,
-                           dsw(v_base + C::kTileBytes, kk * 2048, kBN * 128), idPV, acc_started);
+                           dsw(v_base + C::kTileBytes, kk * 2048, C::kKBox), idPV, acc_started);
             acc_started = 1;
           }
           if (has_h) {
-            kf::tc::mma_ts(tmem + kAccCol, p_col + 32 + kk * 8,
-                           dsw(v_base, kk * 2048, kBN * 128), idPV, acc_started);
+            kf::tc::mma_ts(tmem + kAccCol, p_col + BN / 2 + kk * 8,
+                           dsw(v_base, kk * 2048, C::kKBox), idPV, acc_started);
             acc_started = 1;
           }
         }
@@ -366,7 +403,7 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       kf::tc::commit(bars.acc_full);
     }
   } else {
-    const int group = warp >> 2;   // softmax warpgroup: keys [32 group, 32 group + 32) of every tile
+    const int group = warp >> 2;   // softmax warpgroup: keys [KG group, KG group + KG) of every tile
     const int quarter = warp & 3;  // TMEM lanes [32 quarter, 32 quarter + 32)
     const int row = quarter * 32 + lane;
     const int qrow = q0 + row;
@@ -388,20 +425,20 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       kf::tc::fence_after_sync();
-      const uint32_t s_col = lane_base + kBufCol + 128 * buf + 32 * group;
-      const uint32_t p_col = lane_base + kPCol + 64 * buf + 16 * group;  // 16-bit: 16 columns per 32 keys
-      const int kc = j * kBN + 32 * group;
-      const bool full = kc + 32 <= limit;  // no masking inside these 32 keys for this row
-      uint32_t sr[32], tr[32], pp[16], hh[16];
-      kf::tc::ld_32x32b_x32(s_col, sr);
-      if (has_h) kf::tc::ld_32x32b_x32(s_col + 64, tr);
+      const uint32_t s_col = lane_base + L::kS + 2 * BN * buf + KG * group;
+      const uint32_t p_col = lane_base + L::kP + BN * buf + (KG / 2) * group;  // 16-bit: 2 keys per column
+      const int kc = j * BN + KG * group;
+      const bool full = kc + KG <= limit;  // no masking inside these keys for this row
+      uint32_t sr[KG], tr[KG], pp[KG / 2], hh[KG / 2];
+      tm_load<KG>(s_col, sr);
+      if (has_h) tm_load<KG>(s_col + BN, tr);
       kf::tc::wait_ld();
       // This thread's share of buffer j & 1 is read: tile j+2's scores may go there (its share
       // of the k_full phase of tile j+2).
       kf::tc::fence_before_sync();
       kf::mbar_arrive(&bars.k_full[(j + 2) % C::kKStages]);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < KG / 2; ++i) {
         const float2 a = kf::f2_unpack(kf::f2_fma(kf::f2_pack(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])),
                                                   c2, nl2));
         float p0 = ex2(a.x), p1 = ex2(a.y);
@@ -418,11 +455,11 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
           hh[i] = pack2(hf.x, hf.y, kBf16);
         }
       }
-      kf::tc::st_32x32b_x16(p_col, pp);
-      if (has_h) kf::tc::st_32x32b_x16(p_col + 32, hh);
+      tm_store<KG / 2>(p_col, pp);
+      if (has_h) tm_store<KG / 2>(p_col + BN / 2, hh);
       kf::tc::wait_st();
       kf::tc::fence_before_sync();
-      kf::mbar_arrive(&bars.v_full[j % C::kVStages]);
+      kf::mbar_arrive(kFoldP ? &bars.v_full[j % C::kVStages] : &bars.p_full[buf]);
     }
     const float2 cs = kf::f2_unpack(csum2);
     row_sums[group * kBM + row] = cs.x + cs.y;
@@ -483,6 +520,7 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 // rescaled in TMEM after the previous tile's output MMAs have completed. Tensor memory:
 //   D = 128: [0, 128) G (tO accumulator) | [128, 384) S / dS double buffer | [384, 512) U
 //   D = 64:  [0, 64) U | [64, 128) G | [128, 384) S / dS double buffer
+//   D = 256 (forward only, head dims 136..256): [0, 256) U | [256, 512) S double buffer
 // P and H (16-bit) overwrite the first 16 columns of each warpgroup's 32-column S / dS half, so
 // tile j's score MMAs wait for tile j-2's output MMAs (same buffer).
 // The scores are issued as in the standalone kernel ([S | Q tK^T] = Q [K ; tK]^T, then
@@ -493,8 +531,8 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 template <int D>
 struct FusedCols {
   static constexpr bool kMerge = D == 64;
-  static constexpr uint32_t kU = kMerge ? 0 : 384;  // U: E V
-  static constexpr uint32_t kG = kMerge ? 64 : 0;   // G: H V + E tV (the tO accumulator)
+  static constexpr uint32_t kU = D == 128 ? 384 : 0;  // U: E V
+  static constexpr uint32_t kG = kMerge ? 64 : 0;     // G: H V + E tV (the tO accumulator)
 };
 constexpr float kRescaleThreshold = 8.f;  // log2 units
 
@@ -504,11 +542,12 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
                       const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_tk,
                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_tv,
                       const FaArgs p) {
-  using C = Cfg<D>;
+  using C = Cfg<D, kJvp>;
+  static_assert(D <= 128 || !kJvp, "D = 256 tensor memory holds the forward's accumulator only");
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (kf::smem_u32(smem_raw) & 1023u)) & 1023u);
-  const Bars<D> bars(smem);
+  const Bars<D, kJvp> bars(smem);
   float* tile_max = reinterpret_cast<float*>(smem + C::kScratchOffset);  // [2 buffers][2 groups][kBM]
   float* part_sums = tile_max + 4 * kBM;                                   // [2 groups][kBM]
   volatile int* abort_flag = reinterpret_cast<volatile int*>(part_sums + 2 * kBM);
@@ -554,9 +593,9 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         if (!(ok = kf::mbar_wait_or_abort<true>(&bars.k_full[st], (j / C::kKStages) & 1, &g_fa_error, abort_flag)))
           break;
         kf::tc::fence_after_sync();
-        const uint32_t k_base = kf::smem_u32(smem + C::kKOffset + st * 2 * C::kTileBytes);
-        const uint32_t s_col = tmem + kBufCol + 128 * buf;
-        issue_scores<D>(q_addr, tq_addr, k_base, s_col, has_tq, has_tk, kBf16);
+        const uint32_t k_base = kf::smem_u32(smem + C::kKOffset + st * C::kStageBytes);
+        const uint32_t s_col = tmem + C::kBufCol + 128 * buf;
+        issue_scores<D, C::kKPair, C::kKBox, kBN>(q_addr, tq_addr, k_base, s_col, has_tq, has_tk, kBf16);
         kf::tc::commit(&bars.s_full[buf]);
         kf::tc::commit(&bars.k_empty[st]);
       }
@@ -576,8 +615,8 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         if (!(ok = kf::mbar_wait_or_abort<true>(&bars.v_full[st], (j / C::kVStages) & 1, &g_fa_error, abort_flag)))
           break;
         kf::tc::fence_after_sync();
-        const uint32_t v_base = kf::smem_u32(smem + C::kVOffset + st * 2 * C::kTileBytes);
-        const uint32_t p_col = tmem + kBufCol + 128 * buf;
+        const uint32_t v_base = kf::smem_u32(smem + C::kVOffset + st * C::kStageBytes);
+        const uint32_t p_col = tmem + C::kBufCol + 128 * buf;
         const uint32_t h_col = p_col + 64;
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
@@ -627,7 +666,7 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       if (ok) ok = kf::mbar_wait_or_abort(&bars.s_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag);
       ok = __all_sync(0xffffffffu, ok);  // the tcgen05 copies below are .sync.aligned
       kf::tc::fence_after_sync();
-      const uint32_t s_col = lane_base + kBufCol + 128 * buf + group * 32;
+      const uint32_t s_col = lane_base + C::kBufCol + 128 * buf + group * 32;
       const uint32_t ts_col = s_col + 64;
       uint32_t sr[32], tr[32];
       float mx = -INFINITY;
@@ -784,15 +823,16 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
 
 template <typename T, int D>
 int launch_jvp(const FaArgs& a, int dtype, cudaStream_t stream) {
-  using C = Cfg<D>;
+  constexpr int BN = JvpLayout<D>::kN;
+  using C = Cfg<D, true, BN>;
   CUtensorMap mq, mtq, mk, mtk, mv, mtv;
-  // The maps carry the real head dim: boxes past it (D < 128) read as zeros.
+  // The maps carry the real head dim: boxes past it (D < 128 or < 256) read as zeros.
   if (!encode_bnhd(&mq, a.q, dtype, a.B, a.Nq, a.Hq, a.D, kBM) ||
       !encode_bnhd(&mtq, a.tq ? a.tq : a.q, dtype, a.B, a.Nq, a.Hq, a.D, kBM) ||
-      !encode_bnhd(&mk, a.k, dtype, a.B, a.Nk, a.Hkv, a.D, kBN) ||
-      !encode_bnhd(&mtk, a.tk ? a.tk : a.k, dtype, a.B, a.Nk, a.Hkv, a.D, kBN) ||
-      !encode_bnhd(&mv, a.v, dtype, a.B, a.Nk, a.Hkv, a.D, kBN) ||
-      !encode_bnhd(&mtv, a.tv ? a.tv : a.v, dtype, a.B, a.Nk, a.Hkv, a.D, kBN))
+      !encode_bnhd(&mk, a.k, dtype, a.B, a.Nk, a.Hkv, a.D, BN) ||
+      !encode_bnhd(&mtk, a.tk ? a.tk : a.k, dtype, a.B, a.Nk, a.Hkv, a.D, BN) ||
+      !encode_bnhd(&mv, a.v, dtype, a.B, a.Nk, a.Hkv, a.D, BN) ||
+      !encode_bnhd(&mtv, a.tv ? a.tv : a.v, dtype, a.B, a.Nk, a.Hkv, a.D, BN))
     return KF_ERR_CUDA;
   auto kernel = fa_jvp_sm100_kernel<T, D>;
   const int prep = kf_host::prepare_kernel(reinterpret_cast<const void*>(kernel), kThreads, C::kSmemBytes, nullptr);
@@ -805,7 +845,7 @@ int launch_jvp(const FaArgs& a, int dtype, cudaStream_t stream) {
 
 template <typename T, int D, bool kJvp>
 int launch_fused(const FaArgs& a, int dtype, cudaStream_t stream) {
-  using C = Cfg<D>;
+  using C = Cfg<D, kJvp>;
   CUtensorMap mq, mtq, mk, mtk, mv, mtv;
   // The maps carry the real head dim: boxes past it (D < 128) read as zeros.
   if (!encode_bnhd(&mq, a.q, dtype, a.B, a.Nq, a.Hq, a.D, kBM) ||
@@ -841,21 +881,26 @@ namespace kf::fa {
 
 // Head dims up to 128 (multiples of 8): 8..56 run the D = 64 kernels and 72..120 the D = 128
 // kernels on zero-padded tiles (TMA fills the columns past D with zeros; the epilogues store
-// only real columns).
+// only real columns). The forward alone also runs 136..248 on the D = 256 kernel.
 bool sm100_head_dim(int d) { return d >= 8 && d <= 128; }
 
 bool sm100_jvp_supported(const FaArgs& a) {
-  return sm100_head_dim(a.D) && (a.tq != nullptr || a.tk != nullptr || a.tv != nullptr);
+  return a.D >= 8 && a.D <= 256 && (a.tq != nullptr || a.tk != nullptr || a.tv != nullptr);
 }
 
 bool sm100_fused_supported(const FaArgs& a, int mode) {
+  if (mode == kModeFwd) return a.D >= 8 && a.D <= 256;
   if (!sm100_head_dim(a.D)) return false;
-  if (mode == kModeFwd) return true;
   return a.tq != nullptr || a.tk != nullptr || a.tv != nullptr;
 }
 
 int launch_sm100_fused(const FaArgs& a, int mode, int dtype, cudaStream_t s) {
   const bool jvp = mode == kModeFwdJvp;
+  if (a.D > 128) {
+    if (jvp) return KF_ERR_UNSUPPORTED;
+    return dtype == KF_DTYPE_BF16 ? launch_fused<__nv_bfloat16, 256, false>(a, dtype, s)
+                                  : launch_fused<__half, 256, false>(a, dtype, s);
+  }
   if (dtype == KF_DTYPE_BF16) {
     if (a.D <= 64) return jvp ? launch_fused<__nv_bfloat16, 64, true>(a, dtype, s) : launch_fused<__nv_bfloat16, 64, false>(a, dtype, s);
     return jvp ? launch_fused<__nv_bfloat16, 128, true>(a, dtype, s) : launch_fused<__nv_bfloat16, 128, false>(a, dtype, s);
@@ -865,7 +910,11 @@ int launch_sm100_fused(const FaArgs& a, int mode, int dtype, cudaStream_t s) {
 }
 
 int launch_sm100_jvp(const FaArgs& a, int dtype, cudaStream_t s) {
-  if (dtype == KF_DTYPE_BF16) return a.D <= 64 ? launch_jvp<__nv_bfloat16, 64>(a, dtype, s) : launch_jvp<__nv_bfloat16, 128>(a, dtype, s);
+  if (dtype == KF_DTYPE_BF16) {
+    if (a.D > 128) return launch_jvp<__nv_bfloat16, 256>(a, dtype, s);
+    return a.D <= 64 ? launch_jvp<__nv_bfloat16, 64>(a, dtype, s) : launch_jvp<__nv_bfloat16, 128>(a, dtype, s);
+  }
+  if (a.D > 128) return launch_jvp<__half, 256>(a, dtype, s);
   return a.D <= 64 ? launch_jvp<__half, 64>(a, dtype, s) : launch_jvp<__half, 128>(a, dtype, s);
 }
 

@@ -121,6 +121,50 @@ def test_standalone_jvp(fa, case, dtype):
         assert torch.count_nonzero(actual[:, :q.shape[1] - k.shape[1]]) == 0
 
 
+# Head dims 136..256: the forward runs the D = 256 tcgen05 kernel (zero-padded past D); several
+# query and key tiles, causal with empty rows, GQA.
+WIDE_FORWARD_CASES = (
+    (1, 300, 257, 4, 2, 256, True, None),
+    (2, 129, 200, 2, 2, 192, False, 0.11),
+    (1, 77, 530, 3, 1, 136, False, None),
+    (1, 200, 64, 2, 2, 256, True, None),
+    (1, 1, 1, 2, 2, 248, False, None),
+)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("case", WIDE_FORWARD_CASES)
+def test_forward_wide_head_dims(fa, case, dtype):
+    q, k, v = make_inputs(case, dtype)[:3]
+    kwargs = dict(causal=case[-2], softmax_scale=case[-1])
+    out, lse = fa.flash_attention(q, k, v, return_lse=True, **kwargs)
+    ref_out, _ = attention_jvp(*double_reference((q, k, v, q, k, v)), **kwargs)
+    assert_stated_bar(out, ref_out, dtype)
+    assert_lse_bar(lse, attention_lse(*double_reference((q, k)), **kwargs))
+    if kwargs["causal"] and q.shape[1] > k.shape[1]:
+        empty = q.shape[1] - k.shape[1]
+        assert torch.count_nonzero(out[:, :empty]) == 0 and torch.isinf(lse[:, :, :empty]).all()
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("case", WIDE_FORWARD_CASES)
+def test_jvp_wide_head_dims(fa, case, dtype):
+    """Head dims 136..256 on the D = 256 tcgen05 kernels (32-key tiles): the standalone JVP
+    from the forward's O and LSE, and the one-pass entry point (forward, then the JVP)."""
+    q, k, v, tq, tk, tv = make_inputs(case, dtype)
+    kwargs = dict(causal=case[-2], softmax_scale=case[-1])
+    ref_out, ref_tangent = attention_jvp(*double_reference((q, k, v, tq, tk, tv)), **kwargs)
+    out, lse = fa.flash_attention(q, k, v, return_lse=True, **kwargs)
+    tangent = fa.flash_attention_jvp(q, k, v, tq, tk, tv, out, lse, **kwargs)
+    assert_tangent_bar(tangent, ref_tangent, dtype)
+    out2, lse2, tangent2 = fa.flash_attention_fwd_jvp(q, k, v, tq, tk, tv, **kwargs)
+    assert torch.equal(out2, out) and torch.equal(lse2, lse) and torch.equal(tangent2, tangent)
+    value_only = fa.flash_attention_jvp(q, k, v, None, None, tv, out, lse, **kwargs)
+    ref_value_only = attention_jvp(*double_reference((q, k, v, torch.zeros_like(q), torch.zeros_like(k), tv)),
+                                   **kwargs)[1]
+    assert_tangent_bar(value_only, ref_value_only, dtype)
+
+
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("case", CASES)
 def test_one_pass_forward_and_jvp(fa, case, dtype):
