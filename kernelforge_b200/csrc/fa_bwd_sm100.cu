@@ -37,7 +37,6 @@ using kf::fa::encode_bnhd;
 __device__ unsigned int g_fa_bwd_error = 0;
 
 constexpr int kRows = 128;     // stationary rows per CTA
-constexpr int kTile = 64;      // streamed rows per tile
 constexpr int kThreads = 352;  // 11 warps
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
@@ -45,8 +44,12 @@ constexpr int kOutWarp = 10;
 constexpr uint32_t kTmemCols = 512;
 
 // Shared memory: the stationary pair (Q, dO or K, V), a ring of streamed pairs (K, V or Q, dO)
-// with, per stage, 64 row statistics of each kind (dkdv only), then the barriers.
+// with, per stage, the tile's row statistics of each kind (dkdv only), then the barriers.
+// D = 256: the stationary pair takes 128 KB, so the streamed tiles are 32 rows (3 stages of
+// 2 x 16 KB), and the dK / dV accumulators (2 x 256 columns together) are split by head-dim
+// halves over two CTAs per key block, each recomputing the key block's scores.
 template <int D> struct Cfg {
+  static constexpr int kTile = D <= 128 ? 64 : 32;       // streamed rows per tile
   static constexpr int kKB = D / 64;                     // 128-byte boxes along the head dim
   static constexpr int kStatBytes = kKB * kRows * 128;   // one stationary operand
   static constexpr int kTileBytes = kKB * kTile * 128;   // one streamed operand tile
@@ -55,8 +58,17 @@ template <int D> struct Cfg {
   static constexpr int kRowStatOffset = kRingOffset + kStages * 2 * kTileBytes;
   static constexpr int kBarOffset = kRowStatOffset + kStages * 2 * kTile * 4;
   static constexpr int kSmemBytes = kBarOffset + 256 + 1024;  // + alignment slack
-  // Score buffers in TMEM (128 columns each) of the dK/dV kernel: dV and dK take 2 D columns.
-  static constexpr int kDkdvBufs = (512 - 2 * D) / 128;
+  static_assert(kSmemBytes <= 232448, "shared memory");
+  static constexpr int kBufCols = 2 * kTile;             // S and dP (or S^T and dP^T) of a buffer
+  // Score buffers may not outnumber ring stages: a buffer's "free" commit for tile t + bufs
+  // must land in that tile's phase of its stage.
+  static constexpr uint32_t kDqBuf = D <= 128 ? 128 : 256;  // dQ accumulator below it
+  static constexpr int kDqBufs = (512 - kDqBuf) / kBufCols < kStages ? (512 - kDqBuf) / kBufCols : kStages;
+  static constexpr int kAccN = D == 256 ? 128 : D;       // dV / dK columns per CTA
+  static constexpr int kHalves = D / kAccN;              // CTAs per key block
+  static constexpr uint32_t kDkdvBuf = 2 * kAccN;        // dV at 0, dK at kAccN
+  static constexpr int kDkdvBufs =
+      (512 - kDkdvBuf) / kBufCols < kStages ? (512 - static_cast<int>(kDkdvBuf)) / kBufCols : kStages;
 };
 constexpr int kMaxBufs = 3;
 
@@ -98,11 +110,11 @@ template <int D> struct Bars {
   }
 };
 
-// Streamed tile t of a CTA: head h_base + t / count, rows (first + t % count) * kTile.
+// Streamed tile t of a CTA: head h_base + t / count, rows (first + t % count) * tile.
 struct TileWalk {
-  int h_base, first, count;
+  int h_base, first, count, tile;
   __device__ int head(int t) const { return h_base + t / count; }
-  __device__ int row0(int t) const { return (first + t % count) * kTile; }
+  __device__ int row0(int t) const { return (first + t % count) * tile; }
 };
 
 // TMA producer (one thread). kRowStats: each stage also carries the tile's 64 row statistics.
@@ -119,7 +131,7 @@ __device__ void produce(const Bars<D>& bars, uint8_t* smem, const CUtensorMap* t
     kf::tma_load_4d(smem + kb * kRows * 128, tm_s0, bars.stat_full, kb * 64, stat_head, stat_row0, b);
     kf::tma_load_4d(smem + C::kStatBytes + kb * kRows * 128, tm_s1, bars.stat_full, kb * 64, stat_head, stat_row0, b);
   }
-  constexpr uint32_t kStageTx = 2 * C::kTileBytes + (kRowStats ? 2 * kTile * 4 : 0);
+  constexpr uint32_t kStageTx = 2 * C::kTileBytes + (kRowStats ? 2 * C::kTile * 4 : 0);
   for (int t = 0; t < ntiles; ++t) {
     const int st = t % C::kStages;
     if (t >= C::kStages &&
@@ -129,47 +141,61 @@ __device__ void produce(const Bars<D>& bars, uint8_t* smem, const CUtensorMap* t
     const int h = walk.head(t), r0 = walk.row0(t);
     kf::mbar_arrive_expect_tx(&bars.ring_full[st], kStageTx);
     for (int kb = 0; kb < C::kKB; ++kb) {
-      kf::tma_load_4d(base + kb * kTile * 128, tm_t0, &bars.ring_full[st], kb * 64, h, r0, b);
-      kf::tma_load_4d(base + C::kTileBytes + kb * kTile * 128, tm_t1, &bars.ring_full[st], kb * 64, h, r0, b);
+      kf::tma_load_4d(base + kb * C::kTile * 128, tm_t0, &bars.ring_full[st], kb * 64, h, r0, b);
+      kf::tma_load_4d(base + C::kTileBytes + kb * C::kTile * 128, tm_t1, &bars.ring_full[st], kb * 64, h, r0, b);
     }
     if (kRowStats) {
-      // r0 + 64 <= NqP and NqP is a multiple of 128: 16-byte aligned, in bounds.
+      // r0 + kTile <= NqP and NqP is a multiple of 128: 16-byte aligned, in bounds.
       const int64_t off = (static_cast<int64_t>(b) * p.Hq + h) * p.NqP + r0;
-      float* rs = reinterpret_cast<float*>(smem + C::kRowStatOffset + st * 2 * kTile * 4);
-      kf::bulk_load(rs, p.row_nlse + off, kTile * 4, &bars.ring_full[st]);
-      kf::bulk_load(rs + kTile, p.row_ndelta + off, kTile * 4, &bars.ring_full[st]);
+      float* rs = reinterpret_cast<float*>(smem + C::kRowStatOffset + st * 2 * C::kTile * 4);
+      kf::bulk_load(rs, p.row_nlse + off, C::kTile * 4, &bars.ring_full[st]);
+      kf::bulk_load(rs + C::kTile, p.row_ndelta + off, C::kTile * 4, &bars.ring_full[st]);
     }
   }
 }
 
-// D[128 x 64] = A[128 x D] B[64 x D]^T; A, B K-major 128-byte-swizzled tiles.
+// D[128 x TILE] = A[128 x D] B[TILE x D]^T; A, B K-major 128-byte-swizzled tiles.
 // The descriptors are built once; each K step only adds a constant offset, which keeps the
 // issuing thread's instruction count per MMA small.
-template <int D>
+template <int D, int TILE>
 __device__ __forceinline__ void issue_scores(uint32_t a_addr, uint32_t b_addr, uint32_t d_col, uint32_t idesc) {
   const uint64_t a_desc = kf::tc::desc_sw128(a_addr, 16, 1024), b_desc = kf::tc::desc_sw128(b_addr, 16, 1024);
 #pragma unroll
   for (int k = 0; k < D / 16; ++k) {
     const uint32_t aoff = (k >> 2) * kRows * 128 + (k & 3) * 32;
-    const uint32_t boff = (k >> 2) * kTile * 128 + (k & 3) * 32;
+    const uint32_t boff = (k >> 2) * TILE * 128 + (k & 3) * 32;
     kf::tc::mma_ss(d_col, kf::tc::desc_advance(a_desc, aoff), kf::tc::desc_advance(b_desc, boff), idesc, k > 0);
   }
 }
 
-// D[128 x D] += A[128 x 64] B[64 x D]; A 16-bit in TMEM (8 columns per 16 of K), B an MN-major
-// 128-byte-swizzled tile (64-element blocks kTile * 128 bytes apart). kSplitA: K rows
-// [32 g, 32 g + 32) of A start at column 32 g (each softmax warpgroup packed its 32 values into
-// the first 16 of its own 32 columns); otherwise A is packed contiguously.
-template <int D, bool kSplitA>
+// D[128 x N] += A[128 x TILE] B[TILE x N]; A 16-bit in TMEM (8 columns per 16 of K), B an
+// MN-major 128-byte-swizzled tile (64-element blocks TILE * 128 bytes apart). kSplitA: K rows
+// [G g, G g + G) of A (G = TILE / 2) start at column G g (each softmax warpgroup packed its G
+// values into the first G / 2 of its own G columns); otherwise A is packed contiguously.
+template <int TILE, bool kSplitA>
 __device__ __forceinline__ void issue_accumulate(uint32_t d_col, uint32_t a_col, uint32_t b_addr, uint32_t idesc,
                                                  uint32_t& started) {
-  const uint64_t b_desc = kf::tc::desc_sw128(b_addr, kTile * 128, 1024);
+  constexpr int kG = TILE / 2, kSteps = kG / 16;  // K16 steps per warpgroup's keys
+  const uint64_t b_desc = kf::tc::desc_sw128(b_addr, TILE * 128, 1024);
 #pragma unroll
-  for (int kk = 0; kk < kTile / 16; ++kk) {
-    const uint32_t acol = kSplitA ? (kk >> 1) * 32 + (kk & 1) * 8 : kk * 8;
+  for (int kk = 0; kk < TILE / 16; ++kk) {
+    const uint32_t acol = kSplitA ? (kk / kSteps) * kG + (kk % kSteps) * 8 : kk * 8;
     kf::tc::mma_ts(d_col, a_col + acol, kf::tc::desc_advance(b_desc, kk * 2048), idesc, started);
     started = 1;
   }
+}
+
+// Tensor-memory copies of one softmax warpgroup's G scores (G = 32 or 16) and G / 2 packed
+// 16-bit results per row.
+template <int N>
+__device__ __forceinline__ void tm_load(uint32_t taddr, uint32_t (&r)[N]) {
+  if constexpr (N == 32) kf::tc::ld_32x32b_x32(taddr, r);
+  else kf::tc::ld_32x32b_x16(taddr, r);
+}
+template <int N>
+__device__ __forceinline__ void tm_store(uint32_t taddr, const uint32_t (&r)[N]) {
+  if constexpr (N == 16) kf::tc::st_32x32b_x16(taddr, r);
+  else kf::tc::st_32x32b_x8(taddr, r);
 }
 
 __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
@@ -209,20 +235,19 @@ __device__ __forceinline__ void store_row32(T* dst, const uint32_t (&acc)[32], f
 }
 
 // ============================================================================================
-// dQ. Tensor memory: [0, D) dQ accumulator | three score buffers, S_b at 128 + 128 b and dP_b
-// 64 further. Warpgroup g reads keys [32 g, 32 g + 32) of S_b and dP_b and writes dS (16-bit)
-// over the first 16 of its 32 S_b columns, so tile t+3's score MMAs wait for tile t's
-// accumulating MMAs.
+// dQ. Tensor memory: [0, D) dQ accumulator | kDqBufs score buffers, S_b at kDqBuf + kBufCols b
+// and dP_b kTile further. Warpgroup g reads keys [G g, G g + G) of S_b and dP_b (G = kTile / 2)
+// and writes dS (16-bit) over the first G / 2 of its G S_b columns, so tile t+kDqBufs's score
+// MMAs wait for tile t's accumulating MMAs.
 // ============================================================================================
-constexpr uint32_t kDqAcc = 0, kDqBuf = 128;
-constexpr int kDqBufs = 3;
-
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, 1)
 fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                        const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                        const BwdArgs p) {
   using C = Cfg<D>;
+  constexpr int TILE = C::kTile, G = TILE / 2;
+  constexpr uint32_t kDqAcc = 0;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (kf::smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -234,7 +259,7 @@ fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
   const int kvh = h / (p.Hq / p.Hkv);
   int k_end = p.Nk;
   if (p.causal) k_end = min(p.Nk, max(0, q0 + kRows + p.Nk - p.Nq));
-  const int ntiles = (k_end + kTile - 1) / kTile;
+  const int ntiles = (k_end + TILE - 1) / TILE;
 
   if (threadIdx.x == 0) {
     bars.init();
@@ -249,20 +274,21 @@ fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
 
   if (warp == kProducerWarp) {
     if (lane == 0)
-      produce<D, false>(bars, smem, &tm_q, &tm_do, &tm_k, &tm_v, h, q0, b, TileWalk{kvh, 0, max(ntiles, 1)}, ntiles, p);
+      produce<D, false>(bars, smem, &tm_q, &tm_do, &tm_k, &tm_v, h, q0, b, TileWalk{kvh, 0, max(ntiles, 1), TILE},
+                        ntiles, p);
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
-      constexpr uint32_t idS = kf::tc::idesc_f16(kBf16 ? 1 : 0, kRows, kTile, false, false);
+      constexpr uint32_t idS = kf::tc::idesc_f16(kBf16 ? 1 : 0, kRows, TILE, false, false);
       const uint32_t q_addr = kf::smem_u32(smem), do_addr = q_addr + C::kStatBytes;
       bool ok = wait_relaxed(bars.stat_full, 0, abort);
       for (int t = 0; ok && t < ntiles; ++t) {
-        const int buf = t % kDqBufs, st = t % C::kStages;
+        const int buf = t % C::kDqBufs, st = t % C::kStages;
         if (!(ok = wait_relaxed(&bars.ring_full[st], (t / C::kStages) & 1, abort))) break;
         kf::tc::fence_after_sync();
         const uint32_t k_addr = kf::smem_u32(smem + C::kRingOffset + st * 2 * C::kTileBytes);
-        const uint32_t s_col = tmem + kDqBuf + 128 * buf;
-        issue_scores<D>(q_addr, k_addr, s_col, idS);                        // S  = Q K^T
-        issue_scores<D>(do_addr, k_addr + C::kTileBytes, s_col + 64, idS);  // dP = dO V^T
+        const uint32_t s_col = tmem + C::kDqBuf + C::kBufCols * buf;
+        issue_scores<D, TILE>(q_addr, k_addr, s_col, idS);                          // S  = Q K^T
+        issue_scores<D, TILE>(do_addr, k_addr + C::kTileBytes, s_col + TILE, idS);  // dP = dO V^T
         kf::tc::commit(&bars.s_full[buf]);
       }
     }
@@ -272,17 +298,18 @@ fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
       uint32_t started = 0;
       bool ok = true;
       // Score buffers start free: the first kDqBufs tiles' buffer arrivals.
-      for (int t = 0; t < kDqBufs; ++t) kf::mbar_arrive(&bars.ring_full[t % C::kStages]);
+      for (int t = 0; t < C::kDqBufs; ++t) kf::mbar_arrive(&bars.ring_full[t % C::kStages]);
       for (int t = 0; ok && t < ntiles; ++t) {
-        const int buf = t % kDqBufs, st = t % C::kStages;
-        if (!(ok = wait_relaxed(&bars.p_full[buf], (t / kDqBufs) & 1, abort))) break;
+        const int buf = t % C::kDqBufs, st = t % C::kStages;
+        if (!(ok = wait_relaxed(&bars.p_full[buf], (t / C::kDqBufs) & 1, abort))) break;
         kf::tc::fence_after_sync();
         const uint32_t k_addr = kf::smem_u32(smem + C::kRingOffset + st * 2 * C::kTileBytes);
-        issue_accumulate<D, true>(tmem + kDqAcc, tmem + kDqBuf + 128 * buf, k_addr, idA, started);  // dQ += dS K
+        issue_accumulate<TILE, true>(tmem + kDqAcc, tmem + C::kDqBuf + C::kBufCols * buf, k_addr, idA,
+                                     started);  // dQ += dS K
         kf::tc::commit(&bars.ring_empty[st]);
         // Buffer `buf` is free for tile t + kDqBufs (that tile's ring stage: its phase is the
         // next one to complete there, as the score thread already waited for tile t).
-        kf::tc::commit(&bars.ring_full[(t + kDqBufs) % C::kStages]);
+        kf::tc::commit(&bars.ring_full[(t + C::kDqBufs) % C::kStages]);
       }
       kf::tc::commit(bars.acc_full);
     }
@@ -298,19 +325,19 @@ fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
     const uint64_t nd2 = kf::f2_pack(ndelta, ndelta);
     bool ok = true;
     for (int t = 0; t < ntiles; ++t) {
-      const int buf = t % kDqBufs;
-      ok = __all_sync(0xffffffffu, wait(&bars.s_full[buf], (t / kDqBufs) & 1, abort));  // .sync.aligned copies follow
+      const int buf = t % C::kDqBufs;
+      ok = __all_sync(0xffffffffu, wait(&bars.s_full[buf], (t / C::kDqBufs) & 1, abort));  // .sync.aligned copies follow
       if (!ok) break;
       kf::tc::fence_after_sync();
-      const uint32_t s_col = lane_base + kDqBuf + 128 * buf + 32 * group;  // this warpgroup's 32 keys
-      const int kc = t * kTile + 32 * group;
-      const bool full = kc + 32 <= limit;
-      uint32_t sv[32], dv[32], dd[16];
-      kf::tc::ld_32x32b_x32(s_col, sv);
-      kf::tc::ld_32x32b_x32(s_col + 64, dv);
+      const uint32_t s_col = lane_base + C::kDqBuf + C::kBufCols * buf + G * group;  // this warpgroup's G keys
+      const int kc = t * TILE + G * group;
+      const bool full = kc + G <= limit;
+      uint32_t sv[G], dv[G], dd[G / 2];
+      tm_load<G>(s_col, sv);
+      tm_load<G>(s_col + TILE, dv);
       kf::tc::wait_ld();
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < G / 2; ++i) {
         const float2 a = kf::f2_unpack(
             kf::f2_fma(kf::f2_pack(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1])), c2, nl2));
         float p0 = ex2(a.x), p1 = ex2(a.y);
@@ -323,7 +350,7 @@ fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
         const float2 df = kf::f2_unpack(ds);
         dd[i] = pack2(df.x, df.y, kBf16);
       }
-      kf::tc::st_32x32b_x16(s_col, dd);
+      tm_store<G / 2>(s_col, dd);
       kf::tc::wait_st();
       kf::tc::fence_before_sync();
       kf::mbar_arrive(&bars.p_full[buf]);
@@ -353,10 +380,12 @@ fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
 }
 
 // ============================================================================================
-// dK, dV. Tensor memory: [0, D) dV | [D, 2D) dK | kBufs score buffers: S^T_b at 2D + 128 b,
-// dP^T_b 64 further (3 buffers for D = 64, 2 for D = 128). Warpgroup g reads queries
-// [32 g, 32 g + 32) of S^T_b and dP^T_b and writes P^T and dS^T (16-bit) over the first 16 of
-// those 32 columns, so tile t+kBufs's score MMAs wait for tile t's accumulating MMAs.
+// dK, dV. Tensor memory: [0, kAccN) dV | [kAccN, 2 kAccN) dK | kDkdvBufs score buffers: S^T_b at
+// 2 kAccN + kBufCols b, dP^T_b kTile further (3 buffers for D = 64 and 256, 2 for D = 128).
+// Warpgroup g reads queries [G g, G g + G) of S^T_b and dP^T_b (G = kTile / 2) and writes P^T
+// and dS^T (16-bit) over the first G / 2 of those G columns, so tile t+kBufs's score MMAs wait
+// for tile t's accumulating MMAs. D = 256: CTA 2 k + c of the grid's x axis is key block k and
+// head-dim half c (dV, dK columns [128 c, 128 c + 128)).
 // ============================================================================================
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -364,8 +393,9 @@ fa_bwd_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_
                          const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                          const BwdArgs p) {
   using C = Cfg<D>;
+  constexpr int TILE = C::kTile, G = TILE / 2;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr uint32_t kDv = 0, kDk = D, kBuf = 2 * D;
+  constexpr uint32_t kDv = 0, kDk = C::kAccN, kBuf = C::kDkdvBuf;
   constexpr int kBufs = C::kDkdvBufs;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (kf::smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -373,15 +403,16 @@ fa_bwd_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kvh = blockIdx.y, b = blockIdx.z;
-  const int k0 = blockIdx.x * kRows;
+  const int half = C::kHalves > 1 ? static_cast<int>(blockIdx.x) % C::kHalves : 0;
+  const int k0 = static_cast<int>(blockIdx.x) / C::kHalves * kRows;
   const int group = p.Hq / p.Hkv;
   // Key k is visible to query q iff q >= k + Nq - Nk (causal): queries below k0 + Nq - Nk see
   // none of these keys.
   const int q_first = p.causal ? max(0, k0 + p.Nq - p.Nk) : 0;
-  const int qt_first = q_first / kTile;
-  const int qt_count = max(0, (p.Nq + kTile - 1) / kTile - qt_first);
+  const int qt_first = q_first / TILE;
+  const int qt_count = max(0, (p.Nq + TILE - 1) / TILE - qt_first);
   const int ntiles = group * qt_count;
-  const TileWalk walk{kvh * group, qt_first, max(qt_count, 1)};
+  const TileWalk walk{kvh * group, qt_first, max(qt_count, 1), TILE};
 
   if (threadIdx.x == 0) {
     bars.init();
@@ -398,7 +429,7 @@ fa_bwd_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_
     if (lane == 0) produce<D, true>(bars, smem, &tm_k, &tm_v, &tm_q, &tm_do, kvh, k0, b, walk, ntiles, p);
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
-      constexpr uint32_t idS = kf::tc::idesc_f16(kBf16 ? 1 : 0, kRows, kTile, false, false);
+      constexpr uint32_t idS = kf::tc::idesc_f16(kBf16 ? 1 : 0, kRows, TILE, false, false);
       const uint32_t k_addr = kf::smem_u32(smem), v_addr = k_addr + C::kStatBytes;
       bool ok = wait_relaxed(bars.stat_full, 0, abort);
       for (int t = 0; ok && t < ntiles; ++t) {
@@ -406,15 +437,17 @@ fa_bwd_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_
         if (!(ok = wait_relaxed(&bars.ring_full[st], (t / C::kStages) & 1, abort))) break;
         kf::tc::fence_after_sync();
         const uint32_t q_addr = kf::smem_u32(smem + C::kRingOffset + st * 2 * C::kTileBytes);
-        const uint32_t s_col = tmem + kBuf + 128 * buf;
-        issue_scores<D>(k_addr, q_addr, s_col, idS);                        // S^T  = K Q^T
-        issue_scores<D>(v_addr, q_addr + C::kTileBytes, s_col + 64, idS);   // dP^T = V dO^T
+        const uint32_t s_col = tmem + kBuf + C::kBufCols * buf;
+        issue_scores<D, TILE>(k_addr, q_addr, s_col, idS);                          // S^T  = K Q^T
+        issue_scores<D, TILE>(v_addr, q_addr + C::kTileBytes, s_col + TILE, idS);   // dP^T = V dO^T
         kf::tc::commit(&bars.s_full[buf]);
       }
     }
   } else if (warp == kOutWarp) {
     if (lane == 0) {
-      constexpr uint32_t idA = kf::tc::idesc_f16(kBf16 ? 1 : 0, kRows, D, false, true);
+      constexpr uint32_t idA = kf::tc::idesc_f16(kBf16 ? 1 : 0, kRows, C::kAccN, false, true);
+      // This CTA's head-dim columns of dO and Q: 64-column blocks TILE x 128 bytes apart.
+      const uint32_t bcol = static_cast<uint32_t>(half) * (C::kAccN / 64) * TILE * 128;
       uint32_t v_started = 0, k_started = 0;
       bool ok = true;
       // Score buffers start free: the first kBufs tiles' buffer arrivals.
@@ -423,10 +456,10 @@ fa_bwd_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_
         const int buf = t % kBufs, st = t % C::kStages;
         if (!(ok = wait_relaxed(&bars.p_full[buf], (t / kBufs) & 1, abort))) break;
         kf::tc::fence_after_sync();
-        const uint32_t q_addr = kf::smem_u32(smem + C::kRingOffset + st * 2 * C::kTileBytes);
-        const uint32_t s_col = tmem + kBuf + 128 * buf;
-        issue_accumulate<D, true>(tmem + kDv, s_col, q_addr + C::kTileBytes, idA, v_started);  // dV += P^T dO
-        issue_accumulate<D, true>(tmem + kDk, s_col + 64, q_addr, idA, k_started);             // dK += dS^T Q
+        const uint32_t q_addr = kf::smem_u32(smem + C::kRingOffset + st * 2 * C::kTileBytes) + bcol;
+        const uint32_t s_col = tmem + kBuf + C::kBufCols * buf;
+        issue_accumulate<TILE, true>(tmem + kDv, s_col, q_addr + C::kTileBytes, idA, v_started);  // dV += P^T dO
+        issue_accumulate<TILE, true>(tmem + kDk, s_col + TILE, q_addr, idA, k_started);           // dK += dS^T Q
         kf::tc::commit(&bars.ring_empty[st]);
         kf::tc::commit(&bars.ring_full[(t + kBufs) % C::kStages]);  // buffer free for tile t + kBufs
       }
@@ -445,18 +478,19 @@ fa_bwd_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_
       ok = __all_sync(0xffffffffu, wait(&bars.s_full[buf], (t / kBufs) & 1, abort));
       if (!ok) break;
       kf::tc::fence_after_sync();
-      const uint32_t s_col = lane_base + kBuf + 128 * buf + 32 * wg;  // this warpgroup's 32 queries
-      const int r0 = walk.row0(t) + 32 * wg;
+      const uint32_t s_col = lane_base + kBuf + C::kBufCols * buf + G * wg;  // this warpgroup's G queries
+      const int r0 = walk.row0(t) + G * wg;
       const bool full = r0 >= q_min;
-      const float* rs = reinterpret_cast<const float*>(smem + C::kRowStatOffset + (t % C::kStages) * 2 * kTile * 4) + 32 * wg;
-      uint32_t sv[32], dv[32], pp[16], dd[16];
-      kf::tc::ld_32x32b_x32(s_col, sv);
-      kf::tc::ld_32x32b_x32(s_col + 64, dv);
+      const float* rs =
+          reinterpret_cast<const float*>(smem + C::kRowStatOffset + (t % C::kStages) * 2 * TILE * 4) + G * wg;
+      uint32_t sv[G], dv[G], pp[G / 2], dd[G / 2];
+      tm_load<G>(s_col, sv);
+      tm_load<G>(s_col + TILE, dv);
       kf::tc::wait_ld();
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < G / 2; ++i) {
         const float2 nl = *reinterpret_cast<const float2*>(rs + 2 * i);
-        const float2 nd = *reinterpret_cast<const float2*>(rs + kTile + 2 * i);
+        const float2 nd = *reinterpret_cast<const float2*>(rs + TILE + 2 * i);
         const float2 a = kf::f2_unpack(
             kf::f2_fma(kf::f2_pack(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1])), c2, kf::f2_pack(nl.x, nl.y)));
         float p0 = ex2(a.x), p1 = ex2(a.y);
@@ -471,30 +505,32 @@ fa_bwd_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_
         pp[i] = pack2(p0, p1, kBf16);
         dd[i] = pack2(df.x, df.y, kBf16);
       }
-      kf::tc::st_32x32b_x16(s_col, pp);
-      kf::tc::st_32x32b_x16(s_col + 64, dd);
+      tm_store<G / 2>(s_col, pp);
+      tm_store<G / 2>(s_col + TILE, dd);
       kf::tc::wait_st();
       kf::tc::fence_before_sync();
       kf::mbar_arrive(&bars.p_full[buf]);
     }
-    // Epilogue: dV = acc, dK = gamma acc; warpgroup g writes columns [g D/2, (g + 1) D/2).
+    // Epilogue: dV = acc, dK = gamma acc; warpgroup g writes accumulator columns
+    // [g kAccN / 2, (g + 1) kAccN / 2), head-dim columns half * kAccN further.
     if (ok) ok = wait(bars.acc_full, 0, abort);
     ok = __all_sync(0xffffffffu, ok);
     if (ok) {
       kf::tc::fence_after_sync();
       const int64_t off = ((static_cast<int64_t>(b) * p.Nk + key) * p.Hkv + kvh) * p.D;  // real head dim
-      T* dk = static_cast<T*>(p.dk) + off;
-      T* dv = static_cast<T*>(p.dv) + off;
+      const int col0 = half * C::kAccN;
+      T* dk = static_cast<T*>(p.dk) + off + col0;
+      T* dv = static_cast<T*>(p.dv) + off + col0;
 #pragma unroll
-      for (int cc = 0; cc < D / 64; ++cc) {
-        const int c = wg * (D / 64) + cc;
+      for (int cc = 0; cc < C::kAccN / 64; ++cc) {
+        const int c = wg * (C::kAccN / 64) + cc;
         uint32_t ar[32], br[32];
         kf::tc::ld_32x32b_x32(lane_base + kDv + c * 32, ar);
         kf::tc::ld_32x32b_x32(lane_base + kDk + c * 32, br);
         kf::tc::wait_ld();
-        if (key < p.Nk) {
-          store_row32<T>(dv + c * 32, ar, 1.f, ntiles > 0, p.D - c * 32);
-          store_row32<T>(dk + c * 32, br, p.scale, ntiles > 0, p.D - c * 32);
+        if (key < p.Nk && col0 + c * 32 < p.D) {
+          store_row32<T>(dv + c * 32, ar, 1.f, ntiles > 0, p.D - col0 - c * 32);
+          store_row32<T>(dk + c * 32, br, p.scale, ntiles > 0, p.D - col0 - c * 32);
         }
       }
     }
@@ -512,11 +548,11 @@ int launch(const BwdArgs& a, int dtype, cudaStream_t stream) {
   using C = Cfg<D>;
   {
     CUtensorMap mq, mdo, mk, mv;
-    // The maps carry the real head dim: boxes past it (D < 128) read as zeros.
+    // The maps carry the real head dim: boxes past it (D < 128 or < 256) read as zeros.
     if (!encode_bnhd(&mq, a.q, dtype, a.B, a.Nq, a.Hq, a.D, kRows) ||
         !encode_bnhd(&mdo, a.dout, dtype, a.B, a.Nq, a.Hq, a.D, kRows) ||
-        !encode_bnhd(&mk, a.k, dtype, a.B, a.Nk, a.Hkv, a.D, kTile) ||
-        !encode_bnhd(&mv, a.v, dtype, a.B, a.Nk, a.Hkv, a.D, kTile))
+        !encode_bnhd(&mk, a.k, dtype, a.B, a.Nk, a.Hkv, a.D, C::kTile) ||
+        !encode_bnhd(&mv, a.v, dtype, a.B, a.Nk, a.Hkv, a.D, C::kTile))
       return KF_ERR_CUDA;
     auto kernel = fa_bwd_dq_sm100_kernel<T, D>;
     const int prep = kf_host::prepare_kernel(reinterpret_cast<const void*>(kernel), kThreads, C::kSmemBytes, nullptr);
@@ -528,13 +564,14 @@ int launch(const BwdArgs& a, int dtype, cudaStream_t stream) {
     CUtensorMap mk, mv, mq, mdo;
     if (!encode_bnhd(&mk, a.k, dtype, a.B, a.Nk, a.Hkv, a.D, kRows) ||
         !encode_bnhd(&mv, a.v, dtype, a.B, a.Nk, a.Hkv, a.D, kRows) ||
-        !encode_bnhd(&mq, a.q, dtype, a.B, a.Nq, a.Hq, a.D, kTile) ||
-        !encode_bnhd(&mdo, a.dout, dtype, a.B, a.Nq, a.Hq, a.D, kTile))
+        !encode_bnhd(&mq, a.q, dtype, a.B, a.Nq, a.Hq, a.D, C::kTile) ||
+        !encode_bnhd(&mdo, a.dout, dtype, a.B, a.Nq, a.Hq, a.D, C::kTile))
       return KF_ERR_CUDA;
     auto kernel = fa_bwd_dkdv_sm100_kernel<T, D>;
     const int prep = kf_host::prepare_kernel(reinterpret_cast<const void*>(kernel), kThreads, C::kSmemBytes, nullptr);
     if (prep != KF_OK) return prep;
-    kernel<<<dim3((a.Nk + kRows - 1) / kRows, a.Hkv, a.B), kThreads, C::kSmemBytes, stream>>>(mk, mv, mq, mdo, a);
+    kernel<<<dim3((a.Nk + kRows - 1) / kRows * C::kHalves, a.Hkv, a.B), kThreads, C::kSmemBytes, stream>>>(
+        mk, mv, mq, mdo, a);
     KF_LAUNCH_CHECK();
   }
   return KF_OK;
@@ -555,12 +592,16 @@ int kf_internal_fa_bwd_error(unsigned int* code) {
 
 namespace kf::fa {
 
-// Head dims up to 128: 8..56 run the D = 64 kernels and 72..120 the D = 128 kernels on
-// zero-padded tiles.
-bool sm100_bwd_supported(const BwdArgs& a) { return a.D >= 8 && a.D <= 128; }
+// Head dims up to 256: 8..56 run the D = 64 kernels, 72..120 the D = 128 kernels and 136..248
+// the D = 256 kernels on zero-padded tiles.
+bool sm100_bwd_supported(const BwdArgs& a) { return a.D >= 8 && a.D <= 256; }
 
 int launch_sm100_bwd(const BwdArgs& a, int dtype, cudaStream_t s) {
-  if (dtype == KF_DTYPE_BF16) return a.D <= 64 ? launch<__nv_bfloat16, 64>(a, dtype, s) : launch<__nv_bfloat16, 128>(a, dtype, s);
+  if (dtype == KF_DTYPE_BF16) {
+    if (a.D > 128) return launch<__nv_bfloat16, 256>(a, dtype, s);
+    return a.D <= 64 ? launch<__nv_bfloat16, 64>(a, dtype, s) : launch<__nv_bfloat16, 128>(a, dtype, s);
+  }
+  if (a.D > 128) return launch<__half, 256>(a, dtype, s);
   return a.D <= 64 ? launch<__half, 64>(a, dtype, s) : launch<__half, 128>(a, dtype, s);
 }
 
