@@ -1024,6 +1024,8 @@ def proj_cpu_baseline(C, seconds=5.0):
 FA_CONFIGS = (
     {"name": "fajvp_d64", "B": 4, "H": 16, "N": 4096, "D": 64},
     {"name": "fajvp_d128", "B": 4, "H": 16, "N": 4096, "D": 128},
+    # The reference harness's largest head dim (flash_attention_jvp/test.py allows D <= 256).
+    {"name": "fajvp_d256", "B": 2, "H": 16, "N": 4096, "D": 256},
 )
 FA_SMALL = (
     {"name": "fajvp_d64", "B": 1, "H": 8, "N": 4096, "D": 64},

@@ -21,6 +21,12 @@ int validate(const void* q, const void* k, const void* v, int64_t B, int64_t Nq,
 
 bool aligned16(const void* p) { return p == nullptr || kf::aligned(p, 16); }
 
+// A JVP with every tangent missing is the zero tangent: tO = 0 exactly, no kernel needed.
+int zero_tangent(const FaArgs& a, cudaStream_t stream) {
+  const size_t bytes = static_cast<size_t>(a.B) * a.Nq * a.Hq * a.D * 2;
+  return cudaMemsetAsync(a.to_out, 0, bytes, stream) == cudaSuccess ? KF_OK : KF_ERR_CUDA;
+}
+
 FaArgs make_args(const void* q, const void* k, const void* v, const void* tq, const void* tk,
                  const void* tv, int64_t B, int64_t Nq, int64_t Nk, int64_t Hq, int64_t Hkv,
                  int64_t D, float scale, int causal) {
@@ -51,7 +57,7 @@ KF_API int kf_fa_fwd(const void* q, const void* k, const void* v, void* out, flo
   a.lse_out = lse;
   if (kf::fa::sm100_fused_supported(a, kf::fa::kModeFwd))
     return kf::fa::launch_sm100_fused(a, kf::fa::kModeFwd, dtype, static_cast<cudaStream_t>(stream));
-  return kf::fa::launch_general(a, kf::fa::kModeFwd, dtype, static_cast<cudaStream_t>(stream));
+  return KF_ERR_UNSUPPORTED;
 }
 
 KF_API int kf_fa_jvp(const void* q, const void* k, const void* v, const void* tq, const void* tk,
@@ -70,9 +76,10 @@ KF_API int kf_fa_jvp(const void* q, const void* k, const void* v, const void* tq
   a.o_in = out;
   a.lse_in = lse;
   a.to_out = tangent_out;
+  if (tq == nullptr && tk == nullptr && tv == nullptr) return zero_tangent(a, static_cast<cudaStream_t>(stream));
   if (kf::fa::sm100_jvp_supported(a))
     return kf::fa::launch_sm100_jvp(a, dtype, static_cast<cudaStream_t>(stream));
-  return kf::fa::launch_general(a, kf::fa::kModeJvp, dtype, static_cast<cudaStream_t>(stream));
+  return KF_ERR_UNSUPPORTED;
 }
 
 KF_API int kf_fa_fwd_jvp(const void* q, const void* k, const void* v, const void* tq,
@@ -91,18 +98,18 @@ KF_API int kf_fa_fwd_jvp(const void* q, const void* k, const void* v, const void
   a.o_out = out;
   a.lse_out = lse;
   a.to_out = tangent_out;
-  if (kf::fa::sm100_fused_supported(a, kf::fa::kModeFwdJvp))
-    return kf::fa::launch_sm100_fused(a, kf::fa::kModeFwdJvp, dtype, static_cast<cudaStream_t>(stream));
-  if (kf::fa::sm100_fused_supported(a, kf::fa::kModeFwd) && kf::fa::sm100_jvp_supported(a)) {
-    // Head dims 136..256: tensor memory holds one D = 256 accumulator, not O and tO together, so
-    // the forward (O, LSE) runs first and the standalone JVP reads them back.
-    st = kf::fa::launch_sm100_fused(a, kf::fa::kModeFwd, dtype, static_cast<cudaStream_t>(stream));
-    if (st != KF_OK) return st;
-    a.o_in = out;
-    a.lse_in = lse;
-    return kf::fa::launch_sm100_jvp(a, dtype, static_cast<cudaStream_t>(stream));
-  }
-  return kf::fa::launch_general(a, kf::fa::kModeFwdJvp, dtype, static_cast<cudaStream_t>(stream));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (kf::fa::sm100_fused_supported(a, kf::fa::kModeFwdJvp)) return kf::fa::launch_sm100_fused(a, kf::fa::kModeFwdJvp, dtype, s);
+  if (!kf::fa::sm100_fused_supported(a, kf::fa::kModeFwd)) return KF_ERR_UNSUPPORTED;
+  // Otherwise the forward (O, LSE) runs first: every tangent missing (tO = 0), or head dims
+  // 136..256, where tensor memory holds one D = 256 accumulator, not O and tO together, and the
+  // standalone JVP reads O and LSE back.
+  st = kf::fa::launch_sm100_fused(a, kf::fa::kModeFwd, dtype, s);
+  if (st != KF_OK) return st;
+  if (tq == nullptr && tk == nullptr && tv == nullptr) return zero_tangent(a, s);
+  a.o_in = out;
+  a.lse_in = lse;
+  return kf::fa::sm100_jvp_supported(a) ? kf::fa::launch_sm100_jvp(a, dtype, s) : KF_ERR_UNSUPPORTED;
 }
 
 KF_API size_t kf_fa_bwd_workspace_size(int64_t batch, int64_t q_heads, int64_t q_len) {

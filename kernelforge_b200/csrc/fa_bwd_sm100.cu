@@ -1,12 +1,13 @@
 // FlashAttention backward (reverse-mode VJP) on the 5th-generation tensor cores
-// (tcgen05 + TMEM + TMA), head dims up to 128 (other than 64 and 128 on zero-padded tiles),
-// fp16 / bf16, causal (bottom-right), GQA.
+// (tcgen05 + TMEM + TMA), head dims up to 256 (other than 64, 128 and 256 on zero-padded
+// tiles), fp16 / bf16, causal (bottom-right), GQA.
 //
 // Replaces the flash_attn binary's _flash_attn_backward that FlashAttentionFunction.backward
 // calls (flash_attention_jvp/custom.py:255-266). After the row-statistics pass of fa_bwd.cu
 // (row_nlse = -LSE log2 e, row_ndelta = -rowsum(dO O), padded), two kernels, no atomics:
 //
 //   dq kernel    query-stationary: 128 query rows of one (batch, head) per CTA, 64-key tiles
+//                (32-key tiles at D = 256)
 //                  S  = Q K^T,  dP = dO V^T           score MMAs into three TMEM buffers
 //                  P  = 2^(S gamma log2 e - LSE log2 e),  dS = P (dP - delta)
 //                  dQ += dS K                          A = dS (16-bit, TMEM), B = K (MN-major)

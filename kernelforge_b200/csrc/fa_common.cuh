@@ -52,8 +52,8 @@ struct BwdArgs {
   int causal;
 };
 
-// Row statistics, then dQ, dK, dV (deterministic; no atomics). D up to 128 runs on the tcgen05
-// kernels (zero-padded to 64 or 128), D in 136..256 on the mma.sync ones.
+// Row statistics, then dQ, dK, dV (deterministic; no atomics) on the tcgen05 kernels: head dims
+// up to 256, zero-padded to 64, 128 or 256.
 int launch_bwd(const BwdArgs& a, int dtype, cudaStream_t stream);
 bool sm100_bwd_supported(const BwdArgs& a);
 int launch_sm100_bwd(const BwdArgs& a, int dtype, cudaStream_t stream);
@@ -71,56 +71,13 @@ inline bool encode_bnhd(CUtensorMap* map, const void* base, int dtype, int B, in
                                CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-// cp.async tiles in shared memory for the mma.sync kernels: rows of DP elements at a pitch of a
-// multiple of 64 elements, 16-byte chunk c of row r stored at chunk (c ^ (r & 7)) so that
-// ldmatrix reads are free of bank conflicts.
-namespace tile {
-
-__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
-               "r"(valid ? 16 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
-// Row pitch (elements) of a shared tile: >= 64 and a multiple of 64 so that 16-byte chunk c of
-// row r can be stored at chunk (c ^ (r & 7)) without bank conflicts for ldmatrix.
-template <int DP> struct Pitch { static constexpr int value = DP <= 64 ? 64 : (DP + 63) / 64 * 64; };
-
-template <int PITCH>
-__device__ __forceinline__ uint32_t tile_off(int row, int chunk) {  // bytes
-  return static_cast<uint32_t>(row * PITCH * 2 + ((chunk ^ (row & 7)) << 4));
-}
-
-// cp.async a [nrows x DP] tile (rows `row0..`, stride `stride` elements) into swizzled smem;
-// rows >= rows_valid and columns >= D are zero-filled.
-template <typename T, int DP, int NT>
-__device__ __forceinline__ void load_tile(uint32_t smem, const T* __restrict__ base, int64_t stride,
-                                          int nrows, int rows_valid, int D) {
-  constexpr int kChunks = DP / 8;
-  constexpr int kPitch = Pitch<DP>::value;
-  for (int i = threadIdx.x; i < nrows * kChunks; i += NT) {
-    const int r = i / kChunks, c = i % kChunks;
-    const bool valid = r < rows_valid && c * 8 < D;
-    const T* src = valid ? base + r * stride + c * 8 : base;
-    cp_async_16(smem + tile_off<kPitch>(r, c), src, valid);
-  }
-}
-
-}  // namespace tile
-
-// mma.sync path: any D in 8..256 (multiple of 8), fp16 / bf16.
-int launch_general(const FaArgs& a, int mode, int dtype, cudaStream_t stream);
-
-// tcgen05 / TMEM / TMA path of the standalone JVP: D up to 128 (zero-padded to 64 or 128), at
-// least one tangent.
+// tcgen05 / TMEM / TMA path of the standalone JVP: D up to 256 (zero-padded to 64, 128 or 256),
+// at least one tangent.
 bool sm100_jvp_supported(const FaArgs& a);
 int launch_sm100_jvp(const FaArgs& a, int dtype, cudaStream_t stream);
 
-// tcgen05 / TMEM / TMA path of the forward (kModeFwd) and one-pass forward + JVP
-// (kModeFwdJvp): D up to 128; the one-pass mode needs at least one tangent.
+// tcgen05 / TMEM / TMA path of the forward (kModeFwd, D up to 256) and one-pass forward + JVP
+// (kModeFwdJvp, D up to 128, at least one tangent).
 bool sm100_fused_supported(const FaArgs& a, int mode);
 int launch_sm100_fused(const FaArgs& a, int mode, int dtype, cudaStream_t stream);
 

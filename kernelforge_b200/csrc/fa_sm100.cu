@@ -1,4 +1,5 @@
-// FlashAttention forward-mode JVP on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+// FlashAttention forward-mode JVP and forward on the 5th-generation tensor cores (tcgen05 + TMEM
+// + TMA), head dims up to 256.
 //
 // Standalone JVP from a cached O and LSE (flash_attention_jvp/custom.py:12-120):
 //   P  = exp(gamma * Q K^T - LSE)                     (keys masked to 0)
@@ -879,9 +880,9 @@ int kf_internal_fa_error(unsigned int* code) {
 
 namespace kf::fa {
 
-// Head dims up to 128 (multiples of 8): 8..56 run the D = 64 kernels and 72..120 the D = 128
-// kernels on zero-padded tiles (TMA fills the columns past D with zeros; the epilogues store
-// only real columns). The forward alone also runs 136..248 on the D = 256 kernel.
+// Head dims (multiples of 8): 8..56 run the D = 64 kernels, 72..120 the D = 128 kernels and
+// 136..248 the D = 256 kernels on zero-padded tiles (TMA fills the columns past D with zeros;
+// the epilogues store only real columns). The one-pass forward + JVP kernel stops at 128.
 bool sm100_head_dim(int d) { return d >= 8 && d <= 128; }
 
 bool sm100_jvp_supported(const FaArgs& a) {
