@@ -1030,6 +1030,7 @@ FA_CONFIGS = (
 FA_SMALL = (
     {"name": "fajvp_d64", "B": 1, "H": 8, "N": 4096, "D": 64},
     {"name": "fajvp_d128", "B": 1, "H": 8, "N": 4096, "D": 128},
+    {"name": "fajvp_d256", "B": 1, "H": 8, "N": 4096, "D": 256},
 )
 
 
