@@ -258,7 +258,9 @@ int kf_fa_jvp(const void* q, const void* k, const void* v, const void* tq, const
 /* One-pass forward + JVP (O, LSE and tO with online recurrences; six GEMMs per key tile).
  * Replaces the native forward followed by the JVP launch that torch.func.jvp of
  * flash_attention performs (flash_attention_jvp/custom.py:226-291), fused as
- * flash-attention-jvp-derivation.md sections 7-8 describe. */
+ * flash-attention-jvp-derivation.md sections 7-8 describe. For head dims above 128 (tensor
+ * memory holds O's accumulator or tO's, not both) it runs the forward and then the standalone
+ * JVP on the same stream; with every tangent NULL, the forward and tO = 0. */
 int kf_fa_fwd_jvp(const void* q, const void* k, const void* v, const void* tq, const void* tk,
                   const void* tv, void* out, float* lse, void* tangent_out,
                   int64_t batch, int64_t q_len, int64_t k_len, int64_t q_heads, int64_t kv_heads,
