@@ -54,7 +54,6 @@ constexpr float kLog2e = 1.4426950408889634f;
 // The standalone JVP at D = 256 (128 KB of Q and tQ) takes 32-key tiles, two K stages and one V
 // stage: 224 KB.
 template <int D, bool kTan = true, int BN = kBN> struct Cfg {
-  static constexpr int kKeys = BN;
   static constexpr int kKB = D / 64;                    // 128-byte boxes along the head dim
   static constexpr int kQBytes = kKB * kBM * 128;       // Q or tQ
   static constexpr int kTileBytes = kKB * BN * 128;     // K, tK, V or tV of one tile

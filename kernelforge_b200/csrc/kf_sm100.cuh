@@ -359,6 +359,11 @@ template <> struct Mma<__nv_bfloat16> {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
   }
+  // Exactly rounded (round to nearest even) products of two packed pairs.
+  static __device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t b) {
+    __nv_bfloat162 x = __hmul2(*reinterpret_cast<__nv_bfloat162*>(&a), *reinterpret_cast<__nv_bfloat162*>(&b));
+    return *reinterpret_cast<uint32_t*>(&x);
+  }
 };
 template <> struct Mma<__half> {
   static __device__ __forceinline__ void run(float* d, const uint32_t* a, const uint32_t* b) {
@@ -379,6 +384,10 @@ template <> struct Mma<__half> {
   static __device__ __forceinline__ uint32_t from_f2(float a, float b) {
     __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
+  }
+  static __device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t b) {
+    __half2 x = __hmul2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+    return *reinterpret_cast<uint32_t*>(&x);
   }
 };
 

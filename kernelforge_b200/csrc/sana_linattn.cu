@@ -123,12 +123,21 @@ struct QkNorm {
   int npad;            // tokens per batch in `stats` (N rounded up to kStatsPad)
 };
 
-// Two packed 16-bit values through the reference's two roundings: cast(cast(x r) w).
+// Two packed 16-bit values through the reference's two roundings: cast(cast(x r) w). The
+// second is the product of two 16-bit values, exact in fp32 and rounded once to the dtype:
+// exactly what a packed 16-bit multiply returns, so w2 (the two weights, packed) multiplies
+// the packed normalised values directly.
 template <typename T>
-__device__ __forceinline__ uint32_t qk_apply2(uint32_t v, float r0, float r1, float w0, float w1) {
+__device__ __forceinline__ uint32_t qk_apply2(uint32_t v, float r0, float r1, uint32_t w2) {
   const float2 x = kf::Mma<T>::to_f2(v);
-  const float2 n = kf::Mma<T>::to_f2(kf::Mma<T>::from_f2(x.x * r0, x.y * r1));
-  return kf::Mma<T>::from_f2(n.x * w0, n.y * w1);
+  const float2 n = kf::f2_unpack(kf::f2_mul(kf::f2_pack(x.x, x.y), kf::f2_pack(r0, r1)));
+  return kf::Mma<T>::mul2(kf::Mma<T>::from_f2(n.x, n.y), w2);
+}
+// A 16-bit weight in both halves of a packed pair.
+template <typename T>
+__device__ __forceinline__ uint32_t weight_pair(const void* w, int c) {
+  const uint32_t h = static_cast<const unsigned short*>(w)[c];
+  return h | (h << 16);
 }
 template <typename T>
 __device__ __forceinline__ float qk_apply1(float x, float r, float w) {
@@ -158,9 +167,9 @@ __device__ __forceinline__ void qk_norm_k(uint32_t (&bf)[4][2], const QkNorm& n,
   const float2 ra = stats_pair(n, b, t0 + 2 * tig, 1), rb = stats_pair(n, b, t0 + 8 + 2 * tig, 1);
 #pragma unroll
   for (int nt = 0; nt < 4; ++nt) {
-    const float w = weight_at<T>(n.wk, h * kD + nt * 8 + gid);
-    bf[nt][0] = qk_apply2<T>(bf[nt][0], ra.x, ra.y, w, w);
-    bf[nt][1] = qk_apply2<T>(bf[nt][1], rb.x, rb.y, w, w);
+    const uint32_t w = weight_pair<T>(n.wk, h * kD + nt * 8 + gid);
+    bf[nt][0] = qk_apply2<T>(bf[nt][0], ra.x, ra.y, w);
+    bf[nt][1] = qk_apply2<T>(bf[nt][1], rb.x, rb.y, w);
   }
 }
 
@@ -174,12 +183,12 @@ __device__ __forceinline__ void qk_norm_q(uint32_t (&a)[2][4], const QkNorm& n, 
   const T* w = static_cast<const T*>(n.wq) + h * kD + 2 * tig;
 #pragma unroll
   for (int ks = 0; ks < 2; ++ks) {
-    const float2 lo = kf::Mma<T>::to_f2(__ldg(reinterpret_cast<const unsigned int*>(w + ks * 16)));
-    const float2 hi = kf::Mma<T>::to_f2(__ldg(reinterpret_cast<const unsigned int*>(w + ks * 16 + 8)));
-    a[ks][0] = qk_apply2<T>(a[ks][0], r0, r0, lo.x, lo.y);
-    a[ks][1] = qk_apply2<T>(a[ks][1], r8, r8, lo.x, lo.y);
-    a[ks][2] = qk_apply2<T>(a[ks][2], r0, r0, hi.x, hi.y);
-    a[ks][3] = qk_apply2<T>(a[ks][3], r8, r8, hi.x, hi.y);
+    const uint32_t lo = __ldg(reinterpret_cast<const unsigned int*>(w + ks * 16));
+    const uint32_t hi = __ldg(reinterpret_cast<const unsigned int*>(w + ks * 16 + 8));
+    a[ks][0] = qk_apply2<T>(a[ks][0], r0, r0, lo);
+    a[ks][1] = qk_apply2<T>(a[ks][1], r8, r8, lo);
+    a[ks][2] = qk_apply2<T>(a[ks][2], r0, r0, hi);
+    a[ks][3] = qk_apply2<T>(a[ks][3], r8, r8, hi);
   }
 }
 
@@ -682,12 +691,10 @@ sana_out_tc(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ C
             // channels 8 j .. 8 j + 7 of the head (a head past H is all zero: weights unread)
             const uint4 wv = head < H ? __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(nrm.wq) + head * kD) + j)
                                       : make_uint4(0, 0, 0, 0);
-            const float2 w0 = kf::Mma<T>::to_f2(wv.x), w1 = kf::Mma<T>::to_f2(wv.y);
-            const float2 w2 = kf::Mma<T>::to_f2(wv.z), w3 = kf::Mma<T>::to_f2(wv.w);
-            x.x = qk_apply2<T>(x.x, rq, rq, w0.x, w0.y);
-            x.y = qk_apply2<T>(x.y, rq, rq, w1.x, w1.y);
-            x.z = qk_apply2<T>(x.z, rq, rq, w2.x, w2.y);
-            x.w = qk_apply2<T>(x.w, rq, rq, w3.x, w3.y);
+            x.x = qk_apply2<T>(x.x, rq, rq, wv.x);
+            x.y = qk_apply2<T>(x.y, rq, rq, wv.y);
+            x.z = qk_apply2<T>(x.z, rq, rq, wv.z);
+            x.w = qk_apply2<T>(x.w, rq, rq, wv.w);
           }
           w[4 * j + 0] = kf::Mma<T>::relu2(x.x);
           w[4 * j + 1] = kf::Mma<T>::relu2(x.y);
