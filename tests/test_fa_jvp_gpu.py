@@ -277,6 +277,9 @@ def test_missing_and_value_only_tangents(fa, dtype):
     # A missing tangent and an explicit zero tangent agree exactly.
     zeros = fa.flash_attention_jvp(q, k, v, torch.zeros_like(q), torch.zeros_like(k), tv, out, lse)
     torch.testing.assert_close(zeros, expected, atol=0, rtol=0)
+    # Every tangent missing in the one-pass entry point: the forward, and tO = 0.
+    out2, lse2, none = fa.flash_attention_fwd_jvp(q, k, v, None, None, None)
+    assert torch.equal(out2, out) and torch.equal(lse2, lse) and torch.count_nonzero(none) == 0
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
