@@ -43,6 +43,7 @@ constexpr int kPvWarp = 10;     // issues the output MMAs
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAccCol = 0;
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kMaxScoreBufs = 3;
 
 // Shared-memory plan: Q, tQ once; a ring of {K, tK} stages (a stage is free again once the
 // tile's score MMAs complete: k_empty) and a separate ring of {V, tV} stages (free once the
@@ -62,7 +63,9 @@ template <int D, bool kTan = true, int BN = kBN> struct Cfg {
   // box kb of K and of tK together are the 128 rows of one N = 128 operand [K ; tK].
   static constexpr int kKPair = kTan ? 2 * kKBox : kKBox;  // K box kb to K box kb + 1
   static constexpr int kStageBytes = kTan ? 2 * kTileBytes : kTileBytes;  // {K, tK} or {V, tV}
-  static constexpr int kKStages = D == 64 ? 4 : 2;
+  // The forward at D = 128 takes three K stages (the one-pass kernel's three score buffers need
+  // as many: a buffer's "free" arrival for tile j + 3 lands in that tile's K stage).
+  static constexpr int kKStages = D == 64 ? 4 : (D == 128 && !kTan ? 3 : 2);
   static constexpr int kVStages = D == 64 ? 4 : (D == 256 && kTan ? 1 : 2);
   static constexpr int kKOffset = kTan ? 2 * kQBytes : kQBytes;
   static constexpr int kVOffset = kKOffset + kKStages * kStageBytes;
@@ -71,8 +74,8 @@ template <int D, bool kTan = true, int BN = kBN> struct Cfg {
   // accumulators below kBufCol.
   static constexpr uint32_t kBufCol = D <= 128 ? 128 : 256;
   static constexpr int kScratchOffset = kBarOffset + 512;  // row statistics
-  // [2][kBM] row sums (standalone JVP) or [6][kBM] maxima and sums (one-pass kernel)
-  static constexpr int kScratchBytes = (D == 256 && kTan ? 2 : 6) * kBM * 4;
+  // [2][kBM] row sums (standalone JVP) or [8][kBM] maxima and sums (one-pass kernel)
+  static constexpr int kScratchBytes = (D == 256 && kTan ? 2 : 8) * kBM * 4;
   static constexpr int kSmemBytes = kScratchOffset + kScratchBytes + 64 + 1024;  // + abort flag, slack
   static_assert(kSmemBytes <= 232448, "shared memory");
 };
@@ -84,9 +87,9 @@ template <int D, bool kTan = true, int BN = kBN> struct Bars {
   uint64_t* k_empty;  // [kKStages] the score MMAs of the stage's tile completed
   uint64_t* v_full;   // [kVStages] V / tV of the stage's tile landed (+ v_extra arrivals)
   uint64_t* v_empty;  // [kVStages] the output MMAs of the stage's tile completed
-  uint64_t* s_full;   // [2] scores of tile j complete
-  uint64_t* p_full;   // [2] P / H of tile j written
-  uint64_t* pv_done;  // [2] output MMAs of tile j complete
+  uint64_t* s_full;   // [kMaxScoreBufs] scores of tile j complete
+  uint64_t* p_full;   // [kMaxScoreBufs] P / H of tile j written
+  uint64_t* pv_done;  // [kMaxScoreBufs] output MMAs of tile j complete
   uint64_t* acc_full;
   uint32_t* tmem_slot;
   __device__ explicit Bars(uint8_t* smem) {
@@ -97,9 +100,9 @@ template <int D, bool kTan = true, int BN = kBN> struct Bars {
     v_full = k_empty + C::kKStages;
     v_empty = v_full + C::kVStages;
     s_full = v_empty + C::kVStages;
-    p_full = s_full + 2;
-    pv_done = p_full + 2;
-    acc_full = pv_done + 2;
+    p_full = s_full + kMaxScoreBufs;
+    pv_done = p_full + kMaxScoreBufs;
+    acc_full = pv_done + kMaxScoreBufs;
     tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
   }
   // k_extra / v_extra: arrivals besides the producer's that complete a K or V stage. The kernels
@@ -116,7 +119,7 @@ template <int D, bool kTan = true, int BN = kBN> struct Bars {
       kf::mbar_init(&v_full[s], 1 + v_extra);
       kf::mbar_init(&v_empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kMaxScoreBufs; ++i) {
       kf::mbar_init(&s_full[i], 1);
       kf::mbar_init(&p_full[i], p_arrivals);
       kf::mbar_init(&pv_done[i], 1);
@@ -518,21 +521,28 @@ fa_jvp_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 // tile row maxima through shared memory. The reference max m only moves when a tile's max
 // exceeds it by more than 8 (a factor 256 in E); then the accumulators U, G of that row are
 // rescaled in TMEM after the previous tile's output MMAs have completed. Tensor memory:
-//   D = 128: [0, 128) G (tO accumulator) | [128, 384) S / dS double buffer | [384, 512) U
-//   D = 64:  [0, 64) U | [64, 128) G | [128, 384) S / dS double buffer
-//   D = 256 (forward only, head dims 136..256): [0, 256) U | [256, 512) S double buffer
+//   D = 128 + JVP: [0, 128) G (tO accumulator) | [128, 384) two S / dS buffers | [384, 512) U
+//   D = 128 forward: [0, 128) U | [128, 512) three S buffers
+//   D = 64:  [0, 64) U | [64, 128) G | [128, 512) three S / dS buffers
+//   D = 256 (forward only, head dims 136..256): [0, 256) U | [256, 512) two S buffers
 // P and H (16-bit) overwrite the first 16 columns of each warpgroup's 32-column S / dS half, so
-// tile j's score MMAs wait for tile j-2's output MMAs (same buffer).
+// tile j's score MMAs wait for tile j-NB's output MMAs (same buffer). With two buffers that
+// chain (scores, softmax, output MMAs, buffer free) set the period of the forward at D = 64;
+// three let the scores of tile j+2 run while tiles j and j+1 are in the softmax and output
+// stages.
 // The scores are issued as in the standalone kernel ([S | Q tK^T] = Q [K ; tK]^T, then
 // dS += tQ K^T). For D = 64 the output MMAs are merged the same way, since an N = 64 MMA runs at
 // 2/3 of the tensor core's rate: [U | G] += E [V | tV] (V, tV adjacent: two 64-wide MN blocks)
 // then G += H V. That takes U at [0, 64) and G at [64, 128), next to each other.
 // ============================================================================================
-template <int D>
+template <int D, bool kJvp>
 struct FusedCols {
   static constexpr bool kMerge = D == 64;
-  static constexpr uint32_t kU = D == 128 ? 384 : 0;  // U: E V
-  static constexpr uint32_t kG = kMerge ? 64 : 0;     // G: H V + E tV (the tO accumulator)
+  static constexpr uint32_t kU = D == 128 && kJvp ? 384 : 0;  // U: E V
+  static constexpr uint32_t kG = kMerge ? 64 : 0;             // G: H V + E tV (the tO accumulator)
+  // Score buffers at kBufCol + 128 b: three where the accumulators leave 384 columns (the
+  // forward at D = 64 and 128, forward + JVP at D = 64), else two.
+  static constexpr int kBufs = (D == 64 || (D == 128 && !kJvp)) ? 3 : 2;
 };
 constexpr float kRescaleThreshold = 8.f;  // log2 units
 
@@ -543,13 +553,15 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_tv,
                       const FaArgs p) {
   using C = Cfg<D, kJvp>;
+  constexpr int NB = FusedCols<D, kJvp>::kBufs;  // score buffers
+  static_assert(NB <= C::kKStages, "a buffer's free arrival for tile j + NB lands in that tile's K stage");
   static_assert(D <= 128 || !kJvp, "D = 256 tensor memory holds the forward's accumulator only");
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (kf::smem_u32(smem_raw) & 1023u)) & 1023u);
   const Bars<D, kJvp> bars(smem);
-  float* tile_max = reinterpret_cast<float*>(smem + C::kScratchOffset);  // [2 buffers][2 groups][kBM]
-  float* part_sums = tile_max + 4 * kBM;                                   // [2 groups][kBM]
+  float* tile_max = reinterpret_cast<float*>(smem + C::kScratchOffset);  // [NB buffers][2 groups][kBM]
+  float* part_sums = tile_max + 2 * NB * kBM;                              // [2 groups][kBM]
   volatile int* abort_flag = reinterpret_cast<volatile int*>(part_sums + 2 * kBM);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -564,9 +576,9 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
   const int ntiles = (k_end + kBN - 1) / kBN;
 
   if (threadIdx.x == 0) {
-    // The k_full phase of tile j completes when K / tK of tile j have landed AND tile j-2's output
-    // MMAs (which read the P / H written over score buffer j & 1) are done: the output thread
-    // commits to it. The v_full phase of tile j completes when V / tV of tile j have landed AND
+    // The k_full phase of tile j completes when K / tK of tile j have landed AND tile j-NB's
+    // output MMAs (which read the P / H written over score buffer j % NB) are done: the output
+    // thread commits to it. The v_full phase of tile j completes when V / tV of tile j have landed AND
     // every softmax thread has written tile j's P and H. p_full is not used here.
     bars.init(1, 1, 2 * kBM);
     *abort_flag = 0;
@@ -584,12 +596,12 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
                  q0, b, ntiles, abort_flag);
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
-      // Scores of tile j into buffer j & 1 once K of tile j has landed and tile j-2's output MMAs
+      // Scores of tile j into buffer j % NB once K of tile j has landed and tile j-NB's output MMAs
       // have consumed the P / H that overwrote that buffer (one barrier).
       const uint32_t q_addr = kf::smem_u32(smem), tq_addr = q_addr + C::kQBytes;
       bool ok = kf::mbar_wait_or_abort<true>(bars.q_full, 0, &g_fa_error, abort_flag);
       for (int j = 0; ok && j < ntiles; ++j) {
-        const int buf = j & 1, st = j % C::kKStages;
+        const int buf = j % NB, st = j % C::kKStages;
         if (!(ok = kf::mbar_wait_or_abort<true>(&bars.k_full[st], (j / C::kKStages) & 1, &g_fa_error, abort_flag)))
           break;
         kf::tc::fence_after_sync();
@@ -604,14 +616,13 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
     if (lane == 0) {
       constexpr uint32_t idPV = kf::tc::idesc_f16(kBf16 ? 1 : 0, kBM, D, false, true);
       constexpr uint32_t idPV2 = kf::tc::idesc_f16(kBf16 ? 1 : 0, kBM, 2 * D, false, true);
-      constexpr uint32_t kU = FusedCols<D>::kU, kG = FusedCols<D>::kG;
+      constexpr uint32_t kU = FusedCols<D, kJvp>::kU, kG = FusedCols<D, kJvp>::kG;
       uint32_t u_started = 0, g_started = 0;
       bool ok = true;
-      // Score buffers 0 and 1 start free: this thread's share of tiles 0 and 1's k_full phases.
-      kf::mbar_arrive(&bars.k_full[0]);
-      kf::mbar_arrive(&bars.k_full[1]);
+      // Score buffers start free: this thread's share of tiles 0 .. NB-1's k_full phases.
+      for (int t = 0; t < NB; ++t) kf::mbar_arrive(&bars.k_full[t]);
       for (int j = 0; ok && j < ntiles; ++j) {
-        const int buf = j & 1, st = j % C::kVStages;
+        const int buf = j % NB, st = j % C::kVStages;
         if (!(ok = kf::mbar_wait_or_abort<true>(&bars.v_full[st], (j / C::kVStages) & 1, &g_fa_error, abort_flag)))
           break;
         kf::tc::fence_after_sync();
@@ -623,7 +634,7 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
           // keys [16 kk, 16 kk + 16): warpgroup kk / 2 wrote them at columns 32 (kk / 2) + 8 (kk % 2)
           const uint32_t acol = (kk >> 1) * 32 + (kk & 1) * 8;
           const uint64_t vdesc = dsw(v_base, kk * 2048, kBN * 128);
-          if (FusedCols<D>::kMerge && has_tv) {
+          if (FusedCols<D, kJvp>::kMerge && has_tv) {
             // [U | G] += E [V | tV]: V and tV are the two 64-wide MN blocks of one operand
             kf::tc::mma_ts(tmem + kU, p_col + acol, dsw(v_base, kk * 2048, C::kTileBytes),
                            idPV2, u_started);
@@ -645,7 +656,7 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         }
         kf::tc::commit(&bars.pv_done[buf]);
         kf::tc::commit(&bars.v_empty[st]);
-        kf::tc::commit(&bars.k_full[(j + 2) % C::kKStages]);  // score buffer j & 1 is free for tile j+2
+        kf::tc::commit(&bars.k_full[(j + NB) % C::kKStages]);  // score buffer j % NB is free for tile j+NB
       }
       kf::tc::commit(bars.acc_full);
     }
@@ -662,8 +673,8 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
     const uint64_t c2 = kf::f2_pack(p.scale_log2, p.scale_log2), g2 = kf::f2_pack(p.scale, p.scale);
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
-      const int buf = j & 1;
-      if (ok) ok = kf::mbar_wait_or_abort(&bars.s_full[buf], (j >> 1) & 1, &g_fa_error, abort_flag);
+      const int buf = j % NB;
+      if (ok) ok = kf::mbar_wait_or_abort(&bars.s_full[buf], (j / NB) & 1, &g_fa_error, abort_flag);
       ok = __all_sync(0xffffffffu, ok);  // the tcgen05 copies below are .sync.aligned
       kf::tc::fence_after_sync();
       const uint32_t s_col = lane_base + C::kBufCol + 128 * buf + group * 32;
@@ -703,7 +714,7 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
             // Rescale the accumulators once the previous tile's output MMAs are done (rows
             // with no key seen yet hold zeros: alpha = 1).
             const float alpha = m_ref == -INFINITY ? 1.f : ex2(m_ref - m_new);
-            ok = __all_sync(0xffffffffu, kf::mbar_wait_or_abort(&bars.pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1,
+            ok = __all_sync(0xffffffffu, kf::mbar_wait_or_abort(&bars.pv_done[(j - 1) % NB], ((j - 1) / NB) & 1,
                                                                 &g_fa_error, abort_flag));
             kf::tc::fence_after_sync();
             if (ok) {
@@ -711,17 +722,17 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
               for (int c = 0; c < D / 64; ++c) {
                 const uint32_t col = (group * (D / 2)) + c * 32;
                 uint32_t ar[32];
-                kf::tc::ld_32x32b_x32(lane_base + FusedCols<D>::kU + col, ar);
+                kf::tc::ld_32x32b_x32(lane_base + FusedCols<D, kJvp>::kU + col, ar);
                 kf::tc::wait_ld();
 #pragma unroll
                 for (int i = 0; i < 32; ++i) ar[i] = __float_as_uint(__uint_as_float(ar[i]) * alpha);
-                kf::tc::st_32x32b_x32(lane_base + FusedCols<D>::kU + col, ar);
+                kf::tc::st_32x32b_x32(lane_base + FusedCols<D, kJvp>::kU + col, ar);
                 if (kJvp) {
-                  kf::tc::ld_32x32b_x32(lane_base + FusedCols<D>::kG + col, ar);
+                  kf::tc::ld_32x32b_x32(lane_base + FusedCols<D, kJvp>::kG + col, ar);
                   kf::tc::wait_ld();
 #pragma unroll
                   for (int i = 0; i < 32; ++i) ar[i] = __float_as_uint(__uint_as_float(ar[i]) * alpha);
-                  kf::tc::st_32x32b_x32(lane_base + FusedCols<D>::kG + col, ar);
+                  kf::tc::st_32x32b_x32(lane_base + FusedCols<D, kJvp>::kG + col, ar);
                 }
               }
             }
@@ -786,8 +797,8 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       for (int c = 0; c < D / 64; ++c) {
         const int col = group * (D / 2) + c * 32;
         uint32_t ur[32], gr[32];
-        kf::tc::ld_32x32b_x32(lane_base + FusedCols<D>::kU + col, ur);
-        if (kJvp) kf::tc::ld_32x32b_x32(lane_base + FusedCols<D>::kG + col, gr);
+        kf::tc::ld_32x32b_x32(lane_base + FusedCols<D, kJvp>::kU + col, ur);
+        if (kJvp) kf::tc::ld_32x32b_x32(lane_base + FusedCols<D, kJvp>::kG + col, gr);
         kf::tc::wait_ld();
         if (qrow < p.Nq) {
 #pragma unroll
