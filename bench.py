@@ -903,6 +903,8 @@ PROJ_ATTN_CONFIGS = (
     {"name": "sana_projattn_b1n1024", "B": 1, "N": 1024, "C": 1152},
     {"name": "sana_projattn_cfg2", "B": 2, "N": 16384, "C": 2240},
 )
+# ncu captures: half of config 2 (x 147 MB, above L2), one CTA wave of each kernel.
+PROJ_ATTN_SMALL = ({"name": "sana_projattn_b1n32768", "B": 1, "N": 32768, "C": 2240},)
 
 
 def bench_proj_attn(args, dist, peaks, peak_kind, cfg):
@@ -1450,7 +1452,7 @@ def main():
         for cfg in (PROJ_CONFIGS[:1] if CASE == "ncu-small" else PROJ_CONFIGS):
             workloads[cfg["name"]] = bench_proj(args, dist, peaks, peak_kind, cfg)
     if args.workload in ("all", "proj"):
-        for cfg in PROJ_ATTN_CONFIGS[: 1 if CASE == "ncu-small" else None]:
+        for cfg in (PROJ_ATTN_SMALL if CASE == "ncu-small" else PROJ_ATTN_CONFIGS):
             workloads[cfg["name"]] = bench_proj_attn(args, dist, peaks, peak_kind, cfg)
     if args.workload in ("all", "fajvp"):
         for cfg in (FA_SMALL if CASE == "ncu-small" else FA_CONFIGS):
