@@ -270,16 +270,23 @@ int kf_fa_fwd_jvp(const void* q, const void* k, const void* v, const void* tq, c
  *   P = exp(scale * Q K^T - LSE), dP = dO V^T, dS = P * (dP - rowsum(dO * O)),
  *   dQ = scale * dS K, dK = scale * dS^T Q, dV = P^T dO   (GQA: summed over the group).
  * Replaces flash_attn's _flash_attn_backward called by FlashAttentionFunction.backward
- * (flash_attention_jvp/custom.py:255-266). dq / dk / dv are written in full. The workspace
- * (kf_fa_bwd_workspace_size bytes, 16-byte aligned, contents ignored) holds two fp32 row
- * statistics per (batch, head, query), padded to a multiple of 128 queries: -LSE log2(e) and
- * -rowsum(dO * O).
- * Deterministic: no atomics. */
-size_t kf_fa_bwd_workspace_size(int64_t batch, int64_t q_heads, int64_t q_len);
+ * (flash_attention_jvp/custom.py:255-266), including its `deterministic` flag. dq / dk / dv are
+ * written in full. The workspace (kf_fa_bwd_workspace_size bytes for the same head_dim and
+ * deterministic, 16-byte aligned, contents ignored) holds two fp32 row statistics per (batch,
+ * head, query), padded to a multiple of 128 queries: -LSE log2(e) and -rowsum(dO * O); with
+ * deterministic = 0 and head_dim <= 128 also the fp32 dQ sums (64 or 128 per row).
+ * deterministic = 0: head dims up to 128 run one kernel for dQ, dK and dV whose dQ partials are
+ *   summed at L2, so dq may differ in the last bit from run to run (dk, dv do not), as with
+ *   flash_attn's deterministic=False, which the reference passes.
+ * deterministic != 0 (and head dims 136..256): separate dQ and dK / dV kernels, no atomics,
+ *   bitwise reproducible. */
+size_t kf_fa_bwd_workspace_size(int64_t batch, int64_t q_heads, int64_t q_len, int64_t head_dim,
+                                int deterministic);
 int kf_fa_bwd(const void* q, const void* k, const void* v, const void* out, const void* dout,
               const float* lse, void* dq, void* dk, void* dv, void* workspace, size_t workspace_bytes,
               int64_t batch, int64_t q_len, int64_t k_len, int64_t q_heads, int64_t kv_heads,
-              int64_t head_dim, float softmax_scale, int causal, int dtype, void* stream);
+              int64_t head_dim, float softmax_scale, int causal, int deterministic, int dtype,
+              void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

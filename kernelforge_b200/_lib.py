@@ -62,10 +62,10 @@ SIGNATURES = {
     "kf_fa_fwd_jvp": (ctypes.c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr,
                                      _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_float,
                                      ctypes.c_int, ctypes.c_int, _c_ptr]),
-    "kf_fa_bwd_workspace_size": (ctypes.c_size_t, [_c_i64, _c_i64, _c_i64]),
+    "kf_fa_bwd_workspace_size": (ctypes.c_size_t, [_c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int]),
     "kf_fa_bwd": (ctypes.c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr,
                                  ctypes.c_size_t, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_float,
-                                 ctypes.c_int, ctypes.c_int, _c_ptr]),
+                                 ctypes.c_int, ctypes.c_int, ctypes.c_int, _c_ptr]),
 }
 
 

@@ -112,22 +112,36 @@ KF_API int kf_fa_fwd_jvp(const void* q, const void* k, const void* v, const void
   return kf::fa::sm100_jvp_supported(a) ? kf::fa::launch_sm100_jvp(a, dtype, s) : KF_ERR_UNSUPPORTED;
 }
 
-KF_API size_t kf_fa_bwd_workspace_size(int64_t batch, int64_t q_heads, int64_t q_len) {
-  if (batch <= 0 || q_heads <= 0 || q_len <= 0) return 0;
+namespace {
+
+// Head dim of the fused kernel's dq_acc rows, or 0 when the separate (deterministic) kernels run.
+int64_t fused_dq_cols(int64_t head_dim, int deterministic) {
+  if (deterministic || head_dim > 128) return 0;
+  return head_dim <= 64 ? 64 : 128;
+}
+
+}  // namespace
+
+KF_API size_t kf_fa_bwd_workspace_size(int64_t batch, int64_t q_heads, int64_t q_len, int64_t head_dim,
+                                       int deterministic) {
+  if (batch <= 0 || q_heads <= 0 || q_len <= 0 || head_dim <= 0) return 0;
   const int64_t padded = (q_len + kf::fa::kBwdRowPad - 1) / kf::fa::kBwdRowPad * kf::fa::kBwdRowPad;
-  return 2 * static_cast<size_t>(batch) * q_heads * padded * sizeof(float);
+  const int64_t cols = 2 + fused_dq_cols(head_dim, deterministic);
+  return static_cast<size_t>(cols) * batch * q_heads * padded * sizeof(float);
 }
 
 KF_API int kf_fa_bwd(const void* q, const void* k, const void* v, const void* out, const void* dout,
                      const float* lse, void* dq, void* dk, void* dv, void* workspace, size_t workspace_bytes,
                      int64_t batch, int64_t q_len, int64_t k_len, int64_t q_heads, int64_t kv_heads,
-                     int64_t head_dim, float softmax_scale, int causal, int dtype, void* stream) {
+                     int64_t head_dim, float softmax_scale, int causal, int deterministic, int dtype,
+                     void* stream) {
   int st = validate(q, k, v, batch, q_len, k_len, q_heads, kv_heads, head_dim, softmax_scale, dtype);
   if (st != KF_OK) return st;
   if (out == nullptr || dout == nullptr || lse == nullptr || dq == nullptr || dk == nullptr || dv == nullptr ||
       workspace == nullptr)
     return KF_ERR_INVALID_ARGUMENT;
-  if (workspace_bytes < kf_fa_bwd_workspace_size(batch, q_heads, q_len)) return KF_ERR_WORKSPACE;
+  if (workspace_bytes < kf_fa_bwd_workspace_size(batch, q_heads, q_len, head_dim, deterministic))
+    return KF_ERR_WORKSPACE;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || !aligned16(dout) ||
       !aligned16(dq) || !aligned16(dk) || !aligned16(dv) || !kf::aligned(lse, 4) || !aligned16(workspace))
     return KF_ERR_MISALIGNED;
@@ -137,8 +151,11 @@ KF_API int kf_fa_bwd(const void* q, const void* k, const void* v, const void* ou
   a.B = static_cast<int>(batch); a.Nq = static_cast<int>(q_len); a.Nk = static_cast<int>(k_len);
   a.Hq = static_cast<int>(q_heads); a.Hkv = static_cast<int>(kv_heads); a.D = static_cast<int>(head_dim);
   a.NqP = (a.Nq + kf::fa::kBwdRowPad - 1) / kf::fa::kBwdRowPad * kf::fa::kBwdRowPad;
+  const int64_t rows = static_cast<int64_t>(a.B) * a.Hq * a.NqP;
   a.row_nlse = static_cast<float*>(workspace);
-  a.row_ndelta = a.row_nlse + static_cast<int64_t>(a.B) * a.Hq * a.NqP;
+  a.row_ndelta = a.row_nlse + rows;
+  a.Dp = static_cast<int>(fused_dq_cols(head_dim, deterministic));
+  a.dq_acc = a.Dp > 0 ? a.row_ndelta + rows : nullptr;  // 512-byte aligned: NqP is a multiple of 128
   a.scale = softmax_scale;
   a.scale_log2 = softmax_scale * 1.4426950408889634f;
   a.causal = causal ? 1 : 0;

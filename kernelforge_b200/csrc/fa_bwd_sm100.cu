@@ -4,7 +4,9 @@
 //
 // Replaces the flash_attn binary's _flash_attn_backward that FlashAttentionFunction.backward
 // calls (flash_attention_jvp/custom.py:255-266). After the row-statistics pass of fa_bwd.cu
-// (row_nlse = -LSE log2 e, row_ndelta = -rowsum(dO O), padded), two kernels, no atomics:
+// (row_nlse = -LSE log2 e, row_ndelta = -rowsum(dO O), padded), either one kernel that computes
+// dQ, dK and dV with dQ summed at L2 (fa_bwd_fused_sm100_kernel, head dims up to 128; the
+// default, as flash_attn's deterministic=False) or two kernels with no atomics (deterministic):
 //
 //   dq kernel    query-stationary: 128 query rows of one (batch, head) per CTA, 64-key tiles
 //                (32-key tiles at D = 256)
@@ -36,6 +38,12 @@ using kf::fa::BwdArgs;
 using kf::fa::encode_bnhd;
 
 __device__ unsigned int g_fa_bwd_error = 0;
+// The first bounded wait that gave up: role << 24 | tile (roles: 1 producer, 2 score MMAs,
+// 3 accumulating MMAs, 4 softmax, 5 epilogue, 6 dQ warps).
+__device__ unsigned int g_fa_bwd_where = 0;
+__device__ __forceinline__ void note_gave_up(unsigned int role, int t) {
+  atomicCAS(&g_fa_bwd_where, 0u, (role << 24) | (static_cast<unsigned int>(t) & 0xFFFFFFu));
+}
 
 constexpr int kRows = 128;     // stationary rows per CTA
 constexpr int kThreads = 352;  // 11 warps
@@ -49,19 +57,16 @@ constexpr uint32_t kTmemCols = 512;
 // D = 256: the stationary pair takes 128 KB, so the streamed tiles are 32 rows (3 stages of
 // 2 x 16 KB), and the dK / dV accumulators (2 x 256 columns together) are split by head-dim
 // halves over two CTAs per key block, each recomputing the key block's scores.
-template <int D> struct Cfg {
+// kFused (D <= 128): after the barriers, one 16-bit dS^T tile per score buffer (the dQ MMAs'
+// B operand) and the fp32 dQ tile staged for its reduction into dq_acc.
+template <int D, bool kFused = false> struct Cfg {
   static constexpr int kTile = D <= 128 ? 64 : 32;       // streamed rows per tile
   static constexpr int kKB = D / 64;                     // 128-byte boxes along the head dim
   static constexpr int kStatBytes = kKB * kRows * 128;   // one stationary operand
   static constexpr int kTileBytes = kKB * kTile * 128;   // one streamed operand tile
   static constexpr int kStages = D == 64 ? 4 : 3;
-  static constexpr int kRingOffset = 2 * kStatBytes;
-  static constexpr int kRowStatOffset = kRingOffset + kStages * 2 * kTileBytes;
-  static constexpr int kBarOffset = kRowStatOffset + kStages * 2 * kTile * 4;
-  static constexpr int kSmemBytes = kBarOffset + 256 + 1024;  // + alignment slack
-  static_assert(kSmemBytes <= 232448, "shared memory");
   static constexpr int kBufCols = 2 * kTile;             // S and dP (or S^T and dP^T) of a buffer
-  // Score buffers may not outnumber ring stages: a buffer's "free" commit for tile t + bufs
+  // Score buffers may not outnumber ring stages: a buffer's "free" arrival for tile t + bufs
   // must land in that tile's phase of its stage.
   static constexpr uint32_t kDqBuf = D <= 128 ? 128 : 256;  // dQ accumulator below it
   static constexpr int kDqBufs = (512 - kDqBuf) / kBufCols < kStages ? (512 - kDqBuf) / kBufCols : kStages;
@@ -70,6 +75,14 @@ template <int D> struct Cfg {
   static constexpr uint32_t kDkdvBuf = 2 * kAccN;        // dV at 0, dK at kAccN
   static constexpr int kDkdvBufs =
       (512 - kDkdvBuf) / kBufCols < kStages ? (512 - static_cast<int>(kDkdvBuf)) / kBufCols : kStages;
+  static constexpr int kRingOffset = 2 * kStatBytes;
+  static constexpr int kRowStatOffset = kRingOffset + kStages * 2 * kTileBytes;
+  static constexpr int kBarOffset = kRowStatOffset + kStages * 2 * kTile * 4;
+  static constexpr int kDsBytes = kRows * kTile * 2;
+  static constexpr int kDsOffset = (kBarOffset + 256 + 1023) / 1024 * 1024;
+  static constexpr int kDqStageOffset = kDsOffset + kDkdvBufs * kDsBytes;
+  static constexpr int kSmemBytes = (kFused ? kDqStageOffset + kTile * D * 4 : kBarOffset + 256) + 1024;  // + alignment slack
+  static_assert(kSmemBytes <= 232448, "shared memory");
 };
 constexpr int kMaxBufs = 3;
 
@@ -80,6 +93,8 @@ template <int D> struct Bars {
   uint64_t* s_full;      // [kMaxBufs] score MMAs of tile t complete
   uint64_t* p_full;      // [kMaxBufs] softmax of tile t done (scores read, 16-bit operands written)
   uint64_t* acc_full;
+  uint64_t* dq_full;     // [kMaxBufs] fused kernel: the dQ^T MMAs of tile t complete
+  uint64_t* drain;       // both MMA-issuing threads' MMAs complete (before TMEM is freed)
   uint32_t* tmem_slot;
   int* abort_flag;
   __device__ explicit Bars(uint8_t* smem) {
@@ -90,23 +105,28 @@ template <int D> struct Bars {
     s_full = ring_empty + C::kStages;
     p_full = s_full + kMaxBufs;
     acc_full = p_full + kMaxBufs;
-    tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+    dq_full = acc_full + 1;
+    drain = dq_full + kMaxBufs;
+    tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
   }
-  __device__ void init() const {
+  // buffer_arrivals: how many arrivals free a score buffer (the accumulating thread's commit,
+  // or the fused kernel's four dQ warps), besides the producer's, so the score thread waits on
+  // one barrier per tile.
+  __device__ void init(uint32_t buffer_arrivals) const {
     using C = Cfg<D>;
     kf::mbar_init(stat_full, 1);
     for (int s = 0; s < C::kStages; ++s) {
-      // Two arrivals: the producer's (with the TMA bytes) and the accumulating thread's commit
-      // that frees the tile's score buffer, so the score thread waits on one barrier per tile.
-      kf::mbar_init(&ring_full[s], 2);
+      kf::mbar_init(&ring_full[s], 1 + buffer_arrivals);
       kf::mbar_init(&ring_empty[s], 1);
     }
     for (int i = 0; i < kMaxBufs; ++i) {
       kf::mbar_init(&s_full[i], 1);
       kf::mbar_init(&p_full[i], 2 * kRows);  // both softmax warpgroups
+      kf::mbar_init(&dq_full[i], 1);
     }
     kf::mbar_init(acc_full, 1);
+    kf::mbar_init(drain, 2);
     *abort_flag = 0;
   }
 };
@@ -136,8 +156,10 @@ __device__ void produce(const Bars<D>& bars, uint8_t* smem, const CUtensorMap* t
   for (int t = 0; t < ntiles; ++t) {
     const int st = t % C::kStages;
     if (t >= C::kStages &&
-        !kf::mbar_wait_or_abort<true>(&bars.ring_empty[st], ((t / C::kStages) - 1) & 1, &g_fa_bwd_error, abort))
+        !kf::mbar_wait_or_abort<true>(&bars.ring_empty[st], ((t / C::kStages) - 1) & 1, &g_fa_bwd_error, abort)) {
+      note_gave_up(1, t);
       return;
+    }
     uint8_t* base = smem + C::kRingOffset + st * 2 * C::kTileBytes;
     const int h = walk.head(t), r0 = walk.row0(t);
     kf::mbar_arrive_expect_tx(&bars.ring_full[st], kStageTx);
@@ -213,6 +235,10 @@ __device__ __forceinline__ float ex2(float x) {
 __device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity, const int* abort) {
   return kf::mbar_wait_or_abort(bar, parity, &g_fa_bwd_error, const_cast<volatile int*>(abort));
 }
+// Bounded wait that does not give up early on the CTA's abort flag (draining in-flight MMAs).
+__device__ __forceinline__ bool wait_drain_again(uint64_t* bar) {
+  return kf::mbar_wait_bounded(bar, 0, &g_fa_bwd_error);
+}
 __device__ __forceinline__ bool wait_relaxed(uint64_t* bar, uint32_t parity, const int* abort) {
   return kf::mbar_wait_or_abort<true>(bar, parity, &g_fa_bwd_error, const_cast<volatile int*>(abort));
 }
@@ -263,7 +289,7 @@ fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
   const int ntiles = (k_end + TILE - 1) / TILE;
 
   if (threadIdx.x == 0) {
-    bars.init();
+    bars.init(1);
     kf::fence_mbar_init();
   }
   if (warp == kMmaWarp) kf::tc::tmem_alloc(bars.tmem_slot, kTmemCols);
@@ -416,7 +442,7 @@ fa_bwd_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_
   const TileWalk walk{kvh * group, qt_first, max(qt_count, 1), TILE};
 
   if (threadIdx.x == 0) {
-    bars.init();
+    bars.init(1);
     kf::fence_mbar_init();
   }
   if (warp == kMmaWarp) kf::tc::tmem_alloc(bars.tmem_slot, kTmemCols);
@@ -544,6 +570,273 @@ fa_bwd_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_
   }
 }
 
+// ============================================================================================
+// dQ, dK, dV in one key-stationary kernel (head dims up to 128; dQ summed at L2, so its
+// summation order varies from run to run). The dK / dV kernel's schedule, plus per tile
+//   dQ^T = K^T dS^T     M = head dim, N = 64 queries, K = 128 keys; A = K (MN-major, as loaded),
+//                       B = dS^T (MN-major, written to shared memory by the softmax warps)
+// into the tile's dP^T columns, which the softmax warps have read by then. P^T and dS^T (16-bit)
+// share the S^T columns: warpgroup g's P^T at 32 g, its dS^T at 32 g + 16. Warps 11..14 read
+// dQ^T (one head-dim row per lane), stage it as [query][head dim] fp32 rows and add the tile to
+// dq_acc with one bulk reduction; their reads free the score buffer. At D = 64 the dQ^T MMA is
+// M = 128 over K's block and V's (lanes 64..127, V^T dS^T, are not read).
+// ============================================================================================
+constexpr int kFusedThreads = 480;
+constexpr int kDqWarp0 = 11;
+constexpr uint32_t kDqBar = 1;  // named barrier of the four dQ warps
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kFusedThreads, 1)
+fa_bwd_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                          const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
+                          const BwdArgs p) {
+  using C = Cfg<D, true>;
+  constexpr int TILE = C::kTile, G = TILE / 2;
+  static_assert(TILE == 64 && C::kAccN == D, "64-query tiles, one CTA per key block");
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t kDv = 0, kDk = D, kBuf = C::kDkdvBuf;
+  constexpr int kBufs = C::kDkdvBufs;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (kf::smem_u32(smem_raw) & 1023u)) & 1023u);
+  const Bars<D> bars(smem);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kvh = blockIdx.y, b = blockIdx.z;
+  const int k0 = static_cast<int>(blockIdx.x) * kRows;
+  const int group = p.Hq / p.Hkv;
+  const int q_first = p.causal ? max(0, k0 + p.Nq - p.Nk) : 0;
+  const int qt_first = q_first / TILE;
+  const int qt_count = max(0, (p.Nq + TILE - 1) / TILE - qt_first);
+  const int ntiles = group * qt_count;
+  const TileWalk walk{kvh * group, qt_first, max(qt_count, 1), TILE};
+
+  if (threadIdx.x == 0) {
+    bars.init(4);  // a buffer is free once each dQ warp has read its dQ^T rows
+    kf::fence_mbar_init();
+  }
+  if (warp == kMmaWarp) kf::tc::tmem_alloc(bars.tmem_slot, kTmemCols);
+  kf::tc::fence_before_sync();
+  __syncthreads();
+  kf::tc::fence_after_sync();
+  const uint32_t tmem = *bars.tmem_slot;
+  const int* abort = bars.abort_flag;
+
+  if (warp == kProducerWarp) {
+    if (lane == 0) produce<D, true>(bars, smem, &tm_k, &tm_v, &tm_q, &tm_do, kvh, k0, b, walk, ntiles, p);
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      constexpr uint32_t idS = kf::tc::idesc_f16(kBf16 ? 1 : 0, kRows, TILE, false, false);
+      const uint32_t k_addr = kf::smem_u32(smem), v_addr = k_addr + C::kStatBytes;
+      bool ok = wait_relaxed(bars.stat_full, 0, abort);
+      if (!ok) note_gave_up(2, -1);
+      for (int t = 0; ok && t < ntiles; ++t) {
+        const int buf = t % kBufs, st = t % C::kStages;
+        if (!(ok = wait_relaxed(&bars.ring_full[st], (t / C::kStages) & 1, abort))) {
+          note_gave_up(2, t);
+          break;
+        }
+        kf::tc::fence_after_sync();
+        const uint32_t q_addr = kf::smem_u32(smem + C::kRingOffset + st * 2 * C::kTileBytes);
+        const uint32_t s_col = tmem + kBuf + C::kBufCols * buf;
+        issue_scores<D, TILE>(k_addr, q_addr, s_col, idS);                          // S^T  = K Q^T
+        issue_scores<D, TILE>(v_addr, q_addr + C::kTileBytes, s_col + TILE, idS);   // dP^T = V dO^T
+        kf::tc::commit(&bars.s_full[buf]);
+      }
+      kf::tc::commit(bars.drain);  // completes once every MMA issued above has
+    }
+  } else if (warp == kOutWarp) {
+    if (lane == 0) {
+      constexpr uint32_t idA = kf::tc::idesc_f16(kBf16 ? 1 : 0, kRows, D, false, true);
+      constexpr uint32_t idQ = kf::tc::idesc_f16(kBf16 ? 1 : 0, kRows, TILE, true, true);
+      // K^T: 64-element head-dim blocks one K box (kRows x 128 bytes) apart; at D = 64 the
+      // second block is V's.
+      const uint64_t kt_desc = kf::tc::desc_sw128(kf::smem_u32(smem), kRows * 128, 1024);
+      uint32_t v_started = 0, k_started = 0;
+      bool ok = wait_relaxed(bars.stat_full, 0, abort);
+      if (!ok) note_gave_up(3, -1);
+      for (int t = 0; ok && t < ntiles; ++t) {
+        const int buf = t % kBufs, st = t % C::kStages;
+        if (!(ok = wait_relaxed(&bars.p_full[buf], (t / kBufs) & 1, abort))) {
+          note_gave_up(3, t);
+          break;
+        }
+        kf::tc::fence_after_sync();
+        const uint32_t q_addr = kf::smem_u32(smem + C::kRingOffset + st * 2 * C::kTileBytes);
+        const uint32_t s_col = tmem + kBuf + C::kBufCols * buf;
+        issue_accumulate<TILE, true>(tmem + kDv, s_col, q_addr + C::kTileBytes, idA, v_started);  // dV += P^T dO
+        issue_accumulate<TILE, true>(tmem + kDk, s_col + G / 2, q_addr, idA, k_started);          // dK += dS^T Q
+        kf::tc::commit(&bars.ring_empty[st]);
+        // dQ^T = K^T dS^T over the block's 128 keys, 16 keys (2048 bytes of both operands) a step.
+        const uint64_t ds_desc =
+            kf::tc::desc_sw128(kf::smem_u32(smem + C::kDsOffset + buf * C::kDsBytes), kRows * 128, 1024);
+#pragma unroll
+        for (int kk = 0; kk < kRows / 16; ++kk)
+          kf::tc::mma_ss(s_col + TILE, kf::tc::desc_advance(kt_desc, kk * 2048),
+                         kf::tc::desc_advance(ds_desc, kk * 2048), idQ, kk > 0);
+        kf::tc::commit(&bars.dq_full[buf]);
+      }
+      kf::tc::commit(bars.acc_full);
+      kf::tc::commit(bars.drain);
+    }
+  } else if (warp >= kDqWarp0) {
+    const int quarter = warp & 3;
+    const int d = quarter * 32 + lane;   // this lane's head-dim row of dQ^T
+    const bool live = quarter * 32 < D;  // warp-uniform
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    float* stage = reinterpret_cast<float*>(smem + C::kDqStageOffset);
+    const bool issuer = warp == kDqWarp0 && lane == 0;
+    // Score buffers start free: the first kBufs tiles' buffer arrivals.
+    if (lane == 0)
+      for (int t = 0; t < kBufs; ++t) kf::mbar_arrive(&bars.ring_full[t % C::kStages]);
+    for (int t = 0; t < ntiles; ++t) {
+      const int buf = t % kBufs;
+      bool ok = __all_sync(0xffffffffu, wait(&bars.dq_full[buf], (t / kBufs) & 1, abort));
+      if (!ok && lane == 0) note_gave_up(6, t);
+      uint32_t va[32], vb[32];  // queries 0..31, 32..63 of the tile
+      if (ok) {
+        kf::tc::fence_after_sync();
+        if (live) {
+          const uint32_t col = lane_base + kBuf + C::kBufCols * buf + TILE;
+          kf::tc::ld_32x32b_x32(col, va);
+          kf::tc::ld_32x32b_x32(col + 32, vb);
+          kf::tc::wait_ld();
+        }
+        kf::tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) kf::mbar_arrive(&bars.ring_full[(t + kBufs) % C::kStages]);  // free for tile t + kBufs
+      }
+      if (issuer) kf::tma_store_wait_read0();  // the previous reduction has read the staging rows
+      __syncwarp();
+      if (!kf::named_bar_and(kDqBar, 128, ok)) break;  // every dQ warp leaves together
+      if (live) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          stage[j * D + d] = __uint_as_float(va[j]);
+          stage[(j + 32) * D + d] = __uint_as_float(vb[j]);
+        }
+      }
+      kf::fence_proxy_async_smem();  // the bulk reduction reads the rows through the async proxy
+      __syncwarp();
+      kf::named_bar_sync(kDqBar, 128);
+      if (issuer) {
+        const int64_t row = (static_cast<int64_t>(b) * p.Hq + walk.head(t)) * p.NqP + walk.row0(t);
+        kf::bulk_reduce_add_f32(p.dq_acc + row * D, stage, TILE * D * 4);  // rows r0..r0+63 < NqP
+        kf::tma_store_commit();
+      }
+      __syncwarp();
+    }
+    if (issuer) kf::tma_store_wait_all0();
+  } else {
+    const int wg = warp >> 2, quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int key = k0 + row;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const int q_min = p.causal ? key + p.Nq - p.Nk : INT_MIN;  // queries [q_min, Nq) see this key
+    const uint64_t c2 = kf::f2_pack(p.scale_log2, p.scale_log2);
+    bool ok = true;
+    for (int t = 0; t < ntiles; ++t) {
+      const int buf = t % kBufs;
+      ok = __all_sync(0xffffffffu, wait(&bars.s_full[buf], (t / kBufs) & 1, abort));
+      if (!ok) {
+        if (lane == 0) note_gave_up(4, t);
+        break;
+      }
+      kf::tc::fence_after_sync();
+      const uint32_t s_col = lane_base + kBuf + C::kBufCols * buf + G * wg;  // this warpgroup's G queries
+      const int r0 = walk.row0(t) + G * wg;
+      const bool full = r0 >= q_min;
+      const float* rs =
+          reinterpret_cast<const float*>(smem + C::kRowStatOffset + (t % C::kStages) * 2 * TILE * 4) + G * wg;
+      uint32_t sv[G], dv[G], pp[G / 2], dd[G / 2];
+      tm_load<G>(s_col, sv);
+      tm_load<G>(s_col + TILE, dv);
+      kf::tc::wait_ld();
+#pragma unroll
+      for (int i = 0; i < G / 2; ++i) {
+        const float2 nl = *reinterpret_cast<const float2*>(rs + 2 * i);
+        const float2 nd = *reinterpret_cast<const float2*>(rs + TILE + 2 * i);
+        const float2 a = kf::f2_unpack(
+            kf::f2_fma(kf::f2_pack(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1])), c2, kf::f2_pack(nl.x, nl.y)));
+        float p0 = ex2(a.x), p1 = ex2(a.y);
+        if (!full) {
+          p0 = r0 + 2 * i >= q_min ? p0 : 0.f;
+          p1 = r0 + 2 * i + 1 >= q_min ? p1 : 0.f;
+        }
+        const uint64_t ds = kf::f2_mul(
+            kf::f2_pack(p0, p1),
+            kf::f2_add(kf::f2_pack(__uint_as_float(dv[2 * i]), __uint_as_float(dv[2 * i + 1])), kf::f2_pack(nd.x, nd.y)));
+        const float2 df = kf::f2_unpack(ds);
+        pp[i] = pack2(p0, p1, kBf16);
+        dd[i] = pack2(df.x, df.y, kBf16);
+      }
+      tm_store<G / 2>(s_col, pp);
+      tm_store<G / 2>(s_col + G / 2, dd);
+      // dS^T row `row` (128 bytes: 64 queries), this warpgroup's 64-byte half, 128-byte swizzle.
+      uint8_t* ds_row = smem + C::kDsOffset + buf * C::kDsBytes + row * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<uint4*>(ds_row + (((4 * wg + c) ^ (row & 7)) << 4)) =
+            make_uint4(dd[4 * c], dd[4 * c + 1], dd[4 * c + 2], dd[4 * c + 3]);
+      kf::fence_proxy_async_smem();  // the dQ MMAs read dS^T through the async proxy
+      kf::tc::wait_st();
+      kf::tc::fence_before_sync();
+      kf::mbar_arrive(&bars.p_full[buf]);
+    }
+    // Epilogue: dV = acc, dK = gamma acc; warpgroup g writes columns [g D / 2, (g + 1) D / 2).
+    if (ok && !wait(bars.acc_full, 0, abort)) {
+      ok = false;
+      note_gave_up(5, 0);
+    }
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok) {
+      kf::tc::fence_after_sync();
+      const int64_t off = ((static_cast<int64_t>(b) * p.Nk + key) * p.Hkv + kvh) * p.D;  // real head dim
+      T* dk = static_cast<T*>(p.dk) + off;
+      T* dv = static_cast<T*>(p.dv) + off;
+#pragma unroll
+      for (int cc = 0; cc < D / 64; ++cc) {
+        const int c = wg * (D / 64) + cc;
+        uint32_t ar[32], br[32];
+        kf::tc::ld_32x32b_x32(lane_base + kDv + c * 32, ar);
+        kf::tc::ld_32x32b_x32(lane_base + kDk + c * 32, br);
+        kf::tc::wait_ld();
+        if (key < p.Nk && c * 32 < p.D) {
+          store_row32<T>(dv + c * 32, ar, 1.f, ntiles > 0, p.D - c * 32);
+          store_row32<T>(dk + c * 32, br, p.scale, ntiles > 0, p.D - c * 32);
+        }
+      }
+    }
+  }
+  kf::tc::fence_before_sync();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    // Tensor memory is freed only once both issuing threads' MMAs have completed, also when a
+    // wait above gave up with MMAs in flight.
+    if (lane == 0 && !wait(bars.drain, 0, abort) && !wait_drain_again(bars.drain)) note_gave_up(7, 0);
+    __syncwarp();
+    kf::tc::fence_after_sync();
+    kf::tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <typename T, int D>
+int launch_fused(const BwdArgs& a, int dtype, cudaStream_t stream) {
+  using C = Cfg<D, true>;
+  if (a.dq_acc == nullptr || a.Dp != D) return KF_ERR_INVALID_ARGUMENT;
+  CUtensorMap mk, mv, mq, mdo;
+  if (!encode_bnhd(&mk, a.k, dtype, a.B, a.Nk, a.Hkv, a.D, kRows) ||
+      !encode_bnhd(&mv, a.v, dtype, a.B, a.Nk, a.Hkv, a.D, kRows) ||
+      !encode_bnhd(&mq, a.q, dtype, a.B, a.Nq, a.Hq, a.D, C::kTile) ||
+      !encode_bnhd(&mdo, a.dout, dtype, a.B, a.Nq, a.Hq, a.D, C::kTile))
+    return KF_ERR_CUDA;
+  auto kernel = fa_bwd_fused_sm100_kernel<T, D>;
+  const int prep = kf_host::prepare_kernel(reinterpret_cast<const void*>(kernel), kFusedThreads, C::kSmemBytes, nullptr);
+  if (prep != KF_OK) return prep;
+  kernel<<<dim3((a.Nk + kRows - 1) / kRows, a.Hkv, a.B), kFusedThreads, C::kSmemBytes, stream>>>(mk, mv, mq, mdo, a);
+  KF_LAUNCH_CHECK();
+  return KF_OK;
+}
+
 template <typename T, int D>
 int launch(const BwdArgs& a, int dtype, cudaStream_t stream) {
   using C = Cfg<D>;
@@ -586,8 +879,16 @@ int kf_internal_fa_bwd_error(unsigned int* code) {
   if (v != 0) {
     const unsigned int zero = 0;
     KF_CUDA_TRY(cudaMemcpyToSymbol(g_fa_bwd_error, &zero, sizeof(zero)));
+    KF_CUDA_TRY(cudaMemcpyToSymbol(g_fa_bwd_where, &zero, sizeof(zero)));
   }
   *code = v;
+  return KF_OK;
+}
+
+// Where the first bounded wait of the backward kernels gave up (role << 24 | tile), 0 if none;
+// read before kf_internal_fa_bwd_error clears it.
+int kf_internal_fa_bwd_where(unsigned int* where) {
+  KF_CUDA_TRY(cudaMemcpyFromSymbol(where, g_fa_bwd_where, sizeof(*where)));
   return KF_OK;
 }
 
@@ -598,6 +899,12 @@ namespace kf::fa {
 bool sm100_bwd_supported(const BwdArgs& a) { return a.D >= 8 && a.D <= 256; }
 
 int launch_sm100_bwd(const BwdArgs& a, int dtype, cudaStream_t s) {
+  if (a.dq_acc != nullptr) {  // one kernel, dQ summed at L2 (head dims up to 128)
+    if (a.D > 128) return KF_ERR_INVALID_ARGUMENT;
+    if (dtype == KF_DTYPE_BF16)
+      return a.D <= 64 ? launch_fused<__nv_bfloat16, 64>(a, dtype, s) : launch_fused<__nv_bfloat16, 128>(a, dtype, s);
+    return a.D <= 64 ? launch_fused<__half, 64>(a, dtype, s) : launch_fused<__half, 128>(a, dtype, s);
+  }
   if (dtype == KF_DTYPE_BF16) {
     if (a.D > 128) return launch<__nv_bfloat16, 256>(a, dtype, s);
     return a.D <= 64 ? launch<__nv_bfloat16, 64>(a, dtype, s) : launch<__nv_bfloat16, 128>(a, dtype, s);

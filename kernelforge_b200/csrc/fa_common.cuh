@@ -42,6 +42,8 @@ struct BwdArgs {
   const float* lse;
   float* row_nlse;
   float* row_ndelta;
+  float* dq_acc;  // non-deterministic schedule: fp32 dQ sums [B, Hq, NqP, Dp], else null
+  int Dp;         // head dim of the dq_acc rows (the kernel's zero-padded head dim)
   void* dq;
   void* dk;
   void* dv;
@@ -52,8 +54,10 @@ struct BwdArgs {
   int causal;
 };
 
-// Row statistics, then dQ, dK, dV (deterministic; no atomics) on the tcgen05 kernels: head dims
-// up to 256, zero-padded to 64, 128 or 256.
+// Row statistics, then dQ, dK, dV on the tcgen05 kernels: head dims up to 256, zero-padded to
+// 64, 128 or 256. With dq_acc set (head dims up to 128), one kernel computes all three and adds
+// its dQ partials into dq_acc at L2 (summation order varies from run to run), then a conversion
+// pass writes dq; otherwise separate dQ and dK / dV kernels, no atomics (deterministic).
 int launch_bwd(const BwdArgs& a, int dtype, cudaStream_t stream);
 bool sm100_bwd_supported(const BwdArgs& a);
 int launch_sm100_bwd(const BwdArgs& a, int dtype, cudaStream_t stream);

@@ -22,7 +22,7 @@ KF_API const char* kf_status_string(int status) {
   }
 }
 
-KF_API int kf_abi_version(void) { return 1; }
+KF_API int kf_abi_version(void) { return 2; }  // 2: kf_fa_bwd takes `deterministic`
 
 namespace {
 

@@ -15,7 +15,8 @@ How this module is organised:
 * ``JvpSchedule`` holds the reference's tile/pipeline arguments. The reference compiles a
   kernel per schedule; the kernels here pick their own tiles, so a schedule is validated over
   the reference's domain, resolved to the same defaults ``get_jvp_config`` reports, and has no
-  effect on the result. Results are deterministic for a given shape.
+  effect on the result. Forward and JVP results are deterministic for a given shape; the
+  backward is too with ``deterministic=True`` (otherwise dq may vary in its last bit).
 * Every kernel is wrapped in an opaque ``torch.library`` operator (``kernelforge_b200::…``), so
   torch.func transforms unwrap their tensors before a raw pointer is taken, and fake kernels
   give shapes to tracing.
@@ -246,26 +247,28 @@ def _(q, k, v, tq, tk, tv, scale, causal):
     return torch.empty_like(q), _lse_like(q), torch.empty_like(q)
 
 
-def _bwd_into(dout, q, k, v, out, lse, dq, dk, dv, scale, causal):
-    """kf_fa_bwd into dense gradient buffers (dq like q, dk/dv like k)."""
-    problem_rows = q.shape[0], q.shape[2], q.shape[1]
-    ws_bytes = _lib.lib.kf_fa_bwd_workspace_size(*problem_rows)
+def _bwd_into(dout, q, k, v, out, lse, dq, dk, dv, scale, causal, deterministic):
+    """kf_fa_bwd into dense gradient buffers (dq like q, dk/dv like k). deterministic=False (what
+    the reference passes to flash_attn) runs one kernel whose dQ partials are summed at L2 for
+    head dims up to 128; True runs the separate dQ and dK/dV kernels (bitwise reproducible)."""
+    flag = int(bool(deterministic))
+    ws_bytes = _lib.lib.kf_fa_bwd_workspace_size(q.shape[0], q.shape[2], q.shape[1], q.shape[3], flag)
     workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
     _abi_call("kf_fa_bwd", q, k, v, out, dout, lse, dq, dk, dv, workspace, ws_bytes, *_sizes(q, k), float(scale),
-              int(bool(causal)), _lib.dtype_code(q.dtype))
+              int(bool(causal)), flag, _lib.dtype_code(q.dtype))
 
 
 @torch.library.custom_op(f"{_OP_NAMESPACE}::flash_attention_backward", mutates_args=(), device_types="cuda")
 def _launch_bwd(dout: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor,
-                lse: torch.Tensor, scale: float, causal: bool
+                lse: torch.Tensor, scale: float, causal: bool, deterministic: bool = False
                 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    _bwd_into(dout, q, k, v, out, lse, dq, dk, dv, scale, causal)
+    _bwd_into(dout, q, k, v, out, lse, dq, dk, dv, scale, causal, deterministic)
     return dq, dk, dv
 
 
 @_launch_bwd.register_fake
-def _(dout, q, k, v, out, lse, scale, causal):
+def _(dout, q, k, v, out, lse, scale, causal, deterministic=False):
     return torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
 
 
@@ -296,12 +299,13 @@ def _flash_attn_backward(dout, q, k, v, out, lse, dq, dk, dv, dropout_p, softmax
                          deterministic=False):
     """Attention's VJP from the saved O and LSE, behind flash_attn's ``_flash_attn_backward``
     signature: fills dq, dk, dv in place (strided destinations through a dense copy) and returns
-    them. Always deterministic (no atomics)."""
+    them. ``deterministic`` has flash_attn's meaning: False (the reference's choice) lets dq vary
+    in the last bit between runs (its partials are summed at L2); True makes it reproducible."""
     _plain_attention_only(dropout_p, window_size_left, window_size_right, softcap, alibi_slopes)
     dense = [t.contiguous() for t in (dout, q, k, v, out)]
     targets = [g if g.is_contiguous() else torch.empty_like(g, memory_format=torch.contiguous_format)
                for g in (dq, dk, dv)]
-    _bwd_into(dense[0], *dense[1:], lse.float().contiguous(), *targets, softmax_scale, causal)
+    _bwd_into(dense[0], *dense[1:], lse.float().contiguous(), *targets, softmax_scale, causal, deterministic)
     for given, written in zip((dq, dk, dv), targets):
         if given is not written:
             given.copy_(written)

@@ -33,7 +33,7 @@ def test_library_exports_declared_symbol(name):
 def test_status_strings_and_version():
     assert _lib.status_string(0) == "ok"
     assert "workspace" in _lib.status_string(4)
-    assert _lib.lib.kf_abi_version() >= 1
+    assert _lib.lib.kf_abi_version() >= 2
 
 
 def test_rmsnorm_rejects_bad_arguments_without_launching():
@@ -77,20 +77,27 @@ def test_linear_validation_without_launching():
 
 def test_fa_bwd_workspace_and_validation():
     ws = _lib.lib.kf_fa_bwd_workspace_size
-    assert ws(2, 4, 100) == 2 * 2 * 4 * 128 * 4  # two fp32 statistics per (batch, head, query), padded to 128
-    assert ws(0, 4, 100) == 0
+    # Two fp32 statistics per (batch, head, query), padded to 128 queries; the fused schedule
+    # (deterministic=0, head dim <= 128) adds the fp32 dQ sums, 64 or 128 per row.
+    assert ws(2, 4, 100, 64, 1) == 2 * 2 * 4 * 128 * 4
+    assert ws(2, 4, 100, 256, 0) == 2 * 2 * 4 * 128 * 4
+    assert ws(2, 4, 100, 40, 0) == (2 + 64) * 2 * 4 * 128 * 4
+    assert ws(2, 4, 100, 96, 0) == (2 + 128) * 2 * 4 * 128 * 4
+    assert ws(0, 4, 100, 64, 0) == 0
+    assert ws(1, 4, 100, 0, 0) == 0
     f = _lib.lib.kf_fa_bwd
-    need = ws(1, 2, 16)
+    need = ws(1, 2, 16, 64, 0)
     ptrs = [256] * 9  # q, k, v, out, dout, lse, dq, dk, dv
-    args = (1, 16, 16, 2, 2, 64, 0.125, 0, 2, None)
+    args = (1, 16, 16, 2, 2, 64, 0.125, 0, 0, 2, None)
     assert f(*ptrs, 256, need - 1, *args) == 4                                       # workspace too small
+    assert f(*ptrs, 256, ws(1, 2, 16, 64, 1), *args) == 4                           # sized for deterministic
     assert f(*ptrs, None, need, *args) == 1                                          # no workspace
     assert f(*ptrs[:6], None, *ptrs[7:], 256, need, *args) == 1                      # no dq
     assert f(*ptrs[:4], 264, *ptrs[5:], 256, need, *args) == 3                       # misaligned dout
-    assert f(*ptrs, 256, need, 1, 16, 16, 2, 2, 72 * 4, 0.125, 0, 2, None) == 2      # head dim > 256
-    assert f(*ptrs, 256, need, 1, 16, 16, 3, 2, 64, 0.125, 0, 2, None) == 2         # Hq % Hkv
-    assert f(*ptrs, 256, need, 1, 16, 16, 2, 2, 64, -1.0, 0, 2, None) == 1          # scale
-    assert f(*ptrs, 256, need, 1, 16, 16, 2, 2, 64, 0.125, 0, 7, None) == 2         # dtype
+    assert f(*ptrs, 256, need, 1, 16, 16, 2, 2, 72 * 4, 0.125, 0, 0, 2, None) == 2   # head dim > 256
+    assert f(*ptrs, 256, need, 1, 16, 16, 3, 2, 64, 0.125, 0, 0, 2, None) == 2      # Hq % Hkv
+    assert f(*ptrs, 256, need, 1, 16, 16, 2, 2, 64, -1.0, 0, 0, 2, None) == 1       # scale
+    assert f(*ptrs, 256, need, 1, 16, 16, 2, 2, 64, 0.125, 0, 0, 7, None) == 2      # dtype
 
 
 def test_python_signature_validation():
