@@ -58,7 +58,7 @@ constexpr uint32_t kTmemCols = 512;
 // 2 x 16 KB), and the dK / dV accumulators (2 x 256 columns together) are split by head-dim
 // halves over two CTAs per key block, each recomputing the key block's scores.
 // kFused (D <= 128): after the barriers, one 16-bit dS^T tile per score buffer (the dQ MMAs'
-// B operand) and the fp32 dQ tile staged for its reduction into dq_acc.
+// B operand).
 template <int D, bool kFused = false> struct Cfg {
   static constexpr int kTile = D <= 128 ? 64 : 32;       // streamed rows per tile
   static constexpr int kKB = D / 64;                     // 128-byte boxes along the head dim
@@ -80,8 +80,7 @@ template <int D, bool kFused = false> struct Cfg {
   static constexpr int kBarOffset = kRowStatOffset + kStages * 2 * kTile * 4;
   static constexpr int kDsBytes = kRows * kTile * 2;
   static constexpr int kDsOffset = (kBarOffset + 256 + 1023) / 1024 * 1024;
-  static constexpr int kDqStageOffset = kDsOffset + kDkdvBufs * kDsBytes;
-  static constexpr int kSmemBytes = (kFused ? kDqStageOffset + kTile * D * 4 : kBarOffset + 256) + 1024;  // + alignment slack
+  static constexpr int kSmemBytes = (kFused ? kDsOffset + kDkdvBufs * kDsBytes : kBarOffset + 256) + 1024;  // + alignment slack
   static_assert(kSmemBytes <= 232448, "shared memory");
 };
 constexpr int kMaxBufs = 3;
@@ -577,13 +576,12 @@ fa_bwd_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_
 //                       B = dS^T (MN-major, written to shared memory by the softmax warps)
 // into the tile's dP^T columns, which the softmax warps have read by then. P^T and dS^T (16-bit)
 // share the S^T columns: warpgroup g's P^T at 32 g, its dS^T at 32 g + 16. Warps 11..14 read
-// dQ^T (one head-dim row per lane), stage it as [query][head dim] fp32 rows and add the tile to
-// dq_acc with one bulk reduction; their reads free the score buffer. At D = 64 the dQ^T MMA is
-// M = 128 over K's block and V's (lanes 64..127, V^T dS^T, are not read).
+// dQ^T (one head-dim row per lane; their reads free the score buffer) and add it to dq_acc with
+// one 128-byte reduction per query and warp, performed at L2. At D = 64 the dQ^T MMA is M = 128
+// over K's block and V's (lanes 64..127, V^T dS^T, are not read).
 // ============================================================================================
 constexpr int kFusedThreads = 480;
 constexpr int kDqWarp0 = 11;
-constexpr uint32_t kDqBar = 1;  // named barrier of the four dQ warps
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kFusedThreads, 1)
@@ -683,49 +681,37 @@ fa_bwd_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid
     const int d = quarter * 32 + lane;   // this lane's head-dim row of dQ^T
     const bool live = quarter * 32 < D;  // warp-uniform
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    float* stage = reinterpret_cast<float*>(smem + C::kDqStageOffset);
-    const bool issuer = warp == kDqWarp0 && lane == 0;
     // Score buffers start free: the first kBufs tiles' buffer arrivals.
     if (lane == 0)
       for (int t = 0; t < kBufs; ++t) kf::mbar_arrive(&bars.ring_full[t % C::kStages]);
     for (int t = 0; t < ntiles; ++t) {
       const int buf = t % kBufs;
-      bool ok = __all_sync(0xffffffffu, wait(&bars.dq_full[buf], (t / kBufs) & 1, abort));
-      if (!ok && lane == 0) note_gave_up(6, t);
-      uint32_t va[32], vb[32];  // queries 0..31, 32..63 of the tile
-      if (ok) {
-        kf::tc::fence_after_sync();
-        if (live) {
-          const uint32_t col = lane_base + kBuf + C::kBufCols * buf + TILE;
-          kf::tc::ld_32x32b_x32(col, va);
-          kf::tc::ld_32x32b_x32(col + 32, vb);
-          kf::tc::wait_ld();
-        }
-        kf::tc::fence_before_sync();
-        __syncwarp();
-        if (lane == 0) kf::mbar_arrive(&bars.ring_full[(t + kBufs) % C::kStages]);  // free for tile t + kBufs
+      if (!__all_sync(0xffffffffu, wait(&bars.dq_full[buf], (t / kBufs) & 1, abort))) {
+        if (lane == 0) note_gave_up(6, t);
+        break;
       }
-      if (issuer) kf::tma_store_wait_read0();  // the previous reduction has read the staging rows
-      __syncwarp();
-      if (!kf::named_bar_and(kDqBar, 128, ok)) break;  // every dQ warp leaves together
+      kf::tc::fence_after_sync();
+      uint32_t va[32], vb[32];  // queries 0..31, 32..63 of the tile
       if (live) {
+        const uint32_t col = lane_base + kBuf + C::kBufCols * buf + TILE;
+        kf::tc::ld_32x32b_x32(col, va);
+        kf::tc::ld_32x32b_x32(col + 32, vb);
+        kf::tc::wait_ld();
+      }
+      kf::tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) kf::mbar_arrive(&bars.ring_full[(t + kBufs) % C::kStages]);  // free for tile t + kBufs
+      if (live) {
+        // Query j's row gets this warp's 32 consecutive head-dim values: one 128-byte reduction
+        // per query (rows r0..r0+63 < NqP).
+        float* dst = p.dq_acc + ((static_cast<int64_t>(b) * p.Hq + walk.head(t)) * p.NqP + walk.row0(t)) * D + d;
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          stage[j * D + d] = __uint_as_float(va[j]);
-          stage[(j + 32) * D + d] = __uint_as_float(vb[j]);
+          kf::red_add_f32(dst + j * D, __uint_as_float(va[j]));
+          kf::red_add_f32(dst + (j + 32) * D, __uint_as_float(vb[j]));
         }
       }
-      kf::fence_proxy_async_smem();  // the bulk reduction reads the rows through the async proxy
-      __syncwarp();
-      kf::named_bar_sync(kDqBar, 128);
-      if (issuer) {
-        const int64_t row = (static_cast<int64_t>(b) * p.Hq + walk.head(t)) * p.NqP + walk.row0(t);
-        kf::bulk_reduce_add_f32(p.dq_acc + row * D, stage, TILE * D * 4);  // rows r0..r0+63 < NqP
-        kf::tma_store_commit();
-      }
-      __syncwarp();
     }
-    if (issuer) kf::tma_store_wait_all0();
   } else {
     const int wg = warp >> 2, quarter = warp & 3;
     const int row = quarter * 32 + lane;
@@ -734,7 +720,7 @@ fa_bwd_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid
     const int q_min = p.causal ? key + p.Nq - p.Nk : INT_MIN;  // queries [q_min, Nq) see this key
     const uint64_t c2 = kf::f2_pack(p.scale_log2, p.scale_log2);
     bool ok = true;
-    for (int t = 0; t < ntiles; ++t) {
+    for (int t = 0; ok && t < ntiles; ++t) {
       const int buf = t % kBufs;
       ok = __all_sync(0xffffffffu, wait(&bars.s_full[buf], (t / kBufs) & 1, abort));
       if (!ok) {

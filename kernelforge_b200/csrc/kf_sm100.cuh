@@ -219,19 +219,6 @@ __device__ __forceinline__ void cluster_sync_all() {
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
-// The same barrier, returning whether `pred` held in every participating thread.
-__device__ __forceinline__ bool named_bar_and(uint32_t id, uint32_t nthreads, bool pred) {
-  uint32_t all;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.and.pred q, %2, %3, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(all)
-      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(nthreads)
-      : "memory");
-  return all != 0;
-}
 
 // ------------------------------------------------------------------------------------------
 // Packed fp32 pairs (sm_100 f32x2 arithmetic: two lanes of work per instruction)
@@ -320,13 +307,10 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       : "memory");
 }
 
-// 1-D bulk reduction shared -> global: dst[i] += src[i] for `bytes` / 4 fp32 values, performed
-// at L2 (16-byte aligned addresses, size a multiple of 16). Completes with the thread's bulk
-// groups (tma_store_commit / tma_store_wait_*).
-__device__ __forceinline__ void bulk_reduce_add_f32(float* dst, const void* src, uint32_t bytes) {
-  asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(dst),
-               "r"(smem_u32(src)), "r"(bytes)
-               : "memory");
+// dst[0] += v at L2 (no return value; the 32 lanes of a warp on consecutive floats make one
+// 128-byte reduction).
+__device__ __forceinline__ void red_add_f32(float* dst, float v) {
+  asm volatile("red.global.add.f32 [%0], %1;" ::"l"(__cvta_generic_to_global(dst)), "f"(v) : "memory");
 }
 
 // Programmatic dependent launch: the primary grid lets its dependent grid start launching;
