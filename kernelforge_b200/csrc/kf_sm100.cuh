@@ -197,6 +197,19 @@ __device__ __forceinline__ uint32_t cluster_map(uint32_t smem_addr, uint32_t ran
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// Arrival with no ordering of this thread's memory operations (a "done reading" signal whose
+// reads have already returned their values).
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// 16-byte store into a CTA of the cluster (shared::cluster address) whose completion counts 16
+// bytes on that CTA's mbarrier `cluster_mbar`; the waiter of that phase sees the data.
+__device__ __forceinline__ void st_async_f4(uint32_t cluster_addr, float4 v, uint32_t cluster_mbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   cluster_addr),
+               "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(cluster_mbar)
+               : "memory");
+}
 // Orders this thread's earlier shared-memory writes before its later operations at cluster
 // scope (before the CTA barrier that hands them to the thread that arrives remotely).
 __device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }

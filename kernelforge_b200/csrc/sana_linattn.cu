@@ -911,13 +911,16 @@ sana_out_generic(const T* __restrict__ qkv, const float* __restrict__ final_vk, 
 // below 2^14, with eps scaled alike.
 //
 // Cluster form (sana_head_cluster): when there are fewer units than SMs, a cluster of CS CTAs
-// shares one unit. CTA rank r takes the r-th of CS equal ranges of K/V tiles and of Q tiles, sums its warp
-// partials into `red`, and the CTAs exchange them through distributed shared memory: each CTA
-// arrives on every peer's `xready` mbarrier once its `red` is written, waits for its own
-// `xready`, sums the CS partials in rank order into `tot` (so every CTA of the cluster holds
-// the same bits, and the result does not depend on timing), then arrives on every peer's
-// `xdone`. A CTA rewrites `red` for its next unit, and leaves the kernel, only after its
-// `xdone` phase for the previous unit has completed (every peer has finished reading it).
+// shares one unit. CTA rank r takes the r-th of CS equal ranges of K/V tiles and of Q tiles and
+// sums its warp partials, and the CTAs combine them by pushing over distributed shared memory
+// (st.async, whose bytes complete on the receiving CTA's own mbarrier, so no cluster-scope
+// fence or remote read is on the path): rank r owns the r-th of CS chunks of [VK ; ksum].
+//   round 1 (reduce-scatter): every CTA pushes each chunk into its owner's receive slot;
+//   round 2 (all-gather): the owner sums its chunk over the ranks in rank order into `tot` and
+//            pushes the sums into every peer's `tot`.
+// Every CTA thus holds the same bits, whatever the timing. For a later unit a CTA pushes only
+// after every peer has signalled `xdone` (re-armed its rounds and finished with its `tot` and
+// receive slots); the last unit sends no signal, so nothing reaches a CTA that has exited.
 // All of these waits are bounded like the ring's. It is its own kernel: one template for both
 // forms measured 2% slower on the one-CTA form (B=2, H=70, N=16384), with identical source for
 // that form.
@@ -941,19 +944,30 @@ struct FusedSmem {
   static constexpr int kBarOff = kRedOff + kFusedPartBytes + 16;            // + two max|B| words
   static constexpr int kBytes = kBarOff + 2 * kFusedStages * 8 + 16 + 1024;
 };
-// Cluster form: the same up to `red` (this CTA's [VK ; ksum]), then the cluster sum `tot`, and
-// two more mbarriers (xready, xdone) after the abort word.
+// Cluster form: the same up to `red` (this CTA's [VK ; ksum]), then the cluster sum `tot`, the
+// receive area of the reduce-scatter (per sending rank, its slice of this CTA's chunk), and three
+// more mbarriers (xready1, xready2, xdone) after the abort word.
+constexpr int kXVec = kFusedPartBytes / 16;  // 16-byte vectors of one [VK ; ksum]
 struct ClusterSmem {
   static constexpr int kRingOff = FusedSmem::kRingOff;
   static constexpr int kPartOff = FusedSmem::kPartOff;
   static constexpr int kRedOff = FusedSmem::kRedOff;
   static constexpr int kTotOff = kRedOff + kFusedPartBytes;
-  static constexpr int kMaxOff = kTotOff + kFusedPartBytes;  // two max|B| words
+  static constexpr int kRecvOff = kTotOff + kFusedPartBytes;
+  static constexpr int kRecvBytes = 4352;                     // >= cs * ceil(kXVec / cs) * 16, cs <= 8
+  static constexpr int kMaxOff = kRecvOff + kRecvBytes;       // two max|B| words
   static constexpr int kBarOff = kMaxOff + 16;
-  static constexpr int kBytes = kBarOff + 2 * kFusedStages * 8 + 16 + 16 + 1024;
+  static constexpr int kBytes = kBarOff + 2 * kFusedStages * 8 + 16 + 24 + 1024;
 };
-static_assert(ClusterSmem::kRedOff % 16 == 0 && ClusterSmem::kTotOff % 16 == 0 && kFusedPartBytes % 16 == 0,
+static_assert(ClusterSmem::kRedOff % 16 == 0 && ClusterSmem::kTotOff % 16 == 0 && ClusterSmem::kRecvOff % 16 == 0 &&
+                  kFusedPartBytes % 16 == 0,
               "the cluster exchange moves 16-byte vectors");
+constexpr int recv_bytes_needed(int cs) { return cs * ((kXVec + cs - 1) / cs) * 16; }
+static_assert(recv_bytes_needed(2) <= ClusterSmem::kRecvBytes && recv_bytes_needed(3) <= ClusterSmem::kRecvBytes &&
+                  recv_bytes_needed(4) <= ClusterSmem::kRecvBytes && recv_bytes_needed(5) <= ClusterSmem::kRecvBytes &&
+                  recv_bytes_needed(6) <= ClusterSmem::kRecvBytes && recv_bytes_needed(7) <= ClusterSmem::kRecvBytes &&
+                  recv_bytes_needed(8) <= ClusterSmem::kRecvBytes && kXVec <= 32 * kFusedWarps,
+              "receive slots of the reduce-scatter; one vector per compute thread");
 constexpr int kFusedMaxCluster = 8;  // portable cluster size limit
 static_assert(kFusedPartBytes <= kFusedSlotBytes && 2 * 2048 <= kFusedSlotBytes, "slot sizes");
 // Ring slot x % kFusedStages is consumed by warp x % kFusedWarps: with equal counts the warp that
@@ -1243,10 +1257,12 @@ sana_head_cluster(const __grid_constant__ CUtensorMap kv_map, const __grid_const
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + ClusterSmem::kBarOff);
   uint64_t* empty = full + kFusedStages;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kFusedStages);
-  uint64_t* xready = empty + kFusedStages + 2;  // past the 16-byte abort word
-  uint64_t* xdone = xready + 1;
+  uint64_t* xready1 = empty + kFusedStages + 2;  // past the 16-byte abort word
+  uint64_t* xready2 = xready1 + 1;
+  uint64_t* xdone = xready2 + 1;
   float* red = reinterpret_cast<float*>(smem + ClusterSmem::kRedOff);
   float* tot = reinterpret_cast<float*>(smem + ClusterSmem::kTotOff);
+  const float4* recv = reinterpret_cast<const float4*>(smem + ClusterSmem::kRecvOff);
   unsigned int* max_bits = reinterpret_cast<unsigned int*>(smem + ClusterSmem::kMaxOff);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1255,6 +1271,11 @@ sana_head_cluster(const __grid_constant__ CUtensorMap kv_map, const __grid_const
   // CS CTAs per unit (one cluster); this CTA is rank `rank`.
   const int cs = static_cast<int>(kf::cluster_nctarank());
   const int rank = static_cast<int>(kf::cluster_ctarank());
+  // Exchange chunks: rank r owns vectors [r c4, min(kXVec, (r + 1) c4)) of [VK ; ksum].
+  const int c4 = (kXVec + cs - 1) / cs;
+  const int own0 = min(kXVec, rank * c4), own1 = min(kXVec, own0 + c4);
+  const uint32_t bytes1 = static_cast<uint32_t>((cs - 1) * (own1 - own0) * 16);  // reduce-scatter in
+  const uint32_t bytes2 = static_cast<uint32_t>((kXVec - (own1 - own0)) * 16);    // all-gather in
   const int first_unit = static_cast<int>(kf::cluster_id_x());
   const int unit_step = static_cast<int>(kf::cluster_count_x());
   // This CTA's share of every unit: K/V tiles [kv0, kv0 + kv_tiles), Q tiles [q0, q0 + q_tiles).
@@ -1274,11 +1295,18 @@ sana_head_cluster(const __grid_constant__ CUtensorMap kv_map, const __grid_const
       kf::mbar_init(&full[s], 1);
       kf::mbar_init(&empty[s], 1);
     }
-    kf::mbar_init(xready, cs > 1 ? cs - 1 : 1);  // one arrival per peer
-    kf::mbar_init(xdone, cs > 1 ? cs - 1 : 1);
+    // xready1 / xready2: this CTA's own arrival with the bytes its peers push in that round
+    // (armed here for the first unit, re-armed before each later unit's exchange can start).
+    kf::mbar_init(xready1, 1);
+    kf::mbar_init(xready2, 1);
+    kf::mbar_init(xdone, cs > 1 ? cs - 1 : 1);  // one arrival per peer
     *abort_flag = 0;
     max_bits[0] = max_bits[1] = 0u;
     kf::fence_mbar_init();
+    if (cs > 1) {
+      kf::mbar_arrive_expect_tx(xready1, bytes1);
+      kf::mbar_arrive_expect_tx(xready2, bytes2);
+    }
   }
   // Peers arrive on this CTA's xready / xdone, so they must be initialised cluster-wide first.
   kf::cluster_sync_all();
@@ -1394,51 +1422,72 @@ sana_head_cluster(const __grid_constant__ CUtensorMap kv_map, const __grid_const
     // Every compute thread is past the previous unit's read of the other word.
     if (threadIdx.x == 0) max_bits[parity ^ 1] = 0u;
     const bool exchange = cs > 1;
-    // Cluster form: every peer has finished reading this CTA's previous `red`.
-    if (exchange && k > 0 && ok)
-      ok = __all_sync(0xffffffffu,
-                      kf::mbar_wait_cluster_or_abort(xdone, (k - 1) & 1, &g_sana_error, abort_flag));
-    // Sum of the 16 partials in warp order, and max|B| for the fp16 scale.
-    float m = 0.f;
-    for (int e = threadIdx.x; e < kRows * kD; e += 32 * kFusedWarps) {
-      float s = 0.f;
-#pragma unroll
-      for (int w = 0; w < kFusedWarps; ++w)
-        s += reinterpret_cast<const float*>(smem + ClusterSmem::kPartOff + w * kFusedSlotBytes)[e];
-      red[e] = s;
-      m = fmaxf(m, fabsf(s));
-    }
-    if (exchange) {
-      // Publish `red` to the peers, then sum the cluster's partials in rank order.
-      kf::fence_acq_rel_cluster();
-      kf::named_bar_sync(kFusedBar, 32 * kFusedWarps);
+    if (exchange && k > 0) {
+      // Every thread has also finished the previous unit's `tot` and receive area: re-arm both
+      // rounds for this unit, then tell the peers that they may push into them.
       if (threadIdx.x == 0) {
+        kf::mbar_arrive_expect_tx(xready1, bytes1);
+        kf::mbar_arrive_expect_tx(xready2, bytes2);
         for (int r = 0; r < cs; ++r)
-          if (r != rank) kf::mbar_arrive_cluster(kf::cluster_map(kf::smem_u32(xready), r));
+          if (r != rank) kf::mbar_arrive_cluster_relaxed(kf::cluster_map(kf::smem_u32(xdone), r));
       }
-      if (ok)
-        ok = __all_sync(0xffffffffu,
-                        kf::mbar_wait_cluster_or_abort(xready, k & 1, &g_sana_error, abort_flag));
-      m = 0.f;
-      const uint32_t red_addr = kf::smem_u32(red);
-      for (int e4 = threadIdx.x; e4 < kRows * kD / 4; e4 += 32 * kFusedWarps) {
-        float4 v[kFusedMaxCluster];
+      // ... and wait until every peer is done with its own (this CTA pushes into them below).
+      if (ok) ok = __all_sync(0xffffffffu, kf::mbar_wait_or_abort(xdone, (k - 1) & 1, &g_sana_error, abort_flag));
+    }
+    // Sum of the 16 partials in warp order, one 16-byte vector per thread, and max|B| for the
+    // fp16 scale.
+    float m = 0.f;
+    const int e4 = threadIdx.x;
+    float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (e4 < kXVec) {
 #pragma unroll
-        for (int r = 0; r < kFusedMaxCluster; ++r)
-          v[r] = (r < cs && ok) ? kf::ld_cluster_f4(kf::cluster_map(red_addr + e4 * 16, r))
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
-        float4 s = v[0];
-#pragma unroll
-        for (int r = 1; r < kFusedMaxCluster; ++r) {
-          if (r < cs) {
-            s.x += v[r].x;
-            s.y += v[r].y;
-            s.z += v[r].z;
-            s.w += v[r].w;
+      for (int w = 0; w < kFusedWarps; ++w) {
+        const float4 v = reinterpret_cast<const float4*>(smem + ClusterSmem::kPartOff + w * kFusedSlotBytes)[e4];
+        s4.x += v.x;
+        s4.y += v.y;
+        s4.z += v.z;
+        s4.w += v.w;
+      }
+    }
+    if (!exchange) {
+      if (e4 < kXVec) {
+        reinterpret_cast<float4*>(red)[e4] = s4;
+        m = fmaxf(fmaxf(fabsf(s4.x), fabsf(s4.y)), fmaxf(fabsf(s4.z), fabsf(s4.w)));
+      }
+    } else {
+      // Round 1 (reduce-scatter): each vector goes to the rank that owns it, into the slot of this
+      // rank. No fence: the bytes complete on the owner's own mbarrier, which its threads wait on.
+      const int owner = e4 / c4;
+      if (e4 < kXVec && owner != rank)
+        kf::st_async_f4(kf::cluster_map(kf::smem_u32(smem + ClusterSmem::kRecvOff) + (rank * c4 + e4 - owner * c4) * 16,
+                                        owner),
+                        s4, kf::cluster_map(kf::smem_u32(xready1), owner));
+      if (ok) ok = __all_sync(0xffffffffu, kf::mbar_wait_or_abort(xready1, k & 1, &g_sana_error, abort_flag));
+      // This rank's chunk summed over the ranks in rank order (the same additions in every CTA of
+      // the cluster), then round 2 (all-gather): the sums go into every peer's `tot`.
+      if (ok && e4 >= own0 && e4 < own1) {
+        float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int r = 0; r < cs; ++r) {
+          const float4 v = r == rank ? s4 : recv[r * c4 + e4 - own0];
+          if (r == 0) {
+            t = v;
+          } else {
+            t.x += v.x;
+            t.y += v.y;
+            t.z += v.z;
+            t.w += v.w;
           }
         }
-        reinterpret_cast<float4*>(tot)[e4] = s;
-        m = fmaxf(fmaxf(m, fmaxf(fabsf(s.x), fabsf(s.y))), fmaxf(fabsf(s.z), fabsf(s.w)));
+        reinterpret_cast<float4*>(tot)[e4] = t;
+        for (int r = 0; r < cs; ++r)
+          if (r != rank)
+            kf::st_async_f4(kf::cluster_map(kf::smem_u32(tot) + e4 * 16, r), t, kf::cluster_map(kf::smem_u32(xready2), r));
+      }
+      if (ok) ok = __all_sync(0xffffffffu, kf::mbar_wait_or_abort(xready2, k & 1, &g_sana_error, abort_flag));
+      kf::named_bar_sync(kFusedBar, 32 * kFusedWarps);  // this CTA's own chunk of `tot` is written
+      if (e4 < kXVec) {
+        const float4 t = reinterpret_cast<const float4*>(tot)[e4];
+        m = fmaxf(fmaxf(fabsf(t.x), fabsf(t.y)), fmaxf(fabsf(t.z), fabsf(t.w)));
       }
     }
     if (kFp16) {
@@ -1447,15 +1496,7 @@ sana_head_cluster(const __grid_constant__ CUtensorMap kv_map, const __grid_const
       if (lane == 0) atomicMax(&max_bits[parity], __float_as_uint(m));  // non-negative floats order as integers
     }
     kf::named_bar_sync(kFusedBar, 32 * kFusedWarps);
-    const float* vk = red;
-    if (exchange) {
-      // Every thread of this CTA has read the peers' `red`.
-      if (threadIdx.x == 0) {
-        for (int r = 0; r < cs; ++r)
-          if (r != rank) kf::mbar_arrive_cluster(kf::cluster_map(kf::smem_u32(xdone), r));
-      }
-      vk = tot;
-    }
+    const float* vk = exchange ? tot : red;
     const float scale = operand_scale(__uint_as_float(max_bits[parity]), kFp16);
     const float eps_s = eps * scale;
     // B fragments (K = q channel c, N = output row r: VK[r][c], r = 32 is ksum[c], rows 33..39 zero)
@@ -1564,9 +1605,8 @@ sana_head_cluster(const __grid_constant__ CUtensorMap kv_map, const __grid_const
     }
   }
   if (lane == 0) kf::tma_store_wait_read0();  // shared memory outlives the stores' reads
-  // Cluster form: this CTA's shared memory also outlives the peers' reads of its last `red`.
-  if (cs > 1 && k > 0 && threadIdx.x == 0)
-    (void)kf::mbar_wait_bounded(xdone, (k - 1) & 1, &g_sana_error);
+  // Cluster form: no peer reads this CTA's shared memory, and every peer push into it has
+  // completed (this CTA waited for all bytes of each unit); the last unit sends no `xdone`.
 }
 
 // ------------------------------------------------------------------------------------------
