@@ -975,6 +975,14 @@ static_assert(kFusedPartBytes <= kFusedSlotBytes && 2 * 2048 <= kFusedSlotBytes,
 // `full` can see a phase two fills old and no extra arrival can reach `empty`.
 static_assert(kFusedStages == kFusedWarps, "ring depth must equal the number of compute warps");
 
+// Index of element (r, c) of a [VK ; ksum] partial or sum in shared memory (33 rows of 32 fp32).
+// The warp partials are written, and the B fragments read, as float2 pairs by 8 rows x 4
+// column pairs per instruction; with plain 128-byte rows those 8 rows share banks (8-way
+// conflicts). XOR-ing column bits 3-4 with row bits 0-1 spreads them over all banks (two
+// wavefronts per instruction). The sums over partials and across a cluster are elementwise, so
+// they do not depend on the layout.
+__device__ __forceinline__ int part_idx(int r, int c) { return r * kD + (c ^ ((r & 3) << 3)); }
+
 // Byte offset of 16-byte chunk c of row r in a tile of 64-byte rows written with 64-byte swizzle.
 __device__ __forceinline__ uint32_t swz64(uint32_t row, uint32_t chunk) {
   return row * 64 + ((chunk ^ ((row >> 1) & 3)) << 4);
@@ -1113,12 +1121,12 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt) {
         const int r = mt * 16 + gid, c = nt * 8 + tig * 2;
-        *reinterpret_cast<float2*>(pw + r * kD + c) = make_float2(acc[mt][nt][0], acc[mt][nt][1]);
-        *reinterpret_cast<float2*>(pw + (r + 8) * kD + c) = make_float2(acc[mt][nt][2], acc[mt][nt][3]);
+        *reinterpret_cast<float2*>(pw + part_idx(r, c)) = make_float2(acc[mt][nt][0], acc[mt][nt][1]);
+        *reinterpret_cast<float2*>(pw + part_idx(r + 8, c)) = make_float2(acc[mt][nt][2], acc[mt][nt][3]);
       }
     if (tig == 0) {
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) pw[kD * kD + nt * 8 + gid] = ksum[nt];
+      for (int nt = 0; nt < 4; ++nt) pw[part_idx(kD, nt * 8 + gid)] = ksum[nt];
     }
     kf::named_bar_sync(kFusedBar, 32 * kFusedWarps);
     // Every compute thread is past the previous unit's read of the other word.
@@ -1154,8 +1162,9 @@ sana_head_fused(const __grid_constant__ CUtensorMap kv_map, const __grid_constan
           const int c = ks * 16 + tig * 2 + half * 8;
           float x0 = 0.f, x1 = 0.f;
           if (r <= kD) {
-            x0 = red[r * kD + c] * scale;
-            x1 = red[r * kD + c + 1] * scale;
+            const float2 x = *reinterpret_cast<const float2*>(red + part_idx(r, c));  // c even
+            x0 = x.x * scale;
+            x1 = x.y * scale;
           }
           bhi[ks][nt][half] = kf::Mma<T>::from_f2(x0, x1);
           const float2 hf = kf::Mma<T>::to_f2(bhi[ks][nt][half]);
@@ -1411,12 +1420,12 @@ sana_head_cluster(const __grid_constant__ CUtensorMap kv_map, const __grid_const
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt) {
         const int r = mt * 16 + gid, c = nt * 8 + tig * 2;
-        *reinterpret_cast<float2*>(pw + r * kD + c) = make_float2(acc[mt][nt][0], acc[mt][nt][1]);
-        *reinterpret_cast<float2*>(pw + (r + 8) * kD + c) = make_float2(acc[mt][nt][2], acc[mt][nt][3]);
+        *reinterpret_cast<float2*>(pw + part_idx(r, c)) = make_float2(acc[mt][nt][0], acc[mt][nt][1]);
+        *reinterpret_cast<float2*>(pw + part_idx(r + 8, c)) = make_float2(acc[mt][nt][2], acc[mt][nt][3]);
       }
     if (tig == 0) {
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) pw[kD * kD + nt * 8 + gid] = ksum[nt];
+      for (int nt = 0; nt < 4; ++nt) pw[part_idx(kD, nt * 8 + gid)] = ksum[nt];
     }
     kf::named_bar_sync(kFusedBar, 32 * kFusedWarps);
     // Every compute thread is past the previous unit's read of the other word.
@@ -1512,8 +1521,9 @@ sana_head_cluster(const __grid_constant__ CUtensorMap kv_map, const __grid_const
           const int c = ks * 16 + tig * 2 + half * 8;
           float x0 = 0.f, x1 = 0.f;
           if (r <= kD) {
-            x0 = vk[r * kD + c] * scale;
-            x1 = vk[r * kD + c + 1] * scale;
+            const float2 x = *reinterpret_cast<const float2*>(vk + part_idx(r, c));  // c even
+            x0 = x.x * scale;
+            x1 = x.y * scale;
           }
           bhi[ks][nt][half] = kf::Mma<T>::from_f2(x0, x1);
           const float2 hf = kf::Mma<T>::to_f2(bhi[ks][nt][half]);
