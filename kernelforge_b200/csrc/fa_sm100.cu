@@ -66,7 +66,10 @@ template <int D, bool kTan = true, int BN = kBN> struct Cfg {
   // The forward at D = 128 takes three K stages (the one-pass kernel's three score buffers need
   // as many: a buffer's "free" arrival for tile j + 3 lands in that tile's K stage).
   static constexpr int kKStages = D == 64 ? 4 : (D == 128 && !kTan ? 3 : 2);
-  static constexpr int kVStages = D == 64 ? 4 : (D == 256 && kTan ? 1 : 2);
+  // The V ring needs as many stages as the one-pass kernel has score buffers: the softmax
+  // threads' arrival for tile j lands on V stage j % kVStages, and what lets them reach tile
+  // j + NB (the output MMAs of tile j) proves only that the V phases before tile j completed.
+  static constexpr int kVStages = D == 64 ? 4 : (D == 128 && !kTan ? 3 : (D == 256 && kTan ? 1 : 2));
   static constexpr int kKOffset = kTan ? 2 * kQBytes : kQBytes;
   static constexpr int kVOffset = kKOffset + kKStages * kStageBytes;
   static constexpr int kBarOffset = kVOffset + kVStages * kStageBytes;
@@ -555,6 +558,8 @@ fa_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
   using C = Cfg<D, kJvp>;
   constexpr int NB = FusedCols<D, kJvp>::kBufs;  // score buffers
   static_assert(NB <= C::kKStages, "a buffer's free arrival for tile j + NB lands in that tile's K stage");
+  static_assert(NB <= C::kVStages, "the softmax threads reach tile j + NB only after tile j's output MMAs: "
+                "the V phase they arrive on must be the one of their own tile");
   static_assert(D <= 128 || !kJvp, "D = 256 tensor memory holds the forward's accumulator only");
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ uint8_t smem_raw[];
