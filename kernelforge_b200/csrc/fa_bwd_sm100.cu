@@ -609,7 +609,9 @@ fa_bwd_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid
   const TileWalk walk{kvh * group, qt_first, max(qt_count, 1), TILE};
 
   if (threadIdx.x == 0) {
-    bars.init(4);  // a buffer is free once each dQ warp has read its dQ^T rows
+    // A score buffer is free once each dQ warp has read its dQ^T rows and the dV / dK MMAs that
+    // read its P^T and dS^T have completed (the accumulating thread's commit).
+    bars.init(5);
     kf::fence_mbar_init();
   }
   if (warp == kMmaWarp) kf::tc::tmem_alloc(bars.tmem_slot, kTmemCols);
@@ -650,6 +652,8 @@ fa_bwd_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid
       // second block is V's.
       const uint64_t kt_desc = kf::tc::desc_sw128(kf::smem_u32(smem), kRows * 128, 1024);
       uint32_t v_started = 0, k_started = 0;
+      // Score buffers start free: this thread's share of the first kBufs tiles' buffer arrivals.
+      for (int t = 0; t < kBufs; ++t) kf::mbar_arrive(&bars.ring_full[t % C::kStages]);
       bool ok = wait_relaxed(bars.stat_full, 0, abort);
       if (!ok) note_gave_up(3, -1);
       for (int t = 0; ok && t < ntiles; ++t) {
@@ -661,10 +665,8 @@ fa_bwd_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid
         kf::tc::fence_after_sync();
         const uint32_t q_addr = kf::smem_u32(smem + C::kRingOffset + st * 2 * C::kTileBytes);
         const uint32_t s_col = tmem + kBuf + C::kBufCols * buf;
-        issue_accumulate<TILE, true>(tmem + kDv, s_col, q_addr + C::kTileBytes, idA, v_started);  // dV += P^T dO
-        issue_accumulate<TILE, true>(tmem + kDk, s_col + G / 2, q_addr, idA, k_started);          // dK += dS^T Q
-        kf::tc::commit(&bars.ring_empty[st]);
-        // dQ^T = K^T dS^T over the block's 128 keys, 16 keys (2048 bytes of both operands) a step.
+        // dQ^T = K^T dS^T first, over the block's 128 keys (16 keys, 2048 bytes of both operands, a
+        // step): the dQ warps read it out while the dV / dK MMAs run.
         const uint64_t ds_desc =
             kf::tc::desc_sw128(kf::smem_u32(smem + C::kDsOffset + buf * C::kDsBytes), kRows * 128, 1024);
 #pragma unroll
@@ -672,6 +674,10 @@ fa_bwd_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid
           kf::tc::mma_ss(s_col + TILE, kf::tc::desc_advance(kt_desc, kk * 2048),
                          kf::tc::desc_advance(ds_desc, kk * 2048), idQ, kk > 0);
         kf::tc::commit(&bars.dq_full[buf]);
+        issue_accumulate<TILE, true>(tmem + kDv, s_col, q_addr + C::kTileBytes, idA, v_started);  // dV += P^T dO
+        issue_accumulate<TILE, true>(tmem + kDk, s_col + G / 2, q_addr, idA, k_started);          // dK += dS^T Q
+        kf::tc::commit(&bars.ring_empty[st]);
+        kf::tc::commit(&bars.ring_full[(t + kBufs) % C::kStages]);  // P^T, dS^T read: buffer free for t + kBufs
       }
       kf::tc::commit(bars.acc_full);
       kf::tc::commit(bars.drain);
