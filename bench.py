@@ -1154,7 +1154,8 @@ def fa_e2e(args, dist, parts, saved, fused, global_flops):
             pipe.chunk(list(zip(ds, hs)), lambda ds=ds: compute(ds), lambda t, ho=ho: [(ho, t)])
         pipe.end()
 
-    steps = max(3, min(args.steps, args.e2e_steps))
+    # A step is a few ms: four times the e2e steps keep one host-side stall from dominating.
+    steps = max(3, min(args.steps, 4 * args.e2e_steps))
     ems, _ = time_region(step, steps, args.warmup, dist)
     return {"value": round(global_flops / (ems / 1e3) / 1e12, 2), "unit": "TFLOP/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps, "ms_per_step": round(ems, 3),
@@ -1354,7 +1355,7 @@ def fa_bwd_e2e(args, dist, parts, scale, global_flops):
                        lambda res, hg=hg: list(zip(hg, res)))
         pipe.end()
 
-    steps = max(3, min(args.steps, args.e2e_steps))
+    steps = max(3, min(args.steps, 4 * args.e2e_steps))  # a few ms a step, as for the forward-mode calls
     ems, _ = time_region(step, steps, args.warmup, dist)
     return {"value": round(global_flops / (ems / 1e3) / 1e12, 2), "unit": "TFLOP/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps, "ms_per_step": round(ems, 3),
