@@ -320,10 +320,14 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       : "memory");
 }
 
-// dst[0] += v at L2 (no return value; the 32 lanes of a warp on consecutive floats make one
-// 128-byte reduction).
-__device__ __forceinline__ void red_add_f32(float* dst, float v) {
-  asm volatile("red.global.add.f32 [%0], %1;" ::"l"(__cvta_generic_to_global(dst)), "f"(v) : "memory");
+// Tensor reduction shared -> global through TMA: the box at (c0, c1) of the 2-D fp32 map gets the
+// shared tile added to it, at L2. Completion is tracked by the issuing thread's bulk group
+// (tma_store_wait_read0 before the tile's shared memory is rewritten).
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
 }
 
 // Programmatic dependent launch: the primary grid lets its dependent grid start launching;
